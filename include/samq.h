@@ -1,0 +1,164 @@
+/*
+ * samq.h -- C ABI of the B200 (sm_100a) quantized-linear path of SAM.cpp.
+ *
+ * This library replaces, for the quantized linears of SAM 3, the GGML CUDA
+ * backend that SAM.cpp reaches through ggml_backend_sched_graph_compute
+ * (src/runtime/ggml/workspace.hpp:163) -> ggml_cuda_mul_mat -> MMQ/MMVQ with
+ * Q8_1 activation staging (cmake/patches/ggml-native-activation.patch:78-86).
+ * The ABI follows the convention of SAM.cpp's private Q8-RHS extension
+ * (cmake/patches/ggml-native-activation.patch:12-26, looked up by name in
+ * src/runtime/ggml/backends/cuda_activation.hpp:22-25): plain extern "C",
+ * versioned `_v1` symbols, info structs whose first field is `version`.
+ * Differences: every call returns a status code instead of bool, and a
+ * thread-local message explains the last failure.
+ *
+ * Conventions
+ *   - GGML mul_mat(W, X) semantics (src/models/sam3/ops.hpp:40-45): W is
+ *     [n][k] packed GGUF rows (one row per output channel), X is [m][k] f32
+ *     row-major with row stride ldx (elements), Y is [m][n] f32 row-major with
+ *     row stride ldy: Y[i][j] = sum_t W[j][t] * X[i][t] (+ bias[j]).
+ *   - Type ids are GGML's (ggml_type): Q8_0 = 8, Q4_K = 12, Q5_K = 13,
+ *     Q6_K = 14; activation staging Q8_1 = 9.
+ *   - Device pointers are owned by the caller, as is the CUDA stream
+ *     (`stream` is a cudaStream_t; NULL is the legacy default stream).  The
+ *     library owns repacked weights and per-stream scratch memory.
+ *   - Calls that share a stream are ordered by it; calls on one weights
+ *     handle from several host threads must be serialized by the caller (the
+ *     reference serializes sessions with execution_mutex,
+ *     src/models/sam3/image_session.hpp:34,57).
+ *   - No C++ exception crosses this boundary.
+ */
+#ifndef SAMQ_H
+#define SAMQ_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define SAMQ_ABI_VERSION 1
+
+typedef enum samq_status {
+    SAMQ_OK = 0,
+    SAMQ_ERR_INVALID_ARGUMENT = 1, /* shape, stride, alignment or type rejected */
+    SAMQ_ERR_UNSUPPORTED = 2,      /* device is not sm_100 or the library lacks its code */
+    SAMQ_ERR_CUDA = 3,             /* a CUDA runtime call failed (message has the name) */
+    SAMQ_ERR_OUT_OF_MEMORY = 4,
+    SAMQ_ERR_RANGE = 5,            /* activations non-finite or beyond the f16 operand range */
+    SAMQ_ERR_TIMEOUT = 6,          /* a bounded device-side wait gave up */
+    SAMQ_ERR_PAYLOAD = 7           /* packed weight block has a non-finite scale */
+} samq_status;
+
+enum {
+    SAMQ_TYPE_Q8_0 = 8,
+    SAMQ_TYPE_Q8_1 = 9,
+    SAMQ_TYPE_Q4_K = 12,
+    SAMQ_TYPE_Q5_K = 13,
+    SAMQ_TYPE_Q6_K = 14
+};
+
+enum {
+    SAMQ_EPILOGUE_NONE = 0,
+    SAMQ_EPILOGUE_GELU_ERF = 1 /* ggml_gelu_erf after the bias (src/models/sam3/vision.hpp:234-236) */
+};
+
+typedef struct samq_weights samq_weights;
+
+/* Replaces the device checks of make_cuda_backend
+ * (src/runtime/ggml/backends/cuda.hpp:156-189). */
+struct samq_capabilities_v1 {
+    uint32_t version;            /* = 1 */
+    int32_t device;
+    int32_t cc_major, cc_minor;  /* sm_100 required */
+    int32_t sm_count;
+    uint64_t global_memory_bytes;
+    uint64_t max_shared_memory_per_block;
+    char name[256];
+};
+
+/* Mirrors ggml_sam_q8_rhs_info (cmake/patches/ggml-native-activation.patch:10-16). */
+struct samq_counters_v1 {
+    uint32_t version;            /* = 1 */
+    uint32_t path;               /* 1: tcgen05 GEMM over packet weights */
+    uint64_t launches;           /* GEMM launches recorded on this handle */
+    uint64_t payload_bytes;      /* bytes of the last activation staging buffer */
+    uint64_t allocation_bytes;   /* bytes of the scratch allocation that held it */
+    uint64_t weight_bytes;       /* device bytes owned by the handle */
+};
+
+/* Thread-local text of the last failure on the calling thread ("" if none). */
+const char* samq_last_error_v1(void);
+
+/* Select and check `device`; fails with SAMQ_ERR_UNSUPPORTED unless it is an
+ * sm_100 part.  Replaces ggml_backend_reg_by_name("CUDA") + device init
+ * (src/runtime/ggml/backends/cuda.hpp:159-165). */
+samq_status samq_init_v1(int device);
+samq_status samq_capabilities_v1(int device, struct samq_capabilities_v1* info);
+
+/* K4: load-time repack.  `gguf_rows` is HOST memory holding n packed rows of
+ * k elements in GGUF layout (Q8_0 34 B / 32, Q4_K 144 B / 256, Q5_K 176 B /
+ * 256, Q6_K 210 B / 256).  Validates every block scale is finite
+ * (src/models/sam3/weights.hpp:384-425) and repacks on the device into the
+ * library's packet layout.  Replaces ggml_backend_alloc_ctx_tensors +
+ * ggml_backend_tensor_set of a WEIGHTS buffer (src/models/sam3/model.hpp:114-133). */
+samq_status samq_weights_create_v1(int device, int type, int64_t k, int64_t n,
+                                   const void* gguf_rows, size_t bytes, void* stream,
+                                   samq_weights** out);
+samq_status samq_weights_destroy_v1(samq_weights* weights);
+/* Inverse repack into host GGUF rows (bit-exact round trip), synchronous. */
+samq_status samq_weights_export_v1(const samq_weights* weights, void* gguf_rows, size_t bytes);
+/* Device address and size of the packet layout (read-only). */
+samq_status samq_weights_packets_v1(const samq_weights* weights, const void** packets, size_t* bytes);
+
+/* K1: GGML CUDA quantize_q8_1 staging (MMVQ, 36 B per 32 values: f16 d,
+ * f16 sum, int8[32]); x is [rows][ld] f32 on the device, out holds
+ * rows * k/32 blocks.  Contract: tools/validation/verify_q8_rhs_staging.py:24-83. */
+samq_status samq_quantize_q8_1_v1(const float* x, int64_t rows, int64_t k, int64_t ld,
+                                  void* out, void* stream);
+/* K1: GGML CUDA quantize_mmq_q8_1 D4 staging (144 B per 128 values: f32 d[4],
+ * int8[128]; width zero-padded to 512; blocks stored [k/128][rows]).
+ * Contract: tools/validation/verify_q8_mmq_rhs_staging.py:24-67,
+ * tests/runtime/ggml/test_cuda_q8_mmq_scale.cpp:33-93. */
+size_t samq_mmq_d4_bytes_v1(int64_t rows, int64_t k);
+samq_status samq_quantize_mmq_q8_1_v1(const float* x, int64_t rows, int64_t k, int64_t ld,
+                                      void* out, void* stream);
+
+/* K1 + K2: Y = gelu?(X . W^T + bias).  Activations are staged exactly as the
+ * Q8_1 rule above, then multiplied on the tcgen05 tensor cores with f32
+ * accumulation.  Replaces the GGML_OP_MUL_MAT node of sam3_channel_projection
+ * (src/models/sam3/ops.hpp:40-45) and the text/decoder linears.  bias may be
+ * NULL.  ldx % 4 == 0 and ldy % 4 == 0 (16-byte rows). */
+samq_status samq_linear_v1(const samq_weights* weights, const float* x, int64_t m, int64_t ldx,
+                           const float* bias, int epilogue, float* y, int64_t ldy, void* stream);
+/* K2 over already-staged activations: `x_q8_1` holds m * k/32 Q8_1 blocks as
+ * written by samq_quantize_q8_1_v1. */
+samq_status samq_linear_q8_1_v1(const samq_weights* weights, const void* x_q8_1, int64_t m,
+                                const float* bias, int epilogue, float* y, int64_t ldy, void* stream);
+
+/* K1 alone: stage f32 activations into the tensor-core A operand, f16
+ * [rows][k] row-major, each value f16(f32(d) * q) of its Q8_1 block (the
+ * rule of samq_quantize_q8_1_v1).  samq_linear_v1 == this + samq_linear_f16_v1. */
+samq_status samq_stage_f16_v1(const float* x, int64_t rows, int64_t k, int64_t ld, void* out_f16, void* stream);
+/* K2 alone over f16 activations [m][ldx] (ldx % 8 == 0, 16-byte aligned rows).
+ * Same product as the reference's F16 compute mode for a quantized weight
+ * (src/runtime/ggml/backends/cuda.hpp:177-186 selects F16 operands). */
+samq_status samq_linear_f16_v1(const samq_weights* weights, const void* x_f16, int64_t m, int64_t ldx,
+                               const float* bias, int epilogue, float* y, int64_t ldy, void* stream);
+
+/* Counters of a handle.  Mirrors ggml_cuda_sam_q8_rhs_query_v1
+ * (cmake/patches/ggml-native-activation.patch:34-42). */
+samq_status samq_query_v1(const samq_weights* weights, struct samq_counters_v1* out);
+
+/* Synchronize `stream` and report device-side findings recorded since the
+ * last call on `device`: SAMQ_ERR_RANGE for non-finite / out-of-range
+ * activations, SAMQ_ERR_TIMEOUT for a bounded wait that gave up.  Clears them.
+ * Replaces the reference's post-compute RHS range check
+ * (cmake/patches/ggml-native-activation.patch:148-171). */
+samq_status samq_check_v1(int device, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

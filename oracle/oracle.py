@@ -1,0 +1,224 @@
+"""ctypes binding of the CPU oracle (test infrastructure only).
+
+Only tests/, __graft_entry__.smoke() and bench.py's CPU legs import this
+module; it is the checker, never the measured or shipped path.  Every function
+wraps one entry point of samq_oracle.c, which cites the reference file/line it
+restates.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import subprocess
+from pathlib import Path
+
+import numpy as np
+
+HERE = Path(__file__).resolve().parent
+LIB_PATH = HERE / "libsamq_oracle.so"
+
+Q8_0, Q8_1, Q4_K, Q5_K, Q6_K, Q8_K = 8, 9, 12, 13, 14, 15
+TYPE_NAMES = {Q8_0: "Q8_0", Q4_K: "Q4_K", Q5_K: "Q5_K", Q6_K: "Q6_K"}
+NAME_TYPES = {v: k for k, v in TYPE_NAMES.items()}
+EPILOGUE_NONE, EPILOGUE_GELU_ERF = 0, 1
+
+_lib = None
+
+
+def build() -> Path:
+    """Compile the oracle with its Makefile (gcc + OpenMP)."""
+    subprocess.run(["make", "-C", str(HERE), "-s"], check=True)
+    return LIB_PATH
+
+
+def lib() -> ctypes.CDLL:
+    global _lib
+    if _lib is None:
+        if not LIB_PATH.exists():
+            build()
+        _lib = ctypes.CDLL(str(LIB_PATH))
+        i64, i32, vp = ctypes.c_int64, ctypes.c_int, ctypes.c_void_p
+        sig = {
+            "oracle_block_elements": (i64, [i32]),
+            "oracle_block_bytes": (i64, [i32]),
+            "oracle_row_bytes": (i64, [i32, i64]),
+            "oracle_f32_to_f16": (ctypes.c_uint16, [ctypes.c_float]),
+            "oracle_f16_to_f32": (ctypes.c_float, [ctypes.c_uint16]),
+            "oracle_quantize_q8_0": (i32, [vp, i64, vp]),
+            "oracle_quantize_kquant": (i32, [i32, vp, i64, vp]),
+            "oracle_dequantize": (i32, [i32, vp, i64, vp]),
+            "oracle_quantize_q8_1": (i32, [vp, i64, i64, i64, vp]),
+            "oracle_mmq_d4_bytes": (i64, [i64, i64]),
+            "oracle_quantize_mmq_d4": (i32, [vp, i64, i64, i64, vp]),
+            "oracle_act_f16": (i32, [vp, i64, i64, i64, vp]),
+            "oracle_q8_1_decode": (i32, [vp, i64, i64, vp]),
+            "oracle_quantize_q8_k": (i32, [vp, i64, vp]),
+            "oracle_packet_code_bytes": (i64, [i32]),
+            "oracle_packet_bytes": (i64, [i32]),
+            "oracle_packets_size": (i64, [i32, i64, i64]),
+            "oracle_pack_packets": (i32, [i32, i64, i64, vp, vp]),
+            "oracle_unpack_packets": (i32, [i32, i64, i64, vp, vp]),
+            "oracle_weight_f16": (i32, [i32, i64, i64, vp, vp]),
+            "oracle_gemm_f64": (i32, [vp, vp, i64, i64, i64, vp, i32, vp, i32]),
+            "oracle_gemm_f16_f64": (i32, [vp, vp, i64, i64, i64, vp, i32, vp, i32]),
+            "oracle_cpu_linear": (i32, [i32, vp, i64, i64, vp, i64, i64, vp, i32, vp, i64, i32]),
+            "oracle_cpu_has_vnni": (i32, []),
+        }
+        for name, (res, args) in sig.items():
+            fn = getattr(_lib, name)
+            fn.restype = res
+            fn.argtypes = args
+    return _lib
+
+
+def _ptr(a: np.ndarray | None):
+    return None if a is None else ctypes.c_void_p(a.ctypes.data)
+
+
+def _check(rc: int, what: str):
+    if rc != 0:
+        raise ValueError(f"oracle {what} rejected its arguments")
+
+
+def default_threads() -> int:
+    return max(1, len(os.sched_getaffinity(0)))
+
+
+def row_bytes(qtype: int, k: int) -> int:
+    rb = lib().oracle_row_bytes(qtype, k)
+    if rb < 0:
+        raise ValueError("width is not block aligned for this type")
+    return rb
+
+
+def quantize_q8_0(x: np.ndarray) -> np.ndarray:
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    out = np.empty(x.size // 32 * 34, dtype=np.uint8)
+    _check(lib().oracle_quantize_q8_0(_ptr(x), x.size, _ptr(out)), "quantize_q8_0")
+    return out
+
+
+def quantize_kquant(qtype: int, x: np.ndarray) -> np.ndarray:
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    out = np.empty(x.size // 256 * lib().oracle_block_bytes(qtype), dtype=np.uint8)
+    _check(lib().oracle_quantize_kquant(qtype, _ptr(x), x.size, _ptr(out)), "quantize_kquant")
+    return out
+
+
+def quantize(qtype: int, w: np.ndarray) -> np.ndarray:
+    """Pack an [n][k] f32 matrix row by row into GGUF blocks of `qtype`."""
+    w = np.ascontiguousarray(w, dtype=np.float32)
+    return quantize_q8_0(w) if qtype == Q8_0 else quantize_kquant(qtype, w)
+
+
+def dequantize(qtype: int, blocks: np.ndarray, n_elements: int) -> np.ndarray:
+    blocks = np.ascontiguousarray(blocks, dtype=np.uint8)
+    out = np.empty(n_elements, dtype=np.float32)
+    _check(lib().oracle_dequantize(qtype, _ptr(blocks), n_elements, _ptr(out)), "dequantize")
+    return out
+
+
+def quantize_q8_1(x: np.ndarray) -> np.ndarray:
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    rows, k = x.shape
+    out = np.empty(rows * (k // 32) * 36, dtype=np.uint8)
+    _check(lib().oracle_quantize_q8_1(_ptr(x), rows, k, k, _ptr(out)), "quantize_q8_1")
+    return out
+
+
+def quantize_mmq_d4(x: np.ndarray) -> np.ndarray:
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    rows, k = x.shape
+    out = np.empty(lib().oracle_mmq_d4_bytes(rows, k), dtype=np.uint8)
+    _check(lib().oracle_quantize_mmq_d4(_ptr(x), rows, k, k, _ptr(out)), "quantize_mmq_d4")
+    return out
+
+
+def act_f16(x: np.ndarray) -> np.ndarray:
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    rows, k = x.shape
+    out = np.empty((rows, k), dtype=np.uint16)
+    _check(lib().oracle_act_f16(_ptr(x), rows, k, k, _ptr(out)), "act_f16")
+    return out.view(np.float16)
+
+
+def q8_1_decode(q: np.ndarray, rows: int, k: int) -> np.ndarray:
+    q = np.ascontiguousarray(q, dtype=np.uint8)
+    out = np.empty((rows, k), dtype=np.float32)
+    _check(lib().oracle_q8_1_decode(_ptr(q), rows, k, _ptr(out)), "q8_1_decode")
+    return out
+
+
+def quantize_q8_k(x: np.ndarray) -> np.ndarray:
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    out = np.empty(x.size // 256 * 292, dtype=np.uint8)
+    _check(lib().oracle_quantize_q8_k(_ptr(x), x.size, _ptr(out)), "quantize_q8_k")
+    return out
+
+
+def packets_size(qtype: int, k: int, n: int) -> int:
+    return lib().oracle_packets_size(qtype, k, n)
+
+
+def pack_packets(qtype: int, k: int, n: int, rows: np.ndarray) -> np.ndarray:
+    rows = np.ascontiguousarray(rows, dtype=np.uint8)
+    out = np.empty(packets_size(qtype, k, n), dtype=np.uint8)
+    _check(lib().oracle_pack_packets(qtype, k, n, _ptr(rows), _ptr(out)), "pack_packets")
+    return out
+
+
+def unpack_packets(qtype: int, k: int, n: int, packets: np.ndarray) -> np.ndarray:
+    packets = np.ascontiguousarray(packets, dtype=np.uint8)
+    out = np.empty(n * row_bytes(qtype, k), dtype=np.uint8)
+    _check(lib().oracle_unpack_packets(qtype, k, n, _ptr(packets), _ptr(out)), "unpack_packets")
+    return out
+
+
+def weight_f16(qtype: int, k: int, n: int, rows: np.ndarray) -> np.ndarray:
+    rows = np.ascontiguousarray(rows, dtype=np.uint8)
+    out = np.empty((n, k), dtype=np.uint16)
+    _check(lib().oracle_weight_f16(qtype, k, n, _ptr(rows), _ptr(out)), "weight_f16")
+    return out.view(np.float16)
+
+
+def gemm_f64(w: np.ndarray, x: np.ndarray, bias=None, epilogue=EPILOGUE_NONE, threads=None) -> np.ndarray:
+    """Y = X . W^T with f64 accumulation over f32 (or f16) operands."""
+    n, k = w.shape
+    m = x.shape[0]
+    y = np.empty((m, n), dtype=np.float32)
+    b = None if bias is None else np.ascontiguousarray(bias, dtype=np.float32)
+    t = threads or default_threads()
+    if w.dtype == np.float16:
+        w16 = np.ascontiguousarray(w).view(np.uint16)
+        x16 = np.ascontiguousarray(x, dtype=np.float16).view(np.uint16)
+        rc = lib().oracle_gemm_f16_f64(_ptr(w16), _ptr(x16), m, n, k, _ptr(b), epilogue, _ptr(y), t)
+    else:
+        w32 = np.ascontiguousarray(w, dtype=np.float32)
+        x32 = np.ascontiguousarray(x, dtype=np.float32)
+        rc = lib().oracle_gemm_f64(_ptr(w32), _ptr(x32), m, n, k, _ptr(b), epilogue, _ptr(y), t)
+    _check(rc, "gemm")
+    return y
+
+
+def cpu_linear(qtype: int, rows: np.ndarray, k: int, n: int, x: np.ndarray, bias=None,
+               epilogue=EPILOGUE_NONE, threads=None, out=None) -> np.ndarray:
+    """Restated GGML CPU quantized mul_mat (+bias, +erf-GELU)."""
+    rows = np.ascontiguousarray(rows, dtype=np.uint8)
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    m = x.shape[0]
+    y = out if out is not None else np.empty((m, n), dtype=np.float32)
+    b = None if bias is None else np.ascontiguousarray(bias, dtype=np.float32)
+    rc = lib().oracle_cpu_linear(qtype, _ptr(rows), k, n, _ptr(x), m, k, _ptr(b), epilogue, _ptr(y), n,
+                                 threads or default_threads())
+    _check(rc, "cpu_linear")
+    return y
+
+
+def has_vnni() -> bool:
+    return bool(lib().oracle_cpu_has_vnni())
+
+
+def gelu_erf(v: np.ndarray) -> np.ndarray:
+    from math import erf, sqrt
+    f = np.vectorize(lambda t: 0.5 * t * (1.0 + erf(t / sqrt(2.0))))
+    return f(v.astype(np.float64)).astype(np.float32)

@@ -1,0 +1,425 @@
+// capi.cu -- the extern "C" boundary declared in include/samq.h.
+//
+// Every entry point validates its arguments, runs on the device that owns
+// the data (weights handle) or the current device, converts internal errors
+// into a samq_status and records a thread-local message; no exception
+// crosses the boundary (the reference converts codes to std::runtime_error
+// itself, src/runtime/ggml/workspace.hpp:174-177).
+#include <cuda_fp16.h>
+
+#include <cstdio>
+#include <cstring>
+#include <memory>
+#include <vector>
+
+#include "samq_internal.hpp"
+
+namespace samq {
+namespace {
+thread_local std::string g_last_error;
+std::mutex g_states_mutex;
+DeviceState* g_states[64] = {};
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+    static EncodeTiledFn fn = [] {
+        void* ptr = nullptr;
+        cudaDriverEntryPointQueryResult q{};
+        check_cuda(cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q),
+                   "cudaGetDriverEntryPoint(cuTensorMapEncodeTiled)");
+        if (!ptr || q != cudaDriverEntryPointSuccess) fail(SAMQ_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+        return reinterpret_cast<EncodeTiledFn>(ptr);
+    }();
+    return fn;
+}
+
+}  // namespace
+
+void fail(samq_status status, const std::string& message) { throw Error{status, message}; }
+
+void check_cuda(cudaError_t err, const char* what) {
+    if (err == cudaSuccess) return;
+    const samq_status status = err == cudaErrorMemoryAllocation ? SAMQ_ERR_OUT_OF_MEMORY : SAMQ_ERR_CUDA;
+    fail(status, std::string(what) + ": " + cudaGetErrorName(err) + " (" + cudaGetErrorString(err) + ")");
+}
+
+void set_last_error(const std::string& message) { g_last_error = message; }
+
+DeviceGuard::DeviceGuard(int device) {
+    check_cuda(cudaGetDevice(&previous), "cudaGetDevice");
+    if (previous != device) check_cuda(cudaSetDevice(device), "cudaSetDevice");
+}
+
+DeviceGuard::~DeviceGuard() {
+    int current = -1;
+    if (cudaGetDevice(&current) == cudaSuccess && current != previous && previous >= 0) cudaSetDevice(previous);
+}
+
+DeviceState& device_state(int device) {
+    if (device < 0 || device >= 64) fail(SAMQ_ERR_INVALID_ARGUMENT, "device index out of range");
+    std::lock_guard<std::mutex> lock(g_states_mutex);
+    if (g_states[device]) return *g_states[device];
+    int count = 0;
+    check_cuda(cudaGetDeviceCount(&count), "cudaGetDeviceCount");
+    if (device >= count) fail(SAMQ_ERR_INVALID_ARGUMENT, "device index is not visible");
+    cudaDeviceProp prop{};
+    check_cuda(cudaGetDeviceProperties(&prop, device), "cudaGetDeviceProperties");
+    if (prop.major != 10 || prop.minor != 0)
+        fail(SAMQ_ERR_UNSUPPORTED, std::string("samq kernels are built for sm_100a; device '") + prop.name +
+                                       "' is sm_" + std::to_string(prop.major * 10 + prop.minor));
+    DeviceGuard guard(device);
+    auto state = std::make_unique<DeviceState>();
+    state->device = device;
+    state->sm_count = prop.multiProcessorCount;
+    state->cc_major = prop.major;
+    state->cc_minor = prop.minor;
+    check_cuda(cudaMalloc(reinterpret_cast<void**>(&state->status), sizeof(DeviceStatus)), "cudaMalloc(status)");
+    check_cuda(cudaMemset(state->status, 0, sizeof(DeviceStatus)), "cudaMemset(status)");
+    g_states[device] = state.release();
+    return *g_states[device];
+}
+
+Scratch& scratch_for(DeviceState& state, cudaStream_t stream, size_t bytes) {
+    std::lock_guard<std::mutex> lock(state.mutex);
+    Scratch& s = state.scratch[stream];
+    if (s.bytes < bytes) {
+        if (s.ptr) {
+            // The old buffer may still be read by work queued on this stream.
+            check_cuda(cudaStreamSynchronize(stream), "cudaStreamSynchronize(scratch growth)");
+            check_cuda(cudaFree(s.ptr), "cudaFree(scratch)");
+            s.ptr = nullptr;
+            s.bytes = 0;
+        }
+        const size_t rounded = (bytes + (size_t(2) << 20) - 1) / (size_t(2) << 20) * (size_t(2) << 20);
+        check_cuda(cudaMalloc(&s.ptr, rounded), "cudaMalloc(scratch)");
+        s.bytes = rounded;
+    }
+    return s;
+}
+
+void encode_tensor_map_2d(CUtensorMap* map, CUtensorMapDataType dtype, const void* base, uint64_t inner,
+                          uint64_t outer, uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_outer,
+                          CUtensorMapSwizzle swizzle) {
+    const cuuint64_t dims[2] = {inner, outer};
+    const cuuint64_t strides[1] = {row_stride_bytes};
+    const cuuint32_t box[2] = {box_inner, box_outer};
+    const cuuint32_t elem_strides[2] = {1, 1};
+    const CUresult r = encode_fn()(map, dtype, 2, const_cast<void*>(base), dims, strides, box, elem_strides,
+                                   CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) fail(SAMQ_ERR_INVALID_ARGUMENT, "cuTensorMapEncodeTiled rejected a tensor (code " +
+                                                               std::to_string(static_cast<int>(r)) + ")");
+}
+
+namespace {
+
+template <class F>
+samq_status guarded(F&& body) {
+    try {
+        body();
+        g_last_error.clear();
+        return SAMQ_OK;
+    } catch (const Error& e) {
+        g_last_error = e.message;
+        return e.status;
+    } catch (const std::bad_alloc&) {
+        g_last_error = "host allocation failed";
+        return SAMQ_ERR_OUT_OF_MEMORY;
+    } catch (...) {
+        g_last_error = "unexpected internal failure";
+        return SAMQ_ERR_CUDA;
+    }
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+void require(bool condition, const char* message) {
+    if (!condition) fail(SAMQ_ERR_INVALID_ARGUMENT, message);
+}
+
+bool supported_type(int type) {
+    return type == SAMQ_TYPE_Q8_0 || type == SAMQ_TYPE_Q4_K || type == SAMQ_TYPE_Q5_K || type == SAMQ_TYPE_Q6_K;
+}
+
+int current_device() {
+    int device = 0;
+    check_cuda(cudaGetDevice(&device), "cudaGetDevice");
+    return device;
+}
+
+void release(samq_weights* w) {
+    if (!w) return;
+    if (w->device >= 0) {
+        int previous = -1;
+        cudaGetDevice(&previous);
+        cudaSetDevice(w->device);
+        if (w->packets) cudaFree(w->packets);
+        if (w->operand) cudaFree(w->operand);
+        if (previous >= 0) cudaSetDevice(previous);
+    }
+    delete w;
+}
+
+void check_activation_args(int64_t rows, int64_t k, int64_t ld, const void* x, const void* out) {
+    require(rows >= 0 && rows <= (int64_t(1) << 31), "rows out of range");
+    require(k > 0 && k % 32 == 0 && k <= (int64_t(1) << 20), "width must be a positive multiple of 32");
+    require(ld >= k && ld % 4 == 0, "row stride must be >= width and a multiple of 4 floats");
+    require(rows == 0 || (x && out), "null pointer");
+    require(rows == 0 || aligned16(x), "activation pointer must be 16-byte aligned");
+}
+
+}  // namespace
+}  // namespace samq
+
+using namespace samq;
+
+extern "C" {
+
+const char* samq_last_error_v1(void) { return g_last_error.c_str(); }
+
+samq_status samq_init_v1(int device) {
+    return guarded([&] { device_state(device); });
+}
+
+samq_status samq_capabilities_v1(int device, struct samq_capabilities_v1* info) {
+    return guarded([&] {
+        require(info != nullptr, "null info");
+        int count = 0;
+        check_cuda(cudaGetDeviceCount(&count), "cudaGetDeviceCount");
+        require(device >= 0 && device < count, "device index is not visible");
+        cudaDeviceProp prop{};
+        check_cuda(cudaGetDeviceProperties(&prop, device), "cudaGetDeviceProperties");
+        std::memset(info, 0, sizeof(*info));
+        info->version = 1;
+        info->device = device;
+        info->cc_major = prop.major;
+        info->cc_minor = prop.minor;
+        info->sm_count = prop.multiProcessorCount;
+        info->global_memory_bytes = prop.totalGlobalMem;
+        info->max_shared_memory_per_block = prop.sharedMemPerBlockOptin;
+        std::snprintf(info->name, sizeof(info->name), "%s", prop.name);
+    });
+}
+
+samq_status samq_weights_create_v1(int device, int type, int64_t k, int64_t n, const void* gguf_rows, size_t bytes,
+                                   void* stream_ptr, samq_weights** out) {
+    return guarded([&] {
+        require(out != nullptr, "null output handle");
+        *out = nullptr;
+        require(supported_type(type), "weight type must be Q8_0, Q4_K, Q5_K or Q6_K");
+        require(n > 0 && n <= (int64_t(1) << 24), "row count out of range");
+        const int64_t rb = row_bytes(type, k);
+        require(rb > 0, "width is not a whole number of blocks");
+        require(k % 32 == 0 && k <= (int64_t(1) << 20), "width out of range");
+        require(gguf_rows != nullptr && bytes == static_cast<size_t>(rb * n), "GGUF payload size differs from n rows");
+        DeviceState& state = device_state(device);
+        DeviceGuard guard(device);
+        cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
+        std::unique_ptr<samq_weights, void (*)(samq_weights*)> w(new samq_weights, release);
+        w->device = device;
+        w->type = type;
+        w->k = k;
+        w->n = n;
+        const int64_t chunks = (k + 63) / 64;
+        w->packet_bytes = static_cast<size_t>((n + 127) / 128 * chunks * packet_bytes(type));
+        w->operand_bytes = static_cast<size_t>(n * k) * sizeof(__half);
+        void* staging = nullptr;
+        uint32_t* bad = nullptr;
+        struct Cleanup {
+            void*& s;
+            uint32_t*& b;
+            ~Cleanup() {
+                if (s) cudaFree(s);
+                if (b) cudaFree(b);
+            }
+        } cleanup{staging, bad};
+        check_cuda(cudaMalloc(&staging, bytes), "cudaMalloc(weight staging)");
+        check_cuda(cudaMalloc(reinterpret_cast<void**>(&bad), sizeof(uint32_t)), "cudaMalloc(scale check)");
+        check_cuda(cudaMalloc(&w->packets, w->packet_bytes), "cudaMalloc(packets)");
+        check_cuda(cudaMalloc(reinterpret_cast<void**>(&w->operand), w->operand_bytes), "cudaMalloc(operand)");
+        check_cuda(cudaMemsetAsync(bad, 0, sizeof(uint32_t), stream), "cudaMemsetAsync");
+        check_cuda(cudaMemsetAsync(w->packets, 0, w->packet_bytes, stream), "cudaMemsetAsync(packets)");
+        check_cuda(cudaMemcpyAsync(staging, gguf_rows, bytes, cudaMemcpyHostToDevice, stream), "cudaMemcpyAsync(H2D)");
+        launch_gguf_to_packets(type, k, n, static_cast<const uint8_t*>(staging), static_cast<uint8_t*>(w->packets), bad,
+                               stream);
+        uint32_t bad_host = 0;
+        check_cuda(cudaMemcpyAsync(&bad_host, bad, sizeof(bad_host), cudaMemcpyDeviceToHost, stream),
+                   "cudaMemcpyAsync(D2H)");
+        check_cuda(cudaStreamSynchronize(stream), "cudaStreamSynchronize(repack)");
+        if (bad_host) fail(SAMQ_ERR_PAYLOAD, "packed weight has " + std::to_string(bad_host) + " non-finite block scales");
+        launch_packets_to_f16(type, k, n, static_cast<const uint8_t*>(w->packets), w->operand, stream);
+        check_cuda(cudaStreamSynchronize(stream), "cudaStreamSynchronize(expand)");
+        *out = w.release();
+    });
+}
+
+samq_status samq_weights_destroy_v1(samq_weights* weights) {
+    return guarded([&] { release(weights); });
+}
+
+samq_status samq_weights_export_v1(const samq_weights* w, void* gguf_rows, size_t bytes) {
+    return guarded([&] {
+        require(w != nullptr && gguf_rows != nullptr, "null argument");
+        const int64_t rb = row_bytes(w->type, w->k);
+        require(bytes == static_cast<size_t>(rb * w->n), "output size differs from n rows");
+        DeviceGuard guard(w->device);
+        void* rows = nullptr;
+        check_cuda(cudaMalloc(&rows, bytes), "cudaMalloc(export)");
+        struct Free {
+            void* p;
+            ~Free() { cudaFree(p); }
+        } free_rows{rows};
+        launch_packets_to_gguf(w->type, w->k, w->n, static_cast<const uint8_t*>(w->packets),
+                               static_cast<uint8_t*>(rows), nullptr);
+        check_cuda(cudaMemcpy(gguf_rows, rows, bytes, cudaMemcpyDeviceToHost), "cudaMemcpy(export)");
+    });
+}
+
+samq_status samq_weights_packets_v1(const samq_weights* w, const void** packets, size_t* bytes) {
+    return guarded([&] {
+        require(w != nullptr && packets != nullptr && bytes != nullptr, "null argument");
+        *packets = w->packets;
+        *bytes = w->packet_bytes;
+    });
+}
+
+samq_status samq_quantize_q8_1_v1(const float* x, int64_t rows, int64_t k, int64_t ld, void* out, void* stream) {
+    return guarded([&] {
+        check_activation_args(rows, k, ld, x, out);
+        require(rows == 0 || (reinterpret_cast<uintptr_t>(out) & 3u) == 0, "output must be 4-byte aligned");
+        DeviceState& state = device_state(current_device());
+        launch_act_f16(x, rows, k, ld, nullptr, static_cast<uint8_t*>(out), state.status,
+                       static_cast<cudaStream_t>(stream));
+    });
+}
+
+size_t samq_mmq_d4_bytes_v1(int64_t rows, int64_t k) {
+    if (rows < 0 || k <= 0) return 0;
+    const int64_t padded = (k + 511) / 512 * 512;
+    return static_cast<size_t>(rows * (padded / 128) * 144);
+}
+
+samq_status samq_quantize_mmq_q8_1_v1(const float* x, int64_t rows, int64_t k, int64_t ld, void* out, void* stream) {
+    return guarded([&] {
+        check_activation_args(rows, k, ld, x, out);
+        require(rows == 0 || aligned16(out), "output must be 16-byte aligned");
+        device_state(current_device());
+        launch_mmq_d4(x, rows, k, ld, static_cast<uint8_t*>(out), static_cast<cudaStream_t>(stream));
+    });
+}
+
+static void check_linear_args(const samq_weights* w, int64_t m, const float* bias, int epilogue, const float* y,
+                              int64_t ldy) {
+    require(w != nullptr, "null weights");
+    require(m >= 0 && m <= (int64_t(1) << 31), "row count out of range");
+    require(epilogue == SAMQ_EPILOGUE_NONE || epilogue == SAMQ_EPILOGUE_GELU_ERF, "unknown epilogue");
+    require(ldy >= w->n && ldy % 4 == 0, "output row stride must be >= n and a multiple of 4 floats");
+    require(m == 0 || (y != nullptr && aligned16(y)), "output pointer must be 16-byte aligned");
+    (void)bias;
+}
+
+samq_status samq_linear_v1(const samq_weights* w, const float* x, int64_t m, int64_t ldx, const float* bias,
+                           int epilogue, float* y, int64_t ldy, void* stream_ptr) {
+    return guarded([&] {
+        check_linear_args(w, m, bias, epilogue, y, ldy);
+        check_activation_args(m, w->k, ldx, x, y);
+        if (m == 0) return;
+        DeviceGuard guard(w->device);
+        DeviceState& state = device_state(w->device);
+        cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
+        const size_t a_bytes = static_cast<size_t>(m * w->k) * sizeof(__half);
+        Scratch& scratch = scratch_for(state, stream, a_bytes);
+        __half* a = static_cast<__half*>(scratch.ptr);
+        launch_act_f16(x, m, w->k, ldx, a, nullptr, state.status, stream);
+        launch_gemm_f16(a, w->k, w->operand, m, w->n, w->k, bias, epilogue, y, ldy, state, stream);
+        const_cast<samq_weights*>(w)->launches.fetch_add(1);
+        const_cast<samq_weights*>(w)->payload_bytes.store(a_bytes);
+        const_cast<samq_weights*>(w)->allocation_bytes.store(scratch.bytes);
+    });
+}
+
+samq_status samq_linear_q8_1_v1(const samq_weights* w, const void* x_q8_1, int64_t m, const float* bias, int epilogue,
+                                float* y, int64_t ldy, void* stream_ptr) {
+    return guarded([&] {
+        check_linear_args(w, m, bias, epilogue, y, ldy);
+        if (m == 0) return;
+        require(x_q8_1 != nullptr && (reinterpret_cast<uintptr_t>(x_q8_1) & 3u) == 0,
+                "Q8_1 activations must be 4-byte aligned");
+        DeviceGuard guard(w->device);
+        DeviceState& state = device_state(w->device);
+        cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
+        const size_t a_bytes = static_cast<size_t>(m * w->k) * sizeof(__half);
+        Scratch& scratch = scratch_for(state, stream, a_bytes);
+        __half* a = static_cast<__half*>(scratch.ptr);
+        launch_q8_1_to_f16(static_cast<const uint8_t*>(x_q8_1), m, w->k, a, state.status, stream);
+        launch_gemm_f16(a, w->k, w->operand, m, w->n, w->k, bias, epilogue, y, ldy, state, stream);
+        const_cast<samq_weights*>(w)->launches.fetch_add(1);
+        const_cast<samq_weights*>(w)->payload_bytes.store(static_cast<uint64_t>(m * (w->k / 32) * 36));
+        const_cast<samq_weights*>(w)->allocation_bytes.store(scratch.bytes);
+    });
+}
+
+samq_status samq_stage_f16_v1(const float* x, int64_t rows, int64_t k, int64_t ld, void* out_f16, void* stream) {
+    return guarded([&] {
+        check_activation_args(rows, k, ld, x, out_f16);
+        require(rows == 0 || aligned16(out_f16), "output must be 16-byte aligned");
+        DeviceState& state = device_state(current_device());
+        launch_act_f16(x, rows, k, ld, static_cast<__half*>(out_f16), nullptr, state.status,
+                       static_cast<cudaStream_t>(stream));
+    });
+}
+
+samq_status samq_linear_f16_v1(const samq_weights* w, const void* x_f16, int64_t m, int64_t ldx, const float* bias,
+                               int epilogue, float* y, int64_t ldy, void* stream_ptr) {
+    return guarded([&] {
+        check_linear_args(w, m, bias, epilogue, y, ldy);
+        if (m == 0) return;
+        require(x_f16 != nullptr && aligned16(x_f16), "f16 activations must be 16-byte aligned");
+        require(ldx >= w->k && ldx % 8 == 0, "f16 row stride must be >= k and a multiple of 8");
+        DeviceGuard guard(w->device);
+        DeviceState& state = device_state(w->device);
+        launch_gemm_f16(static_cast<const __half*>(x_f16), ldx, w->operand, m, w->n, w->k, bias, epilogue, y, ldy,
+                        state, static_cast<cudaStream_t>(stream_ptr));
+        const_cast<samq_weights*>(w)->launches.fetch_add(1);
+    });
+}
+
+samq_status samq_query_v1(const samq_weights* w, struct samq_counters_v1* out) {
+    return guarded([&] {
+        require(w != nullptr && out != nullptr, "null argument");
+        std::memset(out, 0, sizeof(*out));
+        out->version = 1;
+        out->path = 1;
+        out->launches = w->launches.load();
+        out->payload_bytes = w->payload_bytes.load();
+        out->allocation_bytes = w->allocation_bytes.load();
+        out->weight_bytes = w->packet_bytes + w->operand_bytes;
+    });
+}
+
+samq_status samq_check_v1(int device, void* stream) {
+    samq_status found = SAMQ_OK;
+    const samq_status rc = guarded([&] {
+        DeviceState& state = device_state(device);
+        DeviceGuard guard(device);
+        check_cuda(cudaStreamSynchronize(static_cast<cudaStream_t>(stream)), "cudaStreamSynchronize(check)");
+        DeviceStatus host{};
+        check_cuda(cudaMemcpy(&host, state.status, sizeof(host), cudaMemcpyDeviceToHost), "cudaMemcpy(status)");
+        check_cuda(cudaMemset(state.status, 0, sizeof(DeviceStatus)), "cudaMemset(status)");
+        if (host.flags & kStatusTimeout) {
+            found = SAMQ_ERR_TIMEOUT;
+            fail(SAMQ_ERR_TIMEOUT, "a device-side wait timed out at site " + std::to_string(host.timeout_site));
+        }
+        if (host.flags & kStatusRange) {
+            found = SAMQ_ERR_RANGE;
+            fail(SAMQ_ERR_RANGE, std::to_string(host.range_blocks) +
+                                     " activation warps held non-finite or out-of-range values");
+        }
+    });
+    return rc != SAMQ_OK ? rc : found;
+}
+
+}  // extern "C"

@@ -1,0 +1,263 @@
+// gemm.cu -- K2: Y = epilogue(A . B^T + bias) on the sm_100a tensor cores.
+//
+// A is the f16 activation operand staged by K1 ([m][k], row-major), B the f16
+// weight operand expanded from the K4 packets ([n][k], row-major); Y is f32
+// [m][n] with row stride ldy.  This is GGML mul_mat(W, X) with W = B and
+// X = A (src/models/sam3/ops.hpp:40-45), with the bias add and ggml_gelu_erf
+// of the ViT MLP fused (src/models/sam3/vision.hpp:234-236).
+//
+// Persistent, warp-specialised kernel, one CTA per SM (192 threads):
+//   warp 0     TMA producer: 128x64 A and BNx64 B tiles, 128-byte swizzle,
+//              into a STAGES-deep shared-memory ring (full/empty mbarriers);
+//   warp 1     TMEM owner and MMA issuer: one thread issues
+//              tcgen05.mma.cta_group::1.kind::f16 (M=128, N=BN, K=16) into a
+//              double-buffered f32 accumulator (2 x BN TMEM columns), then
+//              tcgen05.commit to release the smem stage / publish the tile;
+//   warps 2-5  epilogue: tcgen05.ld 32 columns at a time from the TMEM lane
+//              quarter the warp may access, bias + erf-GELU in registers,
+//              swizzled staging in shared memory, TMA store (clipped at the
+//              m / n edges).  The next tile's MMAs overlap this epilogue.
+// No TMA load uses cluster multicast.  Every mbarrier wait is bounded and
+// reports kStatusTimeout instead of hanging.
+#include "samq_internal.hpp"
+
+namespace samq {
+namespace {
+
+constexpr int BM = 128;
+constexpr int BK = 64;   // 64 f16 = 128 bytes = one swizzle row
+constexpr int kThreads = 192;
+constexpr int kEpilogueWarps = 4;
+constexpr int kOutChunkBytes = 32 * 32 * 4;  // 32 rows x 32 f32 columns
+
+template <int BN, int STAGES>
+struct Layout {
+    static constexpr int a_bytes = BM * BK * 2;
+    static constexpr int b_bytes = BN * BK * 2;
+    static constexpr int stage_tx = a_bytes + b_bytes;
+    static constexpr int a_off = 0;
+    static constexpr int b_off = STAGES * a_bytes;
+    static constexpr int out_off = b_off + STAGES * b_bytes;
+    static constexpr int bar_off = out_off + kEpilogueWarps * 2 * kOutChunkBytes;
+    static constexpr int bar_bytes = (2 * STAGES + 5) * 8 + 8;
+    static constexpr int total = bar_off + bar_bytes + 1024;  // + alignment slack
+    static constexpr uint32_t tmem_cols = 2 * BN;               // double-buffered accumulator
+};
+
+__device__ __forceinline__ float gelu_erf(float x) {
+    return 0.5f * x * (1.0f + erff(x * 0.70710678118654752f));
+}
+
+template <int BN, int STAGES>
+__global__ void __launch_bounds__(kThreads, 1)
+gemm_f16_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_b,
+                const __grid_constant__ CUtensorMap tma_y, const float* __restrict__ bias, int epilogue, int m,
+                int n, int k, DeviceStatus* status) {
+    using L = Layout<BN, STAGES>;
+    static_assert(L::total <= 232448, "shared memory budget");
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* sa = smem + L::a_off;
+    uint8_t* sb = smem + L::b_off;
+    uint8_t* sout = smem + L::out_off;
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + L::bar_off);
+    uint64_t* empty = full + STAGES;
+    uint64_t* tfull = empty + STAGES;
+    uint64_t* tempty = tfull + 2;
+    uint64_t* drain = tempty + 2;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int m_tiles = (m + BM - 1) / BM, n_tiles = (n + BN - 1) / BN;
+    const int tiles = m_tiles * n_tiles;
+    const int kblocks = (k + BK - 1) / BK;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&tfull[b], 1);
+            mbar_init(&tempty[b], kEpilogueWarps);
+        }
+        mbar_init(drain, 1);
+        fence_barrier_init();
+        tma_prefetch_desc(&tma_a);
+        tma_prefetch_desc(&tma_b);
+        tma_prefetch_desc(&tma_y);
+    }
+    if (warp == 1) tmem_alloc(tmem_slot, L::tmem_cols);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            int s = 0;
+            uint32_t ph = 0;
+            uint32_t issued = 0, issued_phase = 0;  // per stage: ever issued / parity of last issue
+            bool ok = true;
+            for (int tile = blockIdx.x; tile < tiles && ok; tile += gridDim.x) {
+                const int mt = tile / n_tiles, nt = tile % n_tiles;
+                for (int kb = 0; kb < kblocks; ++kb) {
+                    if (!mbar_wait(&empty[s], ph ^ 1u, status, 1)) {
+                        ok = false;
+                        break;
+                    }
+                    mbar_arrive_expect_tx(&full[s], L::stage_tx);
+                    tma_load_2d(sa + s * L::a_bytes, &tma_a, &full[s], kb * BK, mt * BM);
+                    tma_load_2d(sb + s * L::b_bytes, &tma_b, &full[s], kb * BK, nt * BN);
+                    issued |= 1u << s;
+                    issued_phase = (issued_phase & ~(1u << s)) | (ph << s);
+                    if (++s == STAGES) {
+                        s = 0;
+                        ph ^= 1u;
+                    }
+                }
+            }
+            if (!ok) {
+                // Let every copy already in flight land before the CTA exits.
+                for (int i = 0; i < STAGES; ++i)
+                    if (issued & (1u << i)) mbar_wait(&full[i], (issued_phase >> i) & 1u, status, 5);
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            constexpr uint32_t idesc = idesc_f16_f32(BM, BN);
+            int s = 0;
+            uint32_t ph = 0;
+            int acc = 0;
+            uint32_t acc_ph = 0;
+            bool ok = true;
+            for (int tile = blockIdx.x; tile < tiles && ok; tile += gridDim.x) {
+                if (!mbar_wait(&tempty[acc], acc_ph ^ 1u, status, 2)) break;
+                tc_fence_after();
+                const uint32_t d = tmem_base + static_cast<uint32_t>(acc * BN);
+                for (int kb = 0; kb < kblocks; ++kb) {
+                    if (!mbar_wait(&full[s], ph, status, 3)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t a_addr = smem_u32(sa + s * L::a_bytes);
+                    const uint32_t b_addr = smem_u32(sb + s * L::b_bytes);
+#pragma unroll
+                    for (int kk = 0; kk < BK / 16; ++kk)
+                        tc_mma_f16(d, smem_desc_sw128(a_addr + kk * 32), smem_desc_sw128(b_addr + kk * 32), idesc,
+                                   (kb | kk) != 0 ? 1u : 0u);
+                    tc_commit(&empty[s]);
+                    if (++s == STAGES) {
+                        s = 0;
+                        ph ^= 1u;
+                    }
+                }
+                if (!ok) break;
+                tc_commit(&tfull[acc]);
+                acc ^= 1;
+                if (acc == 0) acc_ph ^= 1u;
+            }
+            // Wait for every MMA this thread issued before TMEM is released.
+            tc_commit(drain);
+            mbar_wait(drain, 0, status, 6);
+        }
+    } else {
+        const int quarter = warp & 3;  // TMEM lanes 32*quarter .. +31
+        uint8_t* stage_buf = sout + (warp - 2) * 2 * kOutChunkBytes;
+        int acc = 0;
+        uint32_t acc_ph = 0;
+        int buf = 0;
+        for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x) {
+            const int mt = tile / n_tiles, nt = tile % n_tiles;
+            if (!mbar_wait(&tfull[acc], acc_ph, status, 4)) break;
+            tc_fence_after();
+            const int row0 = mt * BM + quarter * 32;
+#pragma unroll 1
+            for (int chunk = 0; chunk < BN / 32; ++chunk) {
+                const int col0 = nt * BN + chunk * 32;
+                if (col0 >= n) break;
+                uint32_t r[32];
+                tc_ld_32x32b_x32(tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) +
+                                     static_cast<uint32_t>(acc * BN + chunk * 32),
+                                 r);
+                tc_wait_ld();
+                float v[32];
+#pragma unroll
+                for (int i = 0; i < 32; ++i) {
+                    float x = __uint_as_float(r[i]);
+                    if (bias != nullptr && col0 + i < n) x += __ldg(bias + col0 + i);
+                    if (epilogue == SAMQ_EPILOGUE_GELU_ERF) x = gelu_erf(x);
+                    v[i] = x;
+                }
+                if (lane == 0) bulk_wait_group_read<1>();
+                __syncwarp();
+                uint8_t* sbuf = stage_buf + buf * kOutChunkBytes;
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                    const float4 val = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+                    *reinterpret_cast<float4*>(sbuf + lane * 128 + ((j ^ (lane & 7)) << 4)) = val;
+                }
+                fence_proxy_async_smem();
+                __syncwarp();
+                if (lane == 0 && row0 < m) {
+                    tma_store_2d(&tma_y, sbuf, col0, row0);
+                    bulk_commit_group();
+                }
+                buf ^= 1;
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&tempty[acc]);
+            acc ^= 1;
+            if (acc == 0) acc_ph ^= 1u;
+        }
+        if (lane == 0) bulk_wait_group_all();
+        __syncwarp();
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem_base, L::tmem_cols);
+    }
+}
+
+template <int BN, int STAGES>
+void run(const __half* a, int64_t lda, const __half* b, int64_t m, int64_t n, int64_t k, const float* bias, int epilogue,
+         float* y, int64_t ldy, DeviceState& state, cudaStream_t stream) {
+    using L = Layout<BN, STAGES>;
+    CUtensorMap ta, tb, ty;
+    encode_tensor_map_2d(&ta, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, a, k, m, lda * 2, BK, BM,
+                         CU_TENSOR_MAP_SWIZZLE_128B);
+    encode_tensor_map_2d(&tb, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, b, k, n, k * 2, BK, BN,
+                         CU_TENSOR_MAP_SWIZZLE_128B);
+    encode_tensor_map_2d(&ty, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, y, n, m, ldy * 4, 32, 32,
+                         CU_TENSOR_MAP_SWIZZLE_128B);
+    auto kernel = gemm_f16_kernel<BN, STAGES>;
+    static bool configured[64] = {};
+    if (!configured[state.device & 63]) {
+        check_cuda(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, L::total),
+                   "cudaFuncSetAttribute(gemm smem)");
+        configured[state.device & 63] = true;
+    }
+    const int64_t tiles = ((m + BM - 1) / BM) * ((n + BN - 1) / BN);
+    const int grid = static_cast<int>(tiles < state.sm_count ? tiles : state.sm_count);
+    kernel<<<grid, kThreads, L::total, stream>>>(ta, tb, ty, bias, epilogue, static_cast<int>(m),
+                                                 static_cast<int>(n), static_cast<int>(k), state.status);
+    check_cuda(cudaGetLastError(), "gemm_f16_kernel launch");
+}
+
+}  // namespace
+
+void launch_gemm_f16(const __half* a, int64_t lda, const __half* b, int64_t m, int64_t n, int64_t k,
+                     const float* bias, int epilogue, float* y, int64_t ldy, DeviceState& state,
+                     cudaStream_t stream) {
+    if (m == 0) return;
+    if (n <= 128)
+        run<128, 6>(a, lda, b, m, n, k, bias, epilogue, y, ldy, state, stream);
+    else
+        run<256, 4>(a, lda, b, m, n, k, bias, epilogue, y, ldy, state, stream);
+}
+
+}  // namespace samq

@@ -1,0 +1,201 @@
+// quantize.cu -- K1: activation staging for the quantized linears.
+//
+// Restates GGML CUDA's quantize_q8_1 (MMVQ staging, 36-byte blocks) and
+// quantize_mmq_q8_1 (MMQ D4 staging, 144-byte blocks) as pinned by SAM.cpp's
+// verifiers (tools/validation/verify_q8_rhs_staging.py:24-83,
+// tools/validation/verify_q8_mmq_rhs_staging.py:24-67) and its scale rule
+// patch (cmake/patches/ggml-precise-cuda.patch:623-633: the inverse scale is
+// an IEEE round-to-nearest division).  The deterministic rule used here:
+//   amax = max |x| over 32 values
+//   d    = amax / 127            (f32, IEEE division; stored as f16 for Q8_1)
+//   q    = roundf(x * (127/amax)) (half away from zero; 0 when amax == 0)
+//   sum  = f16 of the f32 sum in 32-lane xor-butterfly order
+// Besides the staged bytes, the kernel writes the tensor-core A operand of the
+// GEMM: f16(f32(d_f16) * q), the exact decoded Q8_1 value rounded once.
+//
+// Memory layout: every thread owns 8 consecutive values (two 16-byte loads,
+// one 16-byte f16 store); four neighbouring lanes form one 32-value block.
+#include "samq_internal.hpp"
+
+namespace samq {
+namespace {
+
+constexpr float kOperandLimit = 65000.0f;  // |x| above this could overflow the f16 operand
+
+__device__ __forceinline__ void load8(const float* __restrict__ p, float (&v)[8]) {
+    const float4 a = __ldg(reinterpret_cast<const float4*>(p));
+    const float4 b = __ldg(reinterpret_cast<const float4*>(p) + 1);
+    v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+    v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+}
+
+// amax over the 4-lane group (32 values).
+__device__ __forceinline__ float group_amax(const float (&v)[8]) {
+    float a = 0.0f;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) a = fmaxf(a, fabsf(v[j]));
+    a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, 1));
+    a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, 2));
+    return a;
+}
+
+// Sum of the 32 values in the order of a 32-lane xor butterfly with offsets
+// 16, 8, 4, 2, 1.  Element e = 8 * lane_in_group + j, so offsets 16 and 8 are
+// lane offsets 2 and 1, and offsets 4, 2, 1 stay inside the thread.
+__device__ __forceinline__ float group_butterfly_sum(const float (&v)[8]) {
+    float s[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) s[j] = __fadd_rn(v[j], __shfl_xor_sync(0xffffffffu, v[j], 2));
+#pragma unroll
+    for (int j = 0; j < 8; ++j) s[j] = __fadd_rn(s[j], __shfl_xor_sync(0xffffffffu, s[j], 1));
+#pragma unroll
+    for (int j = 0; j < 4; ++j) s[j] = __fadd_rn(s[j], s[j + 4]);
+    s[0] = __fadd_rn(s[0], s[2]);
+    s[1] = __fadd_rn(s[1], s[3]);
+    return __fadd_rn(s[0], s[1]);
+}
+
+__device__ __forceinline__ void record_range(bool bad, DeviceStatus* status) {
+    const unsigned any = __ballot_sync(0xffffffffu, bad);
+    if (any && (threadIdx.x & 31) == __ffs(any) - 1 && status) {
+        atomicOr(&status->flags, kStatusRange);
+        atomicAdd(&status->range_blocks, 1u);
+    }
+}
+
+__global__ void __launch_bounds__(256) act_f16_kernel(const float* __restrict__ x, int64_t rows, int64_t k,
+                                                      int64_t ld, __half* __restrict__ a,
+                                                      uint8_t* __restrict__ q8_1, DeviceStatus* status) {
+    const int64_t per_row = k / 8;
+    const int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    const bool active = idx < rows * per_row;
+    const int64_t row = active ? idx / per_row : 0;
+    const int64_t c8 = active ? idx % per_row : 0;
+    float v[8];
+    if (active) {
+        load8(x + row * ld + c8 * 8, v);
+    } else {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) v[j] = 0.0f;
+    }
+    const float amax = group_amax(v);
+    const float d = __fdiv_rn(amax, 127.0f);
+    const __half dh = __float2half_rn(d);
+    const float dq = __half2float(dh);
+    const float inv = amax == 0.0f ? 0.0f : __fdiv_rn(127.0f, amax);
+    bool bad = false;
+    int q[8];
+    __align__(16) __half out[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+        bad |= !(fabsf(v[j]) <= kOperandLimit);
+        q[j] = static_cast<int>(roundf(__fmul_rn(v[j], inv)));
+        out[j] = __float2half_rn(__fmul_rn(dq, static_cast<float>(q[j])));
+    }
+    record_range(bad && active, status);
+    if (q8_1) {
+        const float sum = group_butterfly_sum(v);
+        if (active) {
+            const int lane_in_group = static_cast<int>(c8 & 3);
+            uint8_t* blk = q8_1 + (row * (k / 32) + c8 / 4) * 36;
+            uint32_t lo = 0, hi = 0;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                lo |= (static_cast<uint32_t>(q[j]) & 0xffu) << (8 * j);
+                hi |= (static_cast<uint32_t>(q[j + 4]) & 0xffu) << (8 * j);
+            }
+            uint32_t* words = reinterpret_cast<uint32_t*>(blk);
+            words[1 + 2 * lane_in_group] = lo;
+            words[2 + 2 * lane_in_group] = hi;
+            if (lane_in_group == 0) {
+                const __half hs = __float2half_rn(sum);
+                words[0] = static_cast<uint32_t>(__half_as_ushort(dh)) |
+                           (static_cast<uint32_t>(__half_as_ushort(hs)) << 16);
+            }
+        }
+    }
+    if (active && a) *reinterpret_cast<uint4*>(a + row * k + c8 * 8) = *reinterpret_cast<const uint4*>(out);
+}
+
+__global__ void __launch_bounds__(256) q8_1_to_f16_kernel(const uint8_t* __restrict__ q8_1, int64_t rows, int64_t k,
+                                                          __half* __restrict__ a) {
+    const int64_t per_row = k / 8;
+    const int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (idx >= rows * per_row) return;
+    const int64_t row = idx / per_row, c8 = idx % per_row;
+    const uint8_t* blk = q8_1 + (row * (k / 32) + c8 / 4) * 36;
+    const uint32_t* words = reinterpret_cast<const uint32_t*>(blk);
+    const float dq = __half2float(__ushort_as_half(static_cast<unsigned short>(words[0] & 0xffffu)));
+    const uint32_t lo = words[1 + 2 * (c8 & 3)], hi = words[2 + 2 * (c8 & 3)];
+    __align__(16) __half out[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+        const uint32_t w = j < 4 ? lo : hi;
+        const int q = static_cast<int8_t>((w >> (8 * (j & 3))) & 0xffu);
+        out[j] = __float2half_rn(__fmul_rn(dq, static_cast<float>(q)));
+    }
+    *reinterpret_cast<uint4*>(a + row * k + c8 * 8) = *reinterpret_cast<const uint4*>(out);
+}
+
+// MMQ D4: 128-value blocks {f32 d[4], int8 q[128]}, width padded to 512,
+// stored [block][row].  16 threads per block, 4 per 32-value sub-block.
+__global__ void __launch_bounds__(256) mmq_d4_kernel(const float* __restrict__ x, int64_t rows, int64_t k,
+                                                     int64_t ld, int64_t padded, uint8_t* __restrict__ out) {
+    const int64_t per_row = padded / 8;
+    const int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    const bool active = idx < rows * per_row;
+    const int64_t row = active ? idx / per_row : 0;
+    const int64_t c8 = active ? idx % per_row : 0;
+    float v[8];
+    const int64_t col = c8 * 8;
+    if (active && col < k) {
+        load8(x + row * ld + col, v);
+    } else {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) v[j] = 0.0f;
+    }
+    const float amax = group_amax(v);
+    const float d = __fdiv_rn(amax, 127.0f);
+    const float inv = amax == 0.0f ? 0.0f : __fdiv_rn(127.0f, amax);
+    if (!active) return;
+    uint32_t lo = 0, hi = 0;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        lo |= (static_cast<uint32_t>(static_cast<int>(roundf(__fmul_rn(v[j], inv)))) & 0xffu) << (8 * j);
+        hi |= (static_cast<uint32_t>(static_cast<int>(roundf(__fmul_rn(v[j + 4], inv)))) & 0xffu) << (8 * j);
+    }
+    const int64_t blk = c8 / 16;            // 128-value block index
+    const int sub = static_cast<int>((c8 / 4) & 3), lane_in_group = static_cast<int>(c8 & 3);
+    uint8_t* o = out + (blk * rows + row) * 144;
+    uint32_t* words = reinterpret_cast<uint32_t*>(o);
+    words[4 + 8 * sub + 2 * lane_in_group] = lo;
+    words[5 + 8 * sub + 2 * lane_in_group] = hi;
+    if (lane_in_group == 0) reinterpret_cast<float*>(o)[sub] = d;
+}
+
+unsigned grid_for(int64_t threads) { return static_cast<unsigned>((threads + 255) / 256); }
+
+}  // namespace
+
+void launch_act_f16(const float* x, int64_t rows, int64_t k, int64_t ld, __half* a_out, uint8_t* q8_1_out,
+                    DeviceStatus* status, cudaStream_t stream) {
+    if (rows == 0) return;
+    act_f16_kernel<<<grid_for(rows * (k / 8)), 256, 0, stream>>>(x, rows, k, ld, a_out, q8_1_out, status);
+    check_cuda(cudaGetLastError(), "act_f16_kernel launch");
+}
+
+void launch_q8_1_to_f16(const uint8_t* q8_1, int64_t rows, int64_t k, __half* a_out, DeviceStatus*,
+                        cudaStream_t stream) {
+    if (rows == 0) return;
+    q8_1_to_f16_kernel<<<grid_for(rows * (k / 8)), 256, 0, stream>>>(q8_1, rows, k, a_out);
+    check_cuda(cudaGetLastError(), "q8_1_to_f16_kernel launch");
+}
+
+void launch_mmq_d4(const float* x, int64_t rows, int64_t k, int64_t ld, uint8_t* out, cudaStream_t stream) {
+    if (rows == 0) return;
+    const int64_t padded = (k + 511) / 512 * 512;
+    mmq_d4_kernel<<<grid_for(rows * (padded / 8)), 256, 0, stream>>>(x, rows, k, ld, padded, out);
+    check_cuda(cudaGetLastError(), "mmq_d4_kernel launch");
+}
+
+}  // namespace samq

@@ -1,0 +1,105 @@
+// samq_internal.hpp -- host-side internals shared by the samq translation
+// units: error reporting, per-device state, scratch memory, tensor maps.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <atomic>
+#include <cstdint>
+#include <mutex>
+#include <string>
+#include <unordered_map>
+
+#include "../../include/samq.h"
+#include "samq_device.cuh"
+
+namespace samq {
+
+// Internal exception type; converted to a status at the C boundary.
+struct Error {
+    samq_status status;
+    std::string message;
+};
+
+[[noreturn]] void fail(samq_status status, const std::string& message);
+void check_cuda(cudaError_t err, const char* what);
+void set_last_error(const std::string& message);
+
+// Per-stream scratch buffer, grown on demand (growth is a cudaMalloc and
+// therefore synchronizes the device).
+struct Scratch {
+    void* ptr = nullptr;
+    size_t bytes = 0;
+};
+
+struct DeviceState {
+    int device = -1;
+    int sm_count = 0;
+    int cc_major = 0, cc_minor = 0;
+    DeviceStatus* status = nullptr;  // device memory
+    std::mutex mutex;
+    std::unordered_map<cudaStream_t, Scratch> scratch;
+};
+
+// Checks the device once and returns its state (throws Error otherwise).
+DeviceState& device_state(int device);
+// Scratch of at least `bytes` bytes for work ordered on `stream`.
+Scratch& scratch_for(DeviceState& state, cudaStream_t stream, size_t bytes);
+
+// RAII device switch.
+struct DeviceGuard {
+    int previous = -1;
+    explicit DeviceGuard(int device);
+    ~DeviceGuard();
+};
+
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no link
+// dependency on libcuda).
+void encode_tensor_map_2d(CUtensorMap* map, CUtensorMapDataType dtype, const void* base, uint64_t inner,
+                          uint64_t outer, uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_outer,
+                          CUtensorMapSwizzle swizzle);
+
+}  // namespace samq
+
+// Weight handle (opaque in the C ABI).
+struct samq_weights {
+    int device = -1;
+    int type = 0;
+    int64_t k = 0, n = 0;
+    void* packets = nullptr;      // K4 packet layout (canonical device form)
+    size_t packet_bytes = 0;
+    __half* operand = nullptr;    // f16 [n][k] tensor-core B operand expanded from the packets
+    size_t operand_bytes = 0;
+    std::atomic<uint64_t> launches{0};
+    std::atomic<uint64_t> payload_bytes{0};
+    std::atomic<uint64_t> allocation_bytes{0};
+};
+
+// ---- launchers implemented in the .cu files -------------------------------
+namespace samq {
+
+// K1 quantize.cu
+void launch_act_f16(const float* x, int64_t rows, int64_t k, int64_t ld, __half* a_out, uint8_t* q8_1_out,
+                    DeviceStatus* status, cudaStream_t stream);
+void launch_q8_1_to_f16(const uint8_t* q8_1, int64_t rows, int64_t k, __half* a_out, DeviceStatus* status,
+                        cudaStream_t stream);
+void launch_mmq_d4(const float* x, int64_t rows, int64_t k, int64_t ld, uint8_t* out, cudaStream_t stream);
+
+// K4 repack.cu
+int64_t packet_code_bytes(int type);
+int64_t packet_bytes(int type);
+int64_t row_bytes(int type, int64_t k);
+void launch_gguf_to_packets(int type, int64_t k, int64_t n, const uint8_t* rows, uint8_t* packets,
+                            uint32_t* bad_scales, cudaStream_t stream);
+void launch_packets_to_gguf(int type, int64_t k, int64_t n, const uint8_t* packets, uint8_t* rows,
+                            cudaStream_t stream);
+void launch_packets_to_f16(int type, int64_t k, int64_t n, const uint8_t* packets, __half* out,
+                           cudaStream_t stream);
+
+// K2 gemm.cu
+void launch_gemm_f16(const __half* a, int64_t lda, const __half* b, int64_t m, int64_t n, int64_t k,
+                     const float* bias, int epilogue, float* y, int64_t ldy, DeviceState& state,
+                     cudaStream_t stream);
+
+}  // namespace samq

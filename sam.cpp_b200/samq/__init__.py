@@ -1,0 +1,212 @@
+"""Python binding of libsamq (include/samq.h) for tests, benchmarks and scripts.
+
+The binding is a thin ctypes layer over the C ABI: every call goes to the
+sm_100a kernels in ``libsamq.so``.  There is no fallback of any kind: when the
+library is missing this module raises at import of the first call, and a
+non-sm_100 device is rejected by the library itself.
+
+Device buffers and streams may be given as torch tensors / torch streams or
+as raw integer addresses.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+from pathlib import Path
+
+import numpy as np
+
+PACKAGE_DIR = Path(__file__).resolve().parent.parent
+LIB_PATH = Path(os.environ.get("SAMQ_LIBRARY", PACKAGE_DIR / "libsamq.so"))
+
+Q8_0, Q8_1, Q4_K, Q5_K, Q6_K = 8, 9, 12, 13, 14
+TYPE_NAMES = {Q8_0: "Q8_0", Q4_K: "Q4_K", Q5_K: "Q5_K", Q6_K: "Q6_K"}
+NAME_TYPES = {v: k for k, v in TYPE_NAMES.items()}
+EPILOGUE_NONE, EPILOGUE_GELU_ERF = 0, 1
+BLOCK = {Q8_0: (32, 34), Q4_K: (256, 144), Q5_K: (256, 176), Q6_K: (256, 210)}
+
+STATUS_NAMES = {
+    0: "SAMQ_OK", 1: "SAMQ_ERR_INVALID_ARGUMENT", 2: "SAMQ_ERR_UNSUPPORTED", 3: "SAMQ_ERR_CUDA",
+    4: "SAMQ_ERR_OUT_OF_MEMORY", 5: "SAMQ_ERR_RANGE", 6: "SAMQ_ERR_TIMEOUT", 7: "SAMQ_ERR_PAYLOAD",
+}
+
+# Every symbol include/samq.h declares, with its ctypes signature.
+_i64, _i32, _vp, _sz = ctypes.c_int64, ctypes.c_int, ctypes.c_void_p, ctypes.c_size_t
+
+
+class Capabilities(ctypes.Structure):
+    _fields_ = [("version", ctypes.c_uint32), ("device", ctypes.c_int32), ("cc_major", ctypes.c_int32),
+                ("cc_minor", ctypes.c_int32), ("sm_count", ctypes.c_int32),
+                ("global_memory_bytes", ctypes.c_uint64), ("max_shared_memory_per_block", ctypes.c_uint64),
+                ("name", ctypes.c_char * 256)]
+
+
+class Counters(ctypes.Structure):
+    _fields_ = [("version", ctypes.c_uint32), ("path", ctypes.c_uint32), ("launches", ctypes.c_uint64),
+                ("payload_bytes", ctypes.c_uint64), ("allocation_bytes", ctypes.c_uint64),
+                ("weight_bytes", ctypes.c_uint64)]
+
+
+SIGNATURES = {
+    "samq_last_error_v1": (ctypes.c_char_p, []),
+    "samq_init_v1": (_i32, [_i32]),
+    "samq_capabilities_v1": (_i32, [_i32, ctypes.POINTER(Capabilities)]),
+    "samq_weights_create_v1": (_i32, [_i32, _i32, _i64, _i64, _vp, _sz, _vp, ctypes.POINTER(_vp)]),
+    "samq_weights_destroy_v1": (_i32, [_vp]),
+    "samq_weights_export_v1": (_i32, [_vp, _vp, _sz]),
+    "samq_weights_packets_v1": (_i32, [_vp, ctypes.POINTER(_vp), ctypes.POINTER(_sz)]),
+    "samq_quantize_q8_1_v1": (_i32, [_vp, _i64, _i64, _i64, _vp, _vp]),
+    "samq_mmq_d4_bytes_v1": (_sz, [_i64, _i64]),
+    "samq_quantize_mmq_q8_1_v1": (_i32, [_vp, _i64, _i64, _i64, _vp, _vp]),
+    "samq_linear_v1": (_i32, [_vp, _vp, _i64, _i64, _vp, _i32, _vp, _i64, _vp]),
+    "samq_linear_q8_1_v1": (_i32, [_vp, _vp, _i64, _vp, _i32, _vp, _i64, _vp]),
+    "samq_stage_f16_v1": (_i32, [_vp, _i64, _i64, _i64, _vp, _vp]),
+    "samq_linear_f16_v1": (_i32, [_vp, _vp, _i64, _i64, _vp, _i32, _vp, _i64, _vp]),
+    "samq_query_v1": (_i32, [_vp, ctypes.POINTER(Counters)]),
+    "samq_check_v1": (_i32, [_i32, _vp]),
+}
+
+
+class SamqError(RuntimeError):
+    def __init__(self, status: int, message: str):
+        self.status = status
+        super().__init__(f"{STATUS_NAMES.get(status, status)}: {message}")
+
+
+_lib = None
+
+
+def library() -> ctypes.CDLL:
+    """Load libsamq.so (raises if it has not been built)."""
+    global _lib
+    if _lib is None:
+        if not LIB_PATH.exists():
+            raise ImportError(f"{LIB_PATH} is missing; build it with `make -C {PACKAGE_DIR}` "
+                              "(there is no non-CUDA fallback)")
+        lib = ctypes.CDLL(str(LIB_PATH))
+        for name, (res, args) in SIGNATURES.items():
+            fn = getattr(lib, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = lib
+    return _lib
+
+
+def _check(status: int):
+    if status != 0:
+        raise SamqError(status, library().samq_last_error_v1().decode())
+
+
+def _addr(obj) -> int | None:
+    """Device address of a torch tensor / int / None."""
+    if obj is None:
+        return None
+    if isinstance(obj, int):
+        return obj
+    if hasattr(obj, "data_ptr"):
+        return obj.data_ptr()
+    raise TypeError(f"expected a device tensor or address, got {type(obj)!r}")
+
+
+def _stream(stream) -> int | None:
+    if stream is None:
+        try:
+            import torch
+            if torch.cuda.is_available():
+                return torch.cuda.current_stream().cuda_stream
+        except ImportError:
+            pass
+        return None
+    if isinstance(stream, int):
+        return stream
+    return stream.cuda_stream
+
+
+def init(device: int = 0):
+    _check(library().samq_init_v1(device))
+
+
+def capabilities(device: int = 0) -> Capabilities:
+    info = Capabilities()
+    _check(library().samq_capabilities_v1(device, ctypes.byref(info)))
+    return info
+
+
+def row_bytes(qtype: int, k: int) -> int:
+    be, bb = BLOCK[qtype]
+    if k % be:
+        raise ValueError("width is not block aligned")
+    return k // be * bb
+
+
+class Weights:
+    """A repacked weight matrix resident on one device (samq_weights*)."""
+
+    def __init__(self, qtype: int, k: int, n: int, gguf_rows: np.ndarray, device: int = 0, stream=None):
+        rows = np.ascontiguousarray(gguf_rows, dtype=np.uint8).reshape(-1)
+        handle = ctypes.c_void_p()
+        _check(library().samq_weights_create_v1(device, qtype, k, n, rows.ctypes.data, rows.nbytes,
+                                                _stream(stream), ctypes.byref(handle)))
+        self.handle = handle
+        self.qtype, self.k, self.n, self.device = qtype, k, n, device
+
+    def close(self):
+        if self.handle:
+            _check(library().samq_weights_destroy_v1(self.handle))
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def export(self) -> np.ndarray:
+        out = np.empty(self.n * row_bytes(self.qtype, self.k), dtype=np.uint8)
+        _check(library().samq_weights_export_v1(self.handle, out.ctypes.data, out.nbytes))
+        return out
+
+    def packets(self) -> tuple[int, int]:
+        ptr, size = ctypes.c_void_p(), ctypes.c_size_t()
+        _check(library().samq_weights_packets_v1(self.handle, ctypes.byref(ptr), ctypes.byref(size)))
+        return ptr.value, size.value
+
+    def query(self) -> Counters:
+        c = Counters()
+        _check(library().samq_query_v1(self.handle, ctypes.byref(c)))
+        return c
+
+
+def quantize_q8_1(x, rows: int, k: int, ld: int, out, stream=None):
+    _check(library().samq_quantize_q8_1_v1(_addr(x), rows, k, ld, _addr(out), _stream(stream)))
+
+
+def mmq_d4_bytes(rows: int, k: int) -> int:
+    return library().samq_mmq_d4_bytes_v1(rows, k)
+
+
+def quantize_mmq_q8_1(x, rows: int, k: int, ld: int, out, stream=None):
+    _check(library().samq_quantize_mmq_q8_1_v1(_addr(x), rows, k, ld, _addr(out), _stream(stream)))
+
+
+def linear(w: Weights, x, m: int, ldx: int, bias, epilogue: int, y, ldy: int, stream=None):
+    _check(library().samq_linear_v1(w.handle, _addr(x), m, ldx, _addr(bias), epilogue, _addr(y), ldy,
+                                    _stream(stream)))
+
+
+def linear_q8_1(w: Weights, xq, m: int, bias, epilogue: int, y, ldy: int, stream=None):
+    _check(library().samq_linear_q8_1_v1(w.handle, _addr(xq), m, _addr(bias), epilogue, _addr(y), ldy,
+                                         _stream(stream)))
+
+
+def stage_f16(x, rows: int, k: int, ld: int, out, stream=None):
+    _check(library().samq_stage_f16_v1(_addr(x), rows, k, ld, _addr(out), _stream(stream)))
+
+
+def linear_f16(w: Weights, x16, m: int, ldx: int, bias, epilogue: int, y, ldy: int, stream=None):
+    _check(library().samq_linear_f16_v1(w.handle, _addr(x16), m, ldx, _addr(bias), epilogue, _addr(y), ldy,
+                                        _stream(stream)))
+
+
+def check(device: int = 0, stream=None):
+    _check(library().samq_check_v1(device, _stream(stream)))

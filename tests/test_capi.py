@@ -1,0 +1,96 @@
+"""Host-side checks of the C ABI (no GPU needed).
+
+The library must load, export every entry point include/samq.h declares and
+reject malformed arguments with a status code and a message before any
+device work (the reference's boundary validates shapes the same way,
+src/runtime/ggml/backends/cpu.hpp:26-34, src/models/sam3/weights.hpp:384-425).
+"""
+import ctypes
+import re
+import subprocess
+
+import numpy as np
+import pytest
+
+from conftest import PACKAGE, ROOT
+
+
+def header_functions():
+    text = (ROOT / "include" / "samq.h").read_text()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(samq_[a-z0-9_]+_v1)\s*\(", text)))
+
+
+@pytest.fixture(scope="module")
+def samq():
+    lib = PACKAGE / "libsamq.so"
+    if not lib.exists():
+        subprocess.run(["make", "-C", str(PACKAGE), "-s", "-j4"], check=True)
+    import samq as module
+    module.library()
+    return module
+
+
+def test_header_declares_the_expected_surface():
+    names = header_functions()
+    assert "samq_linear_v1" in names and "samq_weights_create_v1" in names
+    assert len(names) >= 14
+
+
+def test_library_exports_every_declared_symbol(samq):
+    lib = samq.library()
+    for name in header_functions():
+        assert hasattr(lib, name), name
+    out = subprocess.run(["nm", "-D", "--defined-only", str(samq.LIB_PATH)], capture_output=True, text=True,
+                         check=True).stdout
+    exported = set(re.findall(r"\bT (samq_[a-z0-9_]+)", out))
+    assert set(header_functions()) <= exported
+
+
+def test_binding_covers_the_header(samq):
+    assert set(samq.SIGNATURES) == set(header_functions())
+
+
+def test_invalid_weight_arguments_are_rejected(samq):
+    lib = samq.library()
+    handle = ctypes.c_void_p()
+    rows = np.zeros(34, dtype=np.uint8)
+    # unsupported type id (Q4_0 = 2)
+    rc = lib.samq_weights_create_v1(0, 2, 32, 1, rows.ctypes.data, rows.nbytes, None, ctypes.byref(handle))
+    assert rc == 1 and b"Q8_0" in lib.samq_last_error_v1()
+    # width not block aligned for Q4_K
+    rc = lib.samq_weights_create_v1(0, 12, 128, 1, rows.ctypes.data, rows.nbytes, None, ctypes.byref(handle))
+    assert rc == 1 and b"block" in lib.samq_last_error_v1()
+    # payload size differs from n rows
+    rc = lib.samq_weights_create_v1(0, 8, 32, 2, rows.ctypes.data, rows.nbytes, None, ctypes.byref(handle))
+    assert rc == 1 and b"size" in lib.samq_last_error_v1()
+    assert handle.value is None
+
+
+def test_invalid_linear_arguments_are_rejected(samq):
+    lib = samq.library()
+    rc = lib.samq_linear_v1(None, None, 4, 32, None, 0, None, 32, None)
+    assert rc == 1 and b"null weights" in lib.samq_last_error_v1()
+    rc = lib.samq_quantize_q8_1_v1(None, 4, 48, 48, None, None)
+    assert rc == 1 and b"multiple of 32" in lib.samq_last_error_v1()
+    rc = lib.samq_quantize_q8_1_v1(None, 4, 64, 62, None, None)
+    assert rc == 1
+
+
+def test_mmq_d4_sizes(samq):
+    assert samq.mmq_d4_bytes(65, 160) == 65 * 4 * 144
+    assert samq.mmq_d4_bytes(1, 512) == 4 * 144
+    assert samq.mmq_d4_bytes(2, 513) == 2 * 8 * 144
+    assert samq.mmq_d4_bytes(0, 32) == 0
+
+
+def test_last_error_is_thread_local(samq):
+    import threading
+    lib = samq.library()
+    lib.samq_linear_v1(None, None, 4, 32, None, 0, None, 32, None)
+    seen = []
+    t = threading.Thread(target=lambda: seen.append(lib.samq_last_error_v1()))
+    t.start()
+    t.join()
+    assert seen == [b""]
+    assert lib.samq_last_error_v1() != b""
