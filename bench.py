@@ -230,12 +230,18 @@ def main():
     ap.add_argument("--e2e-steps", type=int, default=20)
     ap.add_argument("--cpu-budget", type=float, default=12.0, help="seconds of CPU baseline work")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--profile", choices=[l[0] for l in LINEARS],
+                    help="only stage one linear's A operand and launch its GEMM --steps times "
+                         "(small, single-kernel case for ncu captures)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     world, rank, local = dist_setup()
 
     if args.impl == "reference":
         run_reference(args, world, rank)
+        return
+    if args.profile:
+        run_profile_case(args)
         return
 
     import torch
@@ -387,6 +393,30 @@ def main():
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
+
+
+def run_profile_case(args):
+    """One linear's GEMM launched alone, for ncu (-k regex:gemm)."""
+    import torch
+    import samq
+    from oracle import oracle as o
+    torch.cuda.set_device(0)
+    samq.init(0)
+    stream = torch.cuda.current_stream()
+    name, n, k, qtype, epi, seed = next(l for l in LINEARS if l[0] == args.profile)
+    packed, bias = make_weights(o, n, k, qtype, seed)
+    w = samq.Weights(qtype, k, n, packed)
+    x = torch.from_numpy(np.random.default_rng(seed).normal(0, 1, (M, k)).astype(np.float32)).cuda()
+    a16 = torch.empty((M, k), dtype=torch.float16, device="cuda")
+    y = torch.empty((M, n), dtype=torch.float32, device="cuda")
+    b = torch.from_numpy(bias).cuda()
+    samq.stage_f16(x, M, k, k, a16, stream)
+    for _ in range(args.warmup + args.steps):
+        samq.linear_f16(w, a16, M, k, b, epi, y, n, stream)
+    torch.cuda.synchronize()
+    samq.check(0, stream)
+    w.close()
+    print(json.dumps({"profile_case": name, "launches": args.warmup + args.steps}))
 
 
 def gemm_only_durations(samq, weights, xs, ys, biases, stream, reps=50):

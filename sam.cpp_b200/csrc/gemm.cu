@@ -6,17 +6,20 @@
 // X = A (src/models/sam3/ops.hpp:40-45), with the bias add and ggml_gelu_erf
 // of the ViT MLP fused (src/models/sam3/vision.hpp:234-236).
 //
-// Persistent, warp-specialised kernel, one CTA per SM (192 threads):
+// Persistent, warp-specialised kernel, one CTA per SM (320 threads):
 //   warp 0     TMA producer: 128x64 A and BNx64 B tiles, 128-byte swizzle,
 //              into a STAGES-deep shared-memory ring (full/empty mbarriers);
 //   warp 1     TMEM owner and MMA issuer: one thread issues
 //              tcgen05.mma.cta_group::1.kind::f16 (M=128, N=BN, K=16) into a
 //              double-buffered f32 accumulator (2 x BN TMEM columns), then
 //              tcgen05.commit to release the smem stage / publish the tile;
-//   warps 2-5  epilogue: tcgen05.ld 32 columns at a time from the TMEM lane
-//              quarter the warp may access, bias + erf-GELU in registers,
-//              swizzled staging in shared memory, TMA store (clipped at the
-//              m / n edges).  The next tile's MMAs overlap this epilogue.
+//   warps 2-9  epilogue: two warps per TMEM lane quarter (the quarter a warp
+//              may access is warp % 4), each owning half of the tile's
+//              columns; tcgen05.ld 32 columns at a time, bias (one coalesced
+//              load per 32 columns, broadcast by warp shuffles) + erf-GELU in
+//              registers, swizzled staging in shared memory, TMA store
+//              (clipped at the m / n edges).  The next tile's MMAs overlap
+//              this epilogue.
 // No TMA load uses cluster multicast.  Every mbarrier wait is bounded and
 // reports kStatusTimeout instead of hanging.
 #include "samq_internal.hpp"
@@ -26,9 +29,10 @@ namespace {
 
 constexpr int BM = 128;
 constexpr int BK = 64;   // 64 f16 = 128 bytes = one swizzle row
-constexpr int kThreads = 192;
-constexpr int kEpilogueWarps = 4;
+constexpr int kEpilogueWarps = 8;  // two per TMEM lane quarter, each owning half of the tile's columns
+constexpr int kThreads = 64 + 32 * kEpilogueWarps;
 constexpr int kOutChunkBytes = 32 * 32 * 4;  // 32 rows x 32 f32 columns
+constexpr int kOutBuffers = 2;               // staging buffers per epilogue warp
 
 template <int BN, int STAGES>
 struct Layout {
@@ -38,7 +42,7 @@ struct Layout {
     static constexpr int a_off = 0;
     static constexpr int b_off = STAGES * a_bytes;
     static constexpr int out_off = b_off + STAGES * b_bytes;
-    static constexpr int bar_off = out_off + kEpilogueWarps * 2 * kOutChunkBytes;
+    static constexpr int bar_off = out_off + kEpilogueWarps * kOutBuffers * kOutChunkBytes;
     static constexpr int bar_bytes = (2 * STAGES + 5) * 8 + 8;
     static constexpr int total = bar_off + bar_bytes + 1024;  // + alignment slack
     static constexpr uint32_t tmem_cols = 2 * BN;               // double-buffered accumulator
@@ -163,8 +167,9 @@ gemm_f16_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant
             mbar_wait(drain, 0, status, 6);
         }
     } else {
-        const int quarter = warp & 3;  // TMEM lanes 32*quarter .. +31
-        uint8_t* stage_buf = sout + (warp - 2) * 2 * kOutChunkBytes;
+        const int quarter = warp & 3;          // TMEM lanes 32*quarter .. +31
+        const int half = (warp - 2) >> 2;      // columns [half*BN/2, (half+1)*BN/2)
+        uint8_t* stage_buf = sout + (warp - 2) * kOutBuffers * kOutChunkBytes;
         int acc = 0;
         uint32_t acc_ph = 0;
         int buf = 0;
@@ -174,23 +179,23 @@ gemm_f16_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant
             tc_fence_after();
             const int row0 = mt * BM + quarter * 32;
 #pragma unroll 1
-            for (int chunk = 0; chunk < BN / 32; ++chunk) {
+            for (int chunk = half * (BN / 64); chunk < (half + 1) * (BN / 64); ++chunk) {
                 const int col0 = nt * BN + chunk * 32;
                 if (col0 >= n) break;
                 uint32_t r[32];
                 tc_ld_32x32b_x32(tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) +
                                      static_cast<uint32_t>(acc * BN + chunk * 32),
                                  r);
+                const float bias_lane = (bias != nullptr && col0 + lane < n) ? __ldg(bias + col0 + lane) : 0.0f;
                 tc_wait_ld();
                 float v[32];
 #pragma unroll
                 for (int i = 0; i < 32; ++i) {
-                    float x = __uint_as_float(r[i]);
-                    if (bias != nullptr && col0 + i < n) x += __ldg(bias + col0 + i);
+                    float x = __uint_as_float(r[i]) + __shfl_sync(0xffffffffu, bias_lane, i);
                     if (epilogue == SAMQ_EPILOGUE_GELU_ERF) x = gelu_erf(x);
                     v[i] = x;
                 }
-                if (lane == 0) bulk_wait_group_read<1>();
+                if (lane == 0) bulk_wait_group_read<kOutBuffers - 1>();
                 __syncwarp();
                 uint8_t* sbuf = stage_buf + buf * kOutChunkBytes;
 #pragma unroll
@@ -204,7 +209,7 @@ gemm_f16_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant
                     tma_store_2d(&tma_y, sbuf, col0, row0);
                     bulk_commit_group();
                 }
-                buf ^= 1;
+                buf = (buf + 1) % kOutBuffers;
             }
             tc_fence_before();
             __syncwarp();
@@ -255,9 +260,9 @@ void launch_gemm_f16(const __half* a, int64_t lda, const __half* b, int64_t m, i
                      cudaStream_t stream) {
     if (m == 0) return;
     if (n <= 128)
-        run<128, 6>(a, lda, b, m, n, k, bias, epilogue, y, ldy, state, stream);
+        run<128, 5>(a, lda, b, m, n, k, bias, epilogue, y, ldy, state, stream);
     else
-        run<256, 4>(a, lda, b, m, n, k, bias, epilogue, y, ldy, state, stream);
+        run<256, 3>(a, lda, b, m, n, k, bias, epilogue, y, ldy, state, stream);
 }
 
 }  // namespace samq

@@ -11,7 +11,7 @@
 #include <string>
 #include <unordered_map>
 
-#include "../../include/samq.h"
+#include "samq.h"
 #include "samq_device.cuh"
 
 namespace samq {
