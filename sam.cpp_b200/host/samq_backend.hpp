@@ -1,0 +1,119 @@
+// samq_backend.hpp -- C++17 host layer over the samq C ABI, shaped like the
+// reference runtime's backend driver so SAM.cpp's runtime can select it.
+//
+// Mirrors (paths relative to the SAM.cpp tree):
+//   make_samq_backend     <- make_cuda_backend (src/runtime/ggml/backends/cuda.hpp:156-189):
+//                            same argument meaning (visible CUDA device index) and the same
+//                            failure style (std::runtime_error with a message).
+//   QuantizedLinear       <- one ggml_mul_mat(W_packed, X_f32) node built by
+//                            sam3_channel_projection (src/models/sam3/ops.hpp:40-45) with its
+//                            bias add and optional ggml_gelu_erf (src/models/sam3/vision.hpp:234-238).
+//   ActivationCounters    <- CudaActivationPolicy::record (src/runtime/ggml/backends/cuda_activation.hpp:62-77):
+//                            one launch per request, payload and allocation peaks.
+// Header-only; link with libsamq.so.
+#pragma once
+
+#include <cuda_runtime_api.h>
+
+#include <algorithm>
+#include <cstddef>
+#include <cstdint>
+#include <stdexcept>
+#include <string>
+#include <utility>
+
+#include "samq.h"
+
+namespace sam::internal {
+
+enum class LinearEpilogue { None = SAMQ_EPILOGUE_NONE, GeluErf = SAMQ_EPILOGUE_GELU_ERF };
+
+inline void samq_require(samq_status status, const char* what) {
+    if (status != SAMQ_OK) throw std::runtime_error(std::string(what) + ": " + samq_last_error_v1());
+}
+
+// Device-side ownership and identity, as BackendDriver carries them.
+struct SamqDriver {
+    int cuda_device = -1;
+    std::string device_name;
+    int sm_count = 0;
+};
+
+inline SamqDriver make_samq_backend(int device_index) {
+    if (device_index < 0) throw std::runtime_error("requested CUDA device index is out of range for visible devices");
+    struct samq_capabilities_v1 info{};  // "struct": the function of the same name hides the type
+    samq_require(samq_capabilities_v1(device_index, &info), "requested samq CUDA device is unavailable");
+    samq_require(samq_init_v1(device_index), "requested samq CUDA backend failed initialization");
+    SamqDriver driver;
+    driver.cuda_device = device_index;
+    driver.device_name = info.name;
+    driver.sm_count = info.sm_count;
+    return driver;
+}
+
+// Counters in the shape of RuntimeStats' activation fields (include/sam/types.hpp:56-57).
+struct ActivationCounters {
+    std::uint64_t activation_requests = 0, activation_launches = 0;
+    std::uint64_t activation_payload_peak_bytes = 0, activation_allocation_peak_bytes = 0;
+};
+
+// One packed weight matrix resident on the driver's device and the linear it feeds.
+class QuantizedLinear {
+public:
+    QuantizedLinear(const SamqDriver& driver, int ggml_type, std::int64_t k, std::int64_t n, const void* gguf_rows,
+                    std::size_t bytes, cudaStream_t stream = nullptr)
+        : k_(k), n_(n) {
+        samq_require(samq_weights_create_v1(driver.cuda_device, ggml_type, k, n, gguf_rows, bytes, stream, &weights_),
+                     "samq rejected the packed weight");
+    }
+    QuantizedLinear(const QuantizedLinear&) = delete;
+    QuantizedLinear& operator=(const QuantizedLinear&) = delete;
+    QuantizedLinear(QuantizedLinear&& other) noexcept
+        : weights_(std::exchange(other.weights_, nullptr)), k_(other.k_), n_(other.n_) {}
+    ~QuantizedLinear() {
+        if (weights_) samq_weights_destroy_v1(weights_);
+    }
+
+    std::int64_t width() const { return k_; }
+    std::int64_t rows() const { return n_; }
+
+    // Y[m][n] = epilogue(X[m][k] . W^T + bias); device pointers, caller-owned.
+    void forward(const float* x, std::int64_t m, std::int64_t ldx, const float* bias, LinearEpilogue epilogue,
+                 float* y, std::int64_t ldy, cudaStream_t stream, ActivationCounters* counters = nullptr) const {
+        samq_counters_v1 before{};
+        if (counters) samq_require(samq_query_v1(weights_, &before), "samq execution identity missing");
+        samq_require(samq_linear_v1(weights_, x, m, ldx, bias, static_cast<int>(epilogue), y, ldy, stream),
+                     "samq quantized linear failed");
+        if (counters && m > 0) {
+            samq_counters_v1 after{};
+            samq_require(samq_query_v1(weights_, &after), "samq execution identity missing");
+            if (after.version != 1 || after.launches != before.launches + 1 || after.payload_bytes == 0 ||
+                after.allocation_bytes < after.payload_bytes)
+                throw std::runtime_error("samq request did not execute exactly one tensor-core GEMM");
+            ++counters->activation_requests;
+            ++counters->activation_launches;
+            counters->activation_payload_peak_bytes =
+                std::max<std::uint64_t>(counters->activation_payload_peak_bytes, after.payload_bytes);
+            counters->activation_allocation_peak_bytes =
+                std::max<std::uint64_t>(counters->activation_allocation_peak_bytes, after.allocation_bytes);
+        }
+    }
+
+    // Packed bytes back in GGUF layout (bit-exact round trip of the load-time repack).
+    void export_rows(void* gguf_rows, std::size_t bytes) const {
+        samq_require(samq_weights_export_v1(weights_, gguf_rows, bytes), "samq weight export failed");
+    }
+
+    const samq_weights* handle() const { return weights_; }
+
+private:
+    samq_weights* weights_ = nullptr;
+    std::int64_t k_ = 0, n_ = 0;
+};
+
+// Post-compute device findings (range / timeout), as the reference's RHS check raises them.
+inline void samq_check_device(const SamqDriver& driver, cudaStream_t stream) {
+    samq_require(samq_check_v1(driver.cuda_device, stream), "samq device check failed");
+}
+
+}  // namespace sam::internal
