@@ -158,6 +158,28 @@ samq_status samq_query_v1(const samq_weights* weights, struct samq_counters_v1* 
  * (cmake/patches/ggml-native-activation.patch:148-171). */
 samq_status samq_check_v1(int device, void* stream);
 
+/* Allocation-free variant of samq_linear_v1 (same arguments, same result).
+ * It has no counterpart in the reference.  It serves callers that cannot let a
+ * library call cudaMalloc: a framework whose caching allocator already owns the
+ * device memory (a library cudaMalloc would fail or fragment its pool), serving
+ * loops that cannot absorb cudaMalloc's implicit device synchronization, and
+ * hosts that must not meet an out-of-memory error in the middle of a request.
+ * The staged activation operand lives in a file-scope device array of
+ * SAMQ_STATIC_OPERAND_ELEMENTS f16 values (32 MiB, held by every GPU that loads
+ * the library until the process exits) instead of library scratch; the call
+ * makes no cudaMalloc, cudaFree or other allocating call.  m * k above
+ * SAMQ_STATIC_OPERAND_ELEMENTS is rejected with SAMQ_ERR_INVALID_ARGUMENT
+ * (split the rows across calls).  The first call on a device looks up the
+ * array's device address once (cudaGetSymbolAddress with that device current);
+ * make that first call before any stream capture.  All calls on a device share
+ * the array and it keeps the last call's contents (nothing in it needs to start
+ * at zero): calls whose GPU work overlaps in time race on it, so order them on
+ * one stream.  Range and timeout findings are not recorded for samq_check_v1 on
+ * this path. */
+#define SAMQ_STATIC_OPERAND_ELEMENTS 16777216
+samq_status samq_linear_static_v1(const samq_weights* weights, const float* x, int64_t m, int64_t ldx,
+                                  const float* bias, int epilogue, float* y, int64_t ldy, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -64,7 +64,9 @@ SIGNATURES = {
     "samq_linear_f16_v1": (_i32, [_vp, _vp, _i64, _i64, _vp, _i32, _vp, _i64, _vp]),
     "samq_query_v1": (_i32, [_vp, ctypes.POINTER(Counters)]),
     "samq_check_v1": (_i32, [_i32, _vp]),
+    "samq_linear_static_v1": (_i32, [_vp, _vp, _i64, _i64, _vp, _i32, _vp, _i64, _vp]),
 }
+STATIC_OPERAND_ELEMENTS = 16777216
 
 
 class SamqError(RuntimeError):
@@ -206,6 +208,12 @@ def stage_f16(x, rows: int, k: int, ld: int, out, stream=None):
 def linear_f16(w: Weights, x16, m: int, ldx: int, bias, epilogue: int, y, ldy: int, stream=None):
     _check(library().samq_linear_f16_v1(w.handle, _addr(x16), m, ldx, _addr(bias), epilogue, _addr(y), ldy,
                                         _stream(stream)))
+
+
+def linear_static(w: Weights, x, m: int, ldx: int, bias, epilogue: int, y, ldy: int, stream=None):
+    """samq_linear_static_v1: samq_linear_v1 without any device allocation."""
+    _check(library().samq_linear_static_v1(w.handle, _addr(x), m, ldx, _addr(bias), epilogue, _addr(y), ldy,
+                                           _stream(stream)))
 
 
 def check(device: int = 0, stream=None):
