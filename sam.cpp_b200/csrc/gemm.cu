@@ -32,7 +32,7 @@ constexpr int BK = 64;   // 64 f16 = 128 bytes = one swizzle row
 constexpr int kEpilogueWarps = 8;  // two per TMEM lane quarter, each owning half of the tile's columns
 constexpr int kThreads = 64 + 32 * kEpilogueWarps;
 constexpr int kOutChunkBytes = 32 * 32 * 4;  // 32 rows x 32 f32 columns
-constexpr int kOutBuffers = 2;               // staging buffers per epilogue warp
+constexpr int kOutBuffers = 1;               // staging buffers per epilogue warp (4 stages fit beside them)
 
 template <int BN, int STAGES>
 struct Layout {
@@ -260,9 +260,9 @@ void launch_gemm_f16(const __half* a, int64_t lda, const __half* b, int64_t m, i
                      cudaStream_t stream) {
     if (m == 0) return;
     if (n <= 128)
-        run<128, 5>(a, lda, b, m, n, k, bias, epilogue, y, ldy, state, stream);
+        run<128, 6>(a, lda, b, m, n, k, bias, epilogue, y, ldy, state, stream);
     else
-        run<256, 3>(a, lda, b, m, n, k, bias, epilogue, y, ldy, state, stream);
+        run<256, 4>(a, lda, b, m, n, k, bias, epilogue, y, ldy, state, stream);
 }
 
 }  // namespace samq

@@ -15,6 +15,9 @@
 //
 // Memory layout: every thread owns 8 consecutive values (two 16-byte loads,
 // one 16-byte f16 store); four neighbouring lanes form one 32-value block.
+#include <algorithm>
+#include <climits>
+
 #include "samq_internal.hpp"
 
 namespace samq {
@@ -63,21 +66,11 @@ __device__ __forceinline__ void record_range(bool bad, DeviceStatus* status) {
     }
 }
 
-__global__ void __launch_bounds__(256) act_f16_kernel(const float* __restrict__ x, int64_t rows, int64_t k,
-                                                      int64_t ld, __half* __restrict__ a,
-                                                      uint8_t* __restrict__ q8_1, DeviceStatus* status) {
-    const int64_t per_row = k / 8;
-    const int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-    const bool active = idx < rows * per_row;
-    const int64_t row = active ? idx / per_row : 0;
-    const int64_t c8 = active ? idx % per_row : 0;
-    float v[8];
-    if (active) {
-        load8(x + row * ld + c8 * 8, v);
-    } else {
-#pragma unroll
-        for (int j = 0; j < 8; ++j) v[j] = 0.0f;
-    }
+// One 8-value unit: staging arithmetic and stores.  Every lane of the warp
+// calls it (shuffles), inactive lanes with zeros.
+__device__ __forceinline__ void stage_unit(const float (&v)[8], bool active, int64_t row, int64_t c8, int64_t k,
+                                           __half* __restrict__ a, uint8_t* __restrict__ q8_1,
+                                           DeviceStatus* status) {
     const float amax = group_amax(v);
     const float d = __fdiv_rn(amax, 127.0f);
     const __half dh = __float2half_rn(d);
@@ -115,6 +108,40 @@ __global__ void __launch_bounds__(256) act_f16_kernel(const float* __restrict__ 
         }
     }
     if (active && a) *reinterpret_cast<uint4*>(a + row * k + c8 * 8) = *reinterpret_cast<const uint4*>(out);
+}
+
+// U units per thread: unit idx + j*T for j < U (T = total threads, a multiple
+// of 4 so 4-lane groups stay aligned to 32-value blocks).  All loads are
+// issued before any unit is processed; the grid is sized so that one wave of
+// resident blocks covers the input.
+template <int U>
+__global__ void __launch_bounds__(256) act_f16_kernel(const float* __restrict__ x, int64_t rows, int64_t k,
+                                                      int64_t ld, __half* __restrict__ a,
+                                                      uint8_t* __restrict__ q8_1, DeviceStatus* status) {
+    const int64_t per_row = k / 8;
+    const int64_t units = rows * per_row;
+    const int64_t total = static_cast<int64_t>(gridDim.x) * blockDim.x;
+    for (int64_t base = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+         base - threadIdx.x % 32 < units; base += total * U) {
+        float v[U][8];
+        bool act[U];
+        int64_t row[U], c8[U];
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+            const int64_t idx = base + u * total;
+            act[u] = idx < units;
+            row[u] = act[u] ? idx / per_row : 0;
+            c8[u] = act[u] ? idx % per_row : 0;
+            if (act[u]) {
+                load8(x + row[u] * ld + c8[u] * 8, v[u]);
+            } else {
+#pragma unroll
+                for (int j = 0; j < 8; ++j) v[u][j] = 0.0f;
+            }
+        }
+#pragma unroll
+        for (int u = 0; u < U; ++u) stage_unit(v[u], act[u], row[u], c8[u], k, a, q8_1, status);
+    }
 }
 
 __global__ void __launch_bounds__(256) q8_1_to_f16_kernel(const uint8_t* __restrict__ q8_1, int64_t rows, int64_t k,
@@ -177,10 +204,52 @@ unsigned grid_for(int64_t threads) { return static_cast<unsigned>((threads + 255
 
 }  // namespace
 
+// Units per thread (1..4): each extra unit keeps two more 16-byte loads in
+// flight but costs registers, i.e. resident blocks.  The choice minimizes
+// (waves of resident blocks) x (units per thread), the length of the
+// critical path in units per thread.
+int choose_units_per_thread(int64_t units, int device) {
+    static int sms[64] = {};
+    static int occupancy[64][5] = {};
+    if (!sms[device & 63]) {
+        check_cuda(cudaDeviceGetAttribute(&sms[device & 63], cudaDevAttrMultiProcessorCount, device),
+                   "cudaDeviceGetAttribute");
+        const void* kernels[5] = {nullptr, reinterpret_cast<const void*>(act_f16_kernel<1>),
+                                  reinterpret_cast<const void*>(act_f16_kernel<2>),
+                                  reinterpret_cast<const void*>(act_f16_kernel<3>),
+                                  reinterpret_cast<const void*>(act_f16_kernel<4>)};
+        for (int u = 1; u <= 4; ++u)
+            check_cuda(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occupancy[device & 63][u], kernels[u], 256, 0),
+                       "cudaOccupancyMaxActiveBlocksPerMultiprocessor");
+    }
+    int best = 1;
+    int64_t best_cost = INT64_MAX;
+    for (int u = 1; u <= 4; ++u) {
+        const int64_t blocks = (units + 256 * u - 1) / (256 * u);
+        const int64_t resident = static_cast<int64_t>(sms[device & 63]) * std::max(occupancy[device & 63][u], 1);
+        const int64_t cost = (blocks + resident - 1) / resident * u;
+        if (cost < best_cost) {
+            best_cost = cost;
+            best = u;
+        }
+    }
+    return best;
+}
+
 void launch_act_f16(const float* x, int64_t rows, int64_t k, int64_t ld, __half* a_out, uint8_t* q8_1_out,
                     DeviceStatus* status, cudaStream_t stream) {
     if (rows == 0) return;
-    act_f16_kernel<<<grid_for(rows * (k / 8)), 256, 0, stream>>>(x, rows, k, ld, a_out, q8_1_out, status);
+    int device = 0;
+    check_cuda(cudaGetDevice(&device), "cudaGetDevice");
+    const int64_t units = rows * (k / 8);
+    const int u = choose_units_per_thread(units, device);
+    const unsigned grid = grid_for((units + u - 1) / u);
+    switch (u) {
+        case 1: act_f16_kernel<1><<<grid, 256, 0, stream>>>(x, rows, k, ld, a_out, q8_1_out, status); break;
+        case 2: act_f16_kernel<2><<<grid, 256, 0, stream>>>(x, rows, k, ld, a_out, q8_1_out, status); break;
+        case 3: act_f16_kernel<3><<<grid, 256, 0, stream>>>(x, rows, k, ld, a_out, q8_1_out, status); break;
+        default: act_f16_kernel<4><<<grid, 256, 0, stream>>>(x, rows, k, ld, a_out, q8_1_out, status); break;
+    }
     check_cuda(cudaGetLastError(), "act_f16_kernel launch");
 }
 
