@@ -66,6 +66,23 @@ __device__ __forceinline__ void record_range(bool bad, DeviceStatus* status) {
     }
 }
 
+// roundf() for |y| < 2^22 without float/int conversions: round half away
+// from zero is trunc(|y| + 0.5) with the sign of y; the sum is taken rounding
+// toward zero (so 0.49999997 + 0.5 stays below 1) and the truncation is the
+// exact round-toward-zero add/subtract of 2^23.  Adding +0 at the end turns a
+// negative zero into +0, as the integer code it stands for has no sign.
+__device__ __forceinline__ float round_half_away(float y) {
+    const float t = __fadd_rz(fabsf(y), 0.5f);
+    const float whole = __fsub_rz(__fadd_rz(t, 8388608.0f), 8388608.0f);
+    return __fadd_rn(copysignf(whole, y), 0.0f);
+}
+
+// Low byte of an integral float q with |q| <= 127 (two's complement int8):
+// adding 1.5 * 2^23 places the integer in the low mantissa bits.
+__device__ __forceinline__ uint32_t code_byte(float q) {
+    return __float_as_uint(__fadd_rn(q, 12582912.0f)) & 0xffu;
+}
+
 // One 8-value unit: staging arithmetic and stores.  Every lane of the warp
 // calls it (shuffles), inactive lanes with zeros.
 __device__ __forceinline__ void stage_unit(const float (&v)[8], bool active, int64_t row, int64_t c8, int64_t k,
@@ -77,14 +94,15 @@ __device__ __forceinline__ void stage_unit(const float (&v)[8], bool active, int
     const float dq = __half2float(dh);
     const float inv = amax == 0.0f ? 0.0f : __fdiv_rn(127.0f, amax);
     bool bad = false;
-    int q[8];
-    __align__(16) __half out[8];
+    float q[8];
+    __align__(16) __half2 out[4];
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
         bad |= !(fabsf(v[j]) <= kOperandLimit);
-        q[j] = static_cast<int>(roundf(__fmul_rn(v[j], inv)));
-        out[j] = __float2half_rn(__fmul_rn(dq, static_cast<float>(q[j])));
+        q[j] = round_half_away(__fmul_rn(v[j], inv));
     }
+#pragma unroll
+    for (int j = 0; j < 4; ++j) out[j] = __floats2half2_rn(__fmul_rn(dq, q[2 * j]), __fmul_rn(dq, q[2 * j + 1]));
     record_range(bad && active, status);
     if (q8_1) {
         const float sum = group_butterfly_sum(v);
@@ -94,8 +112,8 @@ __device__ __forceinline__ void stage_unit(const float (&v)[8], bool active, int
             uint32_t lo = 0, hi = 0;
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
-                lo |= (static_cast<uint32_t>(q[j]) & 0xffu) << (8 * j);
-                hi |= (static_cast<uint32_t>(q[j + 4]) & 0xffu) << (8 * j);
+                lo |= code_byte(q[j]) << (8 * j);
+                hi |= code_byte(q[j + 4]) << (8 * j);
             }
             uint32_t* words = reinterpret_cast<uint32_t*>(blk);
             words[1 + 2 * lane_in_group] = lo;
@@ -110,30 +128,28 @@ __device__ __forceinline__ void stage_unit(const float (&v)[8], bool active, int
     if (active && a) *reinterpret_cast<uint4*>(a + row * k + c8 * 8) = *reinterpret_cast<const uint4*>(out);
 }
 
-// U units per thread: unit idx + j*T for j < U (T = total threads, a multiple
-// of 4 so 4-lane groups stay aligned to 32-value blocks).  All loads are
-// issued before any unit is processed; the grid is sized so that one wave of
-// resident blocks covers the input.
-template <int U>
+template <int U, class Index>
 __global__ void __launch_bounds__(256) act_f16_kernel(const float* __restrict__ x, int64_t rows, int64_t k,
                                                       int64_t ld, __half* __restrict__ a,
                                                       uint8_t* __restrict__ q8_1, DeviceStatus* status) {
-    const int64_t per_row = k / 8;
-    const int64_t units = rows * per_row;
-    const int64_t total = static_cast<int64_t>(gridDim.x) * blockDim.x;
-    for (int64_t base = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    // Index arithmetic in `Index` (uint32_t whenever rows * k / 8 < 2^32: a
+    // 64-bit division per unit costs more than the unit's quantization).
+    const Index per_row = static_cast<Index>(k / 8);
+    const Index units = static_cast<Index>(rows) * per_row;
+    const Index total = static_cast<Index>(gridDim.x) * blockDim.x;
+    for (Index base = static_cast<Index>(blockIdx.x) * blockDim.x + threadIdx.x;
          base - threadIdx.x % 32 < units; base += total * U) {
         float v[U][8];
         bool act[U];
-        int64_t row[U], c8[U];
+        Index row[U], c8[U];
 #pragma unroll
         for (int u = 0; u < U; ++u) {
-            const int64_t idx = base + u * total;
+            const Index idx = base + static_cast<Index>(u) * total;
             act[u] = idx < units;
             row[u] = act[u] ? idx / per_row : 0;
-            c8[u] = act[u] ? idx % per_row : 0;
+            c8[u] = act[u] ? idx - row[u] * per_row : 0;
             if (act[u]) {
-                load8(x + row[u] * ld + c8[u] * 8, v[u]);
+                load8(x + static_cast<int64_t>(row[u]) * ld + static_cast<int64_t>(c8[u]) * 8, v[u]);
             } else {
 #pragma unroll
                 for (int j = 0; j < 8; ++j) v[u][j] = 0.0f;
@@ -214,10 +230,10 @@ int choose_units_per_thread(int64_t units, int device) {
     if (!sms[device & 63]) {
         check_cuda(cudaDeviceGetAttribute(&sms[device & 63], cudaDevAttrMultiProcessorCount, device),
                    "cudaDeviceGetAttribute");
-        const void* kernels[5] = {nullptr, reinterpret_cast<const void*>(act_f16_kernel<1>),
-                                  reinterpret_cast<const void*>(act_f16_kernel<2>),
-                                  reinterpret_cast<const void*>(act_f16_kernel<3>),
-                                  reinterpret_cast<const void*>(act_f16_kernel<4>)};
+        const void* kernels[5] = {nullptr, reinterpret_cast<const void*>(act_f16_kernel<1, uint32_t>),
+                                  reinterpret_cast<const void*>(act_f16_kernel<2, uint32_t>),
+                                  reinterpret_cast<const void*>(act_f16_kernel<3, uint32_t>),
+                                  reinterpret_cast<const void*>(act_f16_kernel<4, uint32_t>)};
         for (int u = 1; u <= 4; ++u)
             check_cuda(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occupancy[device & 63][u], kernels[u], 256, 0),
                        "cudaOccupancyMaxActiveBlocksPerMultiprocessor");
@@ -243,12 +259,19 @@ void launch_act_f16(const float* x, int64_t rows, int64_t k, int64_t ld, __half*
     check_cuda(cudaGetDevice(&device), "cudaGetDevice");
     const int64_t units = rows * (k / 8);
     const int u = choose_units_per_thread(units, device);
+    if (units + 4 * 256 >= (int64_t(1) << 32)) {
+        // Beyond 32-bit unit indices: 64-bit index math, 4 units per thread per pass.
+        const unsigned grid = grid_for(std::min<int64_t>((units + 3) / 4, int64_t(1) << 24));
+        act_f16_kernel<4, uint64_t><<<grid, 256, 0, stream>>>(x, rows, k, ld, a_out, q8_1_out, status);
+        check_cuda(cudaGetLastError(), "act_f16_kernel launch");
+        return;
+    }
     const unsigned grid = grid_for((units + u - 1) / u);
     switch (u) {
-        case 1: act_f16_kernel<1><<<grid, 256, 0, stream>>>(x, rows, k, ld, a_out, q8_1_out, status); break;
-        case 2: act_f16_kernel<2><<<grid, 256, 0, stream>>>(x, rows, k, ld, a_out, q8_1_out, status); break;
-        case 3: act_f16_kernel<3><<<grid, 256, 0, stream>>>(x, rows, k, ld, a_out, q8_1_out, status); break;
-        default: act_f16_kernel<4><<<grid, 256, 0, stream>>>(x, rows, k, ld, a_out, q8_1_out, status); break;
+        case 1: act_f16_kernel<1, uint32_t><<<grid, 256, 0, stream>>>(x, rows, k, ld, a_out, q8_1_out, status); break;
+        case 2: act_f16_kernel<2, uint32_t><<<grid, 256, 0, stream>>>(x, rows, k, ld, a_out, q8_1_out, status); break;
+        case 3: act_f16_kernel<3, uint32_t><<<grid, 256, 0, stream>>>(x, rows, k, ld, a_out, q8_1_out, status); break;
+        default: act_f16_kernel<4, uint32_t><<<grid, 256, 0, stream>>>(x, rows, k, ld, a_out, q8_1_out, status); break;
     }
     check_cuda(cudaGetLastError(), "act_f16_kernel launch");
 }
