@@ -6,20 +6,26 @@
 // X = A (src/models/sam3/ops.hpp:40-45), with the bias add and ggml_gelu_erf
 // of the ViT MLP fused (src/models/sam3/vision.hpp:234-236).
 //
-// Persistent, warp-specialised kernel, one CTA per SM (320 threads):
+// Persistent, warp-specialised kernel, one CTA per SM (64 + 32*EW threads):
 //   warp 0     TMA producer: 128x64 A and BNx64 B tiles, 128-byte swizzle,
 //              into a STAGES-deep shared-memory ring (full/empty mbarriers);
 //   warp 1     TMEM owner and MMA issuer: one thread issues
 //              tcgen05.mma.cta_group::1.kind::f16 (M=128, N=BN, K=16) into a
 //              double-buffered f32 accumulator (2 x BN TMEM columns), then
 //              tcgen05.commit to release the smem stage / publish the tile;
-//   warps 2-9  epilogue: two warps per TMEM lane quarter (the quarter a warp
-//              may access is warp % 4), each owning half of the tile's
-//              columns; tcgen05.ld 32 columns at a time, bias (one coalesced
-//              load per 32 columns, broadcast by warp shuffles) + erf-GELU in
-//              registers, swizzled staging in shared memory, TMA store
-//              (clipped at the m / n edges).  The next tile's MMAs overlap
-//              this epilogue.
+//   warps 2..  EW epilogue warps, EW/4 per TMEM lane quarter (the quarter a
+//              warp may access is warp % 4), each owning 1/(EW/4) of the
+//              tile's columns: tcgen05.ld 32 columns at a time, bias (one
+//              coalesced load per 32 columns, broadcast by warp shuffles) and
+//              erf-GELU in registers, swizzled staging in shared memory, TMA
+//              store (clipped at the m / n edges).  The next tile's MMAs
+//              overlap this epilogue.
+// Measured on B200 (ViT shapes, M=5184): without the epilogue the mainloop
+// runs at ~90% of the measured bf16 peak per tile, so the epilogue and wave
+// quantization set the pace.  EW=8 with 4 stages is best without GELU, EW=16
+// with 3 stages with erf-GELU.  A CTA-pair (cta_group::2, 256xBN tile)
+// variant was built and verified but measured slower (qkv mainloop 29.2 vs
+// 26.6 us), so it is not used.
 // No TMA load uses cluster multicast.  Every mbarrier wait is bounded and
 // reports kStatusTimeout instead of hanging.
 #include <algorithm>
@@ -245,184 +251,6 @@ gemm_f16_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant
     }
 }
 
-// ---------------------------------------------------------------------------
-// CTA-pair variant: a cluster of two CTAs on two SMs computes a 256 x BN tile
-// with tcgen05.mma.cta_group::2 (M=256, N=BN, K=16).  CTA r of the pair loads
-// A rows [128r, 128r+128) and B rows [r*BN/2, (r+1)*BN/2) of the tile into its
-// own shared memory; the pair MMA reads both CTAs' halves, and each CTA's TMEM
-// holds its 128 rows x BN columns of the accumulator.  Per SM and K step this
-// moves 32 KB instead of the 48 KB of a 128 x 256 single-CTA tile, for the
-// same tensor work.
-//   even CTA, warp 0 / odd CTA, warp 0: TMA producers of their halves; both
-//       signal the even CTA's `full` barrier (expect_tx covers both halves);
-//   even CTA, warp 1: TMEM (both CTAs allocate together) and the MMA issuer;
-//       its commits release `empty` stages and publish `tfull` in both CTAs;
-//   warps 2-9 of both CTAs: epilogue of their own 128 rows; they return the
-//       accumulator through the even CTA's `tempty` barrier.
-// No TMA load uses multicast; remote signals go through mapa addresses.
-template <int BN, int STAGES, int EW>
-struct PairLayout {
-    static constexpr int a_bytes = 128 * BK * 2;
-    static constexpr int b_bytes = (BN / 2) * BK * 2;
-    static constexpr int stage_tx = 2 * (a_bytes + b_bytes);  // both CTAs' halves
-    static constexpr int a_off = 0;
-    static constexpr int b_off = STAGES * a_bytes;
-    static constexpr int out_off = b_off + STAGES * b_bytes;
-    static constexpr int bar_off = out_off + EW * kOutBuffers * kOutChunkBytes;
-    static constexpr int bar_bytes = (2 * STAGES + 5) * 8 + 8;
-    static constexpr int total = bar_off + bar_bytes + 1024;
-    static constexpr uint32_t tmem_cols = 2 * BN;
-};
-
-template <int BN, int STAGES, int EW>
-__global__ void __launch_bounds__(threads_for(EW), 1)
-gemm_f16_pair_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_b,
-                     const __grid_constant__ CUtensorMap tma_y, const float* __restrict__ bias, int epilogue, int m,
-                     int n, int k, DeviceStatus* status) {
-    using L = PairLayout<BN, STAGES, EW>;
-    static_assert(L::total <= 232448, "shared memory budget");
-    extern __shared__ uint8_t smem_raw[];
-    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    uint8_t* sa = smem + L::a_off;
-    uint8_t* sb = smem + L::b_off;
-    uint8_t* sout = smem + L::out_off;
-    uint64_t* full = reinterpret_cast<uint64_t*>(smem + L::bar_off);
-    uint64_t* empty = full + STAGES;
-    uint64_t* tfull = empty + STAGES;
-    uint64_t* tempty = tfull + 2;
-    uint64_t* drain = tempty + 2;
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
-
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const uint32_t rank = cluster_cta_rank();
-    const int pair = blockIdx.x >> 1, pairs = gridDim.x >> 1;
-    const int m_tiles = (m + 255) / 256, n_tiles = (n + BN - 1) / BN;
-    const int tiles = m_tiles * n_tiles;
-    const int kblocks = (k + BK - 1) / BK;
-
-    if (threadIdx.x == 0) {
-        for (int s = 0; s < STAGES; ++s) {
-            mbar_init(&full[s], 1);
-            mbar_init(&empty[s], 1);
-        }
-        for (int b = 0; b < 2; ++b) {
-            mbar_init(&tfull[b], 1);
-            mbar_init(&tempty[b], 2 * EW);
-        }
-        mbar_init(drain, 1);
-        fence_barrier_init();
-        tma_prefetch_desc(&tma_a);
-        tma_prefetch_desc(&tma_b);
-        tma_prefetch_desc(&tma_y);
-    }
-    if (warp == 1) tmem_alloc_pair(tmem_slot, L::tmem_cols);
-    tc_fence_before();
-    cluster_sync_all();  // barriers of both CTAs initialised, TMEM allocated
-    tc_fence_after();
-    const uint32_t tmem_base = *tmem_slot;
-
-    if (warp == 0) {
-        if (lane == 0) {
-            int s = 0;
-            uint32_t ph = 0;
-            bool ok = true;
-            for (int tile = pair; tile < tiles && ok; tile += pairs) {
-                const int mt = tile / n_tiles, nt = tile % n_tiles;
-                for (int kb = 0; kb < kblocks; ++kb) {
-                    if (!mbar_wait(&empty[s], ph ^ 1u, status, 11)) {
-                        ok = false;
-                        break;
-                    }
-                    const uint32_t full_even = cluster_map(&full[s], 0);
-                    if (rank == 0) mbar_arrive_expect_tx(&full[s], L::stage_tx);
-                    tma_load_2d_pair(sa + s * L::a_bytes, &tma_a, full_even, kb * BK,
-                                     mt * 256 + static_cast<int>(rank) * 128);
-                    tma_load_2d_pair(sb + s * L::b_bytes, &tma_b, full_even, kb * BK,
-                                     nt * BN + static_cast<int>(rank) * (BN / 2));
-                    if (++s == STAGES) {
-                        s = 0;
-                        ph ^= 1u;
-                    }
-                }
-            }
-            if (!ok) {
-                // Copies in flight signal the even CTA's barrier; give them time to land.
-                const uint64_t start = global_timer_ns();
-                while (global_timer_ns() - start < 2000000ull) __nanosleep(1000);
-            }
-        }
-    } else if (warp == 1) {
-        if (lane == 0 && rank == 0) {
-            constexpr uint32_t idesc = idesc_f16_f32(256, BN);
-            int s = 0;
-            uint32_t ph = 0;
-            int acc = 0;
-            uint32_t acc_ph = 0;
-            bool ok = true;
-            for (int tile = pair; tile < tiles && ok; tile += pairs) {
-                if (!mbar_wait<true>(&tempty[acc], acc_ph ^ 1u, status, 12)) break;
-                tc_fence_after();
-                const uint32_t d = tmem_base + static_cast<uint32_t>(acc * BN);
-                for (int kb = 0; kb < kblocks; ++kb) {
-                    if (!mbar_wait(&full[s], ph, status, 13)) {
-                        ok = false;
-                        break;
-                    }
-                    tc_fence_after();
-                    const uint32_t a_addr = smem_u32(sa + s * L::a_bytes);
-                    const uint32_t b_addr = smem_u32(sb + s * L::b_bytes);
-#pragma unroll
-                    for (int kk = 0; kk < BK / 16; ++kk)
-                        tc_mma_f16_pair(d, smem_desc_sw128(a_addr + kk * 32), smem_desc_sw128(b_addr + kk * 32),
-                                        idesc, (kb | kk) != 0 ? 1u : 0u);
-                    tc_commit_pair(cluster_map(&empty[s], 0));
-                    tc_commit_pair(cluster_map(&empty[s], 1));
-                    if (++s == STAGES) {
-                        s = 0;
-                        ph ^= 1u;
-                    }
-                }
-                if (!ok) break;
-                tc_commit_pair(cluster_map(&tfull[acc], 0));
-                tc_commit_pair(cluster_map(&tfull[acc], 1));
-                acc ^= 1;
-                if (acc == 0) acc_ph ^= 1u;
-            }
-            tc_commit_pair(cluster_map(drain, 0));
-            mbar_wait(drain, 0, status, 16);
-        }
-    } else {
-        const int quarter = warp & 3;
-        const int part = (warp - 2) >> 2;
-        uint8_t* stage_buf = sout + (warp - 2) * kOutBuffers * kOutChunkBytes;
-        const uint32_t tempty_even0 = cluster_map(&tempty[0], 0), tempty_even1 = cluster_map(&tempty[1], 0);
-        int acc = 0;
-        uint32_t acc_ph = 0;
-        int buf = 0;
-        for (int tile = pair; tile < tiles; tile += pairs) {
-            const int mt = tile / n_tiles, nt = tile % n_tiles;
-            if (!mbar_wait(&tfull[acc], acc_ph, status, 14)) break;
-            tc_fence_after();
-            const int row0 = mt * 256 + static_cast<int>(rank) * 128 + quarter * 32;
-            drain_tile<BN, EW / 4>(tmem_base, quarter, part, acc, row0, nt * BN, m, n, bias, epilogue, &tma_y, stage_buf, buf,
-                           lane);
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive_cluster(acc ? tempty_even1 : tempty_even0);
-            acc ^= 1;
-            if (acc == 0) acc_ph ^= 1u;
-        }
-        if (lane == 0) bulk_wait_group_all();
-        __syncwarp();
-    }
-    tc_fence_before();
-    cluster_sync_all();  // both CTAs done with TMEM and with each other's barriers
-    if (warp == 1) {
-        tc_fence_after();
-        tmem_dealloc_pair(tmem_base, L::tmem_cols);
-    }
-}
-
 template <int BN, int STAGES, int EW>
 void run(const __half* a, int64_t lda, const __half* b, int64_t m, int64_t n, int64_t k, const float* bias, int epilogue,
          float* y, int64_t ldy, DeviceState& state, cudaStream_t stream) {
@@ -448,43 +276,6 @@ void run(const __half* a, int64_t lda, const __half* b, int64_t m, int64_t n, in
     check_cuda(cudaGetLastError(), "gemm_f16_kernel launch");
 }
 
-template <int BN, int STAGES, int EW>
-void run_pair(const __half* a, int64_t lda, const __half* b, int64_t m, int64_t n, int64_t k, const float* bias,
-              int epilogue, float* y, int64_t ldy, DeviceState& state, cudaStream_t stream) {
-    using L = PairLayout<BN, STAGES, EW>;
-    CUtensorMap ta, tb, ty;
-    encode_tensor_map_2d(&ta, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, a, k, m, lda * 2, BK, 128,
-                         CU_TENSOR_MAP_SWIZZLE_128B);
-    encode_tensor_map_2d(&tb, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, b, k, n, k * 2, BK, BN / 2,
-                         CU_TENSOR_MAP_SWIZZLE_128B);
-    encode_tensor_map_2d(&ty, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, y, n, m, ldy * 4, 32, 32,
-                         CU_TENSOR_MAP_SWIZZLE_128B);
-    auto kernel = gemm_f16_pair_kernel<BN, STAGES, EW>;
-    static bool configured[64] = {};
-    if (!configured[state.device & 63]) {
-        check_cuda(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, L::total),
-                   "cudaFuncSetAttribute(pair gemm smem)");
-        configured[state.device & 63] = true;
-    }
-    const int64_t tiles = ((m + 255) / 256) * ((n + BN - 1) / BN);
-    const int64_t pairs = std::min<int64_t>(tiles, state.sm_count / 2);
-    cudaLaunchConfig_t cfg{};
-    cfg.gridDim = dim3(static_cast<unsigned>(2 * pairs));
-    cfg.blockDim = dim3(threads_for(EW));
-    cfg.dynamicSmemBytes = L::total;
-    cfg.stream = stream;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = 2;
-    attr[0].val.clusterDim.y = 1;
-    attr[0].val.clusterDim.z = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    check_cuda(cudaLaunchKernelEx(&cfg, kernel, ta, tb, ty, bias, epilogue, static_cast<int>(m), static_cast<int>(n),
-                                  static_cast<int>(k), state.status),
-               "gemm_f16_pair_kernel launch");
-}
-
 }  // namespace
 
 void launch_gemm_f16(const __half* a, int64_t lda, const __half* b, int64_t m, int64_t n, int64_t k,
@@ -493,10 +284,12 @@ void launch_gemm_f16(const __half* a, int64_t lda, const __half* b, int64_t m, i
     if (m == 0) return;
     if (n <= 128)
         run<128, 6, 8>(a, lda, b, m, n, k, bias, epilogue, y, ldy, state, stream);
-    else if (m <= 128 || state.sm_count < 2)
-        run<256, 4, 8>(a, lda, b, m, n, k, bias, epilogue, y, ldy, state, stream);
+    else if (epilogue == SAMQ_EPILOGUE_GELU_ERF)
+        // erf-GELU makes the epilogue the longer pipeline: 16 epilogue warps
+        // (3 operand stages fit beside their staging buffers).
+        run<256, 3, 16>(a, lda, b, m, n, k, bias, epilogue, y, ldy, state, stream);
     else
-        run_pair<256, 6, 8>(a, lda, b, m, n, k, bias, epilogue, y, ldy, state, stream);
+        run<256, 4, 8>(a, lda, b, m, n, k, bias, epilogue, y, ldy, state, stream);
 }
 
 }  // namespace samq
