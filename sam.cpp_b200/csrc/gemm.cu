@@ -29,6 +29,7 @@
 // No TMA load uses cluster multicast.  Every mbarrier wait is bounded and
 // reports kStatusTimeout instead of hanging.
 #include <algorithm>
+#include <climits>
 
 #include "samq_internal.hpp"
 
@@ -37,11 +38,21 @@ namespace {
 
 constexpr int BM = 128;
 constexpr int BK = 64;   // 64 f16 = 128 bytes = one swizzle row
+// The two accumulator buffers start 256 TMEM columns apart whatever BN is.
+constexpr int kAccStride = 256;
+
 // Epilogue warps per CTA (EW, 8 or 16): EW/4 warps per TMEM lane quarter,
 // each owning 1/(EW/4) of the tile's columns.
 constexpr int threads_for(int ew) { return 64 + 32 * ew; }
 constexpr int kOutChunkBytes = 32 * 32 * 4;  // 32 rows x 32 f32 columns
 constexpr int kOutBuffers = 1;               // staging buffers per epilogue warp (4 stages fit beside them)
+
+// Operand stages that fit in 227 KB beside EW staging buffers.
+constexpr int stages_for(int bn, int ew) {
+    return (232448 - 1024 - 256 - ew * 1 * 4096) / (128 * 64 * 2 + bn * 64 * 2) > 6
+               ? 6
+               : (232448 - 1024 - 256 - ew * 1 * 4096) / (128 * 64 * 2 + bn * 64 * 2);
+}
 
 template <int BN, int STAGES, int EW>
 struct Layout {
@@ -54,16 +65,35 @@ struct Layout {
     static constexpr int bar_off = out_off + EW * kOutBuffers * kOutChunkBytes;
     static constexpr int bar_bytes = (2 * STAGES + 5) * 8 + 8;
     static constexpr int total = bar_off + bar_bytes + 1024;  // + alignment slack
-    static constexpr uint32_t tmem_cols = 2 * BN;               // double-buffered accumulator
+    static constexpr uint32_t tmem_cols = 2 * kAccStride;       // double-buffered accumulator
 };
 
+// erf-GELU, 0.5 x (1 + erf(x / sqrt 2)), on the FMA pipe only: erf(z) for
+// z = |x|/sqrt(2) in [0, 4] is a degree-17 polynomial in u = (z - 2)/2 (a
+// Chebyshev least-squares fit, coefficients from csrc/fit_erf.py; max absolute
+// error 2.9e-7 in f32), and erf = 1 beyond z = 4 (true value 1 - 1.5e-8).
+// erff would keep the transcendental (XU) pipe saturated: on the fc1 shape it
+// was 84% busy and set the kernel's pace.
 __device__ __forceinline__ float gelu_erf(float x) {
-    return 0.5f * x * (1.0f + erff(x * 0.70710678118654752f));
+    constexpr float c[18] = {0.9953222870826721f,    0.04133397713303566f,  -0.16534042358398438f,
+                             0.38578349351882935f,   -0.5509889125823975f,  0.4188512861728668f,
+                             0.027940375730395317f,  -0.4324592351913452f,  0.4154498875141144f,
+                             -0.02610541321337223f,  -0.2951280176639557f,  0.21479764580726624f,
+                             0.0714806541800499f,    -0.1397237926721573f,  0.005857460666447878f,
+                             0.043319180607795715f,  -0.004593455232679844f, -0.0057971845380961895f};
+    const float z = fminf(fabsf(x) * 0.70710678118654752f, 4.0f);
+    const float u = fmaf(z, 0.5f, -1.0f);
+    float p = c[17];
+#pragma unroll
+    for (int i = 16; i >= 0; --i) p = fmaf(p, u, c[i]);
+    const float e = z >= 4.0f ? 1.0f : p;
+    return 0.5f * x * (1.0f + copysignf(e, x));
 }
 
 // One epilogue warp's share of an accumulator tile: TMEM lanes 32*quarter..+31
-// (output rows row0..row0+31) and columns [part*BN/PARTS, (part+1)*BN/PARTS)
-// of the tile starting at output column col_base.  32 columns at a time: tcgen05.ld,
+// (output rows row0..row0+31) and 32-column chunks [part*C/PARTS,
+// (part+1)*C/PARTS) of the C = BN/32 chunks of the tile starting at output
+// column col_base.  32 columns at a time: tcgen05.ld,
 // bias (one coalesced load, broadcast by shuffles), erf-GELU, swizzled staging
 // in shared memory, TMA store (clipped by the tensor map at the m / n edges).
 template <int BN, int PARTS>
@@ -72,12 +102,13 @@ __device__ __forceinline__ void drain_tile(uint32_t tmem_base, int quarter, int 
                                            int epilogue, const CUtensorMap* tma_y, uint8_t* stage_buf, int& buf,
                                            int lane) {
 #pragma unroll 1
-    for (int chunk = part * (BN / 32 / PARTS); chunk < (part + 1) * (BN / 32 / PARTS); ++chunk) {
+    constexpr int kChunks = BN / 32;
+    for (int chunk = part * kChunks / PARTS; chunk < (part + 1) * kChunks / PARTS; ++chunk) {
         const int col0 = col_base + chunk * 32;
         if (col0 >= n) break;
         uint32_t r[32];
         tc_ld_32x32b_x32(tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) +
-                             static_cast<uint32_t>(acc * BN + chunk * 32),
+                             static_cast<uint32_t>(acc * kAccStride + chunk * 32),
                          r);
         const float bias_lane = (bias != nullptr && col0 + lane < n) ? __ldg(bias + col0 + lane) : 0.0f;
         tc_wait_ld();
@@ -192,7 +223,7 @@ gemm_f16_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant
             for (int tile = blockIdx.x; tile < tiles && ok; tile += gridDim.x) {
                 if (!mbar_wait(&tempty[acc], acc_ph ^ 1u, status, 2)) break;
                 tc_fence_after();
-                const uint32_t d = tmem_base + static_cast<uint32_t>(acc * BN);
+                const uint32_t d = tmem_base + static_cast<uint32_t>(acc * kAccStride);
                 for (int kb = 0; kb < kblocks; ++kb) {
                     if (!mbar_wait(&full[s], ph, status, 3)) {
                         ok = false;
@@ -278,18 +309,49 @@ void run(const __half* a, int64_t lda, const __half* b, int64_t m, int64_t n, in
 
 }  // namespace
 
+// Tile width: the MMA N (multiple of 32 here) that minimizes
+// (waves of tiles over the SMs) x N, i.e. the per-SM critical path; ties go to
+// the wider tile (less operand traffic per FLOP).
+int choose_bn(int64_t m, int64_t n, int sms) {
+    static const int kWidths[4] = {256, 224, 192, 160};
+    int best = 256;
+    int64_t best_cost = INT64_MAX;
+    for (int bn : kWidths) {
+        const int64_t tiles = ((m + BM - 1) / BM) * ((n + bn - 1) / bn);
+        const int64_t cost = (tiles + sms - 1) / sms * bn;
+        if (cost < best_cost) {
+            best_cost = cost;
+            best = bn;
+        }
+    }
+    return best;
+}
+
+template <int EW>
+void run_width(int bn, const __half* a, int64_t lda, const __half* b, int64_t m, int64_t n, int64_t k,
+               const float* bias, int epilogue, float* y, int64_t ldy, DeviceState& state, cudaStream_t stream) {
+    switch (bn) {
+        case 160: run<160, stages_for(160, EW), EW>(a, lda, b, m, n, k, bias, epilogue, y, ldy, state, stream); break;
+        case 192: run<192, stages_for(192, EW), EW>(a, lda, b, m, n, k, bias, epilogue, y, ldy, state, stream); break;
+        case 224: run<224, stages_for(224, EW), EW>(a, lda, b, m, n, k, bias, epilogue, y, ldy, state, stream); break;
+        default: run<256, stages_for(256, EW), EW>(a, lda, b, m, n, k, bias, epilogue, y, ldy, state, stream); break;
+    }
+}
+
 void launch_gemm_f16(const __half* a, int64_t lda, const __half* b, int64_t m, int64_t n, int64_t k,
                      const float* bias, int epilogue, float* y, int64_t ldy, DeviceState& state,
                      cudaStream_t stream) {
     if (m == 0) return;
-    if (n <= 128)
+    if (n <= 128) {
         run<128, 6, 8>(a, lda, b, m, n, k, bias, epilogue, y, ldy, state, stream);
-    else if (epilogue == SAMQ_EPILOGUE_GELU_ERF)
-        // erf-GELU makes the epilogue the longer pipeline: 16 epilogue warps
-        // (3 operand stages fit beside their staging buffers).
-        run<256, 3, 16>(a, lda, b, m, n, k, bias, epilogue, y, ldy, state, stream);
+        return;
+    }
+    const int bn = choose_bn(m, n, state.sm_count);
+    if (epilogue == SAMQ_EPILOGUE_GELU_ERF)
+        // erf-GELU makes the epilogue the longer pipeline: 16 epilogue warps.
+        run_width<16>(bn, a, lda, b, m, n, k, bias, epilogue, y, ldy, state, stream);
     else
-        run<256, 4, 8>(a, lda, b, m, n, k, bias, epilogue, y, ldy, state, stream);
+        run_width<8>(bn, a, lda, b, m, n, k, bias, epilogue, y, ldy, state, stream);
 }
 
 }  // namespace samq

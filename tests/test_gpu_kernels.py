@@ -188,13 +188,14 @@ def test_linear_parity(samq, oracle, qtype, m, n, k):
     w.close()
 
 
-@pytest.mark.parametrize("epilogue", [0, 1])
-def test_linear_bias_gelu_and_strides(samq, oracle, epilogue):
+@pytest.mark.parametrize("epilogue,bias_scale", [(0, 0.5), (1, 0.5), (1, 8.0)])
+def test_linear_bias_gelu_and_strides(samq, oracle, epilogue, bias_scale):
+    """bias_scale 8 drives GELU arguments across the whole erf range (|x| up to ~30)."""
     rng = np.random.default_rng(31 + epilogue)
     qtype, m, n, k = 12, 70, 320, 512
     rows = oracle.quantize(qtype, weights_matrix(rng, n, k))
     x = rng.normal(0, 1, (m, k)).astype(np.float32)
-    bias = rng.normal(0, 0.5, n).astype(np.float32)
+    bias = rng.normal(0, bias_scale, n).astype(np.float32)
     w = samq.Weights(qtype, k, n, rows)
     y = run_linear(samq, w, x, bias=bias, epilogue=epilogue, ldx=k + 12, ldy=n + 8)
     semantic, exact = references(oracle, qtype, rows, x, n, k, bias=bias, epilogue=epilogue)
