@@ -271,7 +271,9 @@ gemm_f16_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant
             acc ^= 1;
             if (acc == 0) acc_ph ^= 1u;
         }
-        if (lane == 0) bulk_wait_group_all();
+        // The CTA may exit once its TMA stores have read their shared-memory
+        // sources; completion of the grid makes the global writes visible.
+        if (lane == 0) bulk_wait_group_read<0>();
         __syncwarp();
     }
     tc_fence_before();
