@@ -181,6 +181,9 @@ gemm_f16_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
+    // Everything above overlaps the previous kernel; A (and the output buffer)
+    // may be in use by it until it completes.
+    pdl_wait();
 
     if (warp == 0) {
         if (lane == 0) {
@@ -206,6 +209,7 @@ gemm_f16_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant
                     }
                 }
             }
+            pdl_trigger();  // all loads issued: the next kernel may begin its prologue
             if (!ok) {
                 // Let every copy already in flight land before the CTA exits.
                 for (int i = 0; i < STAGES; ++i)
@@ -304,9 +308,8 @@ void run(const __half* a, int64_t lda, const __half* b, int64_t m, int64_t n, in
     }
     const int64_t tiles = ((m + BM - 1) / BM) * ((n + BN - 1) / BN);
     const int grid = static_cast<int>(tiles < state.sm_count ? tiles : state.sm_count);
-    kernel<<<grid, threads_for(EW), L::total, stream>>>(ta, tb, ty, bias, epilogue, static_cast<int>(m),
-                                                 static_cast<int>(n), static_cast<int>(k), state.status);
-    check_cuda(cudaGetLastError(), "gemm_f16_kernel launch");
+    launch_pdl(kernel, dim3(grid), dim3(threads_for(EW)), L::total, stream, "gemm_f16_kernel launch", ta, tb, ty, bias,
+               epilogue, static_cast<int>(m), static_cast<int>(n), static_cast<int>(k), state.status);
 }
 
 }  // namespace

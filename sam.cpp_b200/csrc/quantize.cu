@@ -134,6 +134,8 @@ __global__ void __launch_bounds__(256) act_f16_kernel(const float* __restrict__ 
                                                       uint8_t* __restrict__ q8_1, DeviceStatus* status) {
     // Index arithmetic in `Index` (uint32_t whenever rows * k / 8 < 2^32: a
     // 64-bit division per unit costs more than the unit's quantization).
+    pdl_wait();     // X may come from, and the operand buffer may still be read by, the previous kernel
+    pdl_trigger();  // the GEMM that consumes this operand may start its prologue
     const Index per_row = static_cast<Index>(k / 8);
     const Index units = static_cast<Index>(rows) * per_row;
     const Index total = static_cast<Index>(gridDim.x) * blockDim.x;
@@ -262,16 +264,29 @@ void launch_act_f16(const float* x, int64_t rows, int64_t k, int64_t ld, __half*
     if (units + 4 * 256 >= (int64_t(1) << 32)) {
         // Beyond 32-bit unit indices: 64-bit index math, 4 units per thread per pass.
         const unsigned grid = grid_for(std::min<int64_t>((units + 3) / 4, int64_t(1) << 24));
-        act_f16_kernel<4, uint64_t><<<grid, 256, 0, stream>>>(x, rows, k, ld, a_out, q8_1_out, status);
+        launch_pdl(act_f16_kernel<4, uint64_t>, dim3(grid), dim3(256), 0, stream, "act_f16_kernel launch", x, rows, k,
+                   ld, a_out, q8_1_out, status);
         check_cuda(cudaGetLastError(), "act_f16_kernel launch");
         return;
     }
     const unsigned grid = grid_for((units + u - 1) / u);
     switch (u) {
-        case 1: act_f16_kernel<1, uint32_t><<<grid, 256, 0, stream>>>(x, rows, k, ld, a_out, q8_1_out, status); break;
-        case 2: act_f16_kernel<2, uint32_t><<<grid, 256, 0, stream>>>(x, rows, k, ld, a_out, q8_1_out, status); break;
-        case 3: act_f16_kernel<3, uint32_t><<<grid, 256, 0, stream>>>(x, rows, k, ld, a_out, q8_1_out, status); break;
-        default: act_f16_kernel<4, uint32_t><<<grid, 256, 0, stream>>>(x, rows, k, ld, a_out, q8_1_out, status); break;
+        case 1:
+            launch_pdl(act_f16_kernel<1, uint32_t>, dim3(grid), dim3(256), 0, stream, "act_f16_kernel launch", x,
+                       rows, k, ld, a_out, q8_1_out, status);
+            break;
+        case 2:
+            launch_pdl(act_f16_kernel<2, uint32_t>, dim3(grid), dim3(256), 0, stream, "act_f16_kernel launch", x,
+                       rows, k, ld, a_out, q8_1_out, status);
+            break;
+        case 3:
+            launch_pdl(act_f16_kernel<3, uint32_t>, dim3(grid), dim3(256), 0, stream, "act_f16_kernel launch", x,
+                       rows, k, ld, a_out, q8_1_out, status);
+            break;
+        default:
+            launch_pdl(act_f16_kernel<4, uint32_t>, dim3(grid), dim3(256), 0, stream, "act_f16_kernel launch", x, rows,
+                       k, ld, a_out, q8_1_out, status);
+            break;
     }
     check_cuda(cudaGetLastError(), "act_f16_kernel launch");
 }

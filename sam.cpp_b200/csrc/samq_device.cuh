@@ -99,6 +99,14 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, Device
     }
 }
 
+// ---- programmatic dependent launch ---------------------------------------
+// Kernels launched with cudaLaunchAttributeProgrammaticStreamSerialization may
+// start before the previous kernel on the stream has finished; each of them
+// calls pdl_wait() before touching memory the predecessor may write or read,
+// and pdl_trigger() once its own dependents may be scheduled.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 // ---- TMA (cp.async.bulk.tensor), never with .multicast::cluster ----------
 
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {

@@ -10,6 +10,7 @@
 #include <mutex>
 #include <string>
 #include <unordered_map>
+#include <utility>
 
 #include "samq.h"
 #include "samq_device.cuh"
@@ -53,6 +54,24 @@ struct DeviceGuard {
     explicit DeviceGuard(int device);
     ~DeviceGuard();
 };
+
+// Launch `kernel` on `stream` with programmatic stream serialization (the
+// kernel must call pdl_wait() before touching dependent memory).
+template <class... KernelArgs, class... Args>
+void launch_pdl(void (*kernel)(KernelArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                const char* what, Args&&... args) {
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    check_cuda(cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...), what);
+}
 
 // cuTensorMapEncodeTiled through the runtime's driver entry point (no link
 // dependency on libcuda).
