@@ -147,6 +147,22 @@ samq_status samq_stage_f16_v1(const float* x, int64_t rows, int64_t k, int64_t l
 samq_status samq_linear_f16_v1(const samq_weights* weights, const void* x_f16, int64_t m, int64_t ldx,
                                const float* bias, int epilogue, float* y, int64_t ldy, void* stream);
 
+/* K3: RoPE + self-attention of one SAM 3 ViT block.  qkv is the device f32
+ * output of the block's qkv linear (+bias), [grid_h * grid_w][ldq] in raster
+ * token order, columns Q | K | V, each head-major with head_dim = 64.  RoPE
+ * rotates channel pairs of Q and K by freqs_cis[pos][i] = (cos, sin)
+ * ([positions][32][2] f32; positions = window * window for windowed blocks,
+ * grid_w * grid_h for global ones).  Attention is softmax(Q K^T / 8) V within
+ * each window x window tile of the grid (window > 0; the grid must divide) or
+ * over the whole grid (window == 0).  out is [tokens][ldo] f32 in raster order
+ * (head h at columns 64h..64h+63).  Replaces the RoPE, win_part, flash_attn_ext
+ * and win_unpart nodes of sam3_vit_block_forward
+ * (src/models/sam3/vision.hpp:100-148,170-227) and the precise F32 attention
+ * of cmake/patches/ggml-precise-cuda.patch:448-606.  Operands are f16 on the
+ * tensor cores with f32 accumulation and an f32 online softmax. */
+samq_status samq_vit_attention_v1(const float* qkv, int64_t ldq, int grid_w, int grid_h, int heads, int head_dim,
+                                  int window, const float* freqs_cis, float* out, int64_t ldo, void* stream);
+
 /* Counters of a handle.  Mirrors ggml_cuda_sam_q8_rhs_query_v1
  * (cmake/patches/ggml-native-activation.patch:34-42). */
 samq_status samq_query_v1(const samq_weights* weights, struct samq_counters_v1* out);

@@ -63,6 +63,7 @@ def lib() -> ctypes.CDLL:
             "oracle_gemm_f16_f64": (i32, [vp, vp, i64, i64, i64, vp, i32, vp, i32]),
             "oracle_cpu_linear": (i32, [i32, vp, i64, i64, vp, i64, i64, vp, i32, vp, i64, i32]),
             "oracle_cpu_has_vnni": (i32, []),
+            "oracle_vit_attention": (i32, [vp, i64, i32, i32, i32, i32, i32, vp, vp, i64, vp, i64, i32]),
         }
         for name, (res, args) in sig.items():
             fn = getattr(_lib, name)
@@ -212,6 +213,28 @@ def cpu_linear(qtype: int, rows: np.ndarray, k: int, n: int, x: np.ndarray, bias
                                  threads or default_threads())
     _check(rc, "cpu_linear")
     return y
+
+
+def vit_attention(qkv: np.ndarray, grid_w: int, grid_h: int, heads: int, head_dim: int, window: int,
+                  freqs: np.ndarray, rows=None, threads=None) -> np.ndarray:
+    """f64 windowed/global attention with RoPE for the query tokens `rows`."""
+    qkv = np.ascontiguousarray(qkv, dtype=np.float32)
+    freqs = np.ascontiguousarray(freqs, dtype=np.float32)
+    E = heads * head_dim
+    r = None if rows is None else np.ascontiguousarray(rows, dtype=np.int64)
+    n = qkv.shape[0] if r is None else r.size
+    out = np.empty((n, E), dtype=np.float32)
+    rc = lib().oracle_vit_attention(_ptr(qkv), qkv.shape[1], grid_w, grid_h, heads, head_dim, window, _ptr(freqs),
+                                    _ptr(r), n, _ptr(out), E, threads or default_threads())
+    _check(rc, "vit_attention")
+    return out
+
+
+def rope_freqs(positions: int, head_dim: int = 64, seed: int = 0) -> np.ndarray:
+    """Unit-modulus (cos, sin) pairs [positions][head_dim/2][2] (any such table is a valid freqs_cis)."""
+    rng = np.random.default_rng(seed)
+    ang = rng.uniform(-np.pi, np.pi, (positions, head_dim // 2))
+    return np.stack([np.cos(ang), np.sin(ang)], axis=-1).astype(np.float32)
 
 
 def has_vnni() -> bool:

@@ -589,6 +589,73 @@ int oracle_gemm_f16_f64(const uint16_t* w, const uint16_t* x, int64_t m, int64_t
     return rc;
 }
 
+/* ------------------------------------------------------ ViT attention */
+
+static void rope_pair_f64(const float* x, const float* freq_row, int half, double* outv) {
+    for (int i = 0; i < half; ++i) {
+        const double a = x[2 * i], b = x[2 * i + 1];
+        const double c = freq_row[2 * i], sn = freq_row[2 * i + 1];
+        outv[2 * i] = a * c - b * sn;
+        outv[2 * i + 1] = a * sn + b * c;
+    }
+}
+
+int oracle_vit_attention(const float* qkv, int64_t ldq, int grid_w, int grid_h, int heads, int head_dim,
+                         int window, const float* freqs, const int64_t* rows, int64_t nrows, float* out,
+                         int64_t ldo, int threads) {
+    const int64_t tokens = (int64_t)grid_w * grid_h, E = (int64_t)heads * head_dim;
+    if (head_dim % 2 || ldq < 3 * E || ldo < E || grid_w <= 0 || grid_h <= 0) return -1;
+    if (window > 0 && (grid_w % window || grid_h % window)) return -1;
+    const int64_t group = window > 0 ? (int64_t)window * window : tokens;
+    const int half = head_dim / 2;
+    if (!rows) nrows = tokens;
+#ifdef _OPENMP
+#pragma omp parallel for schedule(dynamic, 1) num_threads(threads > 0 ? threads : 1)
+#endif
+    for (int64_t r = 0; r < nrows; ++r) {
+        const int64_t t = rows ? rows[r] : r;
+        const int ty = (int)(t / grid_w), tx = (int)(t % grid_w);
+        /* tokens of the query's attention group, in window-local raster order */
+        int64_t* members = (int64_t*)malloc((size_t)group * sizeof(int64_t));
+        double* qv = (double*)malloc((size_t)head_dim * sizeof(double));
+        double* kv = (double*)malloc((size_t)head_dim * sizeof(double));
+        double* sc = (double*)malloc((size_t)group * sizeof(double));
+        int64_t qpos;
+        if (window > 0) {
+            const int wy = ty / window, wx = tx / window;
+            for (int y = 0; y < window; ++y)
+                for (int x = 0; x < window; ++x)
+                    members[y * window + x] = (int64_t)(wy * window + y) * grid_w + (wx * window + x);
+            qpos = (int64_t)(ty % window) * window + (tx % window);
+        } else {
+            for (int64_t u = 0; u < tokens; ++u) members[u] = u;
+            qpos = t;
+        }
+        for (int h = 0; h < heads; ++h) {
+            rope_pair_f64(qkv + t * ldq + (int64_t)h * head_dim, freqs + qpos * head_dim, half, qv);
+            double mx = -1e300;
+            for (int64_t j = 0; j < group; ++j) {
+                const int64_t u = members[j];
+                rope_pair_f64(qkv + u * ldq + E + (int64_t)h * head_dim, freqs + j * head_dim, half, kv);
+                double d = 0.0;
+                for (int i = 0; i < head_dim; ++i) d += qv[i] * kv[i];
+                sc[j] = d / sqrt((double)head_dim);
+                if (sc[j] > mx) mx = sc[j];
+            }
+            double sum = 0.0;
+            for (int64_t j = 0; j < group; ++j) { sc[j] = exp(sc[j] - mx); sum += sc[j]; }
+            for (int i = 0; i < head_dim; ++i) {
+                double o = 0.0;
+                for (int64_t j = 0; j < group; ++j) o += sc[j] * qkv[members[j] * ldq + 2 * E + (int64_t)h * head_dim + i];
+                out[r * ldo + (int64_t)h * head_dim + i] = (float)(o / sum);
+            }
+        }
+        free(members); free(qv); free(kv); free(sc);
+    }
+    (void)threads;
+    return 0;
+}
+
 /* ------------------------------------------- restated GGML CPU path
  *
  * Weights are decoded once ("prepared", as GGML's CPU repack does at load)

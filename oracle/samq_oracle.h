@@ -120,6 +120,19 @@ int oracle_gemm_f64(const float* w, const float* x, int64_t m, int64_t n, int64_
 int oracle_gemm_f16_f64(const uint16_t* w, const uint16_t* x, int64_t m, int64_t n, int64_t k,
                         const float* bias, int epilogue, float* y, int threads);
 
+/* ViT attention of one block (src/models/sam3/vision.hpp:152-243): qkv is the
+ * f32 output of the qkv linear, [tokens][ldq] with columns Q | K | V, each
+ * head-major (head h at 64h..64h+63); tokens are the raster grid W x H.  RoPE
+ * (vision.hpp:100-148) rotates channel pairs (2i, 2i+1) of Q and K by
+ * (cos, sin) = freqs[pos][i][0..1], pos = window-local raster position (or the
+ * global one when window == 0).  Softmax(Q K^T / sqrt(hd)) V over the tokens of
+ * the same window (24x24 windows of the grid, vision.hpp:170-173) or of the
+ * whole grid.  f64 arithmetic.  Computes the query tokens listed in `rows`
+ * (raster indices; NULL = all) into out[r][ldo] for r = 0..nrows-1. */
+int oracle_vit_attention(const float* qkv, int64_t ldq, int grid_w, int grid_h, int heads, int head_dim,
+                         int window, const float* freqs, const int64_t* rows, int64_t nrows, float* out,
+                         int64_t ldo, int threads);
+
 /* Restated GGML CPU path (the timed CPU baseline): pack X rows to Q8_0
  * (Q8_0 weights) or Q8_K (K-quant weights), integer block dots, f32 scales,
  * f32 output, OpenMP over `threads` host threads; AVX-512 VNNI when the host

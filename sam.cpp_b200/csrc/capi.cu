@@ -114,6 +114,20 @@ void encode_tensor_map_2d(CUtensorMap* map, CUtensorMapDataType dtype, const voi
                                                                std::to_string(static_cast<int>(r)) + ")");
 }
 
+void encode_tensor_map_3d(CUtensorMap* map, CUtensorMapDataType dtype, const void* base, uint64_t d0, uint64_t d1,
+                          uint64_t d2, uint64_t stride1_bytes, uint64_t stride2_bytes, uint32_t box0, uint32_t box1,
+                          CUtensorMapSwizzle swizzle) {
+    const cuuint64_t dims[3] = {d0, d1, d2};
+    const cuuint64_t strides[2] = {stride1_bytes, stride2_bytes};
+    const cuuint32_t box[3] = {box0, box1, 1};
+    const cuuint32_t elem_strides[3] = {1, 1, 1};
+    const CUresult r = encode_fn()(map, dtype, 3, const_cast<void*>(base), dims, strides, box, elem_strides,
+                                   CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) fail(SAMQ_ERR_INVALID_ARGUMENT, "cuTensorMapEncodeTiled rejected a 3-D tensor (code " +
+                                                               std::to_string(static_cast<int>(r)) + ")");
+}
+
 namespace {
 
 template <class F>
@@ -387,6 +401,30 @@ samq_status samq_linear_f16_v1(const samq_weights* w, const void* x_f16, int64_t
     });
 }
 
+samq_status samq_vit_attention_v1(const float* qkv, int64_t ldq, int grid_w, int grid_h, int heads, int head_dim,
+                                  int window, const float* freqs_cis, float* out, int64_t ldo, void* stream_ptr) {
+    return guarded([&] {
+        require(head_dim == 64, "head_dim must be 64");
+        require(heads > 0 && heads <= 64, "heads out of range");
+        require(grid_w > 0 && grid_h > 0 && static_cast<int64_t>(grid_w) * grid_h <= (int64_t(1) << 20),
+                "grid out of range");
+        require(window == 0 || (window > 0 && grid_w % window == 0 && grid_h % window == 0),
+                "window must divide the grid (or be 0 for global attention)");
+        const int64_t E = static_cast<int64_t>(heads) * head_dim;
+        const int64_t group_n = window > 0 ? static_cast<int64_t>(window) * window
+                                           : static_cast<int64_t>(grid_w) * grid_h;
+        require(group_n % 8 == 0, "tokens per attention group must be a multiple of 8");
+        require(ldq >= 3 * E && ldq % 4 == 0, "qkv row stride must be >= 3*heads*64 and a multiple of 4");
+        require(ldo >= E && ldo % 4 == 0, "output row stride must be >= heads*64 and a multiple of 4");
+        require(qkv && out && freqs_cis && aligned16(qkv) && aligned16(out) && aligned16(freqs_cis),
+                "qkv, freqs_cis and out must be 16-byte aligned device pointers");
+        DeviceState& state = device_state(current_device());
+        cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
+        Scratch& scratch = scratch_for(state, stream, attention_scratch_bytes(grid_w, grid_h, heads));
+        launch_vit_attention(qkv, ldq, grid_w, grid_h, heads, window, freqs_cis, out, ldo, scratch.ptr, state, stream);
+    });
+}
+
 samq_status samq_query_v1(const samq_weights* w, struct samq_counters_v1* out) {
     return guarded([&] {
         require(w != nullptr && out != nullptr, "null argument");
@@ -412,6 +450,10 @@ samq_status samq_check_v1(int device, void* stream) {
         if (host.flags & kStatusTimeout) {
             found = SAMQ_ERR_TIMEOUT;
             fail(SAMQ_ERR_TIMEOUT, "a device-side wait timed out at site " + std::to_string(host.timeout_site));
+        }
+        if (host.flags & kStatusLayout) {
+            found = SAMQ_ERR_UNSUPPORTED;
+            fail(SAMQ_ERR_UNSUPPORTED, "a kernel skipped its work: dynamic shared memory base misaligned");
         }
         if (host.flags & kStatusRange) {
             found = SAMQ_ERR_RANGE;

@@ -101,8 +101,8 @@ __device__ __forceinline__ void drain_tile(uint32_t tmem_base, int quarter, int 
                                            int col_base, int m, int n, const float* __restrict__ bias,
                                            int epilogue, const CUtensorMap* tma_y, uint8_t* stage_buf, int& buf,
                                            int lane) {
-#pragma unroll 1
     constexpr int kChunks = BN / 32;
+#pragma unroll 1
     for (int chunk = part * kChunks / PARTS; chunk < (part + 1) * kChunks / PARTS; ++chunk) {
         const int col0 = col_base + chunk * 32;
         if (col0 >= n) break;
@@ -264,7 +264,8 @@ gemm_f16_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant
         int buf = 0;
         for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x) {
             const int mt = tile / n_tiles, nt = tile % n_tiles;
-            if (!mbar_wait(&tfull[acc], acc_ph, status, 4)) break;
+            // Warp-uniform: the tcgen05.ld in drain_tile is warp-collective.
+            if (!__all_sync(0xffffffffu, mbar_wait(&tfull[acc], acc_ph, status, 4))) break;
             tc_fence_after();
             const int row0 = mt * BM + quarter * 32;
             drain_tile<BN, EW / 4>(tmem_base, quarter, part, acc, row0, nt * BN, m, n, bias, epilogue, &tma_y, stage_buf, buf,

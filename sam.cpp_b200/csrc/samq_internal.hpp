@@ -78,6 +78,9 @@ void launch_pdl(void (*kernel)(KernelArgs...), dim3 grid, dim3 block, size_t sme
 void encode_tensor_map_2d(CUtensorMap* map, CUtensorMapDataType dtype, const void* base, uint64_t inner,
                           uint64_t outer, uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_outer,
                           CUtensorMapSwizzle swizzle);
+void encode_tensor_map_3d(CUtensorMap* map, CUtensorMapDataType dtype, const void* base, uint64_t d0, uint64_t d1,
+                          uint64_t d2, uint64_t stride1_bytes, uint64_t stride2_bytes, uint32_t box0, uint32_t box1,
+                          CUtensorMapSwizzle swizzle);
 
 }  // namespace samq
 
@@ -115,6 +118,14 @@ void launch_packets_to_gguf(int type, int64_t k, int64_t n, const uint8_t* packe
                             cudaStream_t stream);
 void launch_packets_to_f16(int type, int64_t k, int64_t n, const uint8_t* packets, __half* out,
                            cudaStream_t stream);
+
+// K3 attention.cu: RoPE + windowed/global attention of one ViT block.
+// qkv [tokens][ldq] f32 (Q | K | V), out [tokens][ldo] f32; `packed` is
+// scratch of attention_scratch_bytes() bytes.
+size_t attention_scratch_bytes(int grid_w, int grid_h, int heads);
+void launch_vit_attention(const float* qkv, int64_t ldq, int grid_w, int grid_h, int heads, int window,
+                          const float* freqs, float* out, int64_t ldo, void* packed, DeviceState& state,
+                          cudaStream_t stream);
 
 // K2 gemm.cu
 void launch_gemm_f16(const __half* a, int64_t lda, const __half* b, int64_t m, int64_t n, int64_t k,

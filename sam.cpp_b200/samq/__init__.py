@@ -65,6 +65,7 @@ SIGNATURES = {
     "samq_query_v1": (_i32, [_vp, ctypes.POINTER(Counters)]),
     "samq_check_v1": (_i32, [_i32, _vp]),
     "samq_linear_static_v1": (_i32, [_vp, _vp, _i64, _i64, _vp, _i32, _vp, _i64, _vp]),
+    "samq_vit_attention_v1": (_i32, [_vp, _i64, _i32, _i32, _i32, _i32, _i32, _vp, _vp, _i64, _vp]),
 }
 STATIC_OPERAND_ELEMENTS = 16777216
 
@@ -214,6 +215,13 @@ def linear_static(w: Weights, x, m: int, ldx: int, bias, epilogue: int, y, ldy: 
     """samq_linear_static_v1: samq_linear_v1 without any device allocation."""
     _check(library().samq_linear_static_v1(w.handle, _addr(x), m, ldx, _addr(bias), epilogue, _addr(y), ldy,
                                            _stream(stream)))
+
+
+def vit_attention(qkv, ldq: int, grid_w: int, grid_h: int, heads: int, window: int, freqs, out, ldo: int,
+                  stream=None, head_dim: int = 64):
+    """samq_vit_attention_v1: RoPE + windowed (window > 0) or global attention."""
+    _check(library().samq_vit_attention_v1(_addr(qkv), ldq, grid_w, grid_h, heads, head_dim, window, _addr(freqs),
+                                           _addr(out), ldo, _stream(stream)))
 
 
 def check(device: int = 0, stream=None):
