@@ -21,9 +21,11 @@
 //                     warp 1 issues tcgen05.mma S = Q K^T (M=128, N=128, K=64)
 //                     into TMEM, then O += P V (M=128, N=64, K=128) into TMEM;
 //                     warps 2-5 own one query row each: online softmax in the
-//                     log2 domain with an FMA-pipe exp2, P (f16) to swizzled
-//                     shared memory, O rescaled in TMEM when the running max
-//                     moves, and finally O / l to the f32 output.
+//                     log2 domain with the MUFU exp2, P (f16) to swizzled
+//                     shared memory, O rescaled in TMEM when the reference
+//                     max moves by more than 8, and finally O / l to f32.
+//                     K and V stages have separate barriers (K is released by
+//                     the S MMA, V by the PV MMA); two CTAs fit per SM.
 // Keys past the group's end are zero-filled by TMA and masked to -inf.  All
 // waits are bounded (kStatusTimeout).  No TMA load uses multicast.
 #include <algorithm>
@@ -145,7 +147,7 @@ __device__ __forceinline__ float ex2_mufu(float x) {
 // of at nearly every block.  The final O / l is the same softmax either way.
 constexpr float kLazyRescale = 8.0f;
 
-// Shared memory: 10 mbarriers + the TMEM slot in the first 128 bytes of the
+// Shared memory: 14 mbarriers + the TMEM slot in the first 128 bytes of the
 // dynamic window, then the tiles at the next 1024-byte boundary (SW128
 // atoms).  112 KB of tiles + 1 KB of slack keeps two CTAs resident per SM.
 struct AttnSmem {
@@ -175,15 +177,19 @@ attention_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
     uint8_t* sv = smem + AttnSmem::v_off;
     uint8_t* sp = smem + AttnSmem::p_off;
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem_raw);
+    // K stages are released by the S MMA that read them, V stages by the PV
+    // MMA, so K(j + 1) streams in while PV(j - 1) is still pending.
     uint64_t* q_full = bars + 0;
-    uint64_t* kv_full = bars + 1;   // [2]
-    uint64_t* kv_empty = bars + 3;  // [2]
-    uint64_t* s_full = bars + 5;
-    uint64_t* s_free = bars + 6;
-    uint64_t* p_full = bars + 7;
-    uint64_t* o_done = bars + 8;
-    uint64_t* drain = bars + 9;
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 10);
+    uint64_t* k_full = bars + 1;   // [2]
+    uint64_t* k_empty = bars + 3;  // [2]
+    uint64_t* v_full = bars + 5;   // [2]
+    uint64_t* v_empty = bars + 7;  // [2]
+    uint64_t* s_full = bars + 9;
+    uint64_t* s_free = bars + 10;
+    uint64_t* p_full = bars + 11;
+    uint64_t* o_done = bars + 12;
+    uint64_t* drain = bars + 13;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 14);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int q_tile = blockIdx.x;
@@ -193,10 +199,12 @@ attention_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
 
     if (threadIdx.x == 0) {
         mbar_init(q_full, 1);
-        mbar_init(&kv_full[0], 1);
-        mbar_init(&kv_full[1], 1);
-        mbar_init(&kv_empty[0], 1);
-        mbar_init(&kv_empty[1], 1);
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&k_full[b], 1);
+            mbar_init(&k_empty[b], 1);
+            mbar_init(&v_full[b], 1);
+            mbar_init(&v_empty[b], 1);
+        }
         mbar_init(s_full, 1);
         mbar_init(s_free, 4);
         mbar_init(p_full, 4);
@@ -219,27 +227,38 @@ attention_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
             bool ok = true;
             mbar_arrive_expect_tx(q_full, kQTile * 128);
             tma_load_3d(sq, &tm_q, q_full, 0, q_tile * kQTile, gh);
-            uint32_t issued = 0, issued_phase = 0;
+            // Bit b of k_issued / v_issued: stage b has a load in flight whose
+            // phase parity is the same bit of *_phase.
+            uint32_t k_issued = 0, k_phase = 0, v_issued = 0, v_phase = 0;
             for (int j = 0; j < n_kv && ok; ++j) {
                 const int b = j & 1;
-                const uint32_t use = static_cast<uint32_t>(j >> 1);
-                if (!mbar_wait(&kv_empty[b], (use & 1u) ^ 1u, status, 21)) {
+                const uint32_t par = static_cast<uint32_t>(j >> 1) & 1u;
+                if (!mbar_wait(&k_empty[b], par ^ 1u, status, 21)) {
                     ok = false;
                     break;
                 }
-                mbar_arrive_expect_tx(&kv_full[b], kKvTile * 128 + 2 * kHeadDim * 128);
-                tma_load_3d(sk + b * kKvTile * 128, &tm_k, &kv_full[b], 0, j * kKvTile, gh);
+                mbar_arrive_expect_tx(&k_full[b], kKvTile * 128);
+                tma_load_3d(sk + b * kKvTile * 128, &tm_k, &k_full[b], 0, j * kKvTile, gh);
+                k_issued |= 1u << b;
+                k_phase = (k_phase & ~(1u << b)) | (par << b);
+                if (!mbar_wait(&v_empty[b], par ^ 1u, status, 28)) {
+                    ok = false;
+                    break;
+                }
+                mbar_arrive_expect_tx(&v_full[b], 2 * kHeadDim * 128);
                 uint8_t* vb = sv + b * 2 * kHeadDim * 128;
-                tma_load_3d(vb, &tm_v, &kv_full[b], j * kKvTile, 0, gh);
-                tma_load_3d(vb + kHeadDim * 128, &tm_v, &kv_full[b], j * kKvTile + 64, 0, gh);
-                issued |= 1u << b;
-                issued_phase = (issued_phase & ~(1u << b)) | ((use & 1u) << b);
+                tma_load_3d(vb, &tm_v, &v_full[b], j * kKvTile, 0, gh);
+                tma_load_3d(vb + kHeadDim * 128, &tm_v, &v_full[b], j * kKvTile + 64, 0, gh);
+                v_issued |= 1u << b;
+                v_phase = (v_phase & ~(1u << b)) | (par << b);
             }
             pdl_trigger();
-            if (!ok) {
+            if (!ok) {  // let the loads in flight land before the CTA exits
                 mbar_wait(q_full, 0, status, 25);
-                for (int b = 0; b < 2; ++b)
-                    if (issued & (1u << b)) mbar_wait(&kv_full[b], (issued_phase >> b) & 1u, status, 25);
+                for (int b = 0; b < 2; ++b) {
+                    if (k_issued & (1u << b)) mbar_wait(&k_full[b], (k_phase >> b) & 1u, status, 25);
+                    if (v_issued & (1u << b)) mbar_wait(&v_full[b], (v_phase >> b) & 1u, status, 25);
+                }
             }
         }
     } else if (warp == 1) {
@@ -256,24 +275,27 @@ attention_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
                     tc_mma_f16(tmem_s, smem_desc_sw128(q_addr + kk * 32), smem_desc_sw128(k_addr + kk * 32), idesc_s,
                                kk != 0 ? 1u : 0u);
                 tc_commit(s_full);
+                tc_commit(&k_empty[j & 1]);
             };
             // S(j + 1) is issued as soon as the softmax warps have copied S(j)
             // out of TMEM, so it runs under their exponentials; PV(j) follows
             // once P(j) is in shared memory.
-            bool ok = mbar_wait(q_full, 0, status, 22) && mbar_wait(&kv_full[0], 0, status, 23);
+            bool ok = mbar_wait(q_full, 0, status, 22) && mbar_wait(&k_full[0], 0, status, 23);
             if (ok) {
                 tc_fence_after();
                 issue_s(0);
             }
             for (int j = 0; j < n_kv && ok; ++j) {
                 if (j + 1 < n_kv) {
-                    if (!mbar_wait(&kv_full[(j + 1) & 1], static_cast<uint32_t>((j + 1) >> 1) & 1u, status, 23) ||
+                    if (!mbar_wait(&k_full[(j + 1) & 1], static_cast<uint32_t>((j + 1) >> 1) & 1u, status, 23) ||
                         !mbar_wait(s_free, static_cast<uint32_t>(j) & 1u, status, 24))
                         break;
                     tc_fence_after();
                     issue_s(j + 1);
                 }
-                if (!mbar_wait(p_full, static_cast<uint32_t>(j) & 1u, status, 26)) break;
+                if (!mbar_wait(p_full, static_cast<uint32_t>(j) & 1u, status, 26) ||
+                    !mbar_wait(&v_full[j & 1], static_cast<uint32_t>(j >> 1) & 1u, status, 29))
+                    break;
                 tc_fence_after();
                 const uint32_t v_addr = smem_u32(sv + (j & 1) * 2 * kHeadDim * 128);
 #pragma unroll
@@ -284,7 +306,7 @@ attention_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
                                (j > 0 || kk > 0) ? 1u : 0u);
                 }
                 tc_commit(o_done);
-                tc_commit(&kv_empty[j & 1]);
+                tc_commit(&v_empty[j & 1]);
             }
             tc_commit(drain);
             mbar_wait(drain, 0, status, 27);
@@ -335,35 +357,40 @@ attention_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
             const float m_new = move ? mx : m;
             const float alpha = move ? ex2_mufu(m - m_new) : 1.0f;
             m = m_new;
+            // P = 2^(s log2e - m) as f16, kept in registers until PV(j-1) has
+            // released P's shared-memory tile.
+            const float neg_m = -m;
+            float rs[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+            uint32_t packed[16][4];
+#pragma unroll
+            for (int u = 0; u < 16; ++u) {
+                const int c = u >> 2, base_i = (u & 3) * 8;
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    const float x0 = fmaf(__uint_as_float(s[c][base_i + 2 * e]), kLog2e, neg_m);
+                    const float x1 = fmaf(__uint_as_float(s[c][base_i + 2 * e + 1]), kLog2e, neg_m);
+                    const float p0 = ex2_mufu(x0);
+                    const float p1 = ex2_mufu(x1);
+                    rs[e] += p0 + p1;
+                    const __half2 hp = __floats2half2_rn(p0, p1);
+                    packed[u][e] = *reinterpret_cast<const uint32_t*>(&hp);
+                }
+            }
             if (j > 0) {
-                // PV(j-1) has finished: P's buffer is free and O is stable.
+                // PV(j-1) has finished: P's tile is free and O is stable.
                 if (!__all_sync(0xffffffffu, mbar_wait(o_done, static_cast<uint32_t>(j - 1) & 1u, status, 32))) {
                     ok = false;
                     break;
                 }
                 tc_fence_after();
             }
-            // P = 2^(s log2e - m) as f16 into the swizzled A tile: keys 0..63
-            // in the first 128-byte row, 64..127 in the second, 16-byte units
-            // permuted by row & 7.
-            const float neg_m = -m;
-            float rs[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+            // P row into the swizzled A tile: keys 0..63 in the first 128-byte
+            // row, 64..127 in the second, 16-byte units permuted by row & 7.
 #pragma unroll
             for (int u = 0; u < 16; ++u) {
-                const int c = u >> 2, base_i = (u & 3) * 8;
-                uint32_t packed[4];
-#pragma unroll
-                for (int e = 0; e < 4; ++e) {
-                    const float p0 = ex2_mufu(fmaf(__uint_as_float(s[c][base_i + 2 * e]), kLog2e, neg_m));
-                    const float p1 = ex2_mufu(fmaf(__uint_as_float(s[c][base_i + 2 * e + 1]), kLog2e, neg_m));
-                    rs[e] += p0 + p1;
-                    const __half2 hp = __floats2half2_rn(p0, p1);
-                    packed[e] = *reinterpret_cast<const uint32_t*>(&hp);
-                }
                 uint8_t* base = u < 8 ? prow0 : prow1;
-                const int unit = u & 7;
-                *reinterpret_cast<uint4*>(base + ((unit ^ (row & 7)) << 4)) =
-                    make_uint4(packed[0], packed[1], packed[2], packed[3]);
+                *reinterpret_cast<uint4*>(base + (((u & 7) ^ (row & 7)) << 4)) =
+                    make_uint4(packed[u][0], packed[u][1], packed[u][2], packed[u][3]);
             }
             l = l * alpha + ((rs[0] + rs[1]) + (rs[2] + rs[3]));
             // O rescale after P is out (S no longer live): rows whose reference
