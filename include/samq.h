@@ -163,6 +163,50 @@ samq_status samq_linear_f16_v1(const samq_weights* weights, const void* x_f16, i
 samq_status samq_vit_attention_v1(const float* qkv, int64_t ldq, int grid_w, int grid_h, int heads, int head_dim,
                                   int window, const float* freqs_cis, float* out, int64_t ldo, void* stream);
 
+/* One SAM 3 ViT block, pre-LN (src/models/sam3/vision.hpp:152-243):
+ *   x = x + proj(attn(RoPE(qkv(LN1(x)))))   (windowed or global attention)
+ *   x = x + fc2(GELU_erf(fc1(LN2(x))))
+ * Every linear consumes its input through the Q8_1 staging rule of
+ * samq_quantize_q8_1_v1, as GGML's CUDA path does for quantized weights.
+ * Parameters are device f32 arrays of the reference tensors
+ * (src/models/sam3/tensors.hpp:108-126): LayerNorm weight / bias [E], linear
+ * biases [N], freqs_cis [positions][32][2].  Linears are weight handles:
+ * qkv E -> 3E, proj E -> E, fc1 E -> MLP, fc2 MLP -> E, with E = 64 * heads
+ * and E in {256, 512, 1024}; MLP % 32 == 0. */
+typedef struct samq_vit_block_v1 {
+    uint32_t version;  /* 1 */
+    int32_t window;    /* 24: windowed blocks (grid divisible by it), 0: global */
+    const float* norm1_w;
+    const float* norm1_b;
+    const samq_weights* qkv;
+    const float* qkv_b;
+    const samq_weights* proj;
+    const float* proj_b;
+    const float* norm2_w;
+    const float* norm2_b;
+    const samq_weights* fc1;
+    const float* fc1_b;
+    const samq_weights* fc2;
+    const float* fc2_b;
+    const float* freqs_cis;
+} samq_vit_block_v1;
+
+/* Runs one block in place on the residual stream x, device f32
+ * [grid_h * grid_w][E] in raster token order (the reference's [E, W, H, 1]). */
+samq_status samq_vit_block_forward_v1(const samq_vit_block_v1* block, float* x, int grid_w, int grid_h,
+                                      void* stream);
+
+/* Backbone prefix (src/models/sam3/vision.hpp:252-282): patch embedding (an
+ * unpadded patch x patch convolution without bias, weight [E][3][patch][patch]
+ * f32), + pos_embed ([pos_grid][pos_grid][E] f32, tiled over the token grid),
+ * then ln_pre (weight / bias [E]).  image is device f32 [3][height][width]
+ * (normalized, channel planes); x receives [tokens][E] f32, tokens =
+ * (height / patch) * (width / patch) in raster order.  The convolution runs on
+ * the tensor cores with f16 operands and f32 accumulation. */
+samq_status samq_vit_prefix_v1(const float* image, int width, int height, int patch, const float* patch_w,
+                               int64_t embed, const float* pos_embed, int pos_grid, const float* ln_w,
+                               const float* ln_b, float* x, void* stream);
+
 /* Counters of a handle.  Mirrors ggml_cuda_sam_q8_rhs_query_v1
  * (cmake/patches/ggml-native-activation.patch:34-42). */
 samq_status samq_query_v1(const samq_weights* weights, struct samq_counters_v1* out);

@@ -245,3 +245,57 @@ def gelu_erf(v: np.ndarray) -> np.ndarray:
     from math import erf, sqrt
     f = np.vectorize(lambda t: 0.5 * t * (1.0 + erf(t / sqrt(2.0))))
     return f(v.astype(np.float64)).astype(np.float32)
+
+
+def layer_norm(x: np.ndarray, w: np.ndarray, b: np.ndarray, eps: float = 1e-5) -> np.ndarray:
+    """ggml_norm(eps) * w + b in f64 (src/models/sam3/ops.hpp:56-66), rounded to f32."""
+    x64 = np.asarray(x, dtype=np.float64)
+    c = x64 - x64.mean(axis=1, keepdims=True)
+    var = (c * c).mean(axis=1, keepdims=True)
+    return (c / np.sqrt(var + eps) * np.asarray(w, np.float64) + np.asarray(b, np.float64)).astype(np.float32)
+
+
+def staged_linear(w16: np.ndarray, x: np.ndarray, bias=None, epilogue=EPILOGUE_NONE, threads=None) -> np.ndarray:
+    """A quantized linear as GGML's CUDA path computes it: x staged to Q8_1
+    (act_f16 gives the exact decoded operand), weights decoded (w16 =
+    weight_f16), f64 dot products, bias and erf-GELU, f32 result."""
+    return gemm_f64(w16, act_f16(x), bias, epilogue, threads)
+
+
+def vit_block(x: np.ndarray, blk: dict, grid_w: int, grid_h: int, rows=None, threads=None) -> np.ndarray:
+    """One SAM 3 ViT block (src/models/sam3/vision.hpp:152-243) in f64 with
+    Q8_1 staging in front of every quantized linear:
+      x1 = x + proj(attn(RoPE(qkv(LN1(x)))));  out = x1 + fc2(GELU(fc1(LN2(x1)))).
+    blk holds window, norm1_w/b, norm2_w/b, the decoded f16 weights qkv_w16,
+    proj_w16, fc1_w16, fc2_w16 ([n][k]), the biases and freqs.  x is
+    [tokens][E] f32 in raster order.  Returns the block output for the tokens
+    in `rows` (all when None): K and V cover every token, the rest only `rows`."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    E = x.shape[1]
+    heads = E // 64
+    h = layer_norm(x, blk["norm1_w"], blk["norm1_b"])
+    qkv = staged_linear(blk["qkv_w16"], h, blk["qkv_b"], threads=threads)
+    sel = np.arange(x.shape[0]) if rows is None else np.asarray(rows, dtype=np.int64)
+    att = vit_attention(qkv, grid_w, grid_h, heads, 64, blk["window"], blk["freqs"], rows=sel, threads=threads)
+    x1 = (x[sel] + staged_linear(blk["proj_w16"], att, blk["proj_b"], threads=threads)).astype(np.float32)
+    h2 = layer_norm(x1, blk["norm2_w"], blk["norm2_b"])
+    f = staged_linear(blk["fc1_w16"], h2, blk["fc1_b"], EPILOGUE_GELU_ERF, threads=threads)
+    return (x1 + staged_linear(blk["fc2_w16"], f, blk["fc2_b"], threads=threads)).astype(np.float32)
+
+
+def vit_prefix(image: np.ndarray, patch: int, patch_w: np.ndarray, pos_embed: np.ndarray, ln_w: np.ndarray,
+               ln_b: np.ndarray, threads=None) -> np.ndarray:
+    """Backbone prefix (src/models/sam3/vision.hpp:252-282) in f64: unpadded
+    patch x patch convolution without bias (image [3][H][W], weight
+    [E][3][patch][patch]), + pos_embed [pg][pg][E] tiled over the grid, then
+    ln_pre.  Returns [tokens][E] f32, tokens in raster order."""
+    image = np.asarray(image, dtype=np.float64)
+    C, H, W = image.shape
+    gh, gw = H // patch, W // patch
+    cols = image.reshape(C, gh, patch, gw, patch).transpose(1, 3, 0, 2, 4).reshape(gh * gw, C * patch * patch)
+    E = patch_w.shape[0]
+    y = cols @ np.asarray(patch_w, np.float64).reshape(E, -1).T
+    pg = pos_embed.shape[0]
+    py, px = np.divmod(np.arange(gh * gw), gw)
+    y += np.asarray(pos_embed, np.float64)[py % pg, px % pg]
+    return layer_norm(y, ln_w, ln_b)

@@ -162,8 +162,8 @@ struct AttnSmem {
 
 __global__ void __launch_bounds__(kAttnThreads, 2)
 attention_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
-                 const __grid_constant__ CUtensorMap tm_v, Geometry geo, float* __restrict__ out, int64_t ldo,
-                 DeviceStatus* status) {
+                 const __grid_constant__ CUtensorMap tm_v, Geometry geo, float* __restrict__ out,
+                 __half* __restrict__ out_h, int64_t ldo, DeviceStatus* status) {
     extern __shared__ __align__(128) uint8_t smem_raw[];
     const uintptr_t raw = reinterpret_cast<uintptr_t>(smem_raw);
     const uintptr_t aligned = (raw + AttnSmem::header + 1023) & ~uintptr_t(1023);
@@ -421,9 +421,28 @@ attention_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
             tc_ld_32x32b_x32(tmem_o, o[0]);
             tc_ld_32x32b_x32(tmem_o + 32, o[1]);
             tc_wait_ld();
-            if (n < geo.group_n) {
-                const int tok = group_token(geo, g, n);
-                float* dst = out + static_cast<int64_t>(tok) * ldo + h * kHeadDim;
+            const bool valid_row = n < geo.group_n;
+            const int64_t tok = valid_row ? group_token(geo, g, n) : 0;
+            if (out_h != nullptr) {
+                // Q8_1 operand of the proj linear, staged from the f32 values
+                // the f32 path would store (two 32-channel blocks per row).
+                uint4* dst = reinterpret_cast<uint4*>(out_h + tok * ldo + h * kHeadDim);
+#pragma unroll
+                for (int c = 0; c < 2; ++c) {
+                    float v[32];
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(o[c][i]) * inv;
+                    uint32_t packed[16];
+                    const bool bad = stage_q8_1<1, 32>(v, packed);
+                    record_range(bad && valid_row, status);
+                    if (valid_row) {
+#pragma unroll
+                        for (int j = 0; j < 4; ++j)
+                            dst[c * 4 + j] = make_uint4(packed[4 * j], packed[4 * j + 1], packed[4 * j + 2], packed[4 * j + 3]);
+                    }
+                }
+            } else if (valid_row) {
+                float* dst = out + tok * ldo + h * kHeadDim;
 #pragma unroll
                 for (int c = 0; c < 2; ++c)
 #pragma unroll
@@ -457,16 +476,10 @@ size_t attention_scratch_bytes(int grid_w, int grid_h, int heads) {
     return static_cast<size_t>(3) * grid_w * grid_h * heads * kHeadDim * sizeof(__half) + 256;
 }
 
-void launch_vit_attention(const float* qkv, int64_t ldq, int grid_w, int grid_h, int heads, int window,
-                          const float* freqs, float* out, int64_t ldo, void* packed, DeviceState& state,
-                          cudaStream_t stream) {
+void launch_attention_packed(const __half* qp, const __half* kp, const __half* vt, int grid_w, int grid_h, int heads,
+                             int window, float* out, __half* out_h, int64_t ldo, DeviceState& state,
+                             cudaStream_t stream) {
     const Geometry geo = make_geometry(grid_w, grid_h, heads, window);
-    const int64_t per = static_cast<int64_t>(geo.groups) * heads * geo.group_n * kHeadDim;
-    __half* qp = static_cast<__half*>(packed);
-    __half* kp = qp + per;
-    __half* vt = kp + per;
-    launch_pdl(rope_pack_kernel, dim3((geo.group_n + 63) / 64, heads, geo.groups), dim3(256), 0, stream,
-               "rope_pack_kernel launch", qkv, ldq, freqs, geo, qp, kp, vt);
     const uint64_t gh = static_cast<uint64_t>(geo.groups) * heads;
     CUtensorMap tq, tk, tv;
     encode_tensor_map_3d(&tq, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, qp, kHeadDim, geo.group_n, gh, kHeadDim * 2,
@@ -485,8 +498,21 @@ void launch_vit_attention(const float* qkv, int64_t ldq, int grid_w, int grid_h,
         configured[state.device & 63] = true;
     }
     launch_pdl(attention_kernel, dim3((geo.group_n + kQTile - 1) / kQTile, static_cast<unsigned>(gh)),
-               dim3(kAttnThreads), AttnSmem::total, stream, "attention_kernel launch", tq, tk, tv, geo, out, ldo,
+               dim3(kAttnThreads), AttnSmem::total, stream, "attention_kernel launch", tq, tk, tv, geo, out, out_h, ldo,
                state.status);
+}
+
+void launch_vit_attention(const float* qkv, int64_t ldq, int grid_w, int grid_h, int heads, int window,
+                          const float* freqs, float* out, int64_t ldo, void* packed, DeviceState& state,
+                          cudaStream_t stream) {
+    const Geometry geo = make_geometry(grid_w, grid_h, heads, window);
+    const int64_t per = static_cast<int64_t>(geo.groups) * heads * geo.group_n * kHeadDim;
+    __half* qp = static_cast<__half*>(packed);
+    __half* kp = qp + per;
+    __half* vt = kp + per;
+    launch_pdl(rope_pack_kernel, dim3((geo.group_n + 63) / 64, heads, geo.groups), dim3(256), 0, stream,
+               "rope_pack_kernel launch", qkv, ldq, freqs, geo, qp, kp, vt);
+    launch_attention_packed(qp, kp, vt, grid_w, grid_h, heads, window, out, nullptr, ldo, state, stream);
 }
 
 }  // namespace samq

@@ -425,6 +425,76 @@ samq_status samq_vit_attention_v1(const float* qkv, int64_t ldq, int grid_w, int
     });
 }
 
+samq_status samq_vit_block_forward_v1(const samq_vit_block_v1* block, float* x, int grid_w, int grid_h,
+                                      void* stream_ptr) {
+    return guarded([&] {
+        require(block != nullptr && block->version == 1, "block descriptor missing or not version 1");
+        const samq_vit_block_v1& b = *block;
+        require(b.qkv && b.proj && b.fc1 && b.fc2, "null weight handle");
+        const int64_t E = b.qkv->k, mlp = b.fc1->n;
+        require(E == 256 || E == 512 || E == 1024, "embedding width must be 256, 512 or 1024");
+        require(b.qkv->n == 3 * E && b.proj->k == E && b.proj->n == E && b.fc1->k == E && b.fc2->k == mlp &&
+                    b.fc2->n == E,
+                "linear shapes must be qkv E->3E, proj E->E, fc1 E->MLP, fc2 MLP->E");
+        require(mlp % 32 == 0, "MLP width must be a multiple of 32");
+        require(grid_w > 0 && grid_h > 0 && static_cast<int64_t>(grid_w) * grid_h <= (int64_t(1) << 20),
+                "grid out of range");
+        const int window = b.window;
+        require(window == 0 || (window > 0 && grid_w % window == 0 && grid_h % window == 0),
+                "window must divide the grid (or be 0 for global attention)");
+        const int64_t group_n = window > 0 ? static_cast<int64_t>(window) * window
+                                           : static_cast<int64_t>(grid_w) * grid_h;
+        require(group_n % 8 == 0, "tokens per attention group must be a multiple of 8");
+        const float* params[] = {b.norm1_w, b.norm1_b, b.qkv_b, b.proj_b, b.norm2_w, b.norm2_b, b.fc1_b, b.fc2_b,
+                                 b.freqs_cis, x};
+        for (const float* p : params) require(p != nullptr && aligned16(p), "parameters must be 16-byte aligned device pointers");
+        const int device = current_device();
+        const samq_weights* handles[] = {b.qkv, b.proj, b.fc1, b.fc2};
+        for (const samq_weights* w : handles) require(w->device == device, "weight handle belongs to another device");
+        DeviceState& state = device_state(device);
+        cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
+        const int64_t tokens = static_cast<int64_t>(grid_w) * grid_h;
+        Scratch& scratch = scratch_for(state, stream, vit_block_scratch_bytes(tokens, E, mlp));
+        VitBlockArgs args;
+        args.window = window;
+        args.norm1_w = b.norm1_w;
+        args.norm1_b = b.norm1_b;
+        args.norm2_w = b.norm2_w;
+        args.norm2_b = b.norm2_b;
+        args.qkv = b.qkv;
+        args.proj = b.proj;
+        args.fc1 = b.fc1;
+        args.fc2 = b.fc2;
+        args.qkv_b = b.qkv_b;
+        args.proj_b = b.proj_b;
+        args.fc1_b = b.fc1_b;
+        args.fc2_b = b.fc2_b;
+        args.freqs = b.freqs_cis;
+        launch_vit_block(args, x, grid_w, grid_h, scratch.ptr, state, stream);
+        for (const samq_weights* w : handles) const_cast<samq_weights*>(w)->launches.fetch_add(1);
+    });
+}
+
+samq_status samq_vit_prefix_v1(const float* image, int width, int height, int patch, const float* patch_w,
+                               int64_t embed, const float* pos_embed, int pos_grid, const float* ln_w,
+                               const float* ln_b, float* x, void* stream_ptr) {
+    return guarded([&] {
+        require(embed == 256 || embed == 512 || embed == 1024, "embedding width must be 256, 512 or 1024");
+        require(patch > 0 && patch <= 32 && width > 0 && height > 0 && width % patch == 0 && height % patch == 0,
+                "image sides must be positive multiples of the patch size (patch <= 32)");
+        const int64_t tokens = static_cast<int64_t>(width / patch) * (height / patch);
+        require(tokens <= (int64_t(1) << 20), "too many tokens");
+        require(pos_grid > 0, "pos_grid must be positive");
+        const float* params[] = {image, patch_w, pos_embed, ln_w, ln_b, x};
+        for (const float* p : params) require(p != nullptr && aligned16(p), "arguments must be 16-byte aligned device pointers");
+        DeviceState& state = device_state(current_device());
+        cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
+        Scratch& scratch = scratch_for(state, stream, vit_prefix_scratch_bytes(tokens, embed, patch));
+        launch_vit_prefix(image, width, height, patch, patch_w, embed, pos_embed, pos_grid, ln_w, ln_b, x, scratch.ptr,
+                          state, stream);
+    });
+}
+
 samq_status samq_query_v1(const samq_weights* w, struct samq_counters_v1* out) {
     return guarded([&] {
         require(w != nullptr && out != nullptr, "null argument");

@@ -1,10 +1,16 @@
 // gemm.cu -- K2: Y = epilogue(A . B^T + bias) on the sm_100a tensor cores.
 //
 // A is the f16 activation operand staged by K1 ([m][k], row-major), B the f16
-// weight operand expanded from the K4 packets ([n][k], row-major); Y is f32
-// [m][n] with row stride ldy.  This is GGML mul_mat(W, X) with W = B and
-// X = A (src/models/sam3/ops.hpp:40-45), with the bias add and ggml_gelu_erf
-// of the ViT MLP fused (src/models/sam3/vision.hpp:234-236).
+// weight operand expanded from the K4 packets ([n][k], row-major).  This is
+// GGML mul_mat(W, X) with W = B and X = A (src/models/sam3/ops.hpp:40-45),
+// with the bias add and ggml_gelu_erf of the ViT MLP fused
+// (src/models/sam3/vision.hpp:234-236).  The epilogue writes one of (OutMode):
+//   f32 Y [m][ldy] (TMA store), optionally plus a residual (the ViT block's
+//     shortcut adds, vision.hpp:228,240);
+//   the Q8_1-staged f16 operand of the next linear (fc1 -> fc2), bit-identical
+//     to K1 run on the f32 values this epilogue would have stored;
+//   the qkv split into RoPE'd Q (x 1/8), K and V^T in the attention kernel's
+//     layout (vision.hpp:180-214).
 //
 // Persistent, warp-specialised kernel, one CTA per SM (64 + 32*EW threads):
 //   warp 0     TMA producer: 128x64 A and BNx64 B tiles, 128-byte swizzle,
@@ -91,17 +97,19 @@ __device__ __forceinline__ float gelu_erf(float x) {
 }
 
 // One epilogue warp's share of an accumulator tile: TMEM lanes 32*quarter..+31
-// (output rows row0..row0+31) and 32-column chunks [part*C/PARTS,
-// (part+1)*C/PARTS) of the C = BN/32 chunks of the tile starting at output
-// column col_base.  32 columns at a time: tcgen05.ld,
-// bias (one coalesced load, broadcast by shuffles), erf-GELU, swizzled staging
-// in shared memory, TMA store (clipped by the tensor map at the m / n edges).
+// (output rows row0..row0+31, one row per lane) and 32-column chunks
+// [part*C/PARTS, (part+1)*C/PARTS) of the C = BN/32 chunks of the tile starting
+// at output column col_base.  32 columns at a time: tcgen05.ld, bias (one
+// coalesced load, broadcast by shuffles), erf-GELU, then per OutMode either
+// swizzled staging in shared memory and a TMA store (clipped by the tensor map
+// at the m / n edges), or direct stores of f16 rows.
 template <int BN, int PARTS>
 __device__ __forceinline__ void drain_tile(uint32_t tmem_base, int quarter, int part, int acc, int row0,
-                                           int col_base, int m, int n, const float* __restrict__ bias,
-                                           int epilogue, const CUtensorMap* tma_y, uint8_t* stage_buf, int& buf,
-                                           int lane) {
+                                           int col_base, int m, int n, const Epilogue& ep,
+                                           const CUtensorMap* tma_y, uint8_t* stage_buf, int& buf, int lane,
+                                           DeviceStatus* status) {
     constexpr int kChunks = BN / 32;
+    const int row = row0 + lane;
 #pragma unroll 1
     for (int chunk = part * kChunks / PARTS; chunk < (part + 1) * kChunks / PARTS; ++chunk) {
         const int col0 = col_base + chunk * 32;
@@ -110,14 +118,81 @@ __device__ __forceinline__ void drain_tile(uint32_t tmem_base, int quarter, int 
         tc_ld_32x32b_x32(tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) +
                              static_cast<uint32_t>(acc * kAccStride + chunk * 32),
                          r);
-        const float bias_lane = (bias != nullptr && col0 + lane < n) ? __ldg(bias + col0 + lane) : 0.0f;
+        const float bias_lane = (ep.bias != nullptr && col0 + lane < n) ? __ldg(ep.bias + col0 + lane) : 0.0f;
         tc_wait_ld();
         float v[32];
 #pragma unroll
         for (int i = 0; i < 32; ++i) {
             float x = __uint_as_float(r[i]) + __shfl_sync(0xffffffffu, bias_lane, i);
-            if (epilogue == SAMQ_EPILOGUE_GELU_ERF) x = gelu_erf(x);
+            if (ep.gelu) x = gelu_erf(x);
             v[i] = x;
+        }
+        if (ep.mode == kOutF16Staged) {
+            uint32_t out[16];
+            const bool bad = stage_q8_1<1, 32>(v, out);
+            record_range(bad && row < m, status);
+            if (row < m) {
+                uint4* dst = reinterpret_cast<uint4*>(ep.h + static_cast<int64_t>(row) * ep.ldh + col0);
+#pragma unroll
+                for (int j = 0; j < 4; ++j) dst[j] = make_uint4(out[4 * j], out[4 * j + 1], out[4 * j + 2], out[4 * j + 3]);
+            }
+            continue;
+        }
+        if (ep.mode == kOutQkvPack) {
+            if (row < m) {
+                const int g = row / ep.group_n, nn = row - g * ep.group_n;
+                const int embed = ep.heads * 64;
+                const int sec = col0 / embed, rem = col0 - sec * embed;
+                const int64_t gh = static_cast<int64_t>(g) * ep.heads + (rem >> 6);
+                const int c0 = rem & 63;
+                if (sec < 2) {
+                    // RoPE on channel pairs (2i, 2i+1), i = c0/2 .. c0/2 + 15
+                    // (vision.hpp:100-148); the 1/8 softmax scale folds into Q
+                    // exactly (a power of two).
+                    const float4* fr = reinterpret_cast<const float4*>(ep.freqs + (static_cast<int64_t>(nn) * 32 + c0 / 2) * 2);
+                    const float scale = sec == 0 ? 0.125f : 1.0f;
+                    uint32_t out[16];
+#pragma unroll
+                    for (int p = 0; p < 8; ++p) {
+                        const float4 f = __ldg(fr + p);  // (cos, sin) of pairs 2p and 2p+1
+                        const float x0 = v[4 * p], x1 = v[4 * p + 1], x2 = v[4 * p + 2], x3 = v[4 * p + 3];
+                        const float re0 = __fsub_rn(__fmul_rn(x0, f.x), __fmul_rn(x1, f.y));
+                        const float im0 = __fadd_rn(__fmul_rn(x0, f.y), __fmul_rn(x1, f.x));
+                        const float re1 = __fsub_rn(__fmul_rn(x2, f.z), __fmul_rn(x3, f.w));
+                        const float im1 = __fadd_rn(__fmul_rn(x2, f.w), __fmul_rn(x3, f.z));
+                        const __half2 h0 = __floats2half2_rn(re0 * scale, im0 * scale);
+                        const __half2 h1 = __floats2half2_rn(re1 * scale, im1 * scale);
+                        out[2 * p] = *reinterpret_cast<const uint32_t*>(&h0);
+                        out[2 * p + 1] = *reinterpret_cast<const uint32_t*>(&h1);
+                    }
+                    __half* base = sec == 0 ? ep.q : ep.k;
+                    uint4* dst = reinterpret_cast<uint4*>(base + (gh * ep.group_n + nn) * 64 + c0);
+#pragma unroll
+                    for (int j = 0; j < 4; ++j)
+                        dst[j] = make_uint4(out[4 * j], out[4 * j + 1], out[4 * j + 2], out[4 * j + 3]);
+                } else {
+                    // V^T: lanes are consecutive rows n, so each channel's
+                    // stores from the warp are contiguous.
+                    __half* base = ep.vt + (gh * 64 + c0) * ep.group_n + nn;
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) base[static_cast<int64_t>(i) * ep.group_n] = __float2half_rn(v[i]);
+                }
+            }
+            continue;
+        }
+        if (ep.mode == kOutF32Residual && row < m) {
+            // The ViT shortcut add: residual + (acc + bias), one f32 add.
+            const float4* res = reinterpret_cast<const float4*>(ep.residual + static_cast<int64_t>(row) * ep.ldr + col0);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                if (col0 + 4 * j < n) {
+                    const float4 rv = res[j];
+                    v[4 * j] = __fadd_rn(rv.x, v[4 * j]);
+                    v[4 * j + 1] = __fadd_rn(rv.y, v[4 * j + 1]);
+                    v[4 * j + 2] = __fadd_rn(rv.z, v[4 * j + 2]);
+                    v[4 * j + 3] = __fadd_rn(rv.w, v[4 * j + 3]);
+                }
+            }
         }
         if (lane == 0) bulk_wait_group_read<kOutBuffers - 1>();
         __syncwarp();
@@ -140,8 +215,8 @@ __device__ __forceinline__ void drain_tile(uint32_t tmem_base, int quarter, int 
 template <int BN, int STAGES, int EW>
 __global__ void __launch_bounds__(threads_for(EW), 1)
 gemm_f16_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_b,
-                const __grid_constant__ CUtensorMap tma_y, const float* __restrict__ bias, int epilogue, int m,
-                int n, int k, DeviceStatus* status) {
+                const __grid_constant__ CUtensorMap tma_y, const Epilogue ep, int m, int n, int k,
+                DeviceStatus* status) {
     using L = Layout<BN, STAGES, EW>;
     static_assert(L::total <= 232448, "shared memory budget");
     extern __shared__ uint8_t smem_raw[];
@@ -268,8 +343,8 @@ gemm_f16_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant
             if (!__all_sync(0xffffffffu, mbar_wait(&tfull[acc], acc_ph, status, 4))) break;
             tc_fence_after();
             const int row0 = mt * BM + quarter * 32;
-            drain_tile<BN, EW / 4>(tmem_base, quarter, part, acc, row0, nt * BN, m, n, bias, epilogue, &tma_y, stage_buf, buf,
-                           lane);
+            drain_tile<BN, EW / 4>(tmem_base, quarter, part, acc, row0, nt * BN, m, n, ep, &tma_y, stage_buf, buf,
+                                   lane, status);
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&tempty[acc]);
@@ -290,16 +365,20 @@ gemm_f16_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant
 }
 
 template <int BN, int STAGES, int EW>
-void run(const __half* a, int64_t lda, const __half* b, int64_t m, int64_t n, int64_t k, const float* bias, int epilogue,
-         float* y, int64_t ldy, DeviceState& state, cudaStream_t stream) {
+void run(const __half* a, int64_t lda, const __half* b, int64_t m, int64_t n, int64_t k, const Epilogue& ep,
+         DeviceState& state, cudaStream_t stream) {
     using L = Layout<BN, STAGES, EW>;
     CUtensorMap ta, tb, ty;
     encode_tensor_map_2d(&ta, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, a, k, m, lda * 2, BK, BM,
                          CU_TENSOR_MAP_SWIZZLE_128B);
     encode_tensor_map_2d(&tb, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, b, k, n, k * 2, BK, BN,
                          CU_TENSOR_MAP_SWIZZLE_128B);
-    encode_tensor_map_2d(&ty, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, y, n, m, ldy * 4, 32, 32,
-                         CU_TENSOR_MAP_SWIZZLE_128B);
+    if (ep.mode == kOutF32 || ep.mode == kOutF32Residual)
+        encode_tensor_map_2d(&ty, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, ep.y, n, m, ep.ldy * 4, 32, 32,
+                             CU_TENSOR_MAP_SWIZZLE_128B);
+    else  // unused by the f16 modes: a valid map over A keeps the descriptor prefetch harmless
+        encode_tensor_map_2d(&ty, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, a, k / 2, m, lda * 2, 32, 32,
+                             CU_TENSOR_MAP_SWIZZLE_128B);
     auto kernel = gemm_f16_kernel<BN, STAGES, EW>;
     static bool configured[64] = {};
     if (!configured[state.device & 63]) {
@@ -309,8 +388,8 @@ void run(const __half* a, int64_t lda, const __half* b, int64_t m, int64_t n, in
     }
     const int64_t tiles = ((m + BM - 1) / BM) * ((n + BN - 1) / BN);
     const int grid = static_cast<int>(tiles < state.sm_count ? tiles : state.sm_count);
-    launch_pdl(kernel, dim3(grid), dim3(threads_for(EW)), L::total, stream, "gemm_f16_kernel launch", ta, tb, ty, bias,
-               epilogue, static_cast<int>(m), static_cast<int>(n), static_cast<int>(k), state.status);
+    launch_pdl(kernel, dim3(grid), dim3(threads_for(EW)), L::total, stream, "gemm_f16_kernel launch", ta, tb, ty, ep,
+               static_cast<int>(m), static_cast<int>(n), static_cast<int>(k), state.status);
 }
 
 }  // namespace
@@ -335,29 +414,41 @@ int choose_bn(int64_t m, int64_t n, int sms) {
 
 template <int EW>
 void run_width(int bn, const __half* a, int64_t lda, const __half* b, int64_t m, int64_t n, int64_t k,
-               const float* bias, int epilogue, float* y, int64_t ldy, DeviceState& state, cudaStream_t stream) {
+               const Epilogue& ep, DeviceState& state, cudaStream_t stream) {
     switch (bn) {
-        case 160: run<160, stages_for(160, EW), EW>(a, lda, b, m, n, k, bias, epilogue, y, ldy, state, stream); break;
-        case 192: run<192, stages_for(192, EW), EW>(a, lda, b, m, n, k, bias, epilogue, y, ldy, state, stream); break;
-        case 224: run<224, stages_for(224, EW), EW>(a, lda, b, m, n, k, bias, epilogue, y, ldy, state, stream); break;
-        default: run<256, stages_for(256, EW), EW>(a, lda, b, m, n, k, bias, epilogue, y, ldy, state, stream); break;
+        case 160: run<160, stages_for(160, EW), EW>(a, lda, b, m, n, k, ep, state, stream); break;
+        case 192: run<192, stages_for(192, EW), EW>(a, lda, b, m, n, k, ep, state, stream); break;
+        case 224: run<224, stages_for(224, EW), EW>(a, lda, b, m, n, k, ep, state, stream); break;
+        default: run<256, stages_for(256, EW), EW>(a, lda, b, m, n, k, ep, state, stream); break;
     }
+}
+
+void launch_gemm(const __half* a, int64_t lda, const __half* b, int64_t m, int64_t n, int64_t k, const Epilogue& ep,
+                 DeviceState& state, cudaStream_t stream) {
+    if (m == 0) return;
+    if (n <= 128) {
+        run<128, 6, 8>(a, lda, b, m, n, k, ep, state, stream);
+        return;
+    }
+    const int bn = choose_bn(m, n, state.sm_count);
+    if (ep.gelu || ep.mode == kOutQkvPack)
+        // erf-GELU (or the RoPE / transpose of the qkv split) makes the
+        // epilogue the longer pipeline: 16 epilogue warps.
+        run_width<16>(bn, a, lda, b, m, n, k, ep, state, stream);
+    else
+        run_width<8>(bn, a, lda, b, m, n, k, ep, state, stream);
 }
 
 void launch_gemm_f16(const __half* a, int64_t lda, const __half* b, int64_t m, int64_t n, int64_t k,
                      const float* bias, int epilogue, float* y, int64_t ldy, DeviceState& state,
                      cudaStream_t stream) {
-    if (m == 0) return;
-    if (n <= 128) {
-        run<128, 6, 8>(a, lda, b, m, n, k, bias, epilogue, y, ldy, state, stream);
-        return;
-    }
-    const int bn = choose_bn(m, n, state.sm_count);
-    if (epilogue == SAMQ_EPILOGUE_GELU_ERF)
-        // erf-GELU makes the epilogue the longer pipeline: 16 epilogue warps.
-        run_width<16>(bn, a, lda, b, m, n, k, bias, epilogue, y, ldy, state, stream);
-    else
-        run_width<8>(bn, a, lda, b, m, n, k, bias, epilogue, y, ldy, state, stream);
+    Epilogue ep;
+    ep.mode = kOutF32;
+    ep.gelu = epilogue == SAMQ_EPILOGUE_GELU_ERF ? 1 : 0;
+    ep.bias = bias;
+    ep.y = y;
+    ep.ldy = ldy;
+    launch_gemm(a, lda, b, m, n, k, ep, state, stream);
 }
 
 }  // namespace samq

@@ -23,7 +23,6 @@
 namespace samq {
 namespace {
 
-constexpr float kOperandLimit = 65000.0f;  // |x| above this could overflow the f16 operand
 
 __device__ __forceinline__ void load8(const float* __restrict__ p, float (&v)[8]) {
     const float4 a = __ldg(reinterpret_cast<const float4*>(p));
@@ -56,25 +55,6 @@ __device__ __forceinline__ float group_butterfly_sum(const float (&v)[8]) {
     s[0] = __fadd_rn(s[0], s[2]);
     s[1] = __fadd_rn(s[1], s[3]);
     return __fadd_rn(s[0], s[1]);
-}
-
-__device__ __forceinline__ void record_range(bool bad, DeviceStatus* status) {
-    const unsigned any = __ballot_sync(0xffffffffu, bad);
-    if (any && (threadIdx.x & 31) == __ffs(any) - 1 && status) {
-        atomicOr(&status->flags, kStatusRange);
-        atomicAdd(&status->range_blocks, 1u);
-    }
-}
-
-// roundf() for |y| < 2^22 without float/int conversions: round half away
-// from zero is trunc(|y| + 0.5) with the sign of y; the sum is taken rounding
-// toward zero (so 0.49999997 + 0.5 stays below 1) and the truncation is the
-// exact round-toward-zero add/subtract of 2^23.  Adding +0 at the end turns a
-// negative zero into +0, as the integer code it stands for has no sign.
-__device__ __forceinline__ float round_half_away(float y) {
-    const float t = __fadd_rz(fabsf(y), 0.5f);
-    const float whole = __fsub_rz(__fadd_rz(t, 8388608.0f), 8388608.0f);
-    return __fadd_rn(copysignf(whole, y), 0.0f);
 }
 
 // Low byte of an integral float q with |q| <= 127 (two's complement int8):

@@ -103,6 +103,66 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, Device
     }
 }
 
+// ---- Q8_1 activation operand ---------------------------------------------
+// The staging rule of GGML CUDA's quantize_q8_1 as pinned by SAM.cpp's
+// verifiers (tools/validation/verify_q8_rhs_staging.py:24-83) and scale patch
+// (cmake/patches/ggml-precise-cuda.patch:623-633), restated per 32-value block:
+//   amax = max |x|, d = amax / 127 (IEEE), q = round_half_away(x * (127/amax)),
+// and the tensor-core A operand is f16(f32(f16(d)) * q).  Shared by K1 and by
+// the fused producers (LayerNorm, GEMM and attention epilogues) so that every
+// path stages bit-identically from the same f32 values.
+
+// |x| above this could overflow the f16 operand (65504) after rounding.
+constexpr float kOperandLimit = 65000.0f;
+
+// roundf() for |y| < 2^22 without float/int conversions: round half away
+// from zero is trunc(|y| + 0.5) with the sign of y; the sum is taken rounding
+// toward zero (so 0.49999997 + 0.5 stays below 1) and the truncation is the
+// exact round-toward-zero add/subtract of 2^23.  Adding +0 at the end turns a
+// negative zero into +0, as the integer code it stands for has no sign.
+__device__ __forceinline__ float round_half_away(float y) {
+    const float t = __fadd_rz(fabsf(y), 0.5f);
+    const float whole = __fsub_rz(__fadd_rz(t, 8388608.0f), 8388608.0f);
+    return __fadd_rn(copysignf(whole, y), 0.0f);
+}
+
+// Stages V consecutive values of one thread whose 32-value block is spread
+// over LANES aligned neighbouring lanes (V * LANES == 32; every lane of the
+// warp must call it).  out[j] holds the f16 operand pair of v[2j], v[2j+1].
+// Returns true when a value is non-finite or beyond kOperandLimit.
+template <int LANES, int V>
+__device__ __forceinline__ bool stage_q8_1(const float (&v)[V], uint32_t (&out)[V / 2]) {
+    static_assert(LANES * V == 32, "one Q8_1 block is 32 values");
+    float amax = 0.0f;
+    bool bad = false;
+#pragma unroll
+    for (int j = 0; j < V; ++j) {
+        amax = fmaxf(amax, fabsf(v[j]));
+        bad |= !(fabsf(v[j]) <= kOperandLimit);
+    }
+#pragma unroll
+    for (int o = 1; o < LANES; o <<= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    const float dq = __half2float(__float2half_rn(__fdiv_rn(amax, 127.0f)));
+    const float inv = amax == 0.0f ? 0.0f : __fdiv_rn(127.0f, amax);
+#pragma unroll
+    for (int j = 0; j < V / 2; ++j) {
+        const float q0 = round_half_away(__fmul_rn(v[2 * j], inv));
+        const float q1 = round_half_away(__fmul_rn(v[2 * j + 1], inv));
+        const __half2 h = __floats2half2_rn(__fmul_rn(dq, q0), __fmul_rn(dq, q1));
+        out[j] = *reinterpret_cast<const uint32_t*>(&h);
+    }
+    return bad;
+}
+
+// Records a range failure once per warp (every lane must call it).
+__device__ __forceinline__ void record_range(bool bad, DeviceStatus* status) {
+    const unsigned any = __ballot_sync(0xffffffffu, bad);
+    if (any && (threadIdx.x & 31) == __ffs(any) - 1 && status) {
+        atomicOr(&status->flags, kStatusRange);
+        atomicAdd(&status->range_blocks, 1u);
+    }
+}
+
 // ---- programmatic dependent launch ---------------------------------------
 // Kernels launched with cudaLaunchAttributeProgrammaticStreamSerialization may
 // start before the previous kernel on the stream has finished; each of them

@@ -126,10 +126,65 @@ size_t attention_scratch_bytes(int grid_w, int grid_h, int heads);
 void launch_vit_attention(const float* qkv, int64_t ldq, int grid_w, int grid_h, int heads, int window,
                           const float* freqs, float* out, int64_t ldo, void* packed, DeviceState& state,
                           cudaStream_t stream);
+// Attention over already packed f16 inputs (Q x 1/8 and K RoPE'd,
+// [group * heads + head][group_n][64]; V^T [group * heads + head][64][group_n]),
+// output in raster token order: f32 `out`, or, when out_h is given, the
+// Q8_1-staged f16 operand of the proj linear.
+void launch_attention_packed(const __half* q, const __half* k, const __half* vt, int grid_w, int grid_h, int heads,
+                             int window, float* out, __half* out_h, int64_t ldo, DeviceState& state,
+                             cudaStream_t stream);
 
 // K2 gemm.cu
+// What the GEMM epilogue writes.  Rows of the output are rows of A.
+enum OutMode : int {
+    kOutF32 = 0,          // y = act(acc + bias), f32 [m][ldy]
+    kOutF32Residual = 1,  // y = residual + (acc + bias), f32 (y may alias residual)
+    kOutF16Staged = 2,    // h = Q8_1 operand of act(acc + bias), f16 [m][ldh] (n % 32 == 0)
+    kOutQkvPack = 3,      // acc + bias split into RoPE'd f16 Q (x 1/8), K and V^T (attention layout)
+};
+struct Epilogue {
+    int mode = kOutF32;
+    int gelu = 0;                   // erf-GELU after the bias
+    const float* bias = nullptr;    // [n] or null
+    float* y = nullptr;             // kOutF32 / kOutF32Residual
+    int64_t ldy = 0;
+    const float* residual = nullptr;
+    int64_t ldr = 0;
+    __half* h = nullptr;            // kOutF16Staged
+    int64_t ldh = 0;
+    // kOutQkvPack: A rows are window-major (row = group * group_n + n), the
+    // columns Q | K | V with heads of 64 channels; Q, K are
+    // [group * heads + head][group_n][64], V^T is [group * heads + head][64][group_n].
+    __half* q = nullptr;
+    __half* k = nullptr;
+    __half* vt = nullptr;
+    const float* freqs = nullptr;   // [group_n][32][2] (cos, sin) of position n
+    int heads = 0, group_n = 0;
+};
+void launch_gemm(const __half* a, int64_t lda, const __half* b, int64_t m, int64_t n, int64_t k, const Epilogue& ep,
+                 DeviceState& state, cudaStream_t stream);
+// f32 output with bias and optional erf-GELU (epilogue = SAMQ_EPILOGUE_*).
 void launch_gemm_f16(const __half* a, int64_t lda, const __half* b, int64_t m, int64_t n, int64_t k,
                      const float* bias, int epilogue, float* y, int64_t ldy, DeviceState& state,
                      cudaStream_t stream);
+
+
+// vit.cu: the ViT block / backbone prefix around K2 and K3.
+struct VitBlockArgs {
+    int window = 0;
+    const float *norm1_w = nullptr, *norm1_b = nullptr, *norm2_w = nullptr, *norm2_b = nullptr;
+    const samq_weights *qkv = nullptr, *proj = nullptr, *fc1 = nullptr, *fc2 = nullptr;
+    const float *qkv_b = nullptr, *proj_b = nullptr, *fc1_b = nullptr, *fc2_b = nullptr;
+    const float* freqs = nullptr;
+};
+size_t vit_block_scratch_bytes(int64_t tokens, int64_t embed, int64_t mlp);
+void launch_vit_block(const VitBlockArgs& blk, float* x, int grid_w, int grid_h, void* scratch, DeviceState& state,
+                      cudaStream_t stream);
+void launch_ln_stage(const float* x, int64_t rows, int64_t embed, int grid_w, int window, const float* w,
+                     const float* b, __half* a, DeviceState& state, cudaStream_t stream);
+size_t vit_prefix_scratch_bytes(int64_t tokens, int64_t embed, int patch);
+void launch_vit_prefix(const float* image, int width, int height, int patch, const float* patch_w, int64_t embed,
+                       const float* pos, int pos_grid, const float* ln_w, const float* ln_b, float* x,
+                       void* scratch, DeviceState& state, cudaStream_t stream);
 
 }  // namespace samq

@@ -1,0 +1,283 @@
+// vit.cu -- the SAM 3 ViT block and backbone prefix around K2 / K3.
+//
+// Reference: src/models/sam3/vision.hpp:152-243 (sam3_vit_block_forward) and
+// :252-282 (sam3_build_vit_prefix_graph); LayerNorm is ggml_norm(eps 1e-5)
+// then * w + b (src/models/sam3/ops.hpp:56-66).
+//
+// One block is seven launches, every activation hand-off in the layout its
+// consumer reads and every quantized linear fed the Q8_1 operand GGML's CUDA
+// path would stage (vision.hpp linears via ops.hpp:40-45):
+//   1 ln_stage_kernel   x -> LN1 -> Q8_1 operand, rows gathered window-major
+//                       (ggml_win_part, vision.hpp:170-173)
+//   2 gemm (qkv)        + bias -> RoPE'd Q (x 1/8), K, V^T in f16
+//   3 attention_kernel  -> Q8_1 operand of proj, raster order (win_unpart)
+//   4 gemm (proj)       x = x + (acc + bias)
+//   5 ln_stage_kernel   x -> LN2 -> Q8_1 operand
+//   6 gemm (fc1)        + bias -> erf-GELU -> Q8_1 operand of fc2
+//   7 gemm (fc2)        x = x + (acc + bias)
+// The prefix is im2col of the 14x14 patches (f16), the patch-embedding GEMM
+// and one kernel for + tiled pos_embed and ln_pre.  All launches use
+// programmatic dependent launch; each kernel waits for its predecessor before
+// touching memory.
+#include <algorithm>
+
+#include "samq_internal.hpp"
+
+namespace samq {
+namespace {
+
+constexpr float kLnEps = 1e-5f;
+
+// Source raster token of window-major row r (identity for global blocks).
+__device__ __forceinline__ int64_t window_row_token(int64_t r, int grid_w, int window) {
+    if (window == 0) return r;
+    const int64_t group_n = static_cast<int64_t>(window) * window;
+    const int64_t g = r / group_n, n = r - g * group_n;
+    const int per_row = grid_w / window;
+    const int64_t wy = g / per_row, wx = g - wy * per_row;
+    const int64_t ly = n / window, lx = n - ly * window;
+    return (wy * window + ly) * grid_w + wx * window + lx;
+}
+
+// LayerNorm of one row held by a warp: lane l owns elements 128 i + 4 l .. +3
+// (i < NV).  f32 arithmetic: mean, centred values, biased variance, 1/sqrt.
+template <int NV>
+__device__ __forceinline__ void layer_norm_row(float (&v)[NV][4], const float* __restrict__ w,
+                                               const float* __restrict__ b, int lane) {
+    constexpr float inv_e = 1.0f / (128.0f * NV);
+    float sum = 0.0f;
+#pragma unroll
+    for (int i = 0; i < NV; ++i) sum += (v[i][0] + v[i][1]) + (v[i][2] + v[i][3]);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+    const float mean = sum * inv_e;
+    float sq = 0.0f;
+#pragma unroll
+    for (int i = 0; i < NV; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            v[i][j] -= mean;
+            sq = fmaf(v[i][j], v[i][j], sq);
+        }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, o);
+    const float rstd = 1.0f / sqrtf(sq * inv_e + kLnEps);
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+        const float4 wv = __ldg(reinterpret_cast<const float4*>(w) + i * 32 + lane);
+        const float4 bv = __ldg(reinterpret_cast<const float4*>(b) + i * 32 + lane);
+        v[i][0] = fmaf(v[i][0] * rstd, wv.x, bv.x);
+        v[i][1] = fmaf(v[i][1] * rstd, wv.y, bv.y);
+        v[i][2] = fmaf(v[i][2] * rstd, wv.z, bv.z);
+        v[i][3] = fmaf(v[i][3] * rstd, wv.w, bv.w);
+    }
+}
+
+// One warp per output row r (window-major when window > 0): LayerNorm of the
+// raster row it gathers, then the Q8_1 operand (8 lanes per 32-value block).
+template <int NV>
+__global__ void __launch_bounds__(256) ln_stage_kernel(const float* __restrict__ x, int64_t rows, int grid_w,
+                                                       int window, const float* __restrict__ w,
+                                                       const float* __restrict__ b, __half* __restrict__ a,
+                                                       DeviceStatus* status) {
+    pdl_wait();
+    pdl_trigger();
+    constexpr int E = 128 * NV;
+    const int lane = threadIdx.x & 31;
+    const int64_t r = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+    if (r >= rows) return;  // whole warps only: rows are warp-uniform
+    const float4* src = reinterpret_cast<const float4*>(x + window_row_token(r, grid_w, window) * E);
+    float v[NV][4];
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+        const float4 t = src[i * 32 + lane];
+        v[i][0] = t.x; v[i][1] = t.y; v[i][2] = t.z; v[i][3] = t.w;
+    }
+    layer_norm_row<NV>(v, w, b, lane);
+    uint2* dst = reinterpret_cast<uint2*>(a + r * E);
+    bool bad = false;
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+        uint32_t out[2];
+        bad |= stage_q8_1<8, 4>(v[i], out);
+        dst[i * 32 + lane] = make_uint2(out[0], out[1]);
+    }
+    record_range(bad, status);
+}
+
+// x[t] = LayerNorm(x[t] + pos[(py % pg) * pg + px % pg]) in place, f32
+// (ggml_repeat of the 24x24 pos_embed, vision.hpp:264-272, then ln_pre).
+template <int NV>
+__global__ void __launch_bounds__(256) embed_ln_kernel(float* __restrict__ x, int64_t rows, int grid_w,
+                                                       const float* __restrict__ pos, int pos_grid,
+                                                       const float* __restrict__ w, const float* __restrict__ b) {
+    pdl_wait();
+    pdl_trigger();
+    constexpr int E = 128 * NV;
+    const int lane = threadIdx.x & 31;
+    const int64_t r = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+    if (r >= rows) return;
+    const int py = static_cast<int>(r / grid_w), px = static_cast<int>(r % grid_w);
+    const float4* p = reinterpret_cast<const float4*>(pos + static_cast<int64_t>((py % pos_grid) * pos_grid + px % pos_grid) * E);
+    float4* row = reinterpret_cast<float4*>(x + r * E);
+    float v[NV][4];
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+        const float4 t = row[i * 32 + lane];
+        const float4 q = __ldg(p + i * 32 + lane);
+        v[i][0] = t.x + q.x; v[i][1] = t.y + q.y; v[i][2] = t.z + q.z; v[i][3] = t.w + q.w;
+    }
+    layer_norm_row<NV>(v, w, b, lane);
+#pragma unroll
+    for (int i = 0; i < NV; ++i) row[i * 32 + lane] = make_float4(v[i][0], v[i][1], v[i][2], v[i][3]);
+}
+
+// Patch columns: a[t][c * P*P + ky * P + kx] = f16(image[c][py*P + ky][px*P + kx])
+// for token t = py * grid_w + px (ggml_im2col of the stride-P, unpadded patch
+// convolution, ops.hpp sam3_conv_2d), zero in the padding columns kp..ld-1.
+__global__ void __launch_bounds__(256) im2col_kernel(const float* __restrict__ image, int width, int height,
+                                                     int patch, int grid_w, int64_t tokens, int kp, int ld,
+                                                     __half* __restrict__ a) {
+    pdl_wait();
+    pdl_trigger();
+    const int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (idx >= tokens * ld) return;
+    const int64_t t = idx / ld;
+    const int col = static_cast<int>(idx - t * ld);
+    float v = 0.0f;
+    if (col < kp) {
+        const int pp = patch * patch;
+        const int c = col / pp, rem = col - c * pp, ky = rem / patch, kx = rem - ky * patch;
+        const int py = static_cast<int>(t / grid_w), px = static_cast<int>(t % grid_w);
+        v = __ldg(image + (static_cast<int64_t>(c) * height + py * patch + ky) * width + px * patch + kx);
+    }
+    a[idx] = __float2half_rn(v);
+}
+
+// f32 [n][k] -> f16 [n][ld], zero padded (the patch-embedding B operand).
+__global__ void __launch_bounds__(256) pad_f16_kernel(const float* __restrict__ src, int64_t n, int k, int ld,
+                                                      __half* __restrict__ dst) {
+    pdl_wait();
+    pdl_trigger();
+    const int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (idx >= n * ld) return;
+    const int64_t row = idx / ld;
+    const int col = static_cast<int>(idx - row * ld);
+    dst[idx] = __float2half_rn(col < k ? __ldg(src + row * k + col) : 0.0f);
+}
+
+unsigned blocks_for(int64_t threads) { return static_cast<unsigned>((threads + 255) / 256); }
+
+template <class Fn>
+void by_width(int embed, Fn&& fn) {
+    switch (embed) {
+        case 256: fn(std::integral_constant<int, 2>{}); break;
+        case 512: fn(std::integral_constant<int, 4>{}); break;
+        case 1024: fn(std::integral_constant<int, 8>{}); break;
+        default: fail(SAMQ_ERR_INVALID_ARGUMENT, "embedding width must be 256, 512 or 1024");
+    }
+}
+
+}  // namespace
+
+size_t vit_block_scratch_bytes(int64_t tokens, int64_t embed, int64_t mlp) {
+    // A1 [T][E] + packed Q, K, V^T 3 [T][E] + fc2 operand [T][MLP], all f16.
+    return static_cast<size_t>(tokens) * (4 * embed + mlp) * sizeof(__half) + 3 * 256;
+}
+
+void launch_ln_stage(const float* x, int64_t rows, int64_t embed, int grid_w, int window, const float* w,
+                     const float* b, __half* a, DeviceState& state, cudaStream_t stream) {
+    by_width(static_cast<int>(embed), [&](auto nv) {
+        launch_pdl(ln_stage_kernel<decltype(nv)::value>, dim3(blocks_for(rows * 32)), dim3(256), 0, stream,
+                   "ln_stage_kernel launch", x, rows, grid_w, window, w, b, a, state.status);
+    });
+}
+
+void launch_vit_block(const VitBlockArgs& blk, float* x, int grid_w, int grid_h, void* scratch, DeviceState& state,
+                      cudaStream_t stream) {
+    const int64_t embed = blk.qkv->k, mlp = blk.fc1->n;
+    const int heads = static_cast<int>(embed / 64);
+    const int64_t tokens = static_cast<int64_t>(grid_w) * grid_h;
+    const int group_n = blk.window > 0 ? blk.window * blk.window : static_cast<int>(tokens);
+    auto align = [](uintptr_t p) { return (p + 255) & ~uintptr_t(255); };
+    uintptr_t cursor = align(reinterpret_cast<uintptr_t>(scratch));
+    __half* a1 = reinterpret_cast<__half*>(cursor);
+    cursor = align(cursor + tokens * embed * sizeof(__half));
+    __half* packed = reinterpret_cast<__half*>(cursor);
+    cursor = align(cursor + 3 * tokens * embed * sizeof(__half));
+    __half* a3 = reinterpret_cast<__half*>(cursor);
+    __half* q = packed;
+    __half* k = packed + tokens * embed;
+    __half* vt = packed + 2 * tokens * embed;
+
+    launch_ln_stage(x, tokens, embed, grid_w, blk.window, blk.norm1_w, blk.norm1_b, a1, state, stream);
+    Epilogue ep;
+    ep.mode = kOutQkvPack;
+    ep.bias = blk.qkv_b;
+    ep.q = q;
+    ep.k = k;
+    ep.vt = vt;
+    ep.freqs = blk.freqs;
+    ep.heads = heads;
+    ep.group_n = group_n;
+    launch_gemm(a1, embed, blk.qkv->operand, tokens, 3 * embed, embed, ep, state, stream);
+    launch_attention_packed(q, k, vt, grid_w, grid_h, heads, blk.window, nullptr, a1, embed, state, stream);
+    ep = Epilogue{};
+    ep.mode = kOutF32Residual;
+    ep.bias = blk.proj_b;
+    ep.y = x;
+    ep.ldy = embed;
+    ep.residual = x;
+    ep.ldr = embed;
+    launch_gemm(a1, embed, blk.proj->operand, tokens, embed, embed, ep, state, stream);
+    launch_ln_stage(x, tokens, embed, grid_w, 0, blk.norm2_w, blk.norm2_b, a1, state, stream);
+    ep = Epilogue{};
+    ep.mode = kOutF16Staged;
+    ep.gelu = 1;
+    ep.bias = blk.fc1_b;
+    ep.h = a3;
+    ep.ldh = mlp;
+    launch_gemm(a1, embed, blk.fc1->operand, tokens, mlp, embed, ep, state, stream);
+    ep = Epilogue{};
+    ep.mode = kOutF32Residual;
+    ep.bias = blk.fc2_b;
+    ep.y = x;
+    ep.ldy = embed;
+    ep.residual = x;
+    ep.ldr = embed;
+    launch_gemm(a3, mlp, blk.fc2->operand, tokens, embed, mlp, ep, state, stream);
+}
+
+size_t vit_prefix_scratch_bytes(int64_t tokens, int64_t embed, int patch) {
+    const int64_t ld = (3 * patch * patch + 63) / 64 * 64;
+    return static_cast<size_t>(tokens + embed) * ld * sizeof(__half) + 2 * 256;
+}
+
+void launch_vit_prefix(const float* image, int width, int height, int patch, const float* patch_w, int64_t embed,
+                       const float* pos, int pos_grid, const float* ln_w, const float* ln_b, float* x,
+                       void* scratch, DeviceState& state, cudaStream_t stream) {
+    const int grid_w = width / patch, grid_h = height / patch;
+    const int64_t tokens = static_cast<int64_t>(grid_w) * grid_h;
+    const int kp = 3 * patch * patch;
+    const int ld = (kp + 63) / 64 * 64;
+    auto align = [](uintptr_t p) { return (p + 255) & ~uintptr_t(255); };
+    uintptr_t cursor = align(reinterpret_cast<uintptr_t>(scratch));
+    __half* cols = reinterpret_cast<__half*>(cursor);
+    cursor = align(cursor + tokens * ld * sizeof(__half));
+    __half* wp = reinterpret_cast<__half*>(cursor);
+    launch_pdl(im2col_kernel, dim3(blocks_for(tokens * ld)), dim3(256), 0, stream, "im2col_kernel launch", image,
+               width, height, patch, grid_w, tokens, kp, ld, cols);
+    launch_pdl(pad_f16_kernel, dim3(blocks_for(embed * ld)), dim3(256), 0, stream, "pad_f16_kernel launch", patch_w,
+               embed, kp, ld, wp);
+    Epilogue ep;
+    ep.mode = kOutF32;
+    ep.y = x;
+    ep.ldy = embed;
+    launch_gemm(cols, ld, wp, tokens, embed, ld, ep, state, stream);
+    by_width(static_cast<int>(embed), [&](auto nv) {
+        launch_pdl(embed_ln_kernel<decltype(nv)::value>, dim3(blocks_for(tokens * 32)), dim3(256), 0, stream,
+                   "embed_ln_kernel launch", x, tokens, grid_w, pos, pos_grid, ln_w, ln_b);
+    });
+}
+
+}  // namespace samq

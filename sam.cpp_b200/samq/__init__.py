@@ -47,6 +47,13 @@ class Counters(ctypes.Structure):
                 ("weight_bytes", ctypes.c_uint64)]
 
 
+class VitBlockDesc(ctypes.Structure):
+    """struct samq_vit_block_v1."""
+    _fields_ = [("version", ctypes.c_uint32), ("window", ctypes.c_int32), ("norm1_w", _vp), ("norm1_b", _vp),
+                ("qkv", _vp), ("qkv_b", _vp), ("proj", _vp), ("proj_b", _vp), ("norm2_w", _vp), ("norm2_b", _vp),
+                ("fc1", _vp), ("fc1_b", _vp), ("fc2", _vp), ("fc2_b", _vp), ("freqs_cis", _vp)]
+
+
 SIGNATURES = {
     "samq_last_error_v1": (ctypes.c_char_p, []),
     "samq_init_v1": (_i32, [_i32]),
@@ -66,6 +73,8 @@ SIGNATURES = {
     "samq_check_v1": (_i32, [_i32, _vp]),
     "samq_linear_static_v1": (_i32, [_vp, _vp, _i64, _i64, _vp, _i32, _vp, _i64, _vp]),
     "samq_vit_attention_v1": (_i32, [_vp, _i64, _i32, _i32, _i32, _i32, _i32, _vp, _vp, _i64, _vp]),
+    "samq_vit_block_forward_v1": (_i32, [ctypes.POINTER(VitBlockDesc), _vp, _i32, _i32, _vp]),
+    "samq_vit_prefix_v1": (_i32, [_vp, _i32, _i32, _i32, _vp, _i64, _vp, _i32, _vp, _vp, _vp, _vp]),
 }
 STATIC_OPERAND_ELEMENTS = 16777216
 
@@ -226,3 +235,31 @@ def vit_attention(qkv, ldq: int, grid_w: int, grid_h: int, heads: int, window: i
 
 def check(device: int = 0, stream=None):
     _check(library().samq_check_v1(device, _stream(stream)))
+
+
+class VitBlock:
+    """One ViT block's device parameters (samq_vit_block_v1).
+
+    The f32 parameters are device tensors (kept alive here); the four linears
+    are Weights handles.  window is 24 for windowed blocks and 0 for global
+    ones; freqs is [positions][32][2] (cos, sin)."""
+
+    def __init__(self, window: int, norm1_w, norm1_b, qkv: Weights, qkv_b, proj: Weights, proj_b, norm2_w, norm2_b,
+                 fc1: Weights, fc1_b, fc2: Weights, fc2_b, freqs):
+        self._keep = (norm1_w, norm1_b, qkv, qkv_b, proj, proj_b, norm2_w, norm2_b, fc1, fc1_b, fc2, fc2_b, freqs)
+        self.window = window
+        self.desc = VitBlockDesc(1, window, _addr(norm1_w), _addr(norm1_b), qkv.handle, _addr(qkv_b), proj.handle,
+                                 _addr(proj_b), _addr(norm2_w), _addr(norm2_b), fc1.handle, _addr(fc1_b), fc2.handle,
+                                 _addr(fc2_b), _addr(freqs))
+
+
+def vit_block_forward(block: VitBlock, x, grid_w: int, grid_h: int, stream=None):
+    """samq_vit_block_forward_v1: one pre-LN ViT block in place on x [tokens][E] f32."""
+    _check(library().samq_vit_block_forward_v1(ctypes.byref(block.desc), _addr(x), grid_w, grid_h, _stream(stream)))
+
+
+def vit_prefix(image, width: int, height: int, patch: int, patch_w, embed: int, pos_embed, pos_grid: int, ln_w, ln_b,
+               x, stream=None):
+    """samq_vit_prefix_v1: patch embedding + tiled pos_embed + ln_pre into x [tokens][E] f32."""
+    _check(library().samq_vit_prefix_v1(_addr(image), width, height, patch, _addr(patch_w), embed, _addr(pos_embed),
+                                        pos_grid, _addr(ln_w), _addr(ln_b), _addr(x), _stream(stream)))
