@@ -1,26 +1,26 @@
 #!/usr/bin/env python3
-"""Benchmark of the B200 quantized-linear path (driver contract: one JSON line).
+"""Benchmark of the B200 SAM 3 quantized path (driver contract: one JSON line).
 
-Workload (BASELINE config 2 at M = 5184 tokens, the headline Q4_K profile):
-one "step" is one ViT block's four quantized linears, each from F32
-activations (K1 staging + K2 tcgen05 GEMM), with bias and F32 output:
-  qkv  1024 -> 3072  Q4_K
-  proj 1024 -> 1024  Q4_K
-  fc1  1024 -> 4736  Q4_K  + erf-GELU
-  fc2  4736 -> 1024  Q8_0  (K = 4736 is not a multiple of 256; the reference
-                            stores fc2 as Q8_0 in every K-quant profile,
-                            src/models/sam3/weights.hpp:148-164)
-Weights are N(0, 0.02^2) with 1% of entries x8, seeds 0-3; activations
-N(0, 1).  Synthetic data: no checkpoint exists on the box.
+Headline workload: the full SAM 3 vision backbone on one
+1008 x 1008 image per GPU, batch 1: patch embedding + pos_embed + ln_pre, then
+32 pre-LN ViT blocks (width 1024, 16 heads, MLP 4736, 2D RoPE; windowed 24x24
+attention except global blocks 7, 15, 23, 31) with Q4_K qkv / proj / fc1 and
+Q8_0 fc2 (src/models/sam3/weights.hpp:148-164), every linear fed Q8_1-staged
+activations.  One "step" is one image through samq_vit_prefix_v1 and 32
+samq_vit_block_forward_v1 calls.  `value` is images/s over all ranks with the
+image resident in HBM; `e2e` adds, every step, the pinned host->device copy of
+the normalized image and the device->host read of the 5184 x 1024 features.
+Weights are random-init (N(0, 0.02^2), 1% x8), the image U[0,1] normalized:
+synthetic, no checkpoint exists on the box.
 
-`value` is q-GEMM throughput (2*M*N*K summed over the 4 linears, all ranks)
-with inputs resident in HBM; `e2e` is the same metric through the C ABI with
-host buffers (pinned H2D of X and D2H of Y inside the timed region).
-Multi-GPU: images shard across GPUs with no exchange (weak scaling, one
-process per GPU, no collective on the data path).
+`qgemm` reports BASELINE config 2 beside it: one ViT block's four quantized
+linears at M = 5184 from f32 activations (K1 staging + K2 GEMM) in q-GEMM
+TOPS, with the GEMM roofline.  Multi-GPU: images shard across GPUs with no
+exchange (weak scaling, one process per GPU, no collective on the data path).
 
 `--impl reference` times the CPU restatement of the reference's GGML CPU path
-(oracle/, GGML itself is not buildable here) on the box's host cores.
+(oracle/; GGML itself is not buildable here) on the box's host cores over a
+bounded sample of the backbone and reports the same images/s metric.
 """
 from __future__ import annotations
 
@@ -47,8 +47,21 @@ LINEARS = [  # name, n, k, weight type, epilogue, seed
     ("fc1", 4736, 1024, 12, 1, 2),
     ("fc2", 1024, 4736, 8, 0, 3),
 ]
-WORKLOAD = "vit_block_linears_q4k_m5184"
-METRIC = "SAM3 ViT-block quantized-linear throughput (q-GEMM TOPS, Q4_K + Q8_0 fc2, 5184 tokens)"
+QGEMM_WORKLOAD = "vit_block_linears_q4k_m5184"
+QGEMM_METRIC = "SAM3 ViT-block quantized-linear throughput (q-GEMM TOPS, Q4_K + Q8_0 fc2, 5184 tokens)"
+WORKLOAD = "sam3_vit_backbone_q4k_1008px_batch1"
+METRIC = "SAM3 vision backbone images/s (Q4_K, fc2 Q8_0, 1008x1008, batch 1 per GPU)"
+E, MLP, HEADS, GRID, PATCH, IMAGE, POS_GRID, DEPTH, WINDOW = 1024, 4736, 16, 72, 14, 1008, 24, 32, 24
+GLOBAL_BLOCKS = (7, 15, 23, 31)
+
+
+def backbone_ops():
+    """Algorithmic work of one image: 2 M N K over the 128 block linears and
+    the patch GEMM, plus 4 N_q N_k hd per head of attention."""
+    lin = DEPTH * step_ops() + 2.0 * M * E * 3 * PATCH * PATCH
+    attn = (DEPTH - len(GLOBAL_BLOCKS)) * 4.0 * (GRID // WINDOW) ** 2 * (WINDOW * WINDOW) ** 2 * 64 * HEADS
+    attn += len(GLOBAL_BLOCKS) * 4.0 * M * M * 64 * HEADS
+    return lin, attn
 
 
 def step_ops(m=M):
@@ -155,8 +168,8 @@ def dist_setup():
     return world, rank, local
 
 
-def cpu_sample_rate(oracle_mod, weights, threads, budget_s):
-    """Oracle (restated GGML CPU path) throughput on a bounded sample of rows."""
+def cpu_linears_rate(oracle_mod, weights, threads, budget_s):
+    """Oracle (restated GGML CPU path) q-GEMM throughput on a bounded row sample."""
     rng = np.random.default_rng(99)
     rows = 16
     xs = {name: rng.normal(0, 1, (rows, k)).astype(np.float32) for name, n, k, *_ in LINEARS}
@@ -169,71 +182,152 @@ def cpu_sample_rate(oracle_mod, weights, threads, budget_s):
         return time.perf_counter() - t0
 
     run(rows)  # warm-up (first-touch, thread pool)
-    t = run(rows)
-    per_row = t / rows
+    per_row = run(rows) / rows
     sample_rows = int(max(rows, min(M, budget_s / max(per_row, 1e-9) / 2)))
     reps, total, start = 0, 0.0, time.perf_counter()
     while reps < 1 or (time.perf_counter() - start < budget_s and reps < 400):
         total += run(sample_rows)
         reps += 1
-    ops = step_ops(sample_rows) * reps
-    return ops / total / 1e12, sample_rows, reps, total
+    return step_ops(sample_rows) * reps / total / 1e12, sample_rows, reps, total
+
+
+class CpuBackbone:
+    """Bounded samples of the CPU backbone, extrapolated to seconds per image.
+
+    The reference's CPU path is GGML's: quantized mul_mat (restated by
+    oracle_cpu_linear: Q8_K / Q8_0 activation packing, integer block dots,
+    OpenMP, AVX-512 VNNI when present), f32 attention, LayerNorm and the f32
+    patch convolution (numpy f32 / BLAS here).  One sample (`step`) is:
+    `rows` token rows through one block's 4 linears (+2 LayerNorms), one
+    24x24 window of 16-head attention, and `qrows` query rows of one head of
+    global attention over all 5184 keys.  The patch convolution is timed once.
+    """
+
+    def __init__(self, oracle_mod, rows=1024, qrows=256):
+        self.o = oracle_mod
+        self.threads = oracle_mod.default_threads()
+        self.rows, self.qrows = rows, qrows
+        self.weights = [make_weights(oracle_mod, n, k, qtype, seed) for _, n, k, qtype, _, seed in LINEARS]
+        rng = np.random.default_rng(11)
+        self.x = {name: rng.normal(0, 1, (rows, k)).astype(np.float32) for name, n, k, *_ in LINEARS}
+        self.y = {name: np.empty((rows, n), np.float32) for name, n, *_ in LINEARS}
+        self.ln = rng.normal(0, 1, (rows, E)).astype(np.float32)
+        self.qw = rng.normal(0, 1, (HEADS, WINDOW * WINDOW, 64)).astype(np.float32)
+        self.kw = rng.normal(0, 1, (HEADS, WINDOW * WINDOW, 64)).astype(np.float32)
+        self.vw = rng.normal(0, 1, (HEADS, WINDOW * WINDOW, 64)).astype(np.float32)
+        self.qg = rng.normal(0, 1, (qrows, 64)).astype(np.float32)
+        self.kg = rng.normal(0, 1, (M, 64)).astype(np.float32)
+        self.vg = rng.normal(0, 1, (M, 64)).astype(np.float32)
+        cols = rng.normal(0, 1, (M, 3 * PATCH * PATCH)).astype(np.float32)
+        pw = rng.normal(0, 0.02, (3 * PATCH * PATCH, E)).astype(np.float32)
+        t0 = time.perf_counter()
+        for _ in range(3):
+            cols @ pw
+        self.prefix_s = (time.perf_counter() - t0) / 3
+
+    @staticmethod
+    def _softmax_av(s, v):
+        s = s - s.max(axis=-1, keepdims=True)
+        np.exp(s, out=s)
+        s /= s.sum(axis=-1, keepdims=True)
+        return s @ v
+
+    def step(self):
+        """One sample; returns the seconds per image it implies."""
+        t0 = time.perf_counter()
+        for (name, n, k, qtype, epi, _), (packed, bias) in zip(LINEARS, self.weights):
+            self.o.cpu_linear(qtype, packed, k, n, self.x[name], bias=bias, epilogue=epi, threads=self.threads,
+                              out=self.y[name])
+        for _ in range(2):
+            c = self.ln - self.ln.mean(axis=1, keepdims=True)
+            c / np.sqrt((c * c).mean(axis=1, keepdims=True) + 1e-5)
+        t1 = time.perf_counter()
+        self._softmax_av(np.matmul(self.qw, self.kw.transpose(0, 2, 1)) * 0.125, self.vw)
+        t2 = time.perf_counter()
+        self._softmax_av((self.qg @ self.kg.T) * 0.125, self.vg)
+        t3 = time.perf_counter()
+        per_block_rows = (t1 - t0) * M / self.rows
+        windowed = (t2 - t1) * (GRID // WINDOW) ** 2
+        global_ = (t3 - t2) * (M / self.qrows) * HEADS
+        return (DEPTH * per_block_rows + (DEPTH - len(GLOBAL_BLOCKS)) * windowed + len(GLOBAL_BLOCKS) * global_
+                + self.prefix_s)
+
+    def describe(self):
+        return (f"per sample: {self.rows} of {M} token rows through one block's 4 linears + 2 LayerNorms "
+                f"(restated GGML CPU mul_mat, OpenMP{', AVX-512 VNNI' if self.o.has_vnni() else ''}), one 24x24 "
+                f"window of 16-head f32 attention, {self.qrows} query rows of one global-attention head "
+                f"(numpy f32 BLAS); patch conv timed once; extrapolated to 32 blocks (4 global) per image; "
+                "GGML itself unavailable")
 
 
 def run_reference(args, world, rank):
-    """CPU reference arm: rank 0 times the restated GGML CPU path."""
+    """CPU reference arm: rank 0 times the restated CPU backbone (images/s)."""
     if rank != 0:
         return
     from oracle import oracle as o
     o.lib()
-    threads = o.default_threads()
-    weights = [make_weights(o, n, k, qtype, seed) for _, n, k, qtype, _, seed in LINEARS]
-    rng = np.random.default_rng(7)
-    # Size each step's row sample so the whole run stays within ~2 minutes.
-    probe = {name: rng.normal(0, 1, (8, k)).astype(np.float32) for name, n, k, *_ in LINEARS}
-    t0 = time.perf_counter()
-    for (name, n, k, qtype, epi, _), (packed, bias) in zip(LINEARS, weights):
-        o.cpu_linear(qtype, packed, k, n, probe[name], bias=bias, epilogue=epi, threads=threads)
-    per_row = (time.perf_counter() - t0) / 8
-    budget = 100.0 / max(args.steps + args.warmup, 1)
-    rows = int(max(8, min(M, budget / max(per_row, 1e-9))))
-    xs = {name: rng.normal(0, 1, (rows, k)).astype(np.float32) for name, n, k, *_ in LINEARS}
-    ys = {name: np.empty((rows, n), np.float32) for name, n, *_ in LINEARS}
-
-    def step():
-        for (name, n, k, qtype, epi, _), (packed, bias) in zip(LINEARS, weights):
-            o.cpu_linear(qtype, packed, k, n, xs[name], bias=bias, epilogue=epi, threads=threads, out=ys[name])
-
+    cpu = CpuBackbone(o)
     for _ in range(args.warmup):
-        step()
+        cpu.step()
     t0 = time.perf_counter()
-    for _ in range(args.steps):
-        step()
+    per_image = [cpu.step() for _ in range(args.steps)]
     elapsed = time.perf_counter() - t0
-    value = step_ops(rows) * args.steps / elapsed / 1e12
+    value = 1.0 / float(np.mean(per_image))
     line = {
-        "impl": "reference", "metric": METRIC, "value": value, "unit": "TOPS", "n_gpus": world,
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "images/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": elapsed / args.steps * 1e3,
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8xint8->f32",
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8xint8->f32 / f32",
         "data": "synthetic",
-        "config": {"workload": WORKLOAD, "rows_per_step": rows, "tokens": M,
-                   "linears": [l[0] for l in LINEARS], "formats": ["Q4_K", "Q4_K", "Q4_K", "Q8_0"]},
-        "cpu_baseline": {"value": value, "unit": "TOPS", "cores": threads, "kind": "port",
-                         "sample": f"{rows} of {M} token rows per step through the 4 linears; "
-                                   "CPU restatement of GGML's CPU mul_mat (Q8_0xQ8_0, K-quant xQ8_K, "
-                                   f"OpenMP, AVX-512 VNNI={'yes' if o.has_vnni() else 'no'}); GGML unavailable"},
-        "e2e": {"value": value, "unit": "TOPS", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "config": {"workload": WORKLOAD, "image": IMAGE, "tokens": M, "blocks": DEPTH,
+                   "global_blocks": list(GLOBAL_BLOCKS), "formats": {"qkv/proj/fc1": "Q4_K", "fc2": "Q8_0"}},
+        "cpu_baseline": {"value": value, "unit": "images/s", "cores": cpu.threads, "kind": "port",
+                         "sample": cpu.describe()},
+        "e2e": {"value": value, "unit": "images/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
+
+
+def make_backbone(samq, o, torch, device, rank):
+    """Random-init SAM 3 vision backbone on `device` (config 3 statistics)."""
+    dev = torch.device("cuda", device)
+    blocks, keep = [], []
+    base = np.random.default_rng(2024 + rank)
+    freqs_w = torch.from_numpy(o.rope_freqs(WINDOW * WINDOW, seed=1)).to(dev)
+    freqs_g = torch.from_numpy(o.rope_freqs(M, seed=2)).to(dev)
+    for i in range(DEPTH):
+        rng = np.random.default_rng(base.integers(1 << 62))
+        t = {}
+        for name, n, k, qtype in (("qkv", 3 * E, E, 12), ("proj", E, E, 12), ("fc1", MLP, E, 12), ("fc2", E, MLP, 8)):
+            w = rng.standard_normal((n, k), dtype=np.float32) * np.float32(0.02)
+            w[rng.random((n, k), dtype=np.float32) < 0.01] *= 8
+            t[name] = samq.Weights(qtype, k, n, o.quantize(qtype, w), device=device)
+            t[name + "_b"] = torch.from_numpy(rng.normal(0, 0.02, n).astype(np.float32)).to(dev)
+        for name in ("norm1", "norm2"):
+            t[name + "_w"] = torch.from_numpy((1 + rng.normal(0, 0.02, E)).astype(np.float32)).to(dev)
+            t[name + "_b"] = torch.from_numpy(rng.normal(0, 0.02, E).astype(np.float32)).to(dev)
+        window = 0 if i in GLOBAL_BLOCKS else WINDOW
+        blocks.append(samq.VitBlock(window, t["norm1_w"], t["norm1_b"], t["qkv"], t["qkv_b"], t["proj"],
+                                    t["proj_b"], t["norm2_w"], t["norm2_b"], t["fc1"], t["fc1_b"], t["fc2"],
+                                    t["fc2_b"], freqs_g if window == 0 else freqs_w))
+        keep.append(t)
+    rng = np.random.default_rng(77 + rank)
+    prefix = {
+        "patch_w": torch.from_numpy(rng.normal(0, 0.02, (E, 3, PATCH, PATCH)).astype(np.float32)).to(dev),
+        "pos": torch.from_numpy(rng.normal(0, 0.02, (POS_GRID, POS_GRID, E)).astype(np.float32)).to(dev),
+        "ln_w": torch.from_numpy((1 + rng.normal(0, 0.02, E)).astype(np.float32)).to(dev),
+        "ln_b": torch.from_numpy(rng.normal(0, 0.02, E).astype(np.float32)).to(dev),
+    }
+    return blocks, prefix, keep
 
 
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=2000)
-    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="samq", choices=["samq", "reference"])
     ap.add_argument("--e2e-steps", type=int, default=20)
+    ap.add_argument("--qgemm-steps", type=int, default=500)
     ap.add_argument("--cpu-budget", type=float, default=12.0, help="seconds of CPU baseline work")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--profile", choices=[l[0] for l in LINEARS],
@@ -262,31 +356,31 @@ def main():
     samq.init(local)
     stream = torch.cuda.current_stream()
 
-    weights, biases, xs, ys, host = [], [], [], [], []
-    for name, n, k, qtype, epi, seed in LINEARS:
-        packed, bias = make_weights(o, n, k, qtype, seed + 4 * rank)
-        weights.append(samq.Weights(qtype, k, n, packed, device=local))
-        biases.append(torch.from_numpy(bias).cuda())
-        rng = np.random.default_rng(1000 + seed + 17 * rank)
-        x = rng.normal(0, 1, (M, k)).astype(np.float32)
-        xs.append(torch.from_numpy(x).cuda())
-        ys.append(torch.empty((M, n), dtype=torch.float32, device="cuda"))
-        host.append((torch.from_numpy(x).pin_memory(), torch.empty((M, n), dtype=torch.float32).pin_memory()))
+    def max_over_ranks(ms):
+        t = torch.tensor([ms], dtype=torch.float64, device="cuda")
+        if world > 1:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
 
-    def launch(i):
-        name, n, k, qtype, epi, _ = LINEARS[i]
-        samq.linear(weights[i], xs[i], M, k, biases[i], epi, ys[i], n, stream)
+    # ---- backbone (config 3): one image per step per GPU ------------------
+    blocks, prefix, keep = make_backbone(samq, o, torch, local, rank)
+    rng = np.random.default_rng(500 + rank)
+    image_host = torch.from_numpy(((rng.random((3, IMAGE, IMAGE), dtype=np.float32) - 0.5) / 0.5)).pin_memory()
+    image = image_host.cuda()
+    feats = torch.empty((M, E), dtype=torch.float32, device="cuda")
+    feats_host = torch.empty((M, E), dtype=torch.float32).pin_memory()
 
-    # Warm-up (also grows the per-stream scratch before timing).
+    def forward():
+        samq.vit_prefix(image, IMAGE, IMAGE, PATCH, prefix["patch_w"], E, prefix["pos"], POS_GRID, prefix["ln_w"],
+                        prefix["ln_b"], feats, stream)
+        for blk in blocks:
+            samq.vit_block_forward(blk, feats, GRID, GRID, stream)
+
     for _ in range(args.warmup):
-        for i in range(len(LINEARS)):
-            launch(i)
+        forward()
     torch.cuda.synchronize()
     samq.check(local, stream)
 
-    # Timed region: K steps, barrier + synchronize on both sides, max over ranks.
-    sample_every = max(1, args.steps // 200)
-    events = []
     sampler = ClockSampler(int(os.environ.get("CUDA_VISIBLE_DEVICES", str(local)).split(",")[0])
                            if os.environ.get("CUDA_VISIBLE_DEVICES", "").split(",")[0].isdigit() else local)
     sampler.start()
@@ -295,48 +389,25 @@ def main():
     torch.cuda.synchronize()
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     start.record(stream)
-    for s in range(args.steps):
-        if s % sample_every == 0:
-            evs = [torch.cuda.Event(enable_timing=True) for _ in range(2 * len(LINEARS))]
-            for i in range(len(LINEARS)):
-                evs[2 * i].record(stream)
-                launch(i)
-                evs[2 * i + 1].record(stream)
-            events.append(evs)
-        else:
-            for i in range(len(LINEARS)):
-                launch(i)
+    for _ in range(args.steps):
+        forward()
     end.record(stream)
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
     clocks = sampler.stop()
-    elapsed_ms = start.elapsed_time(end)
     samq.check(local, stream)
-    t = torch.tensor([elapsed_ms], dtype=torch.float64, device="cuda")
-    if world > 1:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    elapsed_ms = float(t.item())
-    value = step_ops() * args.steps * world / (elapsed_ms / 1e3) / 1e12
-
-    # Per-launch durations of the sampled steps (linear = K1 + GEMM).
-    per_linear = np.array([[evs[2 * i].elapsed_time(evs[2 * i + 1]) for i in range(len(LINEARS))] for evs in events])
-    linear_ms = per_linear.mean(axis=0)
-
-    # GEMM-only launch durations (dominant kernel) over a separate sampled pass
-    # of the same launches: K1 staging is timed with its own events.
-    gemm_ms = gemm_only_durations(samq, weights, xs, ys, biases, stream)
+    elapsed_ms = max_over_ranks(start.elapsed_time(end))
+    value = args.steps * world / (elapsed_ms / 1e3)
+    feats_ok = bool(torch.isfinite(feats).all().item())
 
     # End to end through the C ABI with host buffers.
     e2e_steps = max(3, args.e2e_steps)
-    h2d = sum(x.numel() * 4 for x, _ in host)
-    d2h = sum(y.numel() * 4 for _, y in host)
 
     def e2e_step():
-        for i, (name, n, k, qtype, epi, _) in enumerate(LINEARS):
-            xs[i].copy_(host[i][0], non_blocking=True)
-            samq.linear(weights[i], xs[i], M, k, biases[i], epi, ys[i], n, stream)
-            host[i][1].copy_(ys[i], non_blocking=True)
+        image.copy_(image_host, non_blocking=True)
+        forward()
+        feats_host.copy_(feats, non_blocking=True)
 
     for _ in range(3):
         e2e_step()
@@ -349,11 +420,42 @@ def main():
         e2e_step()
     e1.record(stream)
     torch.cuda.synchronize()
-    e2e_ms = torch.tensor([e0.elapsed_time(e1)], dtype=torch.float64, device="cuda")
-    if world > 1:
-        dist.all_reduce(e2e_ms, op=dist.ReduceOp.MAX)
-    e2e_value = step_ops() * e2e_steps * world / (float(e2e_ms.item()) / 1e3) / 1e12
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1))
+    e2e_value = e2e_steps * world / (e2e_ms / 1e3)
+    samq.check(local, stream)
+    lin_ops, attn_ops = backbone_ops()
 
+    # ---- q-GEMM (config 2): the four block linears from f32 ----------------
+    weights, biases, xs, ys = [], [], [], []
+    for name, n, k, qtype, epi, seed in LINEARS:
+        packed, bias = make_weights(o, n, k, qtype, seed + 4 * rank)
+        weights.append(samq.Weights(qtype, k, n, packed, device=local))
+        biases.append(torch.from_numpy(bias).cuda())
+        xs.append(torch.from_numpy(np.random.default_rng(1000 + seed + 17 * rank).normal(0, 1, (M, k))
+                                   .astype(np.float32)).cuda())
+        ys.append(torch.empty((M, n), dtype=torch.float32, device="cuda"))
+
+    def qgemm_step():
+        for i, (name, n, k, qtype, epi, _) in enumerate(LINEARS):
+            samq.linear(weights[i], xs[i], M, k, biases[i], epi, ys[i], n, stream)
+
+    for _ in range(args.warmup):
+        qgemm_step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    q0, q1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    q0.record(stream)
+    for _ in range(args.qgemm_steps):
+        qgemm_step()
+    q1.record(stream)
+    torch.cuda.synchronize()
+    qgemm_ms = max_over_ranks(q0.elapsed_time(q1))
+    qgemm_tops = step_ops() * args.qgemm_steps * world / (qgemm_ms / 1e3) / 1e12
+    samq.check(local, stream)
+
+    # GEMM-only launch durations (the dominant kernel) on the same stream.
+    gemm_ms = gemm_only_durations(samq, weights, xs, ys, biases, stream)
     pk = peaks()
     gemm_flops = [2.0 * M * n * k for _, n, k, *_ in LINEARS]
     achieved = sum(gemm_flops) / (sum(gemm_ms) / 1e3) / 1e12
@@ -365,34 +467,42 @@ def main():
                 "traffic": traffic.get("bytes_per_launch") if traffic else None,
                 "traffic_source": traffic.get("source") if traffic else None,
                 "per_linear_gemm_us": {LINEARS[i][0]: gemm_ms[i] * 1e3 for i in range(len(LINEARS))},
-                "per_linear_total_us": {LINEARS[i][0]: float(linear_ms[i]) * 1e3 for i in range(len(LINEARS))}}
+                "measured_on": "the 4 block-linear shapes at M=5184 (f32 epilogue), 50 back-to-back launches "
+                               "each between CUDA events on the launching stream"}
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        threads = o.default_threads()
-        packed = [make_weights(o, n, k, qtype, seed) for _, n, k, qtype, _, seed in LINEARS]
-        rate, rows, reps, secs = cpu_sample_rate(o, packed, threads, args.cpu_budget)
-        cpu = {"value": rate, "unit": "TOPS", "cores": threads, "kind": "port",
-               "sample": f"{reps} x {rows} of {M} token rows through the 4 linears ({secs:.1f} s); CPU "
-                         "restatement of GGML's CPU mul_mat (GGML itself unavailable), OpenMP"
-                         f"{' + AVX-512 VNNI' if o.has_vnni() else ''}"}
+        cb = CpuBackbone(o)
+        cb.step()
+        samples, t0 = [], time.perf_counter()
+        while not samples or (time.perf_counter() - t0 < args.cpu_budget and len(samples) < 200):
+            samples.append(cb.step())
+        cpu = {"value": 1.0 / float(np.mean(samples)), "unit": "images/s", "cores": cb.threads, "kind": "port",
+               "sample": f"{len(samples)} samples; " + cb.describe()}
 
     if rank == 0:
         line = {
-            "metric": METRIC, "value": value, "unit": "TOPS", "n_gpus": world, "steps": args.steps,
+            "metric": METRIC, "value": value, "unit": "images/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": elapsed_ms / args.steps, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "f16", "data": "synthetic",
-            "config": {"workload": WORKLOAD, "tokens": M, "linears": [l[0] for l in LINEARS],
-                       "shapes_nk": [[l[1], l[2]] for l in LINEARS], "formats": ["Q4_K", "Q4_K", "Q4_K", "Q8_0"],
-                       "epilogues": ["bias", "bias", "bias+gelu_erf", "bias"], "input": "f32 activations",
-                       "l2": "inputs exceed L2 (162 MB of X + 204 MB of Y per step)",
-                       "parallelism": f"images sharded, {world} replica(s)"},
+            "config": {"workload": WORKLOAD, "image": f"{IMAGE}x{IMAGE}x3", "patch": PATCH, "tokens": M,
+                       "width": E, "heads": HEADS, "mlp": MLP, "blocks": DEPTH, "window": WINDOW,
+                       "global_blocks": list(GLOBAL_BLOCKS),
+                       "formats": {"qkv/proj/fc1": "Q4_K", "fc2": "Q8_0", "norms/biases/embeddings": "f32"},
+                       "batch_per_gpu": 1, "parallelism": f"images sharded, {world} replica(s)",
+                       "l2": "weights 1.1 GB per replica and 91 MB of block scratch exceed L2",
+                       "tflop_per_image": {"linears": lin_ops / 1e12, "attention": attn_ops / 1e12}},
             "roofline": roofline,
             "cpu_baseline": cpu,
-            "e2e": {"value": e2e_value, "unit": "TOPS", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-                    "steps": e2e_steps},
-            "gpu_launches": args.steps * 2 * len(LINEARS),
+            "e2e": {"value": e2e_value, "unit": "images/s", "h2d_bytes_per_step": image_host.numel() * 4,
+                    "d2h_bytes_per_step": feats_host.numel() * 4, "steps": e2e_steps},
+            "gpu_launches": args.steps * (4 + DEPTH * 7),
             "clocks": clocks,
+            "achieved_tflops": (lin_ops + attn_ops) * value / world / 1e12,
+            "features_finite": feats_ok,
+            "qgemm": {"metric": QGEMM_METRIC, "workload": QGEMM_WORKLOAD, "value": qgemm_tops, "unit": "TOPS",
+                      "steps": args.qgemm_steps, "ms_per_step": qgemm_ms / args.qgemm_steps,
+                      "gpu_launches": args.qgemm_steps * 2 * len(LINEARS)},
         }
         print(json.dumps(line), flush=True)
     for w in weights:
@@ -427,9 +537,11 @@ def run_profile_case(args):
 
 
 def gemm_only_durations(samq, weights, xs, ys, biases, stream, reps=50):
-    """Average device time of each GEMM launch alone: the f16 A operand is
-    staged once (samq_stage_f16_v1), then samq_linear_f16_v1 launches only the
-    tcgen05 GEMM kernel, bracketed by events on the launching stream."""
+    """Average device time of each GEMM launch: the f16 A operand is staged
+    once (samq_stage_f16_v1), then samq_linear_f16_v1 launches only the
+    tcgen05 GEMM kernel, `reps` launches back to back between two events on
+    the launching stream (as the kernel runs inside a step, prologue
+    overlapped with the previous launch)."""
     import torch
     out = []
     for i, (name, n, k, qtype, epi, _) in enumerate(LINEARS):
@@ -438,15 +550,13 @@ def gemm_only_durations(samq, weights, xs, ys, biases, stream, reps=50):
         samq.stage_f16(xs[i], m, k, k, a16, stream)
         for _ in range(3):
             samq.linear_f16(weights[i], a16, m, k, biases[i], epi, ys[i], n, stream)
-        evs = []
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
         for _ in range(reps):
-            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            a.record(stream)
             samq.linear_f16(weights[i], a16, m, k, biases[i], epi, ys[i], n, stream)
-            b.record(stream)
-            evs.append((a, b))
+        b.record(stream)
         torch.cuda.synchronize()
-        out.append(float(np.mean([a.elapsed_time(b) for a, b in evs])))
+        out.append(a.elapsed_time(b) / reps)
     return out
 
 
