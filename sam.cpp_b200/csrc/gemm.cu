@@ -8,7 +8,7 @@
 //   f32 Y [m][ldy] (TMA store), optionally plus a residual (the ViT block's
 //     shortcut adds, vision.hpp:228,240);
 //   the Q8_1-staged f16 operand of the next linear (fc1 -> fc2), bit-identical
-//     to K1 run on the f32 values this epilogue would have stored;
+//     to K1 run on the f32 values the f32 mode stores;
 //   the qkv split into RoPE'd Q (x 1/8), K and V^T in the attention kernel's
 //     layout (vision.hpp:180-214).
 //
@@ -74,26 +74,36 @@ struct Layout {
     static constexpr uint32_t tmem_cols = 2 * kAccStride;       // double-buffered accumulator
 };
 
-// erf-GELU, 0.5 x (1 + erf(x / sqrt 2)), on the FMA pipe only: erf(z) for
-// z = |x|/sqrt(2) in [0, 4] is a degree-17 polynomial in u = (z - 2)/2 (a
-// Chebyshev least-squares fit, coefficients from csrc/fit_erf.py; max absolute
-// error 2.9e-7 in f32), and erf = 1 beyond z = 4 (true value 1 - 1.5e-8).
-// erff would keep the transcendental (XU) pipe saturated: on the fc1 shape it
-// was 84% busy and set the kernel's pace.
+// erf-GELU, 0.5 x (1 + erf(x / sqrt 2)), from Abramowitz & Stegun 7.1.26:
+// for z >= 0, erf(z) = 1 - t (a1 + t (a2 + t (a3 + t (a4 + t a5)))) e^(-z^2)
+// with t = 1 / (1 + p z), |error| <= 1.5e-7.  With q = (1 - erf(|x|/sqrt 2)) / 2,
+// GELU(x) = x (1 - q) for x >= 0 and x q for x < 0.  The reciprocal and the
+// exponential go to the MUFU pipe (rcp.approx, ex2.approx: relative errors
+// ~2^-22), the rest is 11 FMA-pipe operations: about half the issue cost of
+// a polynomial erf of the same accuracy, in the epilogue that bounds fc1.
+__device__ __forceinline__ float rcp_mufu(float x) {
+    float y;
+    asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+__device__ __forceinline__ float ex2_mufu(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
 __device__ __forceinline__ float gelu_erf(float x) {
-    constexpr float c[18] = {0.9953222870826721f,    0.04133397713303566f,  -0.16534042358398438f,
-                             0.38578349351882935f,   -0.5509889125823975f,  0.4188512861728668f,
-                             0.027940375730395317f,  -0.4324592351913452f,  0.4154498875141144f,
-                             -0.02610541321337223f,  -0.2951280176639557f,  0.21479764580726624f,
-                             0.0714806541800499f,    -0.1397237926721573f,  0.005857460666447878f,
-                             0.043319180607795715f,  -0.004593455232679844f, -0.0057971845380961895f};
-    const float z = fminf(fabsf(x) * 0.70710678118654752f, 4.0f);
-    const float u = fmaf(z, 0.5f, -1.0f);
-    float p = c[17];
-#pragma unroll
-    for (int i = 16; i >= 0; --i) p = fmaf(p, u, c[i]);
-    const float e = z >= 4.0f ? 1.0f : p;
-    return 0.5f * x * (1.0f + copysignf(e, x));
+    // a_i / 2 (the 1/2 of q folded in), p, 1/sqrt(2), -log2(e)/2.
+    constexpr float b1 = 0.127414796f, b2 = -0.142248368f, b3 = 0.7107068705f, b4 = -0.7265760135f,
+                    b5 = 0.5307027145f, p = 0.3275911f;
+    const float z = fabsf(x) * 0.70710678118654752f;
+    const float t = rcp_mufu(fmaf(p, z, 1.0f));
+    float poly = fmaf(b5, t, b4);
+    poly = fmaf(poly, t, b3);
+    poly = fmaf(poly, t, b2);
+    poly = fmaf(poly, t, b1);
+    poly *= t;
+    const float q = poly * ex2_mufu((x * x) * -0.72134752044448170f);
+    return x * (x >= 0.0f ? 1.0f - q : q);
 }
 
 // One epilogue warp's share of an accumulator tile: TMEM lanes 32*quarter..+31
@@ -119,6 +129,28 @@ __device__ __forceinline__ void drain_tile(uint32_t tmem_base, int quarter, int 
                              static_cast<uint32_t>(acc * kAccStride + chunk * 32),
                          r);
         const float bias_lane = (ep.bias != nullptr && col0 + lane < n) ? __ldg(ep.bias + col0 + lane) : 0.0f;
+        // qkv split: the RoPE table entries of this row's 16 channel pairs,
+        // fetched while the accumulator load is in flight (8-warp epilogues
+        // only: the 16-warp ones have no registers to spare for them).
+        constexpr bool kPrefetchRope = PARTS <= 2;
+        float4 fr[8];
+        int sec = 0, c0 = 0, nn = 0;
+        int64_t gh = 0;
+        if (ep.mode == kOutQkvPack) {
+            const int embed = ep.heads * 64;
+            const int rr = row < m ? row : 0;
+            const int g = rr / ep.group_n;
+            nn = rr - g * ep.group_n;
+            sec = col0 / embed;
+            const int rem = col0 - sec * embed;
+            gh = static_cast<int64_t>(g) * ep.heads + (rem >> 6);
+            c0 = rem & 63;
+            if (kPrefetchRope && sec < 2) {
+                const float4* src = reinterpret_cast<const float4*>(ep.freqs + (static_cast<int64_t>(nn) * 32 + c0 / 2) * 2);
+#pragma unroll
+                for (int p = 0; p < 8; ++p) fr[p] = __ldg(src + p);
+            }
+        }
         tc_wait_ld();
         float v[32];
 #pragma unroll
@@ -140,21 +172,20 @@ __device__ __forceinline__ void drain_tile(uint32_t tmem_base, int quarter, int 
         }
         if (ep.mode == kOutQkvPack) {
             if (row < m) {
-                const int g = row / ep.group_n, nn = row - g * ep.group_n;
-                const int embed = ep.heads * 64;
-                const int sec = col0 / embed, rem = col0 - sec * embed;
-                const int64_t gh = static_cast<int64_t>(g) * ep.heads + (rem >> 6);
-                const int c0 = rem & 63;
                 if (sec < 2) {
                     // RoPE on channel pairs (2i, 2i+1), i = c0/2 .. c0/2 + 15
                     // (vision.hpp:100-148); the 1/8 softmax scale folds into Q
                     // exactly (a power of two).
-                    const float4* fr = reinterpret_cast<const float4*>(ep.freqs + (static_cast<int64_t>(nn) * 32 + c0 / 2) * 2);
                     const float scale = sec == 0 ? 0.125f : 1.0f;
+                    if (!kPrefetchRope) {
+                        const float4* src = reinterpret_cast<const float4*>(ep.freqs + (static_cast<int64_t>(nn) * 32 + c0 / 2) * 2);
+#pragma unroll
+                        for (int p = 0; p < 8; ++p) fr[p] = __ldg(src + p);
+                    }
                     uint32_t out[16];
 #pragma unroll
                     for (int p = 0; p < 8; ++p) {
-                        const float4 f = __ldg(fr + p);  // (cos, sin) of pairs 2p and 2p+1
+                        const float4 f = fr[p];  // (cos, sin) of pairs 2p and 2p+1
                         const float x0 = v[4 * p], x1 = v[4 * p + 1], x2 = v[4 * p + 2], x3 = v[4 * p + 3];
                         const float re0 = __fsub_rn(__fmul_rn(x0, f.x), __fmul_rn(x1, f.y));
                         const float im0 = __fadd_rn(__fmul_rn(x0, f.y), __fmul_rn(x1, f.x));
@@ -431,9 +462,8 @@ void launch_gemm(const __half* a, int64_t lda, const __half* b, int64_t m, int64
         return;
     }
     const int bn = choose_bn(m, n, state.sm_count);
-    if (ep.gelu || ep.mode == kOutQkvPack)
-        // erf-GELU (or the RoPE / transpose of the qkv split) makes the
-        // epilogue the longer pipeline: 16 epilogue warps.
+    if (ep.gelu)
+        // erf-GELU makes the epilogue the longer pipeline: 16 epilogue warps.
         run_width<16>(bn, a, lda, b, m, n, k, ep, state, stream);
     else
         run_width<8>(bn, a, lda, b, m, n, k, ep, state, stream);
