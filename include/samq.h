@@ -218,7 +218,9 @@ samq_status samq_query_v1(const samq_weights* weights, struct samq_counters_v1* 
  * (cmake/patches/ggml-native-activation.patch:148-171). */
 samq_status samq_check_v1(int device, void* stream);
 
-/* Allocation-free variant of samq_linear_v1 (same arguments, same result).
+/* Allocation-free variant of samq_linear_v1 (same arguments; the same result
+ * for m > 64, and within the linear tolerance for m <= 64, where
+ * samq_linear_v1 streams the packed weights with split-K accumulation).
  * It has no counterpart in the reference.  It serves callers that cannot let a
  * library call cudaMalloc: a framework whose caching allocator already owns the
  * device memory (a library cudaMalloc would fail or fragment its pool), serving

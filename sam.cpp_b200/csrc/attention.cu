@@ -133,13 +133,8 @@ __global__ void __launch_bounds__(256) rope_pack_kernel(const float* __restrict_
 
 // ---------------------------------------------------------------- attention
 
-// 2^x on the MUFU pipe (PTX ex2.approx.ftz: relative error ~2^-22, far below
-// the f16 rounding of P; ex2(-inf) = +0, which masks keys for free).
-__device__ __forceinline__ float ex2_mufu(float x) {
-    float y;
-    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
-    return y;
-}
+// 2^x is ex2_mufu (samq_device.cuh): PTX ex2.approx.ftz, relative error ~2^-22,
+// far below the f16 rounding of P; ex2(-inf) = +0, which masks keys for free.
 
 // Rows keep a reference maximum m (log2 units) and only move it when a block's
 // maximum exceeds it by more than this, so P = 2^(s - m) <= 2^8 (exact in

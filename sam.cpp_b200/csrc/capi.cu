@@ -100,6 +100,16 @@ Scratch& scratch_for(DeviceState& state, cudaStream_t stream, size_t bytes) {
     return s;
 }
 
+uint32_t* tickets_for(DeviceState& state, cudaStream_t stream) {
+    std::lock_guard<std::mutex> lock(state.mutex);
+    uint32_t*& t = state.tickets[stream];
+    if (t == nullptr) {
+        check_cuda(cudaMalloc(&t, kTicketSlots * sizeof(uint32_t)), "cudaMalloc(tickets)");
+        check_cuda(cudaMemset(t, 0, kTicketSlots * sizeof(uint32_t)), "cudaMemset(tickets)");
+    }
+    return t;
+}
+
 void encode_tensor_map_2d(CUtensorMap* map, CUtensorMapDataType dtype, const void* base, uint64_t inner,
                           uint64_t outer, uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_outer,
                           CUtensorMapSwizzle swizzle) {
@@ -335,6 +345,23 @@ static void check_linear_args(const samq_weights* w, int64_t m, const float* bia
     (void)bias;
 }
 
+// K2 over an f16 operand: M <= kStreamMaxRows streams the packed weights
+// (stream.cu), larger M runs the f16 tensor-core GEMM on the expanded weights.
+size_t linear_scratch_bytes(const samq_weights* w, int64_t m, size_t operand_bytes, const DeviceState& state) {
+    const size_t head = (operand_bytes + 255) / 256 * 256;
+    return head + (stream_eligible(w, m) ? stream_partial_bytes(w, m, state.sm_count) : 0);
+}
+
+void run_linear(const samq_weights* w, const __half* a, int64_t lda, int64_t m, const float* bias, int epilogue,
+                float* y, int64_t ldy, void* scratch, size_t operand_bytes, DeviceState& state, cudaStream_t stream) {
+    if (stream_eligible(w, m)) {
+        float* partials = reinterpret_cast<float*>(static_cast<uint8_t*>(scratch) + (operand_bytes + 255) / 256 * 256);
+        launch_linear_stream(w, a, lda, m, bias, epilogue, y, ldy, partials, tickets_for(state, stream), state, stream);
+    } else {
+        launch_gemm_f16(a, lda, w->operand, m, w->n, w->k, bias, epilogue, y, ldy, state, stream);
+    }
+}
+
 samq_status samq_linear_v1(const samq_weights* w, const float* x, int64_t m, int64_t ldx, const float* bias,
                            int epilogue, float* y, int64_t ldy, void* stream_ptr) {
     return guarded([&] {
@@ -345,10 +372,10 @@ samq_status samq_linear_v1(const samq_weights* w, const float* x, int64_t m, int
         DeviceState& state = device_state(w->device);
         cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
         const size_t a_bytes = static_cast<size_t>(m * w->k) * sizeof(__half);
-        Scratch& scratch = scratch_for(state, stream, a_bytes);
+        Scratch& scratch = scratch_for(state, stream, linear_scratch_bytes(w, m, a_bytes, state));
         __half* a = static_cast<__half*>(scratch.ptr);
         launch_act_f16(x, m, w->k, ldx, a, nullptr, state.status, stream);
-        launch_gemm_f16(a, w->k, w->operand, m, w->n, w->k, bias, epilogue, y, ldy, state, stream);
+        run_linear(w, a, w->k, m, bias, epilogue, y, ldy, scratch.ptr, a_bytes, state, stream);
         const_cast<samq_weights*>(w)->launches.fetch_add(1);
         const_cast<samq_weights*>(w)->payload_bytes.store(a_bytes);
         const_cast<samq_weights*>(w)->allocation_bytes.store(scratch.bytes);
@@ -366,10 +393,10 @@ samq_status samq_linear_q8_1_v1(const samq_weights* w, const void* x_q8_1, int64
         DeviceState& state = device_state(w->device);
         cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
         const size_t a_bytes = static_cast<size_t>(m * w->k) * sizeof(__half);
-        Scratch& scratch = scratch_for(state, stream, a_bytes);
+        Scratch& scratch = scratch_for(state, stream, linear_scratch_bytes(w, m, a_bytes, state));
         __half* a = static_cast<__half*>(scratch.ptr);
         launch_q8_1_to_f16(static_cast<const uint8_t*>(x_q8_1), m, w->k, a, state.status, stream);
-        launch_gemm_f16(a, w->k, w->operand, m, w->n, w->k, bias, epilogue, y, ldy, state, stream);
+        run_linear(w, a, w->k, m, bias, epilogue, y, ldy, scratch.ptr, a_bytes, state, stream);
         const_cast<samq_weights*>(w)->launches.fetch_add(1);
         const_cast<samq_weights*>(w)->payload_bytes.store(static_cast<uint64_t>(m * (w->k / 32) * 36));
         const_cast<samq_weights*>(w)->allocation_bytes.store(scratch.bytes);
@@ -395,8 +422,11 @@ samq_status samq_linear_f16_v1(const samq_weights* w, const void* x_f16, int64_t
         require(ldx >= w->k && ldx % 8 == 0, "f16 row stride must be >= k and a multiple of 8");
         DeviceGuard guard(w->device);
         DeviceState& state = device_state(w->device);
-        launch_gemm_f16(static_cast<const __half*>(x_f16), ldx, w->operand, m, w->n, w->k, bias, epilogue, y, ldy,
-                        state, static_cast<cudaStream_t>(stream_ptr));
+        cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
+        void* scratch = nullptr;
+        if (stream_eligible(w, m) && stream_partial_bytes(w, m, state.sm_count) > 0)
+            scratch = scratch_for(state, stream, linear_scratch_bytes(w, m, 0, state)).ptr;
+        run_linear(w, static_cast<const __half*>(x_f16), ldx, m, bias, epilogue, y, ldy, scratch, 0, state, stream);
         const_cast<samq_weights*>(w)->launches.fetch_add(1);
     });
 }

@@ -74,38 +74,6 @@ struct Layout {
     static constexpr uint32_t tmem_cols = 2 * kAccStride;       // double-buffered accumulator
 };
 
-// erf-GELU, 0.5 x (1 + erf(x / sqrt 2)), from Abramowitz & Stegun 7.1.26:
-// for z >= 0, erf(z) = 1 - t (a1 + t (a2 + t (a3 + t (a4 + t a5)))) e^(-z^2)
-// with t = 1 / (1 + p z), |error| <= 1.5e-7.  With q = (1 - erf(|x|/sqrt 2)) / 2,
-// GELU(x) = x (1 - q) for x >= 0 and x q for x < 0.  The reciprocal and the
-// exponential go to the MUFU pipe (rcp.approx, ex2.approx: relative errors
-// ~2^-22), the rest is 11 FMA-pipe operations: about half the issue cost of
-// a polynomial erf of the same accuracy, in the epilogue that bounds fc1.
-__device__ __forceinline__ float rcp_mufu(float x) {
-    float y;
-    asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
-    return y;
-}
-__device__ __forceinline__ float ex2_mufu(float x) {
-    float y;
-    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
-    return y;
-}
-__device__ __forceinline__ float gelu_erf(float x) {
-    // a_i / 2 (the 1/2 of q folded in), p, 1/sqrt(2), -log2(e)/2.
-    constexpr float b1 = 0.127414796f, b2 = -0.142248368f, b3 = 0.7107068705f, b4 = -0.7265760135f,
-                    b5 = 0.5307027145f, p = 0.3275911f;
-    const float z = fabsf(x) * 0.70710678118654752f;
-    const float t = rcp_mufu(fmaf(p, z, 1.0f));
-    float poly = fmaf(b5, t, b4);
-    poly = fmaf(poly, t, b3);
-    poly = fmaf(poly, t, b2);
-    poly = fmaf(poly, t, b1);
-    poly *= t;
-    const float q = poly * ex2_mufu((x * x) * -0.72134752044448170f);
-    return x * (x >= 0.0f ? 1.0f - q : q);
-}
-
 // One epilogue warp's share of an accumulator tile: TMEM lanes 32*quarter..+31
 // (output rows row0..row0+31, one row per lane) and 32-column chunks
 // [part*C/PARTS, (part+1)*C/PARTS) of the C = BN/32 chunks of the tile starting

@@ -147,6 +147,38 @@ __device__ __forceinline__ void record_range(bool bad, DeviceStatus* status) {
     }
 }
 
+// erf-GELU, 0.5 x (1 + erf(x / sqrt 2)), from Abramowitz & Stegun 7.1.26:
+// for z >= 0, erf(z) = 1 - t (a1 + t (a2 + t (a3 + t (a4 + t a5)))) e^(-z^2)
+// with t = 1 / (1 + p z), |error| <= 1.5e-7.  With q = (1 - erf(|x|/sqrt 2)) / 2,
+// GELU(x) = x (1 - q) for x >= 0 and x q for x < 0.  The reciprocal and the
+// exponential go to the MUFU pipe (rcp.approx, ex2.approx: relative errors
+// ~2^-22), the rest is 11 FMA-pipe operations: about half the issue cost of
+// a polynomial erf of the same accuracy, in the epilogue that bounds fc1.
+__device__ __forceinline__ float rcp_mufu(float x) {
+    float y;
+    asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+__device__ __forceinline__ float ex2_mufu(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+__device__ __forceinline__ float gelu_erf(float x) {
+    // a_i / 2 (the 1/2 of q folded in), p, 1/sqrt(2), -log2(e)/2.
+    constexpr float b1 = 0.127414796f, b2 = -0.142248368f, b3 = 0.7107068705f, b4 = -0.7265760135f,
+                    b5 = 0.5307027145f, p = 0.3275911f;
+    const float z = fabsf(x) * 0.70710678118654752f;
+    const float t = rcp_mufu(fmaf(p, z, 1.0f));
+    float poly = fmaf(b5, t, b4);
+    poly = fmaf(poly, t, b3);
+    poly = fmaf(poly, t, b2);
+    poly = fmaf(poly, t, b1);
+    poly *= t;
+    const float q = poly * ex2_mufu((x * x) * -0.72134752044448170f);
+    return x * (x >= 0.0f ? 1.0f - q : q);
+}
+
 // ---- programmatic dependent launch ---------------------------------------
 // Kernels launched with cudaLaunchAttributeProgrammaticStreamSerialization may
 // start before the previous kernel on the stream has finished; each of them
@@ -167,6 +199,16 @@ __device__ __forceinline__ void tma_load_2d(void* smem_dst, const CUtensorMap* m
         "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];" ::
             "r"(smem_u32(smem_dst)),
         "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y)
+        : "memory");
+}
+
+// 1-D bulk copy global -> shared of `bytes` (multiple of 16, both addresses
+// 16-byte aligned), completing on `bar` (expect_tx must cover it).  No multicast.
+__device__ __forceinline__ void bulk_load_1d(void* smem_dst, const void* src, uint32_t bytes, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+            smem_u32(smem_dst)),
+        "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(smem_u32(bar))
         : "memory");
 }
 
