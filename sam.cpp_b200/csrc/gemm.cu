@@ -81,10 +81,11 @@ struct Layout {
 // coalesced load, broadcast by shuffles), erf-GELU, then per OutMode either
 // swizzled staging in shared memory and a TMA store (clipped by the tensor map
 // at the m / n edges), or direct stores of f16 rows.
-template <int BN, int PARTS>
+template <int BN, int PARTS, int MODE, bool GELU>
 __device__ __forceinline__ void drain_tile(uint32_t tmem_base, int quarter, int part, int acc, int row0,
                                            int col_base, int m, int n, const Epilogue& ep,
-                                           const CUtensorMap* tma_y, uint8_t* stage_buf, int& buf, int lane,
+                                           const CUtensorMap* tma_y, const CUtensorMap* tma_k,
+                                           const CUtensorMap* tma_v, uint8_t* stage_buf, int& buf, int lane,
                                            DeviceStatus* status) {
     constexpr int kChunks = BN / 32;
     const int row = row0 + lane;
@@ -104,7 +105,7 @@ __device__ __forceinline__ void drain_tile(uint32_t tmem_base, int quarter, int 
         float4 fr[8];
         int sec = 0, c0 = 0, nn = 0;
         int64_t gh = 0;
-        if (ep.mode == kOutQkvPack) {
+        if constexpr (MODE == kOutQkvPack) {
             const int embed = ep.heads * 64;
             const int rr = row < m ? row : 0;
             const int g = rr / ep.group_n;
@@ -124,54 +125,97 @@ __device__ __forceinline__ void drain_tile(uint32_t tmem_base, int quarter, int 
 #pragma unroll
         for (int i = 0; i < 32; ++i) {
             float x = __uint_as_float(r[i]) + __shfl_sync(0xffffffffu, bias_lane, i);
-            if (ep.gelu) x = gelu_erf(x);
+            if constexpr (GELU) x = gelu_erf(x);
             v[i] = x;
         }
-        if (ep.mode == kOutF16Staged) {
+        if constexpr (MODE == kOutF16Staged) {
             uint32_t out[16];
             const bool bad = stage_q8_1<1, 32>(v, out);
             record_range(bad && row < m, status);
-            if (row < m) {
-                uint4* dst = reinterpret_cast<uint4*>(ep.h + static_cast<int64_t>(row) * ep.ldh + col0);
+            // 32 rows x 64 bytes through shared memory in the 64-byte swizzle
+            // (16-byte unit u of row r at u ^ ((r >> 1) & 3)), one TMA store.
+            if (lane == 0) bulk_wait_group_read<kOutBuffers - 1>();
+            __syncwarp();
+            uint8_t* sbuf = stage_buf + buf * kOutChunkBytes;
 #pragma unroll
-                for (int j = 0; j < 4; ++j) dst[j] = make_uint4(out[4 * j], out[4 * j + 1], out[4 * j + 2], out[4 * j + 3]);
+            for (int j = 0; j < 4; ++j)
+                *reinterpret_cast<uint4*>(sbuf + lane * 64 + ((j ^ ((lane >> 1) & 3)) << 4)) =
+                    make_uint4(out[4 * j], out[4 * j + 1], out[4 * j + 2], out[4 * j + 3]);
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0 && row0 < m) {
+                tma_store_2d(tma_y, sbuf, col0, row0);
+                bulk_commit_group();
             }
+            buf = (buf + 1) % kOutBuffers;
             continue;
         }
-        if (ep.mode == kOutQkvPack) {
-            if (row < m) {
+        if constexpr (MODE == kOutQkvPack) {
+            // Whole 32-row blocks of one group (group_n % 32 == 0, the ViT's
+            // 576 and 5184): Q / K rows and the V^T tile leave through shared
+            // memory (64-byte swizzle) and one TMA store each.  Otherwise
+            // direct stores.
+            const bool tiled = (ep.group_n & 31) == 0;
+            uint32_t out[16];
+            if (sec < 2) {
+                // RoPE on channel pairs (2i, 2i+1), i = c0/2 .. c0/2 + 15
+                // (vision.hpp:100-148); the 1/8 softmax scale folds into Q
+                // exactly (a power of two).
+                const float scale = sec == 0 ? 0.125f : 1.0f;
+                if (!kPrefetchRope && row < m) {
+                    const float4* src = reinterpret_cast<const float4*>(ep.freqs + (static_cast<int64_t>(nn) * 32 + c0 / 2) * 2);
+#pragma unroll
+                    for (int p = 0; p < 8; ++p) fr[p] = __ldg(src + p);
+                }
+#pragma unroll
+                for (int p = 0; p < 8; ++p) {
+                    const float4 f = fr[p];  // (cos, sin) of pairs 2p and 2p+1
+                    const float x0 = v[4 * p], x1 = v[4 * p + 1], x2 = v[4 * p + 2], x3 = v[4 * p + 3];
+                    const float re0 = __fsub_rn(__fmul_rn(x0, f.x), __fmul_rn(x1, f.y));
+                    const float im0 = __fadd_rn(__fmul_rn(x0, f.y), __fmul_rn(x1, f.x));
+                    const float re1 = __fsub_rn(__fmul_rn(x2, f.z), __fmul_rn(x3, f.w));
+                    const float im1 = __fadd_rn(__fmul_rn(x2, f.w), __fmul_rn(x3, f.z));
+                    const __half2 h0 = __floats2half2_rn(re0 * scale, im0 * scale);
+                    const __half2 h1 = __floats2half2_rn(re1 * scale, im1 * scale);
+                    out[2 * p] = *reinterpret_cast<const uint32_t*>(&h0);
+                    out[2 * p + 1] = *reinterpret_cast<const uint32_t*>(&h1);
+                }
+            }
+            if (tiled) {
+                if (lane == 0) bulk_wait_group_read<kOutBuffers - 1>();
+                __syncwarp();
+                uint8_t* sbuf = stage_buf + buf * kOutChunkBytes;
                 if (sec < 2) {
-                    // RoPE on channel pairs (2i, 2i+1), i = c0/2 .. c0/2 + 15
-                    // (vision.hpp:100-148); the 1/8 softmax scale folds into Q
-                    // exactly (a power of two).
-                    const float scale = sec == 0 ? 0.125f : 1.0f;
-                    if (!kPrefetchRope) {
-                        const float4* src = reinterpret_cast<const float4*>(ep.freqs + (static_cast<int64_t>(nn) * 32 + c0 / 2) * 2);
 #pragma unroll
-                        for (int p = 0; p < 8; ++p) fr[p] = __ldg(src + p);
-                    }
-                    uint32_t out[16];
+                    for (int j = 0; j < 4; ++j)
+                        *reinterpret_cast<uint4*>(sbuf + lane * 64 + ((j ^ ((lane >> 1) & 3)) << 4)) =
+                            make_uint4(out[4 * j], out[4 * j + 1], out[4 * j + 2], out[4 * j + 3]);
+                } else {
+                    // V^T tile: channel rows i, token columns lane.
 #pragma unroll
-                    for (int p = 0; p < 8; ++p) {
-                        const float4 f = fr[p];  // (cos, sin) of pairs 2p and 2p+1
-                        const float x0 = v[4 * p], x1 = v[4 * p + 1], x2 = v[4 * p + 2], x3 = v[4 * p + 3];
-                        const float re0 = __fsub_rn(__fmul_rn(x0, f.x), __fmul_rn(x1, f.y));
-                        const float im0 = __fadd_rn(__fmul_rn(x0, f.y), __fmul_rn(x1, f.x));
-                        const float re1 = __fsub_rn(__fmul_rn(x2, f.z), __fmul_rn(x3, f.w));
-                        const float im1 = __fadd_rn(__fmul_rn(x2, f.w), __fmul_rn(x3, f.z));
-                        const __half2 h0 = __floats2half2_rn(re0 * scale, im0 * scale);
-                        const __half2 h1 = __floats2half2_rn(re1 * scale, im1 * scale);
-                        out[2 * p] = *reinterpret_cast<const uint32_t*>(&h0);
-                        out[2 * p + 1] = *reinterpret_cast<const uint32_t*>(&h1);
-                    }
+                    for (int i = 0; i < 32; ++i)
+                        *reinterpret_cast<__half*>(sbuf + i * 64 + (((lane >> 3) ^ ((i >> 1) & 3)) << 4) + (lane & 7) * 2) =
+                            __float2half_rn(v[i]);
+                }
+                fence_proxy_async_smem();
+                __syncwarp();
+                if (lane == 0 && row0 < m) {
+                    const int nn0 = nn - lane;  // lane 0: nn of row0
+                    if (sec < 2)
+                        tma_store_2d(sec == 0 ? tma_y : tma_k, sbuf, c0, static_cast<int32_t>(gh * ep.group_n + nn0));
+                    else
+                        tma_store_2d(tma_v, sbuf, nn0, static_cast<int32_t>(gh * 64 + c0));
+                    bulk_commit_group();
+                }
+                buf = (buf + 1) % kOutBuffers;
+            } else if (row < m) {
+                if (sec < 2) {
                     __half* base = sec == 0 ? ep.q : ep.k;
                     uint4* dst = reinterpret_cast<uint4*>(base + (gh * ep.group_n + nn) * 64 + c0);
 #pragma unroll
                     for (int j = 0; j < 4; ++j)
                         dst[j] = make_uint4(out[4 * j], out[4 * j + 1], out[4 * j + 2], out[4 * j + 3]);
                 } else {
-                    // V^T: lanes are consecutive rows n, so each channel's
-                    // stores from the warp are contiguous.
                     __half* base = ep.vt + (gh * 64 + c0) * ep.group_n + nn;
 #pragma unroll
                     for (int i = 0; i < 32; ++i) base[static_cast<int64_t>(i) * ep.group_n] = __float2half_rn(v[i]);
@@ -179,7 +223,7 @@ __device__ __forceinline__ void drain_tile(uint32_t tmem_base, int quarter, int 
             }
             continue;
         }
-        if (ep.mode == kOutF32Residual && row < m) {
+        if (MODE == kOutF32Residual && row < m) {
             // The ViT shortcut add: residual + (acc + bias), one f32 add.
             const float4* res = reinterpret_cast<const float4*>(ep.residual + static_cast<int64_t>(row) * ep.ldr + col0);
 #pragma unroll
@@ -211,10 +255,11 @@ __device__ __forceinline__ void drain_tile(uint32_t tmem_base, int quarter, int 
     }
 }
 
-template <int BN, int STAGES, int EW>
+template <int BN, int STAGES, int EW, int MODE, bool GELU>
 __global__ void __launch_bounds__(threads_for(EW), 1)
 gemm_f16_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_b,
-                const __grid_constant__ CUtensorMap tma_y, const Epilogue ep, int m, int n, int k,
+                const __grid_constant__ CUtensorMap tma_y, const __grid_constant__ CUtensorMap tma_k,
+                const __grid_constant__ CUtensorMap tma_v, const Epilogue ep, int m, int n, int k,
                 DeviceStatus* status) {
     using L = Layout<BN, STAGES, EW>;
     static_assert(L::total <= 232448, "shared memory budget");
@@ -249,6 +294,8 @@ gemm_f16_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant
         tma_prefetch_desc(&tma_a);
         tma_prefetch_desc(&tma_b);
         tma_prefetch_desc(&tma_y);
+        tma_prefetch_desc(&tma_k);
+        tma_prefetch_desc(&tma_v);
     }
     if (warp == 1) tmem_alloc(tmem_slot, L::tmem_cols);
     tc_fence_before();
@@ -342,8 +389,8 @@ gemm_f16_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant
             if (!__all_sync(0xffffffffu, mbar_wait(&tfull[acc], acc_ph, status, 4))) break;
             tc_fence_after();
             const int row0 = mt * BM + quarter * 32;
-            drain_tile<BN, EW / 4>(tmem_base, quarter, part, acc, row0, nt * BN, m, n, ep, &tma_y, stage_buf, buf,
-                                   lane, status);
+            drain_tile<BN, EW / 4, MODE, GELU>(tmem_base, quarter, part, acc, row0, nt * BN, m, n, ep, &tma_y, &tma_k, &tma_v,
+                                   stage_buf, buf, lane, status);
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&tempty[acc]);
@@ -363,11 +410,11 @@ gemm_f16_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant
     }
 }
 
-template <int BN, int STAGES, int EW>
+template <int BN, int STAGES, int EW, int MODE, bool GELU>
 void run(const __half* a, int64_t lda, const __half* b, int64_t m, int64_t n, int64_t k, const Epilogue& ep,
          DeviceState& state, cudaStream_t stream) {
     using L = Layout<BN, STAGES, EW>;
-    CUtensorMap ta, tb, ty;
+    CUtensorMap ta, tb, ty, tk, tv;
     encode_tensor_map_2d(&ta, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, a, k, m, lda * 2, BK, BM,
                          CU_TENSOR_MAP_SWIZZLE_128B);
     encode_tensor_map_2d(&tb, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, b, k, n, k * 2, BK, BN,
@@ -375,10 +422,26 @@ void run(const __half* a, int64_t lda, const __half* b, int64_t m, int64_t n, in
     if (ep.mode == kOutF32 || ep.mode == kOutF32Residual)
         encode_tensor_map_2d(&ty, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, ep.y, n, m, ep.ldy * 4, 32, 32,
                              CU_TENSOR_MAP_SWIZZLE_128B);
-    else  // unused by the f16 modes: a valid map over A keeps the descriptor prefetch harmless
-        encode_tensor_map_2d(&ty, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, a, k / 2, m, lda * 2, 32, 32,
-                             CU_TENSOR_MAP_SWIZZLE_128B);
-    auto kernel = gemm_f16_kernel<BN, STAGES, EW>;
+    else if (ep.mode == kOutF16Staged)
+        encode_tensor_map_2d(&ty, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, ep.h, n, m, ep.ldh * 2, 32, 32,
+                             CU_TENSOR_MAP_SWIZZLE_64B);
+    // Maps a mode does not use cover A (valid, never stored to).
+    encode_tensor_map_2d(&tk, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, a, k, m, lda * 2, 32, 32, CU_TENSOR_MAP_SWIZZLE_64B);
+    tv = tk;
+    if (ep.mode == kOutQkvPack) {
+        // Q and K [group * heads + head][group_n][64], V^T [group * heads + head][64][group_n].
+        const uint64_t rows = static_cast<uint64_t>(m / ep.group_n) * ep.heads * ep.group_n;
+        encode_tensor_map_2d(&ty, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, ep.q, 64, rows, 128, 32, 32,
+                             CU_TENSOR_MAP_SWIZZLE_64B);
+        encode_tensor_map_2d(&tk, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, ep.k, 64, rows, 128, 32, 32,
+                             CU_TENSOR_MAP_SWIZZLE_64B);
+        encode_tensor_map_2d(&tv, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, ep.vt, ep.group_n,
+                             static_cast<uint64_t>(m / ep.group_n) * ep.heads * 64,
+                             static_cast<uint64_t>(ep.group_n) * 2, 32, 32, CU_TENSOR_MAP_SWIZZLE_64B);
+    } else if (ep.mode != kOutF32 && ep.mode != kOutF32Residual && ep.mode != kOutF16Staged) {
+        ty = tk;
+    }
+    auto kernel = gemm_f16_kernel<BN, STAGES, EW, MODE, GELU>;
     static bool configured[64] = {};
     if (!configured[state.device & 63]) {
         check_cuda(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, L::total),
@@ -387,8 +450,8 @@ void run(const __half* a, int64_t lda, const __half* b, int64_t m, int64_t n, in
     }
     const int64_t tiles = ((m + BM - 1) / BM) * ((n + BN - 1) / BN);
     const int grid = static_cast<int>(tiles < state.sm_count ? tiles : state.sm_count);
-    launch_pdl(kernel, dim3(grid), dim3(threads_for(EW)), L::total, stream, "gemm_f16_kernel launch", ta, tb, ty, ep,
-               static_cast<int>(m), static_cast<int>(n), static_cast<int>(k), state.status);
+    launch_pdl(kernel, dim3(grid), dim3(threads_for(EW)), L::total, stream, "gemm_f16_kernel launch", ta, tb, ty, tk, tv,
+               ep, static_cast<int>(m), static_cast<int>(n), static_cast<int>(k), state.status);
 }
 
 }  // namespace
@@ -411,30 +474,47 @@ int choose_bn(int64_t m, int64_t n, int sms) {
     return best;
 }
 
-template <int EW>
+template <int EW, int MODE, bool GELU>
 void run_width(int bn, const __half* a, int64_t lda, const __half* b, int64_t m, int64_t n, int64_t k,
                const Epilogue& ep, DeviceState& state, cudaStream_t stream) {
+    if (n <= 128) {
+        run<128, 6, 8, MODE, GELU>(a, lda, b, m, n, k, ep, state, stream);
+        return;
+    }
     switch (bn) {
-        case 160: run<160, stages_for(160, EW), EW>(a, lda, b, m, n, k, ep, state, stream); break;
-        case 192: run<192, stages_for(192, EW), EW>(a, lda, b, m, n, k, ep, state, stream); break;
-        case 224: run<224, stages_for(224, EW), EW>(a, lda, b, m, n, k, ep, state, stream); break;
-        default: run<256, stages_for(256, EW), EW>(a, lda, b, m, n, k, ep, state, stream); break;
+        case 160: run<160, stages_for(160, EW), EW, MODE, GELU>(a, lda, b, m, n, k, ep, state, stream); break;
+        case 192: run<192, stages_for(192, EW), EW, MODE, GELU>(a, lda, b, m, n, k, ep, state, stream); break;
+        case 224: run<224, stages_for(224, EW), EW, MODE, GELU>(a, lda, b, m, n, k, ep, state, stream); break;
+        default: run<256, stages_for(256, EW), EW, MODE, GELU>(a, lda, b, m, n, k, ep, state, stream); break;
     }
 }
 
+// One kernel instantiation per output mode (and erf-GELU), so each carries
+// only its own epilogue's registers.  erf-GELU makes the epilogue the longer
+// pipeline: 16 epilogue warps there, 8 otherwise.
 void launch_gemm(const __half* a, int64_t lda, const __half* b, int64_t m, int64_t n, int64_t k, const Epilogue& ep,
                  DeviceState& state, cudaStream_t stream) {
     if (m == 0) return;
-    if (n <= 128) {
-        run<128, 6, 8>(a, lda, b, m, n, k, ep, state, stream);
-        return;
-    }
     const int bn = choose_bn(m, n, state.sm_count);
-    if (ep.gelu)
-        // erf-GELU makes the epilogue the longer pipeline: 16 epilogue warps.
-        run_width<16>(bn, a, lda, b, m, n, k, ep, state, stream);
-    else
-        run_width<8>(bn, a, lda, b, m, n, k, ep, state, stream);
+    switch (ep.mode) {
+        case kOutF32:
+            if (ep.gelu) run_width<16, kOutF32, true>(bn, a, lda, b, m, n, k, ep, state, stream);
+            else run_width<8, kOutF32, false>(bn, a, lda, b, m, n, k, ep, state, stream);
+            break;
+        case kOutF32Residual:
+            if (ep.gelu) fail(SAMQ_ERR_INVALID_ARGUMENT, "residual epilogue takes no GELU");
+            run_width<8, kOutF32Residual, false>(bn, a, lda, b, m, n, k, ep, state, stream);
+            break;
+        case kOutF16Staged:
+            if (ep.gelu) run_width<16, kOutF16Staged, true>(bn, a, lda, b, m, n, k, ep, state, stream);
+            else run_width<8, kOutF16Staged, false>(bn, a, lda, b, m, n, k, ep, state, stream);
+            break;
+        case kOutQkvPack:
+            if (ep.gelu) fail(SAMQ_ERR_INVALID_ARGUMENT, "qkv split takes no GELU");
+            run_width<8, kOutQkvPack, false>(bn, a, lda, b, m, n, k, ep, state, stream);
+            break;
+        default: fail(SAMQ_ERR_INVALID_ARGUMENT, "unknown GEMM output mode");
+    }
 }
 
 void launch_gemm_f16(const __half* a, int64_t lda, const __half* b, int64_t m, int64_t n, int64_t k,
