@@ -330,9 +330,11 @@ def main():
     ap.add_argument("--qgemm-steps", type=int, default=500)
     ap.add_argument("--cpu-budget", type=float, default=12.0, help="seconds of CPU baseline work")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--profile", choices=[l[0] for l in LINEARS],
-                    help="only stage one linear's A operand and launch its GEMM --steps times "
-                         "(small, single-kernel case for ncu captures)")
+    ap.add_argument("--profile", choices=[l[0] for l in LINEARS] + list(PROFILE_EXTRA),
+                    help="one kernel's case launched --warmup + --steps times, for ncu captures: a block "
+                         "linear's GEMM (A operand staged once), attention_window / attention_global "
+                         "(samq_vit_attention_v1 at 72x72, 16 heads), or text_fc2 (small-M Q8_0 "
+                         "4096 -> 1024 at M = 32, the packet-streaming kernel)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     world, rank, local = dist_setup()
@@ -512,14 +514,44 @@ def main():
         dist.destroy_process_group()
 
 
+PROFILE_EXTRA = ("attention_window", "attention_global", "text_fc2")
+
+
 def run_profile_case(args):
-    """One linear's GEMM launched alone, for ncu (-k regex:gemm)."""
+    """One kernel's case launched alone, for ncu (-k regex:<kernel>)."""
     import torch
     import samq
     from oracle import oracle as o
     torch.cuda.set_device(0)
     samq.init(0)
     stream = torch.cuda.current_stream()
+    launches = args.warmup + args.steps
+    if args.profile.startswith("attention"):
+        window = WINDOW if args.profile == "attention_window" else 0
+        rng = np.random.default_rng(3)
+        qkv = torch.from_numpy(rng.normal(0, 1, (M, 3 * E)).astype(np.float32)).cuda()
+        freqs = torch.from_numpy(o.rope_freqs(WINDOW * WINDOW if window else M)).cuda()
+        out = torch.empty((M, E), dtype=torch.float32, device="cuda")
+        for _ in range(launches):
+            samq.vit_attention(qkv, 3 * E, GRID, GRID, HEADS, window, freqs, out, E, stream)
+    elif args.profile == "text_fc2":
+        n, k, m = 1024, 4096, 32
+        packed, bias = make_weights(o, n, k, 8, 5)
+        w = samq.Weights(8, k, n, packed)
+        x = torch.from_numpy(np.random.default_rng(5).normal(0, 1, (m, k)).astype(np.float32)).cuda()
+        a16 = torch.empty((m, k), dtype=torch.float16, device="cuda")
+        y = torch.empty((m, n), dtype=torch.float32, device="cuda")
+        b = torch.from_numpy(bias).cuda()
+        samq.stage_f16(x, m, k, k, a16, stream)
+        for _ in range(launches):
+            samq.linear_f16(w, a16, m, k, b, 0, y, n, stream)
+        torch.cuda.synchronize()
+        w.close()
+    if args.profile in PROFILE_EXTRA:
+        torch.cuda.synchronize()
+        samq.check(0, stream)
+        print(json.dumps({"profile_case": args.profile, "launches": launches}))
+        return
     name, n, k, qtype, epi, seed = next(l for l in LINEARS if l[0] == args.profile)
     packed, bias = make_weights(o, n, k, qtype, seed)
     w = samq.Weights(qtype, k, n, packed)

@@ -100,16 +100,6 @@ Scratch& scratch_for(DeviceState& state, cudaStream_t stream, size_t bytes) {
     return s;
 }
 
-uint32_t* tickets_for(DeviceState& state, cudaStream_t stream) {
-    std::lock_guard<std::mutex> lock(state.mutex);
-    uint32_t*& t = state.tickets[stream];
-    if (t == nullptr) {
-        check_cuda(cudaMalloc(&t, kTicketSlots * sizeof(uint32_t)), "cudaMalloc(tickets)");
-        check_cuda(cudaMemset(t, 0, kTicketSlots * sizeof(uint32_t)), "cudaMemset(tickets)");
-    }
-    return t;
-}
-
 void encode_tensor_map_2d(CUtensorMap* map, CUtensorMapDataType dtype, const void* base, uint64_t inner,
                           uint64_t outer, uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_outer,
                           CUtensorMapSwizzle swizzle) {
@@ -356,7 +346,7 @@ void run_linear(const samq_weights* w, const __half* a, int64_t lda, int64_t m, 
                 float* y, int64_t ldy, void* scratch, size_t operand_bytes, DeviceState& state, cudaStream_t stream) {
     if (stream_eligible(w, m)) {
         float* partials = reinterpret_cast<float*>(static_cast<uint8_t*>(scratch) + (operand_bytes + 255) / 256 * 256);
-        launch_linear_stream(w, a, lda, m, bias, epilogue, y, ldy, partials, tickets_for(state, stream), state, stream);
+        launch_linear_stream(w, a, lda, m, bias, epilogue, y, ldy, partials, state, stream);
     } else {
         launch_gemm_f16(a, lda, w->operand, m, w->n, w->k, bias, epilogue, y, ldy, state, stream);
     }

@@ -41,17 +41,13 @@ struct DeviceState {
     DeviceStatus* status = nullptr;  // device memory
     std::mutex mutex;
     std::unordered_map<cudaStream_t, Scratch> scratch;
-    std::unordered_map<cudaStream_t, uint32_t*> tickets;  // split-K tickets, zero between launches
 };
 
 // Checks the device once and returns its state (throws Error otherwise).
 DeviceState& device_state(int device);
 // Scratch of at least `bytes` bytes for work ordered on `stream`.
 Scratch& scratch_for(DeviceState& state, cudaStream_t stream, size_t bytes);
-// kTicketSlots zeroed counters for work ordered on `stream`; each user leaves
-// the counters it used at zero.
-constexpr int kTicketSlots = 16384;
-uint32_t* tickets_for(DeviceState& state, cudaStream_t stream);
+
 
 // RAII device switch.
 struct DeviceGuard {
@@ -180,8 +176,8 @@ bool stream_eligible(const samq_weights* w, int64_t m);
 // Bytes of f32 split-K partial sums the streaming path needs (0 when unsplit).
 size_t stream_partial_bytes(const samq_weights* w, int64_t m, int sms);
 void launch_linear_stream(const samq_weights* w, const __half* x16, int64_t ldx, int64_t m, const float* bias,
-                          int epilogue, float* y, int64_t ldy, float* partials, uint32_t* tickets,
-                          DeviceState& state, cudaStream_t stream);
+                          int epilogue, float* y, int64_t ldy, float* partials, DeviceState& state,
+                          cudaStream_t stream);
 
 // vit.cu: the ViT block / backbone prefix around K2 and K3.
 struct VitBlockArgs {

@@ -10,6 +10,9 @@
 //                            bias add and optional ggml_gelu_erf (src/models/sam3/vision.hpp:234-238).
 //   ActivationCounters    <- CudaActivationPolicy::record (src/runtime/ggml/backends/cuda_activation.hpp:62-77):
 //                            one launch per request, payload and allocation peaks.
+//   VitBackbone           <- sam3_build_vit_graph (src/models/sam3/vision.hpp:252-293) as
+//                            encode_image runs it (src/models/sam3/execution.hpp:55-124): the
+//                            prefix, then every block on the device path, in place on x.
 // Header-only; link with libsamq.so.
 #pragma once
 
@@ -21,6 +24,7 @@
 #include <stdexcept>
 #include <string>
 #include <utility>
+#include <vector>
 
 #include "samq.h"
 
@@ -109,6 +113,86 @@ public:
 private:
     samq_weights* weights_ = nullptr;
     std::int64_t k_ = 0, n_ = 0;
+};
+
+// Device pointers to one ViT block's F32 tensors (src/models/sam3/tensors.hpp:108-126).
+struct VitBlockTensors {
+    const float* norm1_w = nullptr;
+    const float* norm1_b = nullptr;
+    const float* qkv_b = nullptr;
+    const float* proj_b = nullptr;
+    const float* norm2_w = nullptr;
+    const float* norm2_b = nullptr;
+    const float* fc1_b = nullptr;
+    const float* fc2_b = nullptr;
+    const float* freqs_cis = nullptr;  // [positions][32][2]
+    int window = 0;                    // 24 windowed, 0 global (hparams.is_global_attn)
+};
+
+// Device pointers to the prefix tensors (tensors.hpp:97-106).
+struct VitPrefixTensors {
+    const float* patch_embed_w = nullptr;  // [E][3][patch][patch]
+    const float* pos_embed = nullptr;      // [pos_grid][pos_grid][E]
+    const float* ln_pre_w = nullptr;
+    const float* ln_pre_b = nullptr;
+    int patch = 14;
+    int pos_grid = 24;
+};
+
+class VitBackbone {
+public:
+    VitBackbone(const SamqDriver& driver, std::int64_t embed) : driver_(driver), embed_(embed) {}
+
+    void set_prefix(const VitPrefixTensors& prefix) { prefix_ = prefix; }
+
+    // Appends a block; the backbone owns its four linears (qkv E->3E, proj
+    // E->E, fc1 E->MLP with GELU, fc2 MLP->E).
+    void add_block(QuantizedLinear qkv, QuantizedLinear proj, QuantizedLinear fc1, QuantizedLinear fc2,
+                   const VitBlockTensors& t) {
+        samq_vit_block_v1 b{};
+        b.version = 1;
+        b.window = t.window;
+        b.norm1_w = t.norm1_w;
+        b.norm1_b = t.norm1_b;
+        b.qkv = qkv.handle();
+        b.qkv_b = t.qkv_b;
+        b.proj = proj.handle();
+        b.proj_b = t.proj_b;
+        b.norm2_w = t.norm2_w;
+        b.norm2_b = t.norm2_b;
+        b.fc1 = fc1.handle();
+        b.fc1_b = t.fc1_b;
+        b.fc2 = fc2.handle();
+        b.fc2_b = t.fc2_b;
+        b.freqs_cis = t.freqs_cis;
+        blocks_.push_back(b);
+        linears_.push_back(std::move(qkv));
+        linears_.push_back(std::move(proj));
+        linears_.push_back(std::move(fc1));
+        linears_.push_back(std::move(fc2));
+    }
+
+    std::size_t depth() const { return blocks_.size(); }
+
+    // image: device [3][height][width] f32, normalized; x: device [tokens][E] f32 (receives the
+    // backbone output, the [E, W, H, 1] tensor the neck consumes).
+    void encode(const float* image, int width, int height, float* x, cudaStream_t stream) const {
+        if (prefix_.patch_embed_w == nullptr) throw std::runtime_error("ViT prefix tensors were not set");
+        samq_require(samq_vit_prefix_v1(image, width, height, prefix_.patch, prefix_.patch_embed_w, embed_,
+                                        prefix_.pos_embed, prefix_.pos_grid, prefix_.ln_pre_w, prefix_.ln_pre_b, x,
+                                        stream),
+                     "samq ViT prefix failed");
+        const int grid_w = width / prefix_.patch, grid_h = height / prefix_.patch;
+        for (const samq_vit_block_v1& b : blocks_)
+            samq_require(samq_vit_block_forward_v1(&b, x, grid_w, grid_h, stream), "samq ViT block failed");
+    }
+
+private:
+    SamqDriver driver_;
+    std::int64_t embed_ = 0;
+    VitPrefixTensors prefix_{};
+    std::vector<QuantizedLinear> linears_;
+    std::vector<samq_vit_block_v1> blocks_;
 };
 
 // Post-compute device findings (range / timeout), as the reference's RHS check raises them.

@@ -48,3 +48,57 @@ def test_cpp_host_layer_on_gpu(tmp_path, oracle, qtype, epilogue):
     compile_test(exe)
     run = subprocess.run([str(exe), str(tmp_path)], capture_output=True, text=True, timeout=120)
     assert run.returncode == 0, run.stdout + run.stderr
+
+
+def compile_program(name, out):
+    cmd = [CXX, "-std=c++17", "-O2", "-Wall", "-Wextra", f"-I{ROOT / 'include'}", f"-I{PACKAGE / 'host'}",
+           f"-I{CUDA}/include", str(ROOT / "tests" / "cpp" / name), "-o", str(out),
+           f"-L{PACKAGE}", "-lsamq", f"-L{CUDA}/lib64", "-lcudart", f"-Wl,-rpath,{PACKAGE}",
+           f"-Wl,-rpath,{CUDA}/lib64"]
+    subprocess.run(cmd, check=True)
+
+
+def test_vit_backbone_host_program_compiles(tmp_path):
+    compile_program("test_vit_backbone.cpp", tmp_path / "test_vit_backbone")
+
+
+@pytest.mark.gpu
+def test_cpp_vit_backbone_on_gpu(tmp_path, oracle):
+    """VitBackbone::encode (prefix + one windowed block) from C++ against the
+    f64 oracle; same bar as the block test on the block's contribution."""
+    rng = np.random.default_rng(11)
+    size, patch, pos_grid, E, MLP, window = 336, 14, 8, 1024, 4736, 24
+    files = {}
+    files["image"] = ((rng.random((3, size, size)) - 0.5) / 0.5).astype(np.float32)
+    files["patch_w"] = rng.normal(0, 0.02, (E, 3, patch, patch)).astype(np.float32)
+    files["pos"] = rng.normal(0, 0.02, (pos_grid, pos_grid, E)).astype(np.float32)
+    files["ln_w"] = (1 + rng.normal(0, 0.02, E)).astype(np.float32)
+    files["ln_b"] = rng.normal(0, 0.02, E).astype(np.float32)
+    blk = {"window": window}
+    for name, n, k, t in (("qkv", 3 * E, E, 12), ("proj", E, E, 12), ("fc1", MLP, E, 12), ("fc2", E, MLP, 8)):
+        w = rng.normal(0, 0.02, (n, k)).astype(np.float32)
+        rows = oracle.quantize(t, w)
+        files[name] = rows
+        blk[name + "_w16"] = oracle.weight_f16(t, k, n, rows)
+        blk[name + "_b"] = files[name + "_b"] = rng.normal(0, 0.02, n).astype(np.float32)
+    for name in ("norm1", "norm2"):
+        blk[name + "_w"] = files[name + "_w"] = (1 + rng.normal(0, 0.02, E)).astype(np.float32)
+        blk[name + "_b"] = files[name + "_b"] = rng.normal(0, 0.02, E).astype(np.float32)
+    blk["freqs"] = files["freqs"] = oracle.rope_freqs(window * window, seed=3)
+    for name, arr in files.items():
+        np.ascontiguousarray(arr).tofile(tmp_path / f"{name}.bin")
+    (tmp_path / "meta.txt").write_text(f"{size} {patch} {pos_grid} {E} {MLP} {window} 12 8\n")
+    exe = tmp_path / "test_vit_backbone"
+    compile_program("test_vit_backbone.cpp", exe)
+    run = subprocess.run([str(exe), str(tmp_path)], capture_output=True, text=True, timeout=180)
+    assert run.returncode == 0, run.stdout + run.stderr
+    grid = size // patch
+    out = np.fromfile(tmp_path / "out.bin", dtype=np.float32).reshape(grid * grid, E)
+    x0 = oracle.vit_prefix(files["image"], patch, files["patch_w"], files["pos"], files["ln_w"], files["ln_b"])
+    ref = oracle.vit_block(x0, blk, grid, grid)
+    d_gpu = (out - x0).astype(np.float64).ravel()
+    d_ref = (ref - x0).astype(np.float64).ravel()
+    cos = float(d_gpu @ d_ref / (np.linalg.norm(d_gpu) * np.linalg.norm(d_ref)))
+    rel = float(np.abs(d_gpu - d_ref).max() / np.abs(d_ref).max())
+    # Prefix error (f16 convolution operands) and block error add up here.
+    assert cos >= 0.9995 and rel <= 3e-2, (cos, rel)
