@@ -94,13 +94,43 @@ __global__ void __launch_bounds__(256) ln_stage_kernel(const float* __restrict__
         v[i][0] = t.x; v[i][1] = t.y; v[i][2] = t.z; v[i][3] = t.w;
     }
     layer_norm_row<NV>(v, w, b, lane);
-    uint2* dst = reinterpret_cast<uint2*>(a + r * E);
+    // Q8_1 operand (the stage_q8_1 rule).  Block q = 4i + lane/8 of the row is
+    // spread over 8 lanes; its two IEEE divisions are done once, by lane q,
+    // and the scale / inverse go back by shuffles (2 divisions per lane per
+    // row instead of 16, the larger part of this kernel's instructions).
+    float amax[NV];
     bool bad = false;
 #pragma unroll
     for (int i = 0; i < NV; ++i) {
-        uint32_t out[2];
-        bad |= stage_q8_1<8, 4>(v[i], out);
-        dst[i * 32 + lane] = make_uint2(out[0], out[1]);
+        float a4 = 0.0f;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            a4 = fmaxf(a4, fabsf(v[i][j]));
+            bad |= !(fabsf(v[i][j]) <= kOperandLimit);
+        }
+#pragma unroll
+        for (int o = 1; o < 8; o <<= 1) a4 = fmaxf(a4, __shfl_xor_sync(0xffffffffu, a4, o));
+        amax[i] = a4;
+    }
+    float my_amax = 0.0f;  // block q = lane: i = q / 4, held by lanes 8 * (q % 4) ..
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+        const float t = __shfl_sync(0xffffffffu, amax[i], (lane & 3) * 8);
+        if ((lane >> 2) == i) my_amax = t;
+    }
+    const float my_dq = __half2float(__float2half_rn(__fdiv_rn(my_amax, 127.0f)));
+    const float my_inv = my_amax == 0.0f ? 0.0f : __fdiv_rn(127.0f, my_amax);
+    uint2* dst = reinterpret_cast<uint2*>(a + r * E);
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+        const int q = 4 * i + (lane >> 3);
+        const float dq = __shfl_sync(0xffffffffu, my_dq, q);
+        const float inv = __shfl_sync(0xffffffffu, my_inv, q);
+        const float q0 = round_half_away(__fmul_rn(v[i][0], inv)), q1 = round_half_away(__fmul_rn(v[i][1], inv));
+        const float q2 = round_half_away(__fmul_rn(v[i][2], inv)), q3 = round_half_away(__fmul_rn(v[i][3], inv));
+        const __half2 h0 = __floats2half2_rn(__fmul_rn(dq, q0), __fmul_rn(dq, q1));
+        const __half2 h1 = __floats2half2_rn(__fmul_rn(dq, q2), __fmul_rn(dq, q3));
+        dst[i * 32 + lane] = make_uint2(*reinterpret_cast<const uint32_t*>(&h0), *reinterpret_cast<const uint32_t*>(&h1));
     }
     record_range(bad, status);
 }
