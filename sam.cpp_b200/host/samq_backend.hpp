@@ -10,6 +10,8 @@
 //                            bias add and optional ggml_gelu_erf (src/models/sam3/vision.hpp:234-238).
 //   ActivationCounters    <- CudaActivationPolicy::record (src/runtime/ggml/backends/cuda_activation.hpp:62-77):
 //                            one launch per request, payload and allocation peaks.
+//   load_quantized_linear <- the WEIGHTS upload of a packed tensor (src/models/sam3/model.hpp:114-133)
+//                            read by samq_io::GgufReader (gguf_reader.hpp, mirrors src/io/gguf_reader.hpp).
 //   VitBackbone           <- sam3_build_vit_graph (src/models/sam3/vision.hpp:252-293) as
 //                            encode_image runs it (src/models/sam3/execution.hpp:55-124): the
 //                            prefix, then every block on the device path, in place on x.
@@ -26,6 +28,7 @@
 #include <utility>
 #include <vector>
 
+#include "gguf_reader.hpp"
 #include "samq.h"
 
 namespace sam::internal {
@@ -114,6 +117,16 @@ private:
     samq_weights* weights_ = nullptr;
     std::int64_t k_ = 0, n_ = 0;
 };
+
+// A packed linear weight straight from a GGUF checkpoint: a 2-D tensor with
+// ne = [K, N] (tensors.hpp T2 weights), its GGUF rows handed to K4 unchanged.
+inline QuantizedLinear load_quantized_linear(const SamqDriver& driver, samq_io::GgufReader& reader,
+                                             const std::string& name, cudaStream_t stream = nullptr) {
+    const samq_io::GgufTensor& t = reader.tensor(name);
+    if (t.dimensions.size() != 2) throw std::runtime_error("GGUF linear weight must be 2-D: " + name);
+    const std::vector<std::uint8_t> bytes = reader.tensor_bytes(t);
+    return QuantizedLinear(driver, t.type, t.dimensions[0], t.dimensions[1], bytes.data(), bytes.size(), stream);
+}
 
 // Device pointers to one ViT block's F32 tensors (src/models/sam3/tensors.hpp:108-126).
 struct VitBlockTensors {

@@ -1,5 +1,6 @@
 // Drives sam::internal::VitBackbone (sam.cpp_b200/host/samq_backend.hpp) the
-// way encode_image would: prefix + blocks on device buffers.  Inputs come from
+// way encode_image would: linears loaded from a GGUF checkpoint by
+// samq_io::GgufReader, prefix + blocks on device buffers.  Inputs come from
 // files written by tests/test_gpu_cpp_host.py; the output x goes back to a file
 // that the Python side compares with the oracle.
 #include <cuda_runtime_api.h>
@@ -50,9 +51,14 @@ int main(int argc, char** argv) {
         pre.patch = patch;
         pre.pos_grid = pos_grid;
         vit.set_prefix(pre);
+        // The four linears come from a GGUF checkpoint (tensor names of tensors.hpp:108-121).
+        samq_io::GgufReader checkpoint(dir + "/weights.gguf");
         auto linear = [&](const char* name, int type, long long k, long long n) {
-            const std::vector<char> rows = read_file(dir + "/" + name + ".bin");
-            return QuantizedLinear(driver, type, k, n, rows.data(), rows.size());
+            const std::string full = std::string("vit.blocks.0.") + name + ".weight";
+            const samq_io::GgufTensor& t = checkpoint.tensor(full);
+            if (t.type != type || t.dimensions.size() != 2 || t.dimensions[0] != k || t.dimensions[1] != n)
+                throw std::runtime_error("unexpected checkpoint tensor " + full);
+            return load_quantized_linear(driver, checkpoint, full);
         };
         VitBlockTensors t;
         t.norm1_w = to_device(read_file(dir + "/norm1_w.bin"));
@@ -65,8 +71,8 @@ int main(int argc, char** argv) {
         t.fc2_b = to_device(read_file(dir + "/fc2_b.bin"));
         t.freqs_cis = to_device(read_file(dir + "/freqs.bin"));
         t.window = window;
-        vit.add_block(linear("qkv", qtype, embed, 3 * embed), linear("proj", qtype, embed, embed),
-                      linear("fc1", qtype, embed, mlp), linear("fc2", fc2_type, mlp, embed), t);
+        vit.add_block(linear("attn.qkv", qtype, embed, 3 * embed), linear("attn.proj", qtype, embed, embed),
+                      linear("mlp.lin1", qtype, embed, mlp), linear("mlp.lin2", fc2_type, mlp, embed), t);
         const float* image = to_device(read_file(dir + "/image.bin"));
         const long long tokens = static_cast<long long>(size / patch) * (size / patch);
         void* x_mem = nullptr;

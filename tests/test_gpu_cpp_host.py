@@ -64,8 +64,9 @@ def test_vit_backbone_host_program_compiles(tmp_path):
 
 @pytest.mark.gpu
 def test_cpp_vit_backbone_on_gpu(tmp_path, oracle):
-    """VitBackbone::encode (prefix + one windowed block) from C++ against the
-    f64 oracle; same bar as the block test on the block's contribution."""
+    """VitBackbone::encode (prefix + one windowed block) from C++, its linears
+    loaded from a gguf-py checkpoint by the host GGUF reader, against the f64
+    oracle; same bar as the block test on the block's contribution."""
     rng = np.random.default_rng(11)
     size, patch, pos_grid, E, MLP, window = 336, 14, 8, 1024, 4736, 24
     files = {}
@@ -75,12 +76,19 @@ def test_cpp_vit_backbone_on_gpu(tmp_path, oracle):
     files["ln_w"] = (1 + rng.normal(0, 0.02, E)).astype(np.float32)
     files["ln_b"] = rng.normal(0, 0.02, E).astype(np.float32)
     blk = {"window": window}
-    for name, n, k, t in (("qkv", 3 * E, E, 12), ("proj", E, E, 12), ("fc1", MLP, E, 12), ("fc2", E, MLP, 8)):
+    import gguf
+    writer = gguf.GGUFWriter(str(tmp_path / "weights.gguf"), "sam3")
+    for name, gname, n, k, t in (("qkv", "attn.qkv", 3 * E, E, 12), ("proj", "attn.proj", E, E, 12),
+                                 ("fc1", "mlp.lin1", MLP, E, 12), ("fc2", "mlp.lin2", E, MLP, 8)):
         w = rng.normal(0, 0.02, (n, k)).astype(np.float32)
         rows = oracle.quantize(t, w)
-        files[name] = rows
+        writer.add_tensor(f"vit.blocks.0.{gname}.weight", rows.reshape(n, -1), raw_dtype=gguf.GGMLQuantizationType(t))
         blk[name + "_w16"] = oracle.weight_f16(t, k, n, rows)
         blk[name + "_b"] = files[name + "_b"] = rng.normal(0, 0.02, n).astype(np.float32)
+    writer.write_header_to_file()
+    writer.write_kv_data_to_file()
+    writer.write_tensors_to_file()
+    writer.close()
     for name in ("norm1", "norm2"):
         blk[name + "_w"] = files[name + "_w"] = (1 + rng.normal(0, 0.02, E)).astype(np.float32)
         blk[name + "_b"] = files[name + "_b"] = rng.normal(0, 0.02, E).astype(np.float32)
