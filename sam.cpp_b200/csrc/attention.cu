@@ -486,12 +486,8 @@ void launch_attention_packed(const __half* qp, const __half* kp, const __half* v
     encode_tensor_map_3d(&tv, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, vt, geo.group_n, kHeadDim, gh,
                          static_cast<uint64_t>(geo.group_n) * 2, static_cast<uint64_t>(geo.group_n) * kHeadDim * 2,
                          64, kHeadDim, CU_TENSOR_MAP_SWIZZLE_128B);
-    static bool configured[64] = {};
-    if (!configured[state.device & 63]) {
-        check_cuda(cudaFuncSetAttribute(attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, AttnSmem::total),
-                   "cudaFuncSetAttribute(attention smem)");
-        configured[state.device & 63] = true;
-    }
+    set_smem_limit_once(state, reinterpret_cast<const void*>(attention_kernel), AttnSmem::total,
+                        "cudaFuncSetAttribute(attention smem)");
     launch_pdl(attention_kernel, dim3((geo.group_n + kQTile - 1) / kQTile, static_cast<unsigned>(gh)),
                dim3(kAttnThreads), AttnSmem::total, stream, "attention_kernel launch", tq, tk, tv, geo, out, out_h, ldo,
                state.status);

@@ -12,6 +12,8 @@
 #include <memory>
 #include <vector>
 
+#include <set>
+
 #include "samq_internal.hpp"
 
 namespace samq {
@@ -98,6 +100,16 @@ Scratch& scratch_for(DeviceState& state, cudaStream_t stream, size_t bytes) {
         s.bytes = rounded;
     }
     return s;
+}
+
+void set_smem_limit_once(DeviceState& state, const void* kernel, int bytes, const char* what) {
+    static std::mutex mutex;
+    static std::set<std::pair<const void*, int>> done;
+    std::lock_guard<std::mutex> lock(mutex);
+    if (done.count({kernel, state.device})) return;
+    DeviceGuard guard(state.device);
+    check_cuda(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes), what);
+    done.insert({kernel, state.device});
 }
 
 void encode_tensor_map_2d(CUtensorMap* map, CUtensorMapDataType dtype, const void* base, uint64_t inner,

@@ -442,12 +442,7 @@ void run(const __half* a, int64_t lda, const __half* b, int64_t m, int64_t n, in
         ty = tk;
     }
     auto kernel = gemm_f16_kernel<BN, STAGES, EW, MODE, GELU>;
-    static bool configured[64] = {};
-    if (!configured[state.device & 63]) {
-        check_cuda(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, L::total),
-                   "cudaFuncSetAttribute(gemm smem)");
-        configured[state.device & 63] = true;
-    }
+    set_smem_limit_once(state, reinterpret_cast<const void*>(kernel), L::total, "cudaFuncSetAttribute(gemm smem)");
     const int64_t tiles = ((m + BM - 1) / BM) * ((n + BN - 1) / BN);
     const int grid = static_cast<int>(tiles < state.sm_count ? tiles : state.sm_count);
     launch_pdl(kernel, dim3(grid), dim3(threads_for(EW)), L::total, stream, "gemm_f16_kernel launch", ta, tb, ty, tk, tv,

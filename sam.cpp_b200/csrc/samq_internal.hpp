@@ -47,6 +47,9 @@ struct DeviceState {
 DeviceState& device_state(int device);
 // Scratch of at least `bytes` bytes for work ordered on `stream`.
 Scratch& scratch_for(DeviceState& state, cudaStream_t stream, size_t bytes);
+// Raises `kernel`'s dynamic shared memory limit to `bytes` on state.device the
+// first time it is asked for there (thread-safe; later calls return at once).
+void set_smem_limit_once(DeviceState& state, const void* kernel, int bytes, const char* what);
 
 
 // RAII device switch.

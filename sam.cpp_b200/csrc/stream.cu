@@ -260,12 +260,7 @@ void run_stream(const samq_weights* w, const __half* x16, int64_t ldx, int64_t m
     encode_tensor_map_2d(&tx, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, x16, w->k, m, ldx * 2, 64, TOK,
                          CU_TENSOR_MAP_SWIZZLE_128B);
     auto kernel = gemm_stream_kernel<TYPE, TOK>;
-    static bool configured[64] = {};
-    if (!configured[state.device & 63]) {
-        check_cuda(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, L::total),
-                   "cudaFuncSetAttribute(stream smem)");
-        configured[state.device & 63] = true;
-    }
+    set_smem_limit_once(state, reinterpret_cast<const void*>(kernel), L::total, "cudaFuncSetAttribute(stream smem)");
     const dim3 grid(p.n_tiles, p.splits);
     launch_pdl(kernel, grid, dim3(kStreamThreads), L::total, stream, "gemm_stream_kernel launch",
                static_cast<const uint8_t*>(w->packets), tx, w->n, static_cast<int>(m), p.chunks, p.per_split,
