@@ -30,7 +30,7 @@ def _weights(rng, n, k):
     return w
 
 
-def make_block(rng, window, positions, qtype=o.Q4_K, fc2_type=o.Q8_0):
+def make_block(rng, window, positions, qtype=o.Q4_K, fc2_type=o.Q8_0, E=E, MLP=MLP):
     """Random-init block with config-3 statistics: K-quant linears (fc2 Q8_0),
     N(0, 0.02^2) weights with 1% scaled x8, LN gamma 1 + N(0, 0.02^2)."""
     dev = torch.device("cuda")
@@ -109,6 +109,21 @@ def test_vit_block_full_grid_global():
     rows = np.sort(rng.choice(72 * 72, 96, replace=False))
     ref = o.vit_block(x, host, 72, 72, rows=rows)
     cos, rel = compare(out[rows], ref, x[rows])
+    assert cos >= COS_MIN and rel <= DELTA_REL_MAX, (cos, rel)
+
+
+@pytest.mark.parametrize("embed,mlp,grid,window", [(256, 1024, 24, 12), (512, 2048, 16, 0)])
+def test_vit_block_other_widths(embed, mlp, grid, window):
+    """E = 256 / 512 (the other widths the entry point takes): LayerNorm with 2 / 4
+    float4 per lane, and 144-token windows, which are not a multiple of 32
+    (the qkv split's direct-store path) and end in a 16-key attention block."""
+    rng = np.random.default_rng(embed + grid)
+    positions = window * window if window else grid * grid
+    host, block = make_block(rng, window, positions, qtype=o.Q5_K, E=embed, MLP=mlp)
+    x = rng.standard_normal((grid * grid, embed)).astype(np.float32)
+    out = run_block(block, x, grid)
+    ref = o.vit_block(x, host, grid, grid)
+    cos, rel = compare(out, ref, x)
     assert cos >= COS_MIN and rel <= DELTA_REL_MAX, (cos, rel)
 
 
