@@ -81,23 +81,51 @@ struct Layout {
 // coalesced load, broadcast by shuffles), erf-GELU, then per OutMode either
 // swizzled staging in shared memory and a TMA store (clipped by the tensor map
 // at the m / n edges), or direct stores of f16 rows.
+// What a chunk needs from global memory besides the accumulator: the bias of
+// column col0 + lane and, for the residual mode, the row's 32 residual values.
+// They are issued together with the chunk's TMEM load; in the residual mode a
+// warp's first chunk loads them before the accumulator is even ready (under
+// the tile's MMAs), as the 128-byte residual read is the longest wait there.
+template <int MODE>
+struct ChunkInputs {
+    float bias = 0.0f;
+    float4 res[MODE == kOutF32Residual ? 8 : 1];
+};
+
+template <int MODE>
+__device__ __forceinline__ void load_chunk_inputs(const Epilogue& ep, int col0, int row, int m, int n, int lane,
+                                                  ChunkInputs<MODE>& in) {
+    in.bias = (ep.bias != nullptr && col0 + lane < n) ? __ldg(ep.bias + col0 + lane) : 0.0f;
+    if constexpr (MODE == kOutF32Residual) {
+        if (row < m) {
+            const float4* res = reinterpret_cast<const float4*>(ep.residual + static_cast<int64_t>(row) * ep.ldr + col0);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) in.res[j] = col0 + 4 * j < n ? res[j] : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+    }
+}
+
 template <int BN, int PARTS, int MODE, bool GELU>
 __device__ __forceinline__ void drain_tile(uint32_t tmem_base, int quarter, int part, int acc, int row0,
                                            int col_base, int m, int n, const Epilogue& ep,
                                            const CUtensorMap* tma_y, const CUtensorMap* tma_k,
                                            const CUtensorMap* tma_v, uint8_t* stage_buf, int& buf, int lane,
-                                           DeviceStatus* status) {
+                                           const ChunkInputs<MODE>& first, DeviceStatus* status) {
     constexpr int kChunks = BN / 32;
     const int row = row0 + lane;
+    const int c_begin = part * kChunks / PARTS, c_end = (part + 1) * kChunks / PARTS;
 #pragma unroll 1
-    for (int chunk = part * kChunks / PARTS; chunk < (part + 1) * kChunks / PARTS; ++chunk) {
+    for (int chunk = c_begin; chunk < c_end; ++chunk) {
         const int col0 = col_base + chunk * 32;
         if (col0 >= n) break;
         uint32_t r[32];
         tc_ld_32x32b_x32(tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) +
                              static_cast<uint32_t>(acc * kAccStride + chunk * 32),
                          r);
-        const float bias_lane = (ep.bias != nullptr && col0 + lane < n) ? __ldg(ep.bias + col0 + lane) : 0.0f;
+        ChunkInputs<MODE> cur;
+        if (MODE == kOutF32Residual && chunk == c_begin) cur = first;
+        else load_chunk_inputs<MODE>(ep, col0, row, m, n, lane, cur);
+        const float bias_lane = cur.bias;
         // qkv split: the RoPE table entries of this row's 16 channel pairs,
         // fetched while the accumulator load is in flight (8-warp epilogues
         // only: the 16-warp ones have no registers to spare for them).
@@ -223,18 +251,15 @@ __device__ __forceinline__ void drain_tile(uint32_t tmem_base, int quarter, int 
             }
             continue;
         }
-        if (MODE == kOutF32Residual && row < m) {
+        if constexpr (MODE == kOutF32Residual) {
             // The ViT shortcut add: residual + (acc + bias), one f32 add.
-            const float4* res = reinterpret_cast<const float4*>(ep.residual + static_cast<int64_t>(row) * ep.ldr + col0);
 #pragma unroll
             for (int j = 0; j < 8; ++j) {
-                if (col0 + 4 * j < n) {
-                    const float4 rv = res[j];
-                    v[4 * j] = __fadd_rn(rv.x, v[4 * j]);
-                    v[4 * j + 1] = __fadd_rn(rv.y, v[4 * j + 1]);
-                    v[4 * j + 2] = __fadd_rn(rv.z, v[4 * j + 2]);
-                    v[4 * j + 3] = __fadd_rn(rv.w, v[4 * j + 3]);
-                }
+                const float4 rv = cur.res[j];
+                v[4 * j] = __fadd_rn(rv.x, v[4 * j]);
+                v[4 * j + 1] = __fadd_rn(rv.y, v[4 * j + 1]);
+                v[4 * j + 2] = __fadd_rn(rv.z, v[4 * j + 2]);
+                v[4 * j + 3] = __fadd_rn(rv.w, v[4 * j + 3]);
             }
         }
         if (lane == 0) bulk_wait_group_read<kOutBuffers - 1>();
@@ -385,12 +410,18 @@ gemm_f16_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant
         int buf = 0;
         for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x) {
             const int mt = tile / n_tiles, nt = tile % n_tiles;
+            const int row0 = mt * BM + quarter * 32;
+            // Residual mode: the first chunk's inputs load while the tile's MMAs run.
+            ChunkInputs<MODE> first;
+            if constexpr (MODE == kOutF32Residual) {
+                const int first_col = nt * BN + (part * (BN / 32) / (EW / 4)) * 32;
+                if (first_col < n) load_chunk_inputs<MODE>(ep, first_col, row0 + lane, m, n, lane, first);
+            }
             // Warp-uniform: the tcgen05.ld in drain_tile is warp-collective.
             if (!__all_sync(0xffffffffu, mbar_wait(&tfull[acc], acc_ph, status, 4))) break;
             tc_fence_after();
-            const int row0 = mt * BM + quarter * 32;
-            drain_tile<BN, EW / 4, MODE, GELU>(tmem_base, quarter, part, acc, row0, nt * BN, m, n, ep, &tma_y, &tma_k, &tma_v,
-                                   stage_buf, buf, lane, status);
+            drain_tile<BN, EW / 4, MODE, GELU>(tmem_base, quarter, part, acc, row0, nt * BN, m, n, ep, &tma_y, &tma_k,
+                                               &tma_v, stage_buf, buf, lane, first, status);
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&tempty[acc]);
