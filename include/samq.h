@@ -207,6 +207,90 @@ samq_status samq_vit_prefix_v1(const float* image, int width, int height, int pa
                                int64_t embed, const float* pos_embed, int pos_grid, const float* ln_w,
                                const float* ln_b, float* x, void* stream);
 
+/* ---- Dense (F32 / F16) modules with F32 semantics -------------------------
+ * The tensors the reference keeps unquantized (neck convolutions, fusion /
+ * decoder / mask-head linears in the F32 profiles: "only ViT linear weights
+ * are quantized, while text, neck, fusion, detector, mask head, and other
+ * tensors remain original F32", tests/data/sam3-vision-quantization-gates.json:8)
+ * are multiplied with F32 semantics:
+ * ggml_cuda_mul_mat routes F32/F16 weights x F32 activations at GGML_PREC_F32
+ * to cuBLAS with CUBLAS_COMPUTE_32F_PEDANTIC (no TF32 narrowing,
+ * cmake/patches/ggml-precise-cuda.patch:288-356), and convolutions keep F32
+ * im2col columns (src/models/sam3/ops.hpp:67-84).  Here both run on the
+ * tcgen05 tensor cores as a three-term TF32 split: each F32 operand x is
+ * hi = rna_tf32(x), lo = rna_tf32(x - hi), and hi*hi + hi*lo + lo*hi is
+ * accumulated in F32 (relative error ~2^-22 per product, F32 level).  F16
+ * weights are promoted exactly.  Layouts are channel-innermost (NHWC, the
+ * reference's [C, W, H] tensors): pixel (x, y) of a width x height image with
+ * C channels is row y * width + x of a [pixels][C] f32 array. */
+enum {
+    SAMQ_TYPE_F32 = 0,
+    SAMQ_TYPE_F16 = 1
+};
+
+enum {
+    SAMQ_DENSE_LINEAR = 0,     /* GGML [k, n] matrix: W[n][k] */
+    SAMQ_DENSE_CONV = 1,       /* GGML conv kernel [kw, kh, cin, cout], kw == kh in {1, 3}: stride 1, pad kw/2 */
+    SAMQ_DENSE_DECONV2X2 = 2   /* GGML ConvTranspose2d kernel [2, 2, cout, cin]: stride 2, no padding */
+};
+
+typedef struct samq_dense samq_dense;
+
+/* Uploads HOST weights (`type` F32 or F16, `bytes` = element count x size) in
+ * the GGML layout of `kind` and splits them on the device.  kind LINEAR:
+ * cin = k, cout = n, kw = kh = 1.  cin % 32 == 0 for CONV and DECONV2X2,
+ * cout % 32 == 0 for DECONV2X2, cin % 4 == 0 for LINEAR. */
+samq_status samq_dense_create_v1(int device, int type, int kind, int kw, int kh, int64_t cin, int64_t cout,
+                                 const void* data, size_t bytes, void* stream, samq_dense** out);
+samq_status samq_dense_destroy_v1(samq_dense* weights);
+
+/* Y[m][n] = X[m][k] W[n][k]^T (+ bias[n]) (then erf-GELU), F32 semantics;
+ * `weights` of kind LINEAR.  ldx % 4 == 0, ldy % 4 == 0, pointers 16-byte
+ * aligned.  Replaces ggml_mul_mat on F32/F16 weights at GGML_PREC_F32. */
+samq_status samq_dense_linear_v1(const samq_dense* weights, const float* x, int64_t m, int64_t ldx,
+                                 const float* bias, int epilogue, float* y, int64_t ldy, void* stream);
+
+/* Convolution of an NHWC image x [height * width][cin] into y (+ bias[cout],
+ * then optional erf-GELU).  CONV: y is [height * width][cout]
+ * (sam3_conv_2d_s1_ph / sam3_conv_2d_sk_p0 with a 1x1 kernel,
+ * src/models/sam3/ops.hpp:86-94).  DECONV2X2: y is [(2 height) * (2 width)][cout],
+ * y(2i + ky, 2j + kx) = sum_c x(i, j)[c] W[c][co][ky][kx] (sam3_deconv_2x2,
+ * ops.hpp:96-117). */
+samq_status samq_conv2d_v1(const samq_dense* weights, const float* x, int width, int height, const float* bias,
+                           int epilogue, float* y, void* stream);
+
+/* 2x2 max pooling with stride 2 of an NHWC image (ggml_pool_2d MAX 2,2,2,2,0,0;
+ * output floor(width / 2) x floor(height / 2)); channels % 4 == 0. */
+samq_status samq_maxpool2x2_v1(const float* x, int width, int height, int64_t channels, float* y, void* stream);
+
+/* The SimpleFPN neck of one path (src/models/sam3/vision.hpp:307-366), tensor
+ * names of src/models/sam3/tensors.hpp:131-160 (E = ViT width, D = 256):
+ *   out[0] (4x):   deconv E->mid, +b, GELU, deconv mid->D, +b, conv1x1, +b, conv3x3, +b
+ *   out[1] (2x):   deconv E->mid, +b, conv1x1 mid->D, +b, conv3x3, +b
+ *   out[2] (1x):   conv1x1 E->D, +b, conv3x3, +b
+ *   out[3] (0.5x): maxpool 2x2, conv1x1 E->D, +b, conv3x3, +b
+ * with mid = 512 in SAM 3 (any multiple of 32 here). */
+typedef struct samq_neck_v1 {
+    uint32_t version;  /* 1 */
+    const samq_dense* s0_deconv1; const float* s0_deconv1_b;
+    const samq_dense* s0_deconv2; const float* s0_deconv2_b;
+    const samq_dense* s0_conv1x1; const float* s0_conv1x1_b;
+    const samq_dense* s0_conv3x3; const float* s0_conv3x3_b;
+    const samq_dense* s1_deconv1; const float* s1_deconv1_b;
+    const samq_dense* s1_conv1x1; const float* s1_conv1x1_b;
+    const samq_dense* s1_conv3x3; const float* s1_conv3x3_b;
+    const samq_dense* s2_conv1x1; const float* s2_conv1x1_b;
+    const samq_dense* s2_conv3x3; const float* s2_conv3x3_b;
+    const samq_dense* s3_conv1x1; const float* s3_conv1x1_b;
+    const samq_dense* s3_conv3x3; const float* s3_conv3x3_b;
+} samq_neck_v1;
+
+/* x: the ViT output, device f32 [grid_h * grid_w][E] (raster tokens = NHWC).
+ * out[i]: device f32 NHWC [(grid_h * 2^(2-i)) * (grid_w * 2^(2-i))][D]
+ * (out[3] is floor(grid / 2) on each side).  Replaces sam3_build_neck_graph. */
+samq_status samq_neck_forward_v1(const samq_neck_v1* neck, const float* x, int grid_w, int grid_h,
+                                 float* const out[4], void* stream);
+
 /* Counters of a handle.  Mirrors ggml_cuda_sam_q8_rhs_query_v1
  * (cmake/patches/ggml-native-activation.patch:34-42). */
 samq_status samq_query_v1(const samq_weights* weights, struct samq_counters_v1* out);

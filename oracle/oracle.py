@@ -299,3 +299,97 @@ def vit_prefix(image: np.ndarray, patch: int, patch_w: np.ndarray, pos_embed: np
     py, px = np.divmod(np.arange(gh * gw), gw)
     y += np.asarray(pos_embed, np.float64)[py % pg, px % pg]
     return layer_norm(y, ln_w, ln_b)
+
+
+# ---- dense F32 modules (neck, fusion / decoder linears in F32 profiles) -----
+# f64 restatements; the device path is held to F32-level error against them.
+
+def gelu_erf64(v: np.ndarray) -> np.ndarray:
+    """ggml_gelu_erf, 0.5 v (1 + erf(v / sqrt 2)), in f64."""
+    from scipy.special import erf
+    v = np.asarray(v, np.float64)
+    return 0.5 * v * (1.0 + erf(v / np.sqrt(2.0)))
+
+
+def dense_linear(x: np.ndarray, w: np.ndarray, bias=None, gelu: bool = False) -> np.ndarray:
+    """ggml_mul_mat on an F32 / F16 weight [n][k] at GGML_PREC_F32, which the
+    reference's CUDA path runs as cuBLAS COMPUTE_32F_PEDANTIC
+    (cmake/patches/ggml-precise-cuda.patch:288-356): x [m][k] . w^T (+ bias)
+    (then erf-GELU), f64."""
+    y = np.asarray(x, np.float64) @ np.asarray(w, np.float64).T
+    if bias is not None:
+        y = y + np.asarray(bias, np.float64)
+    return gelu_erf64(y) if gelu else y
+
+
+def conv2d_nhwc(x: np.ndarray, w: np.ndarray, bias=None, stride: int = 1, pad: int | None = None) -> np.ndarray:
+    """sam3_conv_2d (src/models/sam3/ops.hpp:67-84): im2col + mul_mat over F32
+    columns.  x [H][W][Cin] (the reference's [W, H, C] tensor), w
+    [Cout][Cin][kh][kw] (GGML [kw, kh, Cin, Cout]).  Default stride 1 and pad
+    k // 2 is sam3_conv_2d_s1_ph (:91-94); stride = k, pad = 0 is
+    sam3_conv_2d_sk_p0 (:86-89).  f64 [Ho][Wo][Cout]."""
+    x = np.asarray(x, np.float64)
+    w = np.asarray(w, np.float64)
+    H, W, C = x.shape
+    co, ci, kh, kw = w.shape
+    assert ci == C
+    p = kh // 2 if pad is None else pad
+    xp = np.zeros((H + 2 * p, W + 2 * p, C))
+    xp[p:p + H, p:p + W] = x
+    ho = (H + 2 * p - kh) // stride + 1
+    wo = (W + 2 * p - kw) // stride + 1
+    out = np.zeros((ho, wo, co))
+    for ky in range(kh):
+        for kx in range(kw):
+            patch = xp[ky:ky + stride * (ho - 1) + 1:stride, kx:kx + stride * (wo - 1) + 1:stride]
+            out += patch @ w[:, :, ky, kx].T
+    if bias is not None:
+        out = out + np.asarray(bias, np.float64)
+    return out
+
+
+def deconv2x2_nhwc(x: np.ndarray, w: np.ndarray, bias=None) -> np.ndarray:
+    """sam3_deconv_2x2 (src/models/sam3/ops.hpp:96-117), the stride-2 2x2
+    ConvTranspose2d as one matrix product: x [H][W][Cin], w [Cin][Cout][2][2]
+    (GGML [2, 2, Cout, Cin]); y[2i + ky][2j + kx][co] = sum_c x[i][j][c]
+    w[c][co][ky][kx] (+ bias[co]).  f64 [2H][2W][Cout]."""
+    x = np.asarray(x, np.float64)
+    w = np.asarray(w, np.float64)
+    H, W, C = x.shape
+    ci, co = w.shape[:2]
+    assert ci == C
+    out = np.zeros((2 * H, 2 * W, co))
+    for ky in range(2):
+        for kx in range(2):
+            out[ky::2, kx::2] = x @ w[:, :, ky, kx]
+    if bias is not None:
+        out = out + np.asarray(bias, np.float64)
+    return out
+
+
+def maxpool2x2_nhwc(x: np.ndarray) -> np.ndarray:
+    """ggml_pool_2d(MAX, 2, 2, 2, 2, 0, 0) of an NHWC image (floor sizes)."""
+    H, W, C = x.shape
+    h2, w2 = H // 2, W // 2
+    return np.asarray(x)[:2 * h2, :2 * w2].reshape(h2, 2, w2, 2, C).max(axis=(1, 3))
+
+
+def neck(x: np.ndarray, layers: dict) -> list:
+    """sam3_build_neck_graph (src/models/sam3/vision.hpp:307-366) in f64:
+    x [gh][gw][E]; layers[name] = (weight, bias) with the samq_neck_v1 names.
+    Returns the four NHWC maps (4x, 2x, 1x, 0.5x)."""
+    L = layers
+    s0 = deconv2x2_nhwc(x, *L["s0_deconv1"])
+    s0 = gelu_erf64(s0)
+    s0 = deconv2x2_nhwc(s0, *L["s0_deconv2"])
+    s0 = conv2d_nhwc(s0, *L["s0_conv1x1"])
+    s0 = conv2d_nhwc(s0, *L["s0_conv3x3"])
+    s1 = deconv2x2_nhwc(x, *L["s1_deconv1"])
+    s1 = conv2d_nhwc(s1, *L["s1_conv1x1"])
+    s1 = conv2d_nhwc(s1, *L["s1_conv3x3"])
+    s2 = conv2d_nhwc(x, *L["s2_conv1x1"])
+    s2 = conv2d_nhwc(s2, *L["s2_conv3x3"])
+    s3 = maxpool2x2_nhwc(np.asarray(x, np.float64))
+    s3 = conv2d_nhwc(s3, *L["s3_conv1x1"])
+    s3 = conv2d_nhwc(s3, *L["s3_conv3x3"])
+    return [s0, s1, s2, s3]

@@ -140,6 +140,20 @@ void encode_tensor_map_3d(CUtensorMap* map, CUtensorMapDataType dtype, const voi
                                                                std::to_string(static_cast<int>(r)) + ")");
 }
 
+void encode_tensor_map_3d_box(CUtensorMap* map, CUtensorMapDataType dtype, const void* base, uint64_t d0,
+                              uint64_t d1, uint64_t d2, uint64_t stride1_bytes, uint64_t stride2_bytes, uint32_t box0,
+                              uint32_t box1, uint32_t box2, CUtensorMapSwizzle swizzle) {
+    const cuuint64_t dims[3] = {d0, d1, d2};
+    const cuuint64_t strides[2] = {stride1_bytes, stride2_bytes};
+    const cuuint32_t box[3] = {box0, box1, box2};
+    const cuuint32_t elem_strides[3] = {1, 1, 1};
+    const CUresult r = encode_fn()(map, dtype, 3, const_cast<void*>(base), dims, strides, box, elem_strides,
+                                   CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) fail(SAMQ_ERR_INVALID_ARGUMENT, "cuTensorMapEncodeTiled rejected a 3-D box (code " +
+                                                               std::to_string(static_cast<int>(r)) + ")");
+}
+
 namespace {
 
 template <class F>
@@ -174,6 +188,19 @@ int current_device() {
     int device = 0;
     check_cuda(cudaGetDevice(&device), "cudaGetDevice");
     return device;
+}
+
+void release_dense(samq_dense* w) {
+    if (!w) return;
+    if (w->device >= 0) {
+        int previous = -1;
+        cudaGetDevice(&previous);
+        cudaSetDevice(w->device);
+        if (w->hi) cudaFree(w->hi);
+        if (w->lo) cudaFree(w->lo);
+        if (previous >= 0) cudaSetDevice(previous);
+    }
+    delete w;
 }
 
 void release(samq_weights* w) {
@@ -524,6 +551,145 @@ samq_status samq_vit_prefix_v1(const float* image, int width, int height, int pa
         Scratch& scratch = scratch_for(state, stream, vit_prefix_scratch_bytes(tokens, embed, patch));
         launch_vit_prefix(image, width, height, patch, patch_w, embed, pos_embed, pos_grid, ln_w, ln_b, x, scratch.ptr,
                           state, stream);
+    });
+}
+
+samq_status samq_dense_create_v1(int device, int type, int kind, int kw, int kh, int64_t cin, int64_t cout,
+                                 const void* data, size_t bytes, void* stream_ptr, samq_dense** out) {
+    return guarded([&] {
+        require(out != nullptr, "null output handle");
+        *out = nullptr;
+        require(type == SAMQ_TYPE_F32 || type == SAMQ_TYPE_F16, "dense weight type must be F32 or F16");
+        require(cin > 0 && cout > 0 && cin <= (int64_t(1) << 20) && cout <= (int64_t(1) << 20),
+                "channel counts out of range");
+        int64_t n = 0, k = 0;
+        switch (kind) {
+            case SAMQ_DENSE_LINEAR:
+                require(kw == 1 && kh == 1, "a linear has kw == kh == 1");
+                require(cin % 4 == 0, "linear width must be a multiple of 4");
+                n = cout;
+                k = cin;
+                break;
+            case SAMQ_DENSE_CONV:
+                require(kw == kh && (kw == 1 || kw == 3), "convolution kernels are 1x1 or 3x3");
+                require(cin % 32 == 0, "convolution input channels must be a multiple of 32");
+                n = cout;
+                k = cin * kw * kh;
+                break;
+            case SAMQ_DENSE_DECONV2X2:
+                require(kw == 2 && kh == 2, "the transposed convolution is 2x2");
+                require(cin % 32 == 0 && cout % 32 == 0, "deconvolution channels must be multiples of 32");
+                n = 4 * cout;
+                k = cin;
+                break;
+            default: fail(SAMQ_ERR_INVALID_ARGUMENT, "unknown dense kind");
+        }
+        require(n * k <= (int64_t(1) << 31), "weight too large");
+        const size_t elem = type == SAMQ_TYPE_F32 ? 4 : 2;
+        require(data != nullptr && bytes == static_cast<size_t>(n * k) * elem, "payload size differs from the shape");
+        DeviceState& state = device_state(device);
+        DeviceGuard guard(device);
+        cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
+        std::unique_ptr<samq_dense, void (*)(samq_dense*)> w(new samq_dense, release_dense);
+        w->device = device;
+        w->type = type;
+        w->kind = kind;
+        w->ks = kw;
+        w->cin = cin;
+        w->cout = cout;
+        w->n = n;
+        w->k = k;
+        void* staging = nullptr;
+        struct Free {
+            void*& p;
+            ~Free() {
+                if (p) cudaFree(p);
+            }
+        } free_staging{staging};
+        check_cuda(cudaMalloc(&staging, bytes), "cudaMalloc(dense staging)");
+        check_cuda(cudaMalloc(reinterpret_cast<void**>(&w->hi), static_cast<size_t>(n * k) * 4), "cudaMalloc(dense hi)");
+        check_cuda(cudaMalloc(reinterpret_cast<void**>(&w->lo), static_cast<size_t>(n * k) * 4), "cudaMalloc(dense lo)");
+        check_cuda(cudaMemcpyAsync(staging, data, bytes, cudaMemcpyHostToDevice, stream), "cudaMemcpyAsync(H2D)");
+        launch_dense_prep(staging, type, kind, kw, cin, cout, n, k, w->hi, w->lo, state, stream);
+        check_cuda(cudaStreamSynchronize(stream), "cudaStreamSynchronize(dense prep)");
+        *out = w.release();
+    });
+}
+
+samq_status samq_dense_destroy_v1(samq_dense* weights) {
+    return guarded([&] { release_dense(weights); });
+}
+
+samq_status samq_dense_linear_v1(const samq_dense* w, const float* x, int64_t m, int64_t ldx, const float* bias,
+                                 int epilogue, float* y, int64_t ldy, void* stream_ptr) {
+    return guarded([&] {
+        require(w != nullptr && w->kind == SAMQ_DENSE_LINEAR, "weights must be a dense LINEAR handle");
+        require(m >= 0 && m <= (int64_t(1) << 31), "row count out of range");
+        require(epilogue == SAMQ_EPILOGUE_NONE || epilogue == SAMQ_EPILOGUE_GELU_ERF, "unknown epilogue");
+        require(ldx >= w->k && ldx % 4 == 0, "input row stride must be >= k and a multiple of 4 floats");
+        require(ldy >= w->n && ldy % 4 == 0, "output row stride must be >= n and a multiple of 4 floats");
+        if (m == 0) return;
+        require(x != nullptr && y != nullptr && aligned16(x) && aligned16(y), "pointers must be 16-byte aligned");
+        DeviceGuard guard(w->device);
+        DeviceState& state = device_state(w->device);
+        cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
+        const size_t half = static_cast<size_t>(m * w->k);
+        Scratch& scratch = scratch_for(state, stream, 2 * half * sizeof(float) + 256);
+        float* xh = static_cast<float*>(scratch.ptr);
+        float* xl = xh + (half + 63) / 64 * 64;
+        launch_split_rows(x, m, w->k, ldx, xh, xl, state, stream);
+        launch_dense_gemm(xh, xl, *w, m, 0, 0, bias, epilogue, y, nullptr, ldy, state, stream);
+    });
+}
+
+samq_status samq_conv2d_v1(const samq_dense* w, const float* x, int width, int height, const float* bias,
+                           int epilogue, float* y, void* stream_ptr) {
+    return guarded([&] {
+        require(w != nullptr && (w->kind == SAMQ_DENSE_CONV || w->kind == SAMQ_DENSE_DECONV2X2),
+                "weights must be a dense CONV or DECONV2X2 handle");
+        require(width > 0 && height > 0 && int64_t(width) * height <= (int64_t(1) << 26), "image size out of range");
+        require(epilogue == SAMQ_EPILOGUE_NONE || epilogue == SAMQ_EPILOGUE_GELU_ERF, "unknown epilogue");
+        require(x != nullptr && y != nullptr && aligned16(x) && aligned16(y), "pointers must be 16-byte aligned");
+        DeviceGuard guard(w->device);
+        DeviceState& state = device_state(w->device);
+        cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
+        const int64_t pixels = int64_t(width) * height;
+        const size_t half = static_cast<size_t>(pixels * w->cin);
+        Scratch& scratch = scratch_for(state, stream, 2 * half * sizeof(float) + 256);
+        float* xh = static_cast<float*>(scratch.ptr);
+        float* xl = xh + (half + 63) / 64 * 64;
+        launch_split_rows(x, pixels, w->cin, w->cin, xh, xl, state, stream);
+        if (w->kind == SAMQ_DENSE_DECONV2X2)
+            launch_dense_gemm(xh, xl, *w, pixels, width, 0, bias, epilogue, y, nullptr, w->cout, state, stream);
+        else
+            launch_dense_gemm(xh, xl, *w, pixels, width, height, bias, epilogue, y, nullptr, w->cout, state, stream);
+    });
+}
+
+samq_status samq_maxpool2x2_v1(const float* x, int width, int height, int64_t channels, float* y, void* stream) {
+    return guarded([&] {
+        require(width > 0 && height > 0 && int64_t(width) * height <= (int64_t(1) << 26), "image size out of range");
+        require(channels > 0 && channels % 4 == 0 && channels <= (int64_t(1) << 20), "channels must be a multiple of 4");
+        require(x != nullptr && y != nullptr && aligned16(x) && aligned16(y), "pointers must be 16-byte aligned");
+        DeviceState& state = device_state(current_device());
+        launch_maxpool2x2(x, width, height, channels, y, nullptr, state, static_cast<cudaStream_t>(stream));
+    });
+}
+
+samq_status samq_neck_forward_v1(const samq_neck_v1* neck, const float* x, int grid_w, int grid_h,
+                                 float* const out[4], void* stream_ptr) {
+    return guarded([&] {
+        require(neck != nullptr && neck->version == 1, "neck descriptor must have version 1");
+        require(grid_w >= 2 && grid_h >= 2 && int64_t(grid_w) * grid_h <= (int64_t(1) << 20), "grid out of range");
+        require(x != nullptr && aligned16(x) && out != nullptr, "null or misaligned pointer");
+        for (int i = 0; i < 4; ++i) require(out[i] != nullptr && aligned16(out[i]), "null or misaligned output");
+        const int device = neck->s0_deconv1 ? neck->s0_deconv1->device : -1;
+        require(device >= 0, "neck weight missing");
+        DeviceGuard guard(device);
+        DeviceState& state = device_state(device);
+        cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
+        Scratch& scratch = scratch_for(state, stream, neck_scratch_bytes(*neck, grid_w, grid_h));
+        launch_neck(*neck, x, grid_w, grid_h, out, scratch.ptr, state, stream);
     });
 }
 

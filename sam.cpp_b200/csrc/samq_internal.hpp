@@ -85,6 +85,10 @@ void encode_tensor_map_2d(CUtensorMap* map, CUtensorMapDataType dtype, const voi
 void encode_tensor_map_3d(CUtensorMap* map, CUtensorMapDataType dtype, const void* base, uint64_t d0, uint64_t d1,
                           uint64_t d2, uint64_t stride1_bytes, uint64_t stride2_bytes, uint32_t box0, uint32_t box1,
                           CUtensorMapSwizzle swizzle);
+// 3-D map whose box spans box2 planes (encode_tensor_map_3d takes one).
+void encode_tensor_map_3d_box(CUtensorMap* map, CUtensorMapDataType dtype, const void* base, uint64_t d0,
+                              uint64_t d1, uint64_t d2, uint64_t stride1_bytes, uint64_t stride2_bytes, uint32_t box0,
+                              uint32_t box1, uint32_t box2, CUtensorMapSwizzle swizzle);
 
 }  // namespace samq
 
@@ -100,6 +104,17 @@ struct samq_weights {
     std::atomic<uint64_t> launches{0};
     std::atomic<uint64_t> payload_bytes{0};
     std::atomic<uint64_t> allocation_bytes{0};
+};
+
+// Dense (F32 / F16) weights: the GEMM operand B = W split into TF32 hi / lo
+// (dense.cu).
+struct samq_dense {
+    int device = -1;
+    int type = 0, kind = 0, ks = 1;  // SAMQ_TYPE_F32 / F16, SAMQ_DENSE_*, kernel size
+    int64_t cin = 0, cout = 0;
+    int64_t n = 0, k = 0;            // B is [n][k]: n = cout (x 4 for DECONV2X2), k = cin (x ks^2 for CONV)
+    float* hi = nullptr;
+    float* lo = nullptr;
 };
 
 // ---- launchers implemented in the .cu files -------------------------------
@@ -199,5 +214,24 @@ size_t vit_prefix_scratch_bytes(int64_t tokens, int64_t embed, int patch);
 void launch_vit_prefix(const float* image, int width, int height, int patch, const float* patch_w, int64_t embed,
                        const float* pos, int pos_grid, const float* ln_w, const float* ln_b, float* x,
                        void* scratch, DeviceState& state, cudaStream_t stream);
+
+// dense.cu: F32-semantics linears / convolutions (three-term TF32 split).
+void launch_dense_prep(const void* src, int type, int kind, int ks, int64_t cin, int64_t cout, int64_t n, int64_t k,
+                       float* hi, float* lo, DeviceState& state, cudaStream_t stream);
+// x [rows][ld] -> hi / lo [rows][k].
+void launch_split_rows(const float* x, int64_t rows, int64_t k, int64_t ld, float* hi, float* lo, DeviceState& state,
+                       cudaStream_t stream);
+// y (and lo != nullptr: the hi / lo split) = 2x2 max pooling of NHWC x.
+void launch_maxpool2x2(const float* x, int width, int height, int64_t channels, float* y, float* lo,
+                       DeviceState& state, cudaStream_t stream);
+// A = split activations: [m][k] rows (LINEAR, 1x1 CONV, DECONV2X2 with
+// conv_width = input width) or an NHWC image conv_width x conv_height (CONV);
+// output f32 (y_lo == nullptr) or split, [rows][ldy].
+void launch_dense_gemm(const float* a_hi, const float* a_lo, const samq_dense& w, int64_t m, int conv_width,
+                       int conv_height, const float* bias, int gelu, float* y, float* y_lo, int64_t ldy,
+                       DeviceState& state, cudaStream_t stream);
+size_t neck_scratch_bytes(const samq_neck_v1& neck, int grid_w, int grid_h);
+void launch_neck(const samq_neck_v1& neck, const float* x, int grid_w, int grid_h, float* const out[4], void* scratch,
+                 DeviceState& state, cudaStream_t stream);
 
 }  // namespace samq

@@ -23,6 +23,8 @@ Q8_0, Q8_1, Q4_K, Q5_K, Q6_K = 8, 9, 12, 13, 14
 TYPE_NAMES = {Q8_0: "Q8_0", Q4_K: "Q4_K", Q5_K: "Q5_K", Q6_K: "Q6_K"}
 NAME_TYPES = {v: k for k, v in TYPE_NAMES.items()}
 EPILOGUE_NONE, EPILOGUE_GELU_ERF = 0, 1
+F32, F16 = 0, 1
+DENSE_LINEAR, DENSE_CONV, DENSE_DECONV2X2 = 0, 1, 2
 BLOCK = {Q8_0: (32, 34), Q4_K: (256, 144), Q5_K: (256, 176), Q6_K: (256, 210)}
 
 STATUS_NAMES = {
@@ -54,6 +56,17 @@ class VitBlockDesc(ctypes.Structure):
                 ("fc1", _vp), ("fc1_b", _vp), ("fc2", _vp), ("fc2_b", _vp), ("freqs_cis", _vp)]
 
 
+class NeckDesc(ctypes.Structure):
+    """struct samq_neck_v1: (weights, bias) pairs in the order of NECK_LAYERS."""
+    _fields_ = [("version", ctypes.c_uint32)] + [
+        (f"{name}{suffix}", _vp) for name in ("s0_deconv1", "s0_deconv2", "s0_conv1x1", "s0_conv3x3", "s1_deconv1",
+                                              "s1_conv1x1", "s1_conv3x3", "s2_conv1x1", "s2_conv3x3", "s3_conv1x1",
+                                              "s3_conv3x3") for suffix in ("", "_b")]
+
+
+NECK_LAYERS = ("s0_deconv1", "s0_deconv2", "s0_conv1x1", "s0_conv3x3", "s1_deconv1", "s1_conv1x1", "s1_conv3x3",
+               "s2_conv1x1", "s2_conv3x3", "s3_conv1x1", "s3_conv3x3")
+
 SIGNATURES = {
     "samq_last_error_v1": (ctypes.c_char_p, []),
     "samq_init_v1": (_i32, [_i32]),
@@ -75,6 +88,12 @@ SIGNATURES = {
     "samq_vit_attention_v1": (_i32, [_vp, _i64, _i32, _i32, _i32, _i32, _i32, _vp, _vp, _i64, _vp]),
     "samq_vit_block_forward_v1": (_i32, [ctypes.POINTER(VitBlockDesc), _vp, _i32, _i32, _vp]),
     "samq_vit_prefix_v1": (_i32, [_vp, _i32, _i32, _i32, _vp, _i64, _vp, _i32, _vp, _vp, _vp, _vp]),
+    "samq_dense_create_v1": (_i32, [_i32, _i32, _i32, _i32, _i32, _i64, _i64, _vp, _sz, _vp, ctypes.POINTER(_vp)]),
+    "samq_dense_destroy_v1": (_i32, [_vp]),
+    "samq_dense_linear_v1": (_i32, [_vp, _vp, _i64, _i64, _vp, _i32, _vp, _i64, _vp]),
+    "samq_conv2d_v1": (_i32, [_vp, _vp, _i32, _i32, _vp, _i32, _vp, _vp]),
+    "samq_maxpool2x2_v1": (_i32, [_vp, _i32, _i32, _i64, _vp, _vp]),
+    "samq_neck_forward_v1": (_i32, [ctypes.POINTER(NeckDesc), _vp, _i32, _i32, ctypes.POINTER(_vp), _vp]),
 }
 STATIC_OPERAND_ELEMENTS = 16777216
 
@@ -263,3 +282,79 @@ def vit_prefix(image, width: int, height: int, patch: int, patch_w, embed: int, 
     """samq_vit_prefix_v1: patch embedding + tiled pos_embed + ln_pre into x [tokens][E] f32."""
     _check(library().samq_vit_prefix_v1(_addr(image), width, height, patch, _addr(patch_w), embed, _addr(pos_embed),
                                         pos_grid, _addr(ln_w), _addr(ln_b), _addr(x), _stream(stream)))
+
+
+class Dense:
+    """Dense F32 / F16 weights in their GGML layout (samq_dense*), used with
+    F32 semantics.  kind DENSE_LINEAR: w is [n][k] (k = cin, n = cout);
+    DENSE_CONV: [cout][cin][kh][kw] (kw == kh in {1, 3}); DENSE_DECONV2X2:
+    [cin][cout][2][2]."""
+
+    def __init__(self, kind: int, w: np.ndarray, device: int = 0, stream=None):
+        w = np.ascontiguousarray(w)
+        if w.dtype == np.float32:
+            dtype = F32
+        elif w.dtype == np.float16:
+            dtype = F16
+        else:
+            raise TypeError("dense weights are float32 or float16")
+        if kind == DENSE_LINEAR:
+            cout, cin = w.shape
+            kw = kh = 1
+        elif kind == DENSE_CONV:
+            cout, cin, kh, kw = w.shape
+        elif kind == DENSE_DECONV2X2:
+            cin, cout, kh, kw = w.shape
+        else:
+            raise ValueError("unknown dense kind")
+        handle = ctypes.c_void_p()
+        _check(library().samq_dense_create_v1(device, dtype, kind, kw, kh, cin, cout, w.ctypes.data, w.nbytes,
+                                              _stream(stream), ctypes.byref(handle)))
+        self.handle = handle
+        self.kind, self.cin, self.cout, self.ks, self.device = kind, cin, cout, kw, device
+
+    def close(self):
+        if self.handle:
+            _check(library().samq_dense_destroy_v1(self.handle))
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+def dense_linear(w: Dense, x, m: int, ldx: int, bias, epilogue: int, y, ldy: int, stream=None):
+    """samq_dense_linear_v1: y = gelu?(x w^T + bias), F32 semantics."""
+    _check(library().samq_dense_linear_v1(w.handle, _addr(x), m, ldx, _addr(bias), epilogue, _addr(y), ldy,
+                                          _stream(stream)))
+
+
+def conv2d(w: Dense, x, width: int, height: int, bias, epilogue: int, y, stream=None):
+    """samq_conv2d_v1: NHWC convolution (stride 1, pad ks // 2) or 2x2 deconvolution."""
+    _check(library().samq_conv2d_v1(w.handle, _addr(x), width, height, _addr(bias), epilogue, _addr(y),
+                                    _stream(stream)))
+
+
+def maxpool2x2(x, width: int, height: int, channels: int, y, stream=None):
+    _check(library().samq_maxpool2x2_v1(_addr(x), width, height, channels, _addr(y), _stream(stream)))
+
+
+class Neck:
+    """The SimpleFPN neck (samq_neck_v1): layers maps each NECK_LAYERS name to
+    (Dense, bias device tensor)."""
+
+    def __init__(self, layers: dict):
+        self._keep = layers
+        vals = [1]
+        for name in NECK_LAYERS:
+            w, b = layers[name]
+            vals += [w.handle, _addr(b)]
+        self.desc = NeckDesc(*vals)
+
+
+def neck_forward(neck: Neck, x, grid_w: int, grid_h: int, outs, stream=None):
+    """samq_neck_forward_v1: the four NHWC feature maps of the ViT output x."""
+    arr = (_vp * 4)(*[_addr(o) for o in outs])
+    _check(library().samq_neck_forward_v1(ctypes.byref(neck.desc), _addr(x), grid_w, grid_h, arr, _stream(stream)))
