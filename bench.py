@@ -494,6 +494,11 @@ def main():
                 "measured_on": "the 4 block-linear shapes at M=5184 (f32 epilogue), 50 back-to-back launches "
                                "each between CUDA events on the launching stream"}
 
+    # The SimpleFPN neck (F32 semantics, dense.cu) on this image's 72 x 72 ViT
+    # output: a secondary figure beside the quantized backbone.
+    neck = neck_section(samq, torch, stream, args, max_over_ranks, pk)
+    samq.check(local, stream)
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cb = CpuBackbone(o)
@@ -528,6 +533,7 @@ def main():
             "qgemm": {"metric": QGEMM_METRIC, "workload": QGEMM_WORKLOAD, "value": qgemm_tops, "unit": "TOPS",
                       "steps": args.qgemm_steps, "ms_per_step": qgemm_ms / args.qgemm_steps,
                       "gpu_launches": args.qgemm_steps * 2 * len(LINEARS)},
+            "neck": neck,
         }
         print(json.dumps(line), flush=True)
     for w in weights:
@@ -537,7 +543,65 @@ def main():
         dist.destroy_process_group()
 
 
-PROFILE_EXTRA = ("attention_window", "attention_global", "text_fc2")
+NECK_MID, NECK_D = 512, 256
+
+
+def neck_flops(gw=GRID, gh=GRID):
+    """2 M N K of the neck's 11 dense products (vision.hpp:307-366)."""
+    t = gw * gh
+    e, mid, d = E, NECK_MID, NECK_D
+    macs = (t * e * 4 * mid + 4 * t * mid * 4 * d + 16 * t * d * d + 16 * t * 9 * d * d  # scale 0
+            + t * e * 4 * mid + 4 * t * mid * d + 4 * t * 9 * d * d                      # scale 1
+            + t * e * d + t * 9 * d * d                                                  # scale 2
+            + (gw // 2) * (gh // 2) * (e * d + 9 * d * d))                               # scale 3
+    return 2.0 * macs
+
+
+def make_neck(samq, torch, seed=0):
+    """Random-init neck weights (fan-in scaled normal), SAM 3 shapes."""
+    rng = np.random.default_rng(seed)
+    e, mid, d = E, NECK_MID, NECK_D
+    shapes = {"s0_deconv1": (samq.DENSE_DECONV2X2, (e, mid, 2, 2)), "s0_deconv2": (samq.DENSE_DECONV2X2, (mid, d, 2, 2)),
+              "s0_conv1x1": (samq.DENSE_CONV, (d, d, 1, 1)), "s0_conv3x3": (samq.DENSE_CONV, (d, d, 3, 3)),
+              "s1_deconv1": (samq.DENSE_DECONV2X2, (e, mid, 2, 2)), "s1_conv1x1": (samq.DENSE_CONV, (d, mid, 1, 1)),
+              "s1_conv3x3": (samq.DENSE_CONV, (d, d, 3, 3)), "s2_conv1x1": (samq.DENSE_CONV, (d, e, 1, 1)),
+              "s2_conv3x3": (samq.DENSE_CONV, (d, d, 3, 3)), "s3_conv1x1": (samq.DENSE_CONV, (d, e, 1, 1)),
+              "s3_conv3x3": (samq.DENSE_CONV, (d, d, 3, 3))}
+    layers = {}
+    for name, (kind, shape) in shapes.items():
+        fan_in = shape[0] if kind == samq.DENSE_DECONV2X2 else shape[1] * shape[2] * shape[3]
+        w = (rng.normal(size=shape) / np.sqrt(fan_in)).astype(np.float32)
+        b = rng.normal(0, 0.02, shape[1] if kind == samq.DENSE_DECONV2X2 else shape[0]).astype(np.float32)
+        layers[name] = (samq.Dense(kind, w), torch.from_numpy(b).cuda())
+    return samq.Neck(layers)
+
+
+def neck_section(samq, torch, stream, args, max_over_ranks, pk, steps=10):
+    neck = make_neck(samq, torch)
+    x = torch.from_numpy(np.random.default_rng(7).normal(0, 1, (M, E)).astype(np.float32)).cuda()
+    sizes = [4 * GRID, 2 * GRID, GRID, GRID // 2]
+    outs = [torch.empty(s * s * NECK_D, device="cuda") for s in sizes]
+    for _ in range(max(args.warmup, 3)):
+        samq.neck_forward(neck, x, GRID, GRID, outs, stream)
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record(stream)
+    for _ in range(steps):
+        samq.neck_forward(neck, x, GRID, GRID, outs, stream)
+    b.record(stream)
+    torch.cuda.synchronize()
+    ms = max_over_ranks(a.elapsed_time(b)) / steps
+    f32 = neck_flops() / (ms / 1e3) / 1e12
+    # Three TF32 MMAs per F32 product; the TF32 dense rate is taken as half
+    # the measured bf16 rate (the tensor cores' nominal TF32 : BF16 ratio).
+    tf32_peak = pk["bf16_tflops"] / 2
+    return {"metric": "SAM3 SimpleFPN neck, F32 semantics (ms per image, 72x72 grid)", "value": ms, "unit": "ms",
+            "higher_is_better": False, "steps": steps, "gflop_f32": neck_flops() / 1e9, "tflops_f32_equivalent": f32,
+            "tf32_mma_tflops": 3 * f32, "tf32_peak_estimate": tf32_peak, "frac_of_tf32_estimate": 3 * f32 / tf32_peak,
+            "gpu_launches_per_call": 17, "method": "three-term TF32 split on tcgen05 kind::tf32, segment sums in f32"}
+
+
+PROFILE_EXTRA = ("attention_window", "attention_global", "text_fc2", "neck_conv3x3")
 
 
 def run_profile_case(args):
@@ -549,7 +613,18 @@ def run_profile_case(args):
     samq.init(0)
     stream = torch.cuda.current_stream()
     launches = args.warmup + args.steps
-    if args.profile.startswith("attention"):
+    if args.profile == "neck_conv3x3":
+        # The neck's largest product: conv3x3 256 -> 256 at 288 x 288
+        # (scale 0), operand 2 x 85 MB (inputs larger than L2).
+        rng = np.random.default_rng(3)
+        w = samq.Dense(samq.DENSE_CONV, (rng.normal(size=(256, 256, 3, 3)) / 48).astype(np.float32))
+        x = torch.from_numpy(rng.normal(size=(288 * 288 * 256,)).astype(np.float32)).cuda()
+        y = torch.empty_like(x)
+        for _ in range(launches):
+            samq.conv2d(w, x, 288, 288, None, 0, y, stream)
+        torch.cuda.synchronize()
+        w.close()
+    elif args.profile.startswith("attention"):
         window = WINDOW if args.profile == "attention_window" else 0
         rng = np.random.default_rng(3)
         qkv = torch.from_numpy(rng.normal(0, 1, (M, 3 * E)).astype(np.float32)).cuda()

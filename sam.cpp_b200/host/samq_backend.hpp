@@ -208,6 +208,96 @@ private:
     std::vector<samq_vit_block_v1> blocks_;
 };
 
+// An F32 / F16 tensor the reference keeps unquantized (neck convolutions,
+// fusion / decoder linears), multiplied with F32 semantics.  `kind` is
+// SAMQ_DENSE_LINEAR (ne = [k, n]), SAMQ_DENSE_CONV (ne = [kw, kh, cin, cout])
+// or SAMQ_DENSE_DECONV2X2 (ne = [2, 2, cout, cin]); `data` is host memory.
+class DenseModule {
+public:
+    DenseModule(const SamqDriver& driver, int kind, int ggml_type, const std::int64_t ne[4], const void* data,
+                std::size_t bytes, cudaStream_t stream = nullptr)
+        : kind_(kind) {
+        const int type = ggml_type == 1 ? SAMQ_TYPE_F16 : SAMQ_TYPE_F32;
+        if (ggml_type != 0 && ggml_type != 1) throw std::runtime_error("dense tensor must be F32 or F16");
+        const bool deconv = kind == SAMQ_DENSE_DECONV2X2;
+        const bool linear = kind == SAMQ_DENSE_LINEAR;
+        const int kw = linear ? 1 : static_cast<int>(ne[0]), kh = linear ? 1 : static_cast<int>(ne[1]);
+        cin_ = linear ? ne[0] : (deconv ? ne[3] : ne[2]);
+        cout_ = linear ? ne[1] : (deconv ? ne[2] : ne[3]);
+        samq_require(samq_dense_create_v1(driver.cuda_device, type, kind, kw, kh, cin_, cout_, data, bytes, stream,
+                                          &dense_),
+                     "samq rejected the dense tensor");
+    }
+    DenseModule(const DenseModule&) = delete;
+    DenseModule& operator=(const DenseModule&) = delete;
+    DenseModule(DenseModule&& other) noexcept
+        : dense_(std::exchange(other.dense_, nullptr)), kind_(other.kind_), cin_(other.cin_), cout_(other.cout_) {}
+    ~DenseModule() {
+        if (dense_) samq_dense_destroy_v1(dense_);
+    }
+
+    std::int64_t in_channels() const { return cin_; }
+    std::int64_t out_channels() const { return cout_; }
+    const samq_dense* handle() const { return dense_; }
+
+    // LINEAR: Y[m][n] = epilogue(X[m][k] . W^T + bias) (ggml_mul_mat at GGML_PREC_F32).
+    void linear(const float* x, std::int64_t m, std::int64_t ldx, const float* bias, LinearEpilogue epilogue,
+                float* y, std::int64_t ldy, cudaStream_t stream) const {
+        samq_require(samq_dense_linear_v1(dense_, x, m, ldx, bias, static_cast<int>(epilogue), y, ldy, stream),
+                     "samq dense linear failed");
+    }
+
+    // CONV / DECONV2X2 over an NHWC image (sam3_conv_2d_s1_ph, sam3_deconv_2x2).
+    void conv(const float* x, int width, int height, const float* bias, LinearEpilogue epilogue, float* y,
+              cudaStream_t stream) const {
+        samq_require(samq_conv2d_v1(dense_, x, width, height, bias, static_cast<int>(epilogue), y, stream),
+                     "samq convolution failed");
+    }
+
+private:
+    samq_dense* dense_ = nullptr;
+    int kind_ = 0;
+    std::int64_t cin_ = 0, cout_ = 0;
+};
+
+// A dense tensor straight from a GGUF checkpoint (F32 / F16, GGML dimensions).
+inline DenseModule load_dense(const SamqDriver& driver, samq_io::GgufReader& reader, const std::string& name,
+                              int kind, cudaStream_t stream = nullptr) {
+    const samq_io::GgufTensor& t = reader.tensor(name);
+    std::int64_t ne[4] = {1, 1, 1, 1};
+    for (std::size_t i = 0; i < t.dimensions.size() && i < 4; ++i) ne[i] = t.dimensions[i];
+    const std::vector<std::uint8_t> bytes = reader.tensor_bytes(t);
+    return DenseModule(driver, kind, t.type, ne, bytes.data(), bytes.size(), stream);
+}
+
+// The SimpleFPN neck of one path (src/models/sam3/vision.hpp:307-366).  Layer
+// order and names follow samq_neck_v1 (tensors.hpp:131-160).
+class SimpleFpnNeck {
+public:
+    static constexpr int kLayers = 11;
+    // Device biases per layer, in the order of samq_neck_v1.
+    SimpleFpnNeck(std::vector<DenseModule> layers, const std::vector<const float*>& biases)
+        : layers_(std::move(layers)) {
+        if (layers_.size() != kLayers || biases.size() != kLayers)
+            throw std::runtime_error("the neck has 11 weighted layers");
+        const samq_dense* w[kLayers];
+        for (int i = 0; i < kLayers; ++i) w[i] = layers_[i].handle();
+        desc_ = samq_neck_v1{1,          w[0], biases[0], w[1], biases[1], w[2], biases[2], w[3], biases[3],
+                             w[4],       biases[4], w[5], biases[5], w[6], biases[6], w[7], biases[7],
+                             w[8],       biases[8], w[9], biases[9], w[10], biases[10]};
+    }
+
+    // x: device [grid_h * grid_w][E] f32 (the backbone output); out[i]: the
+    // four NHWC maps (4x, 2x, 1x, 0.5x).
+    void forward(const float* x, int grid_w, int grid_h, float* const out[4], cudaStream_t stream) const {
+        samq_require(samq_neck_forward_v1(&desc_, x, grid_w, grid_h, out, stream), "samq neck failed");
+    }
+
+private:
+    std::vector<DenseModule> layers_;
+    samq_neck_v1 desc_{};
+};
+
 // Post-compute device findings (range / timeout), as the reference's RHS check raises them.
 inline void samq_check_device(const SamqDriver& driver, cudaStream_t stream) {
     samq_require(samq_check_v1(driver.cuda_device, stream), "samq device check failed");

@@ -110,3 +110,49 @@ def test_cpp_vit_backbone_on_gpu(tmp_path, oracle):
     rel = float(np.abs(d_gpu - d_ref).max() / np.abs(d_ref).max())
     # Prefix error (f16 convolution operands) and block error add up here.
     assert cos >= 0.9995 and rel <= 3e-2, (cos, rel)
+
+
+def test_neck_host_program_compiles(tmp_path):
+    compile_program("test_neck.cpp", tmp_path / "test_neck")
+
+
+@pytest.mark.gpu
+def test_cpp_neck_on_gpu(tmp_path, oracle):
+    """SimpleFpnNeck::forward from C++, its 11 F32 layers and biases loaded from
+    a gguf-py checkpoint by the host GGUF reader (reduced widths E = 64, mid =
+    D = 32), against the f64 oracle at a 6 x 4 grid."""
+    import gguf
+    rng = np.random.default_rng(31)
+    gw, gh, E, mid, D = 6, 4, 64, 32, 32
+    shapes = {"0.dconv_2x2_0": (E, mid, 2, 2), "0.dconv_2x2_1": (mid, D, 2, 2), "0.conv_1x1": (D, D, 1, 1),
+              "0.conv_3x3": (D, D, 3, 3), "1.dconv_2x2": (E, mid, 2, 2), "1.conv_1x1": (D, mid, 1, 1),
+              "1.conv_3x3": (D, D, 3, 3), "2.conv_1x1": (D, E, 1, 1), "2.conv_3x3": (D, D, 3, 3),
+              "3.conv_1x1": (D, E, 1, 1), "3.conv_3x3": (D, D, 3, 3)}
+    keys = ("s0_deconv1", "s0_deconv2", "s0_conv1x1", "s0_conv3x3", "s1_deconv1", "s1_conv1x1", "s1_conv3x3",
+            "s2_conv1x1", "s2_conv3x3", "s3_conv1x1", "s3_conv3x3")
+    writer = gguf.GGUFWriter(str(tmp_path / "weights.gguf"), "sam3")
+    layers = {}
+    for key, (name, shape) in zip(keys, shapes.items()):
+        deconv = "dconv" in name
+        fan_in = shape[0] if deconv else shape[1] * shape[2] * shape[3]
+        w = (rng.normal(size=shape) / np.sqrt(fan_in)).astype(np.float32)
+        b = rng.normal(0, 0.02, shape[1] if deconv else shape[0]).astype(np.float32)
+        writer.add_tensor(f"neck.det.{name}.weight", w)
+        writer.add_tensor(f"neck.det.{name}.bias", b)
+        layers[key] = (w, b)
+    writer.write_header_to_file()
+    writer.write_kv_data_to_file()
+    writer.write_tensors_to_file()
+    writer.close()
+    x = rng.normal(size=(gh, gw, E)).astype(np.float32)
+    x.tofile(tmp_path / "x.bin")
+    (tmp_path / "meta.txt").write_text(f"{gw} {gh} {E} {D}\n")
+    exe = tmp_path / "test_neck"
+    compile_program("test_neck.cpp", exe)
+    run = subprocess.run([str(exe), str(tmp_path)], capture_output=True, text=True, timeout=120)
+    assert run.returncode == 0, run.stdout + run.stderr
+    refs = oracle.neck(x, layers)
+    for i, ref in enumerate(refs):
+        out = np.fromfile(tmp_path / f"out{i}.bin", dtype=np.float32).reshape(ref.shape)
+        err = np.abs(out - ref).max() / np.abs(ref).max()
+        assert err <= 2e-6, (i, err)
