@@ -498,6 +498,9 @@ def main():
     # output: a secondary figure beside the quantized backbone.
     neck = neck_section(samq, torch, stream, args, max_over_ranks, pk)
     samq.check(local, stream)
+    # Config 5's batching: the same backbone over 8 images per GPU per step.
+    batch8 = batch_section(samq, torch, stream, args, max_over_ranks, blocks, prefix, world, rank)
+    samq.check(local, stream)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -534,6 +537,7 @@ def main():
                       "steps": args.qgemm_steps, "ms_per_step": qgemm_ms / args.qgemm_steps,
                       "gpu_launches": args.qgemm_steps * 2 * len(LINEARS)},
             "neck": neck,
+            "batch8": batch8,
         }
         print(json.dumps(line), flush=True)
     for w in weights:
@@ -541,6 +545,37 @@ def main():
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
+
+
+def batch_section(samq, torch, stream, args, max_over_ranks, blocks, prefix, world, rank, batch=8, steps=4):
+    """BASELINE config 5's per-GPU batches: 8 seeded images per step, each
+    through samq_vit_prefix_v1, then every block once for the whole batch
+    (samq_vit_block_forward_batch_v1)."""
+    rng = np.random.default_rng(900 + rank)
+    imgs = torch.from_numpy(((rng.random((batch, 3, IMAGE, IMAGE), dtype=np.float32) - 0.5) / 0.5)).cuda()
+    xb = torch.empty((batch, M, E), dtype=torch.float32, device="cuda")
+
+    def fwd():
+        for b in range(batch):
+            samq.vit_prefix(imgs[b], IMAGE, IMAGE, PATCH, prefix["patch_w"], E, prefix["pos"], POS_GRID,
+                            prefix["ln_w"], prefix["ln_b"], xb[b], stream)
+        for blk in blocks:
+            samq.vit_block_forward(blk, xb, GRID, GRID, stream, batch=batch)
+
+    for _ in range(2):
+        fwd()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record(stream)
+    for _ in range(steps):
+        fwd()
+    b.record(stream)
+    torch.cuda.synchronize()
+    ms = max_over_ranks(a.elapsed_time(b))
+    return {"metric": "SAM3 vision backbone images/s, per-GPU batch of 8 (config 5's batching)",
+            "value": steps * batch * world / (ms / 1e3), "unit": "images/s", "batch_per_gpu": batch, "steps": steps,
+            "ms_per_step": ms / steps, "features_finite": bool(torch.isfinite(xb).all().item()),
+            "gpu_launches": steps * batch * 4 + steps * DEPTH * 7}
 
 
 NECK_MID, NECK_D = 512, 256

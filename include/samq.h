@@ -196,6 +196,13 @@ typedef struct samq_vit_block_v1 {
 samq_status samq_vit_block_forward_v1(const samq_vit_block_v1* block, float* x, int grid_w, int grid_h,
                                       void* stream);
 
+/* The same block over `batch` images at once (config 5's per-GPU batches):
+ * x is [batch][grid_h * grid_w][E], image after image.  Each image's result is
+ * bit-identical to samq_vit_block_forward_v1 on that image alone; one call
+ * launches the block's kernels once for the whole batch. */
+samq_status samq_vit_block_forward_batch_v1(const samq_vit_block_v1* block, float* x, int batch, int grid_w,
+                                            int grid_h, void* stream);
+
 /* Backbone prefix (src/models/sam3/vision.hpp:252-282): patch embedding (an
  * unpadded patch x patch convolution without bias, weight [E][3][patch][patch]
  * f32), + pos_embed ([pos_grid][pos_grid][E] f32, tiled over the token grid),

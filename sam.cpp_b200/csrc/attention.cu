@@ -47,9 +47,10 @@ struct Geometry {
     int group_n;  // tokens per group
 };
 
-// Raster token of position n of group g.
+// Raster token of position n of group g (global blocks: one group per image
+// of a batch, stored image after image).
 __device__ __forceinline__ int group_token(const Geometry& geo, int g, int n) {
-    if (geo.window == 0) return n;
+    if (geo.window == 0) return g * geo.group_n + n;
     const int per_row = geo.grid_w / geo.window;
     const int wy = g / per_row, wx = g % per_row;
     const int ly = n / geo.window, lx = n % geo.window;
@@ -456,10 +457,13 @@ attention_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
     }
 }
 
-Geometry make_geometry(int grid_w, int grid_h, int heads, int window) {
-    Geometry geo{grid_w, grid_h, heads, window, 1, grid_w * grid_h};
+// A batch of images is one grid of grid_w x (batch * grid_h) tokens (images
+// stacked vertically): windows never straddle two images since the window
+// divides grid_h; a global block attends within each image (one group each).
+Geometry make_geometry(int grid_w, int grid_h, int heads, int window, int batch) {
+    Geometry geo{grid_w, grid_h * batch, heads, window, batch, grid_w * grid_h};
     if (window > 0) {
-        geo.groups = (grid_w / window) * (grid_h / window);
+        geo.groups = (grid_w / window) * (grid_h * batch / window);
         geo.group_n = window * window;
     }
     return geo;
@@ -472,9 +476,9 @@ size_t attention_scratch_bytes(int grid_w, int grid_h, int heads) {
 }
 
 void launch_attention_packed(const __half* qp, const __half* kp, const __half* vt, int grid_w, int grid_h, int heads,
-                             int window, float* out, __half* out_h, int64_t ldo, DeviceState& state,
+                             int window, int batch, float* out, __half* out_h, int64_t ldo, DeviceState& state,
                              cudaStream_t stream) {
-    const Geometry geo = make_geometry(grid_w, grid_h, heads, window);
+    const Geometry geo = make_geometry(grid_w, grid_h, heads, window, batch);
     const uint64_t gh = static_cast<uint64_t>(geo.groups) * heads;
     CUtensorMap tq, tk, tv;
     encode_tensor_map_3d(&tq, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, qp, kHeadDim, geo.group_n, gh, kHeadDim * 2,
@@ -496,14 +500,14 @@ void launch_attention_packed(const __half* qp, const __half* kp, const __half* v
 void launch_vit_attention(const float* qkv, int64_t ldq, int grid_w, int grid_h, int heads, int window,
                           const float* freqs, float* out, int64_t ldo, void* packed, DeviceState& state,
                           cudaStream_t stream) {
-    const Geometry geo = make_geometry(grid_w, grid_h, heads, window);
+    const Geometry geo = make_geometry(grid_w, grid_h, heads, window, 1);
     const int64_t per = static_cast<int64_t>(geo.groups) * heads * geo.group_n * kHeadDim;
     __half* qp = static_cast<__half*>(packed);
     __half* kp = qp + per;
     __half* vt = kp + per;
     launch_pdl(rope_pack_kernel, dim3((geo.group_n + 63) / 64, heads, geo.groups), dim3(256), 0, stream,
                "rope_pack_kernel launch", qkv, ldq, freqs, geo, qp, kp, vt);
-    launch_attention_packed(qp, kp, vt, grid_w, grid_h, heads, window, out, nullptr, ldo, state, stream);
+    launch_attention_packed(qp, kp, vt, grid_w, grid_h, heads, window, 1, out, nullptr, ldo, state, stream);
 }
 
 }  // namespace samq

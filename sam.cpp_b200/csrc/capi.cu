@@ -484,9 +484,9 @@ samq_status samq_vit_attention_v1(const float* qkv, int64_t ldq, int grid_w, int
     });
 }
 
-samq_status samq_vit_block_forward_v1(const samq_vit_block_v1* block, float* x, int grid_w, int grid_h,
-                                      void* stream_ptr) {
-    return guarded([&] {
+static void vit_block_forward(const samq_vit_block_v1* block, float* x, int batch, int grid_w, int grid_h,
+                              void* stream_ptr) {
+    {
         require(block != nullptr && block->version == 1, "block descriptor missing or not version 1");
         const samq_vit_block_v1& b = *block;
         require(b.qkv && b.proj && b.fc1 && b.fc2, "null weight handle");
@@ -498,6 +498,8 @@ samq_status samq_vit_block_forward_v1(const samq_vit_block_v1* block, float* x, 
         require(mlp % 32 == 0, "MLP width must be a multiple of 32");
         require(grid_w > 0 && grid_h > 0 && static_cast<int64_t>(grid_w) * grid_h <= (int64_t(1) << 20),
                 "grid out of range");
+        require(batch > 0 && static_cast<int64_t>(batch) * grid_w * grid_h <= (int64_t(1) << 22),
+                "batch out of range");
         const int window = b.window;
         require(window == 0 || (window > 0 && grid_w % window == 0 && grid_h % window == 0),
                 "window must divide the grid (or be 0 for global attention)");
@@ -512,7 +514,7 @@ samq_status samq_vit_block_forward_v1(const samq_vit_block_v1* block, float* x, 
         for (const samq_weights* w : handles) require(w->device == device, "weight handle belongs to another device");
         DeviceState& state = device_state(device);
         cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
-        const int64_t tokens = static_cast<int64_t>(grid_w) * grid_h;
+        const int64_t tokens = static_cast<int64_t>(batch) * grid_w * grid_h;
         Scratch& scratch = scratch_for(state, stream, vit_block_scratch_bytes(tokens, E, mlp));
         VitBlockArgs args;
         args.window = window;
@@ -529,9 +531,19 @@ samq_status samq_vit_block_forward_v1(const samq_vit_block_v1* block, float* x, 
         args.fc1_b = b.fc1_b;
         args.fc2_b = b.fc2_b;
         args.freqs = b.freqs_cis;
-        launch_vit_block(args, x, grid_w, grid_h, scratch.ptr, state, stream);
+        launch_vit_block(args, x, batch, grid_w, grid_h, scratch.ptr, state, stream);
         for (const samq_weights* w : handles) const_cast<samq_weights*>(w)->launches.fetch_add(1);
-    });
+    }
+}
+
+samq_status samq_vit_block_forward_v1(const samq_vit_block_v1* block, float* x, int grid_w, int grid_h,
+                                      void* stream_ptr) {
+    return guarded([&] { vit_block_forward(block, x, 1, grid_w, grid_h, stream_ptr); });
+}
+
+samq_status samq_vit_block_forward_batch_v1(const samq_vit_block_v1* block, float* x, int batch, int grid_w,
+                                            int grid_h, void* stream_ptr) {
+    return guarded([&] { vit_block_forward(block, x, batch, grid_w, grid_h, stream_ptr); });
 }
 
 samq_status samq_vit_prefix_v1(const float* image, int width, int height, int patch, const float* patch_w,

@@ -149,8 +149,9 @@ void launch_vit_attention(const float* qkv, int64_t ldq, int grid_w, int grid_h,
 // [group * heads + head][group_n][64]; V^T [group * heads + head][64][group_n]),
 // output in raster token order: f32 `out`, or, when out_h is given, the
 // Q8_1-staged f16 operand of the proj linear.
+// `batch` images of grid_w x grid_h tokens each, stored image after image.
 void launch_attention_packed(const __half* q, const __half* k, const __half* vt, int grid_w, int grid_h, int heads,
-                             int window, float* out, __half* out_h, int64_t ldo, DeviceState& state,
+                             int window, int batch, float* out, __half* out_h, int64_t ldo, DeviceState& state,
                              cudaStream_t stream);
 
 // K2 gemm.cu
@@ -206,8 +207,9 @@ struct VitBlockArgs {
     const float* freqs = nullptr;
 };
 size_t vit_block_scratch_bytes(int64_t tokens, int64_t embed, int64_t mlp);
-void launch_vit_block(const VitBlockArgs& blk, float* x, int grid_w, int grid_h, void* scratch, DeviceState& state,
-                      cudaStream_t stream);
+// x: `batch` images of grid_w x grid_h tokens, image after image.
+void launch_vit_block(const VitBlockArgs& blk, float* x, int batch, int grid_w, int grid_h, void* scratch,
+                      DeviceState& state, cudaStream_t stream);
 void launch_ln_stage(const float* x, int64_t rows, int64_t embed, int grid_w, int window, const float* w,
                      const float* b, __half* a, DeviceState& state, cudaStream_t stream);
 size_t vit_prefix_scratch_bytes(int64_t tokens, int64_t embed, int patch);

@@ -223,12 +223,15 @@ void launch_ln_stage(const float* x, int64_t rows, int64_t embed, int grid_w, in
     });
 }
 
-void launch_vit_block(const VitBlockArgs& blk, float* x, int grid_w, int grid_h, void* scratch, DeviceState& state,
-                      cudaStream_t stream) {
+void launch_vit_block(const VitBlockArgs& blk, float* x, int batch, int grid_w, int grid_h, void* scratch,
+                      DeviceState& state, cudaStream_t stream) {
     const int64_t embed = blk.qkv->k, mlp = blk.fc1->n;
     const int heads = static_cast<int>(embed / 64);
-    const int64_t tokens = static_cast<int64_t>(grid_w) * grid_h;
-    const int group_n = blk.window > 0 ? blk.window * blk.window : static_cast<int>(tokens);
+    // A batch is one grid of batch * grid_h rows (images stacked): the LN1
+    // window gather and the windowed attention see one tall grid, a global
+    // block one attention group per image.
+    const int64_t tokens = static_cast<int64_t>(batch) * grid_w * grid_h;
+    const int group_n = blk.window > 0 ? blk.window * blk.window : grid_w * grid_h;
     auto align = [](uintptr_t p) { return (p + 255) & ~uintptr_t(255); };
     uintptr_t cursor = align(reinterpret_cast<uintptr_t>(scratch));
     __half* a1 = reinterpret_cast<__half*>(cursor);
@@ -251,7 +254,7 @@ void launch_vit_block(const VitBlockArgs& blk, float* x, int grid_w, int grid_h,
     ep.heads = heads;
     ep.group_n = group_n;
     launch_gemm(a1, embed, blk.qkv->operand, tokens, 3 * embed, embed, ep, state, stream);
-    launch_attention_packed(q, k, vt, grid_w, grid_h, heads, blk.window, nullptr, a1, embed, state, stream);
+    launch_attention_packed(q, k, vt, grid_w, grid_h, heads, blk.window, batch, nullptr, a1, embed, state, stream);
     ep = Epilogue{};
     ep.mode = kOutF32Residual;
     ep.bias = blk.proj_b;

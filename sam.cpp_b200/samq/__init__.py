@@ -87,6 +87,7 @@ SIGNATURES = {
     "samq_linear_static_v1": (_i32, [_vp, _vp, _i64, _i64, _vp, _i32, _vp, _i64, _vp]),
     "samq_vit_attention_v1": (_i32, [_vp, _i64, _i32, _i32, _i32, _i32, _i32, _vp, _vp, _i64, _vp]),
     "samq_vit_block_forward_v1": (_i32, [ctypes.POINTER(VitBlockDesc), _vp, _i32, _i32, _vp]),
+    "samq_vit_block_forward_batch_v1": (_i32, [ctypes.POINTER(VitBlockDesc), _vp, _i32, _i32, _i32, _vp]),
     "samq_vit_prefix_v1": (_i32, [_vp, _i32, _i32, _i32, _vp, _i64, _vp, _i32, _vp, _vp, _vp, _vp]),
     "samq_dense_create_v1": (_i32, [_i32, _i32, _i32, _i32, _i32, _i64, _i64, _vp, _sz, _vp, ctypes.POINTER(_vp)]),
     "samq_dense_destroy_v1": (_i32, [_vp]),
@@ -272,9 +273,15 @@ class VitBlock:
                                  _addr(fc2_b), _addr(freqs))
 
 
-def vit_block_forward(block: VitBlock, x, grid_w: int, grid_h: int, stream=None):
-    """samq_vit_block_forward_v1: one pre-LN ViT block in place on x [tokens][E] f32."""
-    _check(library().samq_vit_block_forward_v1(ctypes.byref(block.desc), _addr(x), grid_w, grid_h, _stream(stream)))
+def vit_block_forward(block: VitBlock, x, grid_w: int, grid_h: int, stream=None, batch: int = 1):
+    """samq_vit_block_forward_v1 (batch 1) / samq_vit_block_forward_batch_v1: one
+    pre-LN ViT block in place on x [batch][tokens][E] f32."""
+    if batch == 1:
+        _check(library().samq_vit_block_forward_v1(ctypes.byref(block.desc), _addr(x), grid_w, grid_h,
+                                                   _stream(stream)))
+    else:
+        _check(library().samq_vit_block_forward_batch_v1(ctypes.byref(block.desc), _addr(x), batch, grid_w, grid_h,
+                                                         _stream(stream)))
 
 
 def vit_prefix(image, width: int, height: int, patch: int, patch_w, embed: int, pos_embed, pos_grid: int, ln_w, ln_b,

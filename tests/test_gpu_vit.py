@@ -154,3 +154,23 @@ def test_vit_block_rejects_bad_shapes():
     x = torch.zeros((50 * 50, E), device="cuda")
     with pytest.raises(samq.SamqError):
         samq.vit_block_forward(block, x, 50, 50)  # 24 does not divide 50
+
+
+@pytest.mark.parametrize("window,grid", [(24, 48), (0, 24)])
+def test_vit_block_batch_matches_single_images(window, grid):
+    """samq_vit_block_forward_batch_v1 on 3 images (windowed: one grid of
+    stacked images; global: one attention group per image) gives each image
+    the bits of samq_vit_block_forward_v1 on that image alone."""
+    rng = np.random.default_rng(40 + window)
+    positions = window * window if window else grid * grid
+    host, block = make_block(rng, window, positions)
+    batch = 3
+    xs = rng.standard_normal((batch, grid * grid, E)).astype(np.float32)
+    xd = torch.from_numpy(xs).cuda()
+    samq.vit_block_forward(block, xd, grid, grid, batch=batch)
+    samq.check(0)
+    got = xd.cpu().numpy()
+    for b in range(batch):
+        np.testing.assert_array_equal(got[b], run_block(block, xs[b], grid))
+    cos, rel = compare(got[1], o.vit_block(xs[1], host, grid, grid), xs[1])
+    assert cos >= COS_MIN and rel <= DELTA_REL_MAX, (cos, rel)
