@@ -190,14 +190,25 @@ public:
     // image: device [3][height][width] f32, normalized; x: device [tokens][E] f32 (receives the
     // backbone output, the [E, W, H, 1] tensor the neck consumes).
     void encode(const float* image, int width, int height, float* x, cudaStream_t stream) const {
+        encode_batch(image, 1, width, height, x, stream);
+    }
+
+    // `batch` images ([batch][3][height][width], consecutive) into x
+    // ([batch][tokens][E]); every block runs once for the whole batch.
+    void encode_batch(const float* images, int batch, int width, int height, float* x, cudaStream_t stream) const {
         if (prefix_.patch_embed_w == nullptr) throw std::runtime_error("ViT prefix tensors were not set");
-        samq_require(samq_vit_prefix_v1(image, width, height, prefix_.patch, prefix_.patch_embed_w, embed_,
-                                        prefix_.pos_embed, prefix_.pos_grid, prefix_.ln_pre_w, prefix_.ln_pre_b, x,
-                                        stream),
-                     "samq ViT prefix failed");
         const int grid_w = width / prefix_.patch, grid_h = height / prefix_.patch;
+        const std::int64_t tokens = static_cast<std::int64_t>(grid_w) * grid_h;
+        for (int i = 0; i < batch; ++i)
+            samq_require(samq_vit_prefix_v1(images + static_cast<std::int64_t>(i) * 3 * width * height, width, height,
+                                            prefix_.patch, prefix_.patch_embed_w, embed_, prefix_.pos_embed,
+                                            prefix_.pos_grid, prefix_.ln_pre_w, prefix_.ln_pre_b,
+                                            x + static_cast<std::int64_t>(i) * tokens * embed_, stream),
+                         "samq ViT prefix failed");
         for (const samq_vit_block_v1& b : blocks_)
-            samq_require(samq_vit_block_forward_v1(&b, x, grid_w, grid_h, stream), "samq ViT block failed");
+            samq_require(batch == 1 ? samq_vit_block_forward_v1(&b, x, grid_w, grid_h, stream)
+                                    : samq_vit_block_forward_batch_v1(&b, x, batch, grid_w, grid_h, stream),
+                         "samq ViT block failed");
     }
 
 private:
