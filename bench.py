@@ -592,8 +592,8 @@ def neck_flops(gw=GRID, gh=GRID):
     return 2.0 * macs
 
 
-def make_neck(samq, torch, seed=0):
-    """Random-init neck weights (fan-in scaled normal), SAM 3 shapes."""
+def make_neck(samq, torch, device, seed=0):
+    """Random-init neck weights (fan-in scaled normal), SAM 3 shapes, on `device`."""
     rng = np.random.default_rng(seed)
     e, mid, d = E, NECK_MID, NECK_D
     shapes = {"s0_deconv1": (samq.DENSE_DECONV2X2, (e, mid, 2, 2)), "s0_deconv2": (samq.DENSE_DECONV2X2, (mid, d, 2, 2)),
@@ -607,12 +607,12 @@ def make_neck(samq, torch, seed=0):
         fan_in = shape[0] if kind == samq.DENSE_DECONV2X2 else shape[1] * shape[2] * shape[3]
         w = (rng.normal(size=shape) / np.sqrt(fan_in)).astype(np.float32)
         b = rng.normal(0, 0.02, shape[1] if kind == samq.DENSE_DECONV2X2 else shape[0]).astype(np.float32)
-        layers[name] = (samq.Dense(kind, w), torch.from_numpy(b).cuda())
+        layers[name] = (samq.Dense(kind, w, device=device), torch.from_numpy(b).cuda())
     return samq.Neck(layers)
 
 
 def neck_section(samq, torch, stream, args, max_over_ranks, pk, steps=10):
-    neck = make_neck(samq, torch)
+    neck = make_neck(samq, torch, torch.cuda.current_device())
     x = torch.from_numpy(np.random.default_rng(7).normal(0, 1, (M, E)).astype(np.float32)).cuda()
     sizes = [4 * GRID, 2 * GRID, GRID, GRID // 2]
     outs = [torch.empty(s * s * NECK_D, device="cuda") for s in sizes]

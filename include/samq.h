@@ -251,7 +251,9 @@ samq_status samq_dense_create_v1(int device, int type, int kind, int kw, int kh,
                                  const void* data, size_t bytes, void* stream, samq_dense** out);
 samq_status samq_dense_destroy_v1(samq_dense* weights);
 
-/* Y[m][n] = X[m][k] W[n][k]^T (+ bias[n]) (then erf-GELU), F32 semantics;
+/* Dense calls run on the current device, which must own the handles (else
+ * SAMQ_ERR_INVALID_ARGUMENT).
+ * Y[m][n] = X[m][k] W[n][k]^T (+ bias[n]) (then erf-GELU), F32 semantics;
  * `weights` of kind LINEAR.  ldx % 4 == 0, ldy % 4 == 0, pointers 16-byte
  * aligned.  Replaces ggml_mul_mat on F32/F16 weights at GGML_PREC_F32. */
 samq_status samq_dense_linear_v1(const samq_dense* weights, const float* x, int64_t m, int64_t ldx,

@@ -642,7 +642,7 @@ samq_status samq_dense_linear_v1(const samq_dense* w, const float* x, int64_t m,
         require(ldy >= w->n && ldy % 4 == 0, "output row stride must be >= n and a multiple of 4 floats");
         if (m == 0) return;
         require(x != nullptr && y != nullptr && aligned16(x) && aligned16(y), "pointers must be 16-byte aligned");
-        DeviceGuard guard(w->device);
+        require(w->device == current_device(), "dense handle belongs to another device");
         DeviceState& state = device_state(w->device);
         cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
         const size_t half = static_cast<size_t>(m * w->k);
@@ -662,7 +662,7 @@ samq_status samq_conv2d_v1(const samq_dense* w, const float* x, int width, int h
         require(width > 0 && height > 0 && int64_t(width) * height <= (int64_t(1) << 26), "image size out of range");
         require(epilogue == SAMQ_EPILOGUE_NONE || epilogue == SAMQ_EPILOGUE_GELU_ERF, "unknown epilogue");
         require(x != nullptr && y != nullptr && aligned16(x) && aligned16(y), "pointers must be 16-byte aligned");
-        DeviceGuard guard(w->device);
+        require(w->device == current_device(), "dense handle belongs to another device");
         DeviceState& state = device_state(w->device);
         cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
         const int64_t pixels = int64_t(width) * height;
@@ -695,9 +695,14 @@ samq_status samq_neck_forward_v1(const samq_neck_v1* neck, const float* x, int g
         require(grid_w >= 2 && grid_h >= 2 && int64_t(grid_w) * grid_h <= (int64_t(1) << 20), "grid out of range");
         require(x != nullptr && aligned16(x) && out != nullptr, "null or misaligned pointer");
         for (int i = 0; i < 4; ++i) require(out[i] != nullptr && aligned16(out[i]), "null or misaligned output");
-        const int device = neck->s0_deconv1 ? neck->s0_deconv1->device : -1;
-        require(device >= 0, "neck weight missing");
-        DeviceGuard guard(device);
+        const int device = current_device();
+        const samq_dense* layers[] = {neck->s0_deconv1, neck->s0_deconv2, neck->s0_conv1x1, neck->s0_conv3x3,
+                                      neck->s1_deconv1, neck->s1_conv1x1, neck->s1_conv3x3, neck->s2_conv1x1,
+                                      neck->s2_conv3x3, neck->s3_conv1x1, neck->s3_conv3x3};
+        for (const samq_dense* w : layers) {
+            require(w != nullptr, "neck weight missing");
+            require(w->device == device, "neck weight belongs to another device");
+        }
         DeviceState& state = device_state(device);
         cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
         Scratch& scratch = scratch_for(state, stream, neck_scratch_bytes(*neck, grid_w, grid_h));
