@@ -198,3 +198,17 @@ def test_neck_full_grid_low_scales(samq):
     s3 = o.conv2d_nhwc(o.conv2d_nhwc(o.maxpool2x2_nhwc(x), *host["s3_conv1x1"]), *host["s3_conv3x3"])
     check_close(outs[2], s2, rel=2e-6)
     check_close(outs[3], s3, rel=2e-6)
+
+
+def test_neck_odd_grid(samq):
+    """A 7 x 5 grid: the 0.5x scale floors to 3 x 2 (ggml_pool_2d without
+    padding), the other maps are 28 x 20, 14 x 10 and 7 x 5."""
+    rng = np.random.default_rng(23)
+    host, neck = make_neck(samq, rng, E=256, mid=128, D=64)
+    gw, gh = 7, 5
+    x = rng.normal(size=(gh, gw, 256)).astype(np.float32)
+    outs = run_neck(samq, neck, x.reshape(-1, 256), gw, gh, D=64)
+    refs = o.neck(x, host)
+    assert outs[3].shape == (2, 3, 64)
+    for out, ref in zip(outs, refs):
+        check_close(out, ref, rel=2e-6)
