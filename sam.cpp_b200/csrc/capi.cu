@@ -636,7 +636,7 @@ samq_status samq_dense_linear_v1(const samq_dense* w, const float* x, int64_t m,
                                  int epilogue, float* y, int64_t ldy, void* stream_ptr) {
     return guarded([&] {
         require(w != nullptr && w->kind == SAMQ_DENSE_LINEAR, "weights must be a dense LINEAR handle");
-        require(m >= 0 && m <= (int64_t(1) << 31), "row count out of range");
+        require(m >= 0 && m <= (int64_t(1) << 30), "row count out of range");
         require(epilogue == SAMQ_EPILOGUE_NONE || epilogue == SAMQ_EPILOGUE_GELU_ERF, "unknown epilogue");
         require(ldx >= w->k && ldx % 4 == 0, "input row stride must be >= k and a multiple of 4 floats");
         require(ldy >= w->n && ldy % 4 == 0, "output row stride must be >= n and a multiple of 4 floats");
