@@ -94,3 +94,17 @@ def test_last_error_is_thread_local(samq):
     t.join()
     assert seen == [b""]
     assert lib.samq_last_error_v1() != b""
+
+
+def test_invalid_block_arguments_are_rejected(samq):
+    """The ViT block entries check the descriptor before any device work."""
+    lib = samq.library()
+    x = ctypes.c_void_p(16)
+    rc = lib.samq_vit_block_forward_v1(None, x, 72, 72, None)
+    assert rc == 1 and b"version 1" in lib.samq_last_error_v1()
+    rc = lib.samq_vit_block_forward_batch_v1(None, x, 8, 72, 72, None)
+    assert rc == 1 and b"version 1" in lib.samq_last_error_v1()
+    desc = samq.VitBlockDesc()
+    desc.version = 2
+    rc = lib.samq_vit_block_forward_batch_v1(ctypes.byref(desc), x, 8, 72, 72, None)
+    assert rc == 1 and b"version 1" in lib.samq_last_error_v1()
