@@ -636,7 +636,7 @@ def neck_section(samq, torch, stream, args, max_over_ranks, pk, steps=10):
             "gpu_launches_per_call": 17, "method": "three-term TF32 split on tcgen05 kind::tf32, segment sums in f32"}
 
 
-PROFILE_EXTRA = ("attention_window", "attention_global", "text_fc2", "neck_conv3x3")
+PROFILE_EXTRA = ("attention_window", "attention_global", "text_fc2", "neck_conv3x3", "vit_block")
 
 
 def run_profile_case(args):
@@ -648,7 +648,17 @@ def run_profile_case(args):
     samq.init(0)
     stream = torch.cuda.current_stream()
     launches = args.warmup + args.steps
-    if args.profile == "neck_conv3x3":
+    if args.profile == "vit_block":
+        # One windowed ViT block (block 0 of the backbone) on a 72 x 72 grid,
+        # every launch of it: the LayerNorm-staging, GEMM and attention
+        # kernels in their in-block modes.
+        blocks, _, keep = make_backbone(samq, o, torch, 0, 0)
+        x = torch.from_numpy(np.random.default_rng(3).normal(0, 1, (M, E)).astype(np.float32)).cuda()
+        for _ in range(launches):
+            samq.vit_block_forward(blocks[0], x, GRID, GRID, stream)
+        torch.cuda.synchronize()
+        del keep
+    elif args.profile == "neck_conv3x3":
         # The neck's largest product: conv3x3 256 -> 256 at 288 x 288
         # (scale 0), operand 2 x 85 MB (inputs larger than L2).
         rng = np.random.default_rng(3)
