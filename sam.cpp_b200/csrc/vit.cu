@@ -170,18 +170,27 @@ __global__ void __launch_bounds__(256) im2col_kernel(const float* __restrict__ i
                                                      __half* __restrict__ a) {
     pdl_wait();
     pdl_trigger();
+    // One thread per 8 consecutive columns of a row: a 16-byte store (ld is a
+    // multiple of 64, the row starts 16-byte aligned).
+    const int groups = ld / 8;
     const int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-    if (idx >= tokens * ld) return;
-    const int64_t t = idx / ld;
-    const int col = static_cast<int>(idx - t * ld);
-    float v = 0.0f;
-    if (col < kp) {
-        const int pp = patch * patch;
-        const int c = col / pp, rem = col - c * pp, ky = rem / patch, kx = rem - ky * patch;
-        const int py = static_cast<int>(t / grid_w), px = static_cast<int>(t % grid_w);
-        v = __ldg(image + (static_cast<int64_t>(c) * height + py * patch + ky) * width + px * patch + kx);
+    if (idx >= tokens * groups) return;
+    const int64_t t = idx / groups;
+    const int col0 = static_cast<int>(idx - t * groups) * 8;
+    const int py = static_cast<int>(t / grid_w), px = static_cast<int>(t % grid_w);
+    const int pp = patch * patch;
+    __align__(16) __half out[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+        const int col = col0 + j;
+        float v = 0.0f;
+        if (col < kp) {
+            const int c = col / pp, rem = col - c * pp, ky = rem / patch, kx = rem - ky * patch;
+            v = __ldg(image + (static_cast<int64_t>(c) * height + py * patch + ky) * width + px * patch + kx);
+        }
+        out[j] = __float2half_rn(v);
     }
-    a[idx] = __float2half_rn(v);
+    *reinterpret_cast<uint4*>(a + t * ld + col0) = *reinterpret_cast<const uint4*>(out);
 }
 
 // f32 [n][k] -> f16 [n][ld], zero padded (the patch-embedding B operand).
@@ -298,7 +307,7 @@ void launch_vit_prefix(const float* image, int width, int height, int patch, con
     __half* cols = reinterpret_cast<__half*>(cursor);
     cursor = align(cursor + tokens * ld * sizeof(__half));
     __half* wp = reinterpret_cast<__half*>(cursor);
-    launch_pdl(im2col_kernel, dim3(blocks_for(tokens * ld)), dim3(256), 0, stream, "im2col_kernel launch", image,
+    launch_pdl(im2col_kernel, dim3(blocks_for(tokens * (ld / 8))), dim3(256), 0, stream, "im2col_kernel launch", image,
                width, height, patch, grid_w, tokens, kp, ld, cols);
     launch_pdl(pad_f16_kernel, dim3(blocks_for(embed * ld)), dim3(256), 0, stream, "pad_f16_kernel launch", patch_w,
                embed, kp, ld, wp);
