@@ -55,6 +55,18 @@ E, MLP, HEADS, GRID, PATCH, IMAGE, POS_GRID, DEPTH, WINDOW = 1024, 4736, 16, 72,
 GLOBAL_BLOCKS = (7, 15, 23, 31)
 
 
+def workload_config(world):
+    """The `config` object of both arms' JSON lines (the same workload)."""
+    lin_ops, attn_ops = backbone_ops()
+    return {"workload": WORKLOAD, "image": f"{IMAGE}x{IMAGE}x3", "patch": PATCH, "tokens": M,
+            "width": E, "heads": HEADS, "mlp": MLP, "blocks": DEPTH, "window": WINDOW,
+            "global_blocks": list(GLOBAL_BLOCKS),
+            "formats": {"qkv/proj/fc1": "Q4_K", "fc2": "Q8_0", "norms/biases/embeddings": "f32"},
+            "batch_per_gpu": 1, "parallelism": f"images sharded, {world} replica(s)",
+            "l2": "weights 1.1 GB per replica and 91 MB of block scratch exceed L2",
+            "tflop_per_image": {"linears": lin_ops / 1e12, "attention": attn_ops / 1e12}}
+
+
 def backbone_ops():
     """Algorithmic work of one image: 2 M N K over the 128 block linears and
     the patch GEMM, plus 4 N_q N_k hd per head of attention."""
@@ -78,17 +90,18 @@ def make_weights(oracle_mod, n, k, qtype, seed):
 
 
 def peaks():
-    """Roofline denominators.  The GEMMs run inside a long loop of steps, where
-    the SMs settle at ~1.65 GHz (clock64 against %globaltimer in the kernels),
-    so the sustained bf16 figure is the tensor peak; the fallback is the
-    earlier measurement on this pool."""
+    """Roofline denominators from MEASURED_PEAKS.json: the GEMM roofline is
+    measured on isolated launches (each timed alone between CUDA events after
+    an L2 flush), so its denominator is the burst bf16 figure; the sustained
+    one is reported beside it.  The fallback is the earlier measurement on this
+    pool."""
     p = ROOT / "MEASURED_PEAKS.json"
     if p.exists():
         d = json.loads(p.read_text())
-        return {"bf16_tflops": d.get("bf16_tflops_sustained") or d.get("bf16_tflops"),
-                "bf16_tflops_burst": d.get("bf16_tflops"), "hbm_gbs": d.get("hbm_gbs"),
-                "source": "measured sustained"}
-    return {"bf16_tflops": 1400.0, "bf16_tflops_burst": 1590.0, "hbm_gbs": 6650.0, "source": "fallback"}
+        return {"bf16_tflops": d.get("bf16_tflops") or d.get("bf16_tflops_sustained"),
+                "bf16_tflops_sustained": d.get("bf16_tflops_sustained"), "hbm_gbs": d.get("hbm_gbs"),
+                "source": "measured burst"}
+    return {"bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "hbm_gbs": 6650.0, "source": "fallback burst"}
 
 
 def profiled_traffic():
@@ -196,11 +209,13 @@ class CpuBackbone:
 
     The reference's CPU path is GGML's: quantized mul_mat (restated by
     oracle_cpu_linear: Q8_K / Q8_0 activation packing, integer block dots,
-    OpenMP, AVX-512 VNNI when present), f32 attention, LayerNorm and the f32
-    patch convolution (numpy f32 / BLAS here).  One sample (`step`) is:
-    `rows` token rows through one block's 4 linears (+2 LayerNorms), one
-    24x24 window of 16-head attention, and `qrows` query rows of one head of
-    global attention over all 5184 keys.  The patch convolution is timed once.
+    OpenMP, AVX-512 VNNI when present), flash attention over F32 Q / K / V
+    (restated by oracle_flash_attn_f32: per-row f32 online softmax, OpenMP),
+    LayerNorm and the f32 patch convolution (numpy f32 / BLAS here).  One
+    sample (`step`) is: `rows` token rows through one block's 4 linears (+2
+    LayerNorms), one 24x24 window of 16-head attention, and `qrows` query rows
+    of one head of global attention over all 5184 keys.  The patch convolution
+    is timed once.
     """
 
     def __init__(self, oracle_mod, rows=1024, qrows=256):
@@ -212,25 +227,18 @@ class CpuBackbone:
         self.x = {name: rng.normal(0, 1, (rows, k)).astype(np.float32) for name, n, k, *_ in LINEARS}
         self.y = {name: np.empty((rows, n), np.float32) for name, n, *_ in LINEARS}
         self.ln = rng.normal(0, 1, (rows, E)).astype(np.float32)
-        self.qw = rng.normal(0, 1, (HEADS, WINDOW * WINDOW, 64)).astype(np.float32)
-        self.kw = rng.normal(0, 1, (HEADS, WINDOW * WINDOW, 64)).astype(np.float32)
-        self.vw = rng.normal(0, 1, (HEADS, WINDOW * WINDOW, 64)).astype(np.float32)
+        self.qkv_w = rng.normal(0, 1, (WINDOW * WINDOW, 3 * E)).astype(np.float32)
+        self.att_w = np.empty((WINDOW * WINDOW, E), np.float32)
         self.qg = rng.normal(0, 1, (qrows, 64)).astype(np.float32)
         self.kg = rng.normal(0, 1, (M, 64)).astype(np.float32)
         self.vg = rng.normal(0, 1, (M, 64)).astype(np.float32)
+        self.att_g = np.empty((qrows, 64), np.float32)
         cols = rng.normal(0, 1, (M, 3 * PATCH * PATCH)).astype(np.float32)
         pw = rng.normal(0, 0.02, (3 * PATCH * PATCH, E)).astype(np.float32)
         t0 = time.perf_counter()
         for _ in range(3):
             cols @ pw
         self.prefix_s = (time.perf_counter() - t0) / 3
-
-    @staticmethod
-    def _softmax_av(s, v):
-        s = s - s.max(axis=-1, keepdims=True)
-        np.exp(s, out=s)
-        s /= s.sum(axis=-1, keepdims=True)
-        return s @ v
 
     def step(self):
         """One sample; returns the seconds per image it implies."""
@@ -242,9 +250,12 @@ class CpuBackbone:
             c = self.ln - self.ln.mean(axis=1, keepdims=True)
             c / np.sqrt((c * c).mean(axis=1, keepdims=True) + 1e-5)
         t1 = time.perf_counter()
-        self._softmax_av(np.matmul(self.qw, self.kw.transpose(0, 2, 1)) * 0.125, self.vw)
+        for h in range(HEADS):
+            self.o.flash_attn_f32(self.qkv_w[:, 64 * h:64 * h + 64], self.qkv_w[:, E + 64 * h:E + 64 * h + 64],
+                                  self.qkv_w[:, 2 * E + 64 * h:2 * E + 64 * h + 64], 0.125, threads=self.threads,
+                                  out=self.att_w[:, 64 * h:64 * h + 64])
         t2 = time.perf_counter()
-        self._softmax_av((self.qg @ self.kg.T) * 0.125, self.vg)
+        self.o.flash_attn_f32(self.qg, self.kg, self.vg, 0.125, threads=self.threads, out=self.att_g)
         t3 = time.perf_counter()
         per_block_rows = (t1 - t0) * M / self.rows
         windowed = (t2 - t1) * (GRID // WINDOW) ** 2
@@ -255,13 +266,15 @@ class CpuBackbone:
     def describe(self):
         return (f"per sample: {self.rows} of {M} token rows through one block's 4 linears + 2 LayerNorms "
                 f"(restated GGML CPU mul_mat, OpenMP{', AVX-512 VNNI' if self.o.has_vnni() else ''}), one 24x24 "
-                f"window of 16-head f32 attention, {self.qrows} query rows of one global-attention head "
-                f"(numpy f32 BLAS); patch conv timed once; extrapolated to 32 blocks (4 global) per image; "
-                "GGML itself unavailable")
+                f"window of 16-head attention and {self.qrows} query rows of one global-attention head over "
+                f"{M} keys (restated GGML CPU flash attention, f32 online softmax, OpenMP); patch conv timed once; "
+                "extrapolated to 32 blocks (4 global) per image; GGML itself unavailable")
 
 
 def run_reference(args, world, rank):
-    """CPU reference arm: rank 0 times the restated CPU backbone (images/s)."""
+    """CPU reference arm: rank 0 times the restated CPU backbone (images/s).
+    A step is one image, its time extrapolated from one bounded sample of
+    every component; ms_per_step is that per-image time (1000 / value)."""
     if rank != 0:
         return
     from oracle import oracle as o
@@ -271,15 +284,17 @@ def run_reference(args, world, rank):
         cpu.step()
     t0 = time.perf_counter()
     per_image = [cpu.step() for _ in range(args.steps)]
-    elapsed = time.perf_counter() - t0
-    value = 1.0 / float(np.mean(per_image))
+    wall = time.perf_counter() - t0
+    mean_s = float(np.mean(per_image))
+    value = 1.0 / mean_s
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": "images/s", "n_gpus": world,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": elapsed / args.steps * 1e3,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": mean_s * 1e3,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8xint8->f32 / f32",
         "data": "synthetic",
-        "config": {"workload": WORKLOAD, "image": IMAGE, "tokens": M, "blocks": DEPTH,
-                   "global_blocks": list(GLOBAL_BLOCKS), "formats": {"qkv/proj/fc1": "Q4_K", "fc2": "Q8_0"}},
+        "config": workload_config(world),
+        "step": "one image, extrapolated from one bounded sample of each component",
+        "wall_ms_per_sample": wall / args.steps * 1e3,
         "cpu_baseline": {"value": value, "unit": "images/s", "cores": cpu.threads, "kind": "port",
                          "sample": cpu.describe()},
         "e2e": {"value": value, "unit": "images/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
@@ -358,11 +373,10 @@ def main():
     samq.init(local)
     stream = torch.cuda.current_stream()
 
+    from samq.shard import max_over_ranks as shard_max
+
     def max_over_ranks(ms):
-        t = torch.tensor([ms], dtype=torch.float64, device="cuda")
-        if world > 1:
-            dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return float(t.item())
+        return shard_max(ms, dist if world > 1 else None, torch.device("cuda", local))
 
     # ---- backbone (config 3): one image per step per GPU ------------------
     blocks, prefix, keep = make_backbone(samq, o, torch, local, rank)
@@ -478,7 +492,8 @@ def main():
     qgemm_tops = step_ops() * args.qgemm_steps * world / (qgemm_ms / 1e3) / 1e12
     samq.check(local, stream)
 
-    # GEMM-only launch durations (the dominant kernel) on the same stream.
+    # GEMM-only launch durations (the dominant kernel) on the same stream,
+    # each launch timed alone after an L2 flush: against the burst peak.
     gemm_ms = gemm_only_durations(samq, weights, xs, ys, biases, stream)
     pk = peaks()
     gemm_flops = [2.0 * M * n * k for _, n, k, *_ in LINEARS]
@@ -486,13 +501,18 @@ def main():
     traffic = profiled_traffic()
     roofline = {"bound": "tensor", "kernel": "gemm_f16_kernel (tcgen05 kind::f16, f32 accumulate)",
                 "achieved": achieved, "peak": pk["bf16_tflops"], "unit": "TFLOP/s",
-                "frac": achieved / pk["bf16_tflops"], "peak_source": f"{pk['source']} bf16",
-                "frac_of_burst": achieved / pk["bf16_tflops_burst"],
+                "frac": achieved / pk["bf16_tflops"], "peak_source": f"{pk['source']} bf16 (of measured)",
+                "frac_of_sustained": achieved / pk["bf16_tflops_sustained"],
                 "traffic": traffic.get("bytes_per_launch") if traffic else None,
                 "traffic_source": traffic.get("source") if traffic else None,
-                "per_linear_gemm_us": {LINEARS[i][0]: gemm_ms[i] * 1e3 for i in range(len(LINEARS))},
-                "measured_on": "the 4 block-linear shapes at M=5184 (f32 epilogue), 50 back-to-back launches "
-                               "each between CUDA events on the launching stream"}
+                "per_linear": {LINEARS[i][0]: {"us": gemm_ms[i] * 1e3,
+                                               "tflops": gemm_flops[i] / (gemm_ms[i] / 1e3) / 1e12,
+                                               "frac": gemm_flops[i] / (gemm_ms[i] / 1e3) / 1e12 / pk["bf16_tflops"]}
+                               for i in range(len(LINEARS))},
+                "measured_on": "the 4 block-linear shapes at M=5184 (f32 epilogue, fused bias / GELU): 20 "
+                               "launches each, every launch alone between two CUDA events on the launching "
+                               "stream after a 256 MB write that flushes L2; achieved = sum 2MNK / sum of the "
+                               "average launch times"}
 
     # The SimpleFPN neck (F32 semantics, dense.cu) on this image's 72 x 72 ViT
     # output: a secondary figure beside the quantized backbone.
@@ -500,6 +520,10 @@ def main():
     samq.check(local, stream)
     # Config 5's batching: the same backbone over 8 images per GPU per step.
     batch8 = batch_section(samq, torch, stream, args, max_over_ranks, blocks, prefix, world, rank)
+    samq.check(local, stream)
+    # Config 5's sharding protocol: 64 images cut into contiguous per-rank ranges.
+    sweep = sweep64_section(samq, torch, stream, max_over_ranks, blocks, prefix, world, rank,
+                            dist if world > 1 else None)
     samq.check(local, stream)
 
     cpu = None
@@ -517,13 +541,7 @@ def main():
             "metric": METRIC, "value": value, "unit": "images/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": elapsed_ms / args.steps, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "f16", "data": "synthetic",
-            "config": {"workload": WORKLOAD, "image": f"{IMAGE}x{IMAGE}x3", "patch": PATCH, "tokens": M,
-                       "width": E, "heads": HEADS, "mlp": MLP, "blocks": DEPTH, "window": WINDOW,
-                       "global_blocks": list(GLOBAL_BLOCKS),
-                       "formats": {"qkv/proj/fc1": "Q4_K", "fc2": "Q8_0", "norms/biases/embeddings": "f32"},
-                       "batch_per_gpu": 1, "parallelism": f"images sharded, {world} replica(s)",
-                       "l2": "weights 1.1 GB per replica and 91 MB of block scratch exceed L2",
-                       "tflop_per_image": {"linears": lin_ops / 1e12, "attention": attn_ops / 1e12}},
+            "config": workload_config(world),
             "roofline": roofline,
             "cpu_baseline": cpu,
             "e2e": {"value": e2e_value, "unit": "images/s", "h2d_bytes_per_step": image_host.numel() * 4,
@@ -538,6 +556,7 @@ def main():
                       "gpu_launches": args.qgemm_steps * 2 * len(LINEARS)},
             "neck": neck,
             "batch8": batch8,
+            "sweep64": sweep,
         }
         print(json.dumps(line), flush=True)
     for w in weights:
@@ -576,6 +595,47 @@ def batch_section(samq, torch, stream, args, max_over_ranks, blocks, prefix, wor
             "value": steps * batch * world / (ms / 1e3), "unit": "images/s", "batch_per_gpu": batch, "steps": steps,
             "ms_per_step": ms / steps, "features_finite": bool(torch.isfinite(xb).all().item()),
             "gpu_launches": steps * batch * 4 + steps * DEPTH * 7}
+
+
+def sweep64_section(samq, torch, stream, max_over_ranks, blocks, prefix, world, rank, dist, n_images=64, batch=8):
+    """BASELINE config 5's sharding protocol on the vision backbone: 64
+    distinct seeded images, rank g taking the contiguous range
+    [g * 64 / G, (g + 1) * 64 / G) in per-GPU batches of 8 (prefix per image,
+    then each block once per batch).  The time is the max over ranks of each
+    rank's device time (CUDA events), after a barrier; images/s = 64 / time.
+    The weights are the backbone's replica on every rank; no data crosses GPUs."""
+    from samq.shard import batches, image_range
+    start, end = image_range(n_images, world, rank)
+    own = batches(start, end, batch)
+    imgs = torch.empty((end - start, 3, IMAGE, IMAGE), dtype=torch.float32, device="cuda")
+    for i in range(start, end):
+        rng = np.random.default_rng(10_000 + i)  # image i has the same pixels whatever G is
+        imgs[i - start].copy_(torch.from_numpy(((rng.random((3, IMAGE, IMAGE), dtype=np.float32) - 0.5) / 0.5)))
+    xb = torch.empty((batch, M, E), dtype=torch.float32, device="cuda")
+
+    def run():
+        for b0, b1 in own:
+            for j in range(b1 - b0):
+                samq.vit_prefix(imgs[b0 - start + j], IMAGE, IMAGE, PATCH, prefix["patch_w"], E, prefix["pos"],
+                                POS_GRID, prefix["ln_w"], prefix["ln_b"], xb[j], stream)
+            for blk in blocks:
+                samq.vit_block_forward(blk, xb, GRID, GRID, stream, batch=b1 - b0)
+
+    run()  # warm-up
+    torch.cuda.synchronize()
+    if dist is not None:
+        dist.barrier()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record(stream)
+    run()
+    b.record(stream)
+    torch.cuda.synchronize()
+    ms = max_over_ranks(a.elapsed_time(b))
+    return {"metric": "SAM3 vision backbone images/s, 64 images sharded contiguously, per-GPU batches of 8 "
+                      "(config 5 protocol)", "value": n_images / (ms / 1e3), "unit": "images/s",
+            "scaling": "strong", "images": n_images, "images_this_rank": end - start, "batch_per_gpu": batch,
+            "ms": ms, "features_finite": bool(torch.isfinite(xb).all().item()),
+            "gpu_launches": (end - start) * 4 + len(own) * DEPTH * 7}
 
 
 NECK_MID, NECK_D = 512, 256
@@ -711,13 +771,14 @@ def run_profile_case(args):
     print(json.dumps({"profile_case": name, "launches": args.warmup + args.steps}))
 
 
-def gemm_only_durations(samq, weights, xs, ys, biases, stream, reps=50):
-    """Average device time of each GEMM launch: the f16 A operand is staged
-    once (samq_stage_f16_v1), then samq_linear_f16_v1 launches only the
-    tcgen05 GEMM kernel, `reps` launches back to back between two events on
-    the launching stream (as the kernel runs inside a step, prologue
-    overlapped with the previous launch)."""
+def gemm_only_durations(samq, weights, xs, ys, biases, stream, reps=20):
+    """Average device time of one GEMM launch per shape: the f16 A operand is
+    staged once (samq_stage_f16_v1); then each of `reps` launches of
+    samq_linear_f16_v1 (the tcgen05 GEMM kernel alone) is timed between two
+    CUDA events on the launching stream, after a 256 MB write (twice the L2)
+    so that it starts with its operands in HBM."""
     import torch
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
     out = []
     for i, (name, n, k, qtype, epi, _) in enumerate(LINEARS):
         m = xs[i].shape[0]
@@ -725,13 +786,14 @@ def gemm_only_durations(samq, weights, xs, ys, biases, stream, reps=50):
         samq.stage_f16(xs[i], m, k, k, a16, stream)
         for _ in range(3):
             samq.linear_f16(weights[i], a16, m, k, biases[i], epi, ys[i], n, stream)
-        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        a.record(stream)
-        for _ in range(reps):
+        events = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(reps)]
+        for a, b in events:
+            flush.fill_(1)
+            a.record(stream)
             samq.linear_f16(weights[i], a16, m, k, biases[i], epi, ys[i], n, stream)
-        b.record(stream)
+            b.record(stream)
         torch.cuda.synchronize()
-        out.append(a.elapsed_time(b) / reps)
+        out.append(sum(a.elapsed_time(b) for a, b in events) / reps)
     return out
 
 

@@ -329,8 +329,10 @@ samq_status samq_check_v1(int device, void* stream);
  * make that first call before any stream capture.  All calls on a device share
  * the array and it keeps the last call's contents (nothing in it needs to start
  * at zero): calls whose GPU work overlaps in time race on it, so order them on
- * one stream.  Range and timeout findings are not recorded for samq_check_v1 on
- * this path. */
+ * one stream.  Range and timeout findings go to a second file-scope device
+ * word and are reported by samq_check_v1 like those of samq_linear_v1
+ * (samq_check_v1 itself allocates nothing on a device where only this entry
+ * point has run). */
 #define SAMQ_STATIC_OPERAND_ELEMENTS 16777216
 samq_status samq_linear_static_v1(const samq_weights* weights, const float* x, int64_t m, int64_t ldx,
                                   const float* bias, int epilogue, float* y, int64_t ldy, void* stream);

@@ -64,6 +64,8 @@ def lib() -> ctypes.CDLL:
             "oracle_cpu_linear": (i32, [i32, vp, i64, i64, vp, i64, i64, vp, i32, vp, i64, i32]),
             "oracle_cpu_has_vnni": (i32, []),
             "oracle_vit_attention": (i32, [vp, i64, i32, i32, i32, i32, i32, vp, vp, i64, vp, i64, i32]),
+            "oracle_flash_attn_f32": (i32, [vp, i64, vp, i64, vp, i64, i64, i64, i32, ctypes.c_float, vp, i64,
+                                            i32]),
         }
         for name, (res, args) in sig.items():
             fn = getattr(_lib, name)
@@ -230,6 +232,22 @@ def vit_attention(qkv: np.ndarray, grid_w: int, grid_h: int, heads: int, head_di
     return out
 
 
+def flash_attn_f32(q: np.ndarray, k: np.ndarray, v: np.ndarray, scale: float, threads=None,
+                   out: np.ndarray | None = None) -> np.ndarray:
+    """Restated GGML CPU flash attention (f32 online softmax) of one head:
+    q [n_q][hd], k / v [n_kv][hd] f32 (rows may be strided views of a
+    contiguous last axis)."""
+    for a in (q, k, v):
+        assert a.dtype == np.float32 and a.strides[1] == 4
+    n_q, hd = q.shape
+    y = out if out is not None else np.empty((n_q, hd), dtype=np.float32)
+    rc = lib().oracle_flash_attn_f32(_ptr(q), q.strides[0] // 4, _ptr(k), k.strides[0] // 4, _ptr(v),
+                                     v.strides[0] // 4, n_q, k.shape[0], hd, scale, _ptr(y), y.strides[0] // 4,
+                                     threads or default_threads())
+    _check(rc, "flash_attn_f32")
+    return y
+
+
 def rope_freqs(positions: int, head_dim: int = 64, seed: int = 0) -> np.ndarray:
     """Unit-modulus (cos, sin) pairs [positions][head_dim/2][2] (any such table is a valid freqs_cis)."""
     rng = np.random.default_rng(seed)
@@ -255,32 +273,133 @@ def layer_norm(x: np.ndarray, w: np.ndarray, b: np.ndarray, eps: float = 1e-5) -
     return (c / np.sqrt(var + eps) * np.asarray(w, np.float64) + np.asarray(b, np.float64)).astype(np.float32)
 
 
-def staged_linear(w16: np.ndarray, x: np.ndarray, bias=None, epilogue=EPILOGUE_NONE, threads=None) -> np.ndarray:
-    """A quantized linear as GGML's CUDA path computes it: x staged to Q8_1
-    (act_f16 gives the exact decoded operand), weights decoded (w16 =
-    weight_f16), f64 dot products, bias and erf-GELU, f32 result."""
-    return gemm_f64(w16, act_f16(x), bias, epilogue, threads)
+def staged_linear(w: np.ndarray, x: np.ndarray, bias=None, epilogue=EPILOGUE_NONE) -> np.ndarray:
+    """A quantized linear with GGML MMQ's operand semantics: x is staged to
+    Q8_1 (quantize_q8_1 restated) and the product runs over the DECODED
+    operands, d_x * q_x for the activations and the weight's f32 dequantized
+    values (w = dequantize(...), [n][k] f32, no f16 rounding), in f64; then
+    bias and erf-GELU, rounded to f32 (the reference's F32 output tensor)."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    m, k = x.shape
+    xd = q8_1_decode(quantize_q8_1(x), m, k).astype(np.float64)
+    y = xd @ np.asarray(w, np.float64).T
+    if bias is not None:
+        y += np.asarray(bias, np.float64)
+    if epilogue == EPILOGUE_GELU_ERF:
+        y = gelu_erf64(y)
+    return y.astype(np.float32)
+
+
+def win_part_index(grid_w: int, grid_h: int, window: int) -> np.ndarray:
+    """ggml_win_part as an index map (src/models/sam3/vision.hpp:170-173):
+    the [C, W, H] grid, zero-padded up to multiples of `window`, cut into
+    window x window tiles ordered row-major over the tile grid, each tile's
+    tokens row-major.  Returns [windows][window * window] raster token indices
+    (y * grid_w + x), -1 where the tile covers padding."""
+    nx, ny = -(-grid_w // window), -(-grid_h // window)
+    ly, lx = np.divmod(np.arange(window * window), window)
+    out = np.empty((nx * ny, window * window), dtype=np.int64)
+    for wy in range(ny):
+        for wx in range(nx):
+            y, x = wy * window + ly, wx * window + lx
+            out[wy * nx + wx] = np.where((x < grid_w) & (y < grid_h), y * grid_w + x, -1)
+    return out
+
+
+def win_part(x: np.ndarray, grid_w: int, grid_h: int, window: int) -> np.ndarray:
+    """x [grid_h * grid_w][C] (raster) -> [windows][window * window][C] with
+    zeros in the padding (ggml_win_part)."""
+    idx = win_part_index(grid_w, grid_h, window)
+    x = np.asarray(x)
+    out = np.zeros(idx.shape + x.shape[1:], dtype=x.dtype)
+    valid = idx >= 0
+    out[valid] = x[idx[valid]]
+    return out
+
+
+def win_unpart(parts: np.ndarray, grid_w: int, grid_h: int, window: int) -> np.ndarray:
+    """Inverse of win_part (ggml_win_unpart, vision.hpp:225-227): drops the padding."""
+    idx = win_part_index(grid_w, grid_h, window)
+    out = np.empty((grid_w * grid_h,) + parts.shape[2:], dtype=parts.dtype)
+    valid = idx >= 0
+    out[idx[valid]] = parts[valid]
+    return out
+
+
+def rope64(x: np.ndarray, freqs: np.ndarray) -> np.ndarray:
+    """sam3_apply_rope (vision.hpp:100-148) in f64: channel pairs (2i, 2i+1)
+    of x [n][head_dim] rotated by freqs [n][head_dim/2] (cos, sin)."""
+    x = np.asarray(x, np.float64)
+    f = np.asarray(freqs, np.float64)
+    re, im = x[:, 0::2], x[:, 1::2]
+    c, s = f[..., 0], f[..., 1]
+    out = np.empty_like(x)
+    out[:, 0::2] = re * c - im * s
+    out[:, 1::2] = re * s + im * c
+    return out
+
+
+def attention_np(qkv: np.ndarray, grid_w: int, grid_h: int, heads: int, window: int, freqs: np.ndarray,
+                 rows=None, pad_qkv=None) -> np.ndarray:
+    """f64 RoPE + windowed / global attention of one ViT block
+    (vision.hpp:170-227): qkv [tokens][3E] f32 (Q | K | V, heads of 64),
+    windows from win_part (padding tokens carry `pad_qkv`, the qkv of a zero
+    LayerNorm row, as GGML's zero-padded partition does), RoPE by local
+    position, softmax(Q K^T / 8) V per head, win_unpart.  Returns [rows][E]
+    f32 for the query tokens `rows` (all when None)."""
+    qkv = np.asarray(qkv, np.float32)
+    E = heads * 64
+    tokens = grid_w * grid_h
+    groups = win_part_index(grid_w, grid_h, window) if window else np.arange(tokens)[None, :]
+    want = np.zeros(tokens, dtype=bool)
+    want[np.arange(tokens) if rows is None else np.asarray(rows, np.int64)] = True
+    out = np.zeros((tokens, E), dtype=np.float32)
+    freqs = np.asarray(freqs, np.float64).reshape(groups.shape[1], 32, 2)
+    for g in groups:
+        valid = g >= 0
+        if not want[g[valid]].any():
+            continue
+        rows_g = np.empty((g.size, 3 * E), dtype=np.float64)
+        rows_g[valid] = qkv[g[valid]]
+        if not valid.all():
+            rows_g[~valid] = np.asarray(pad_qkv, np.float64).reshape(3 * E)
+        qsel = np.nonzero(valid & want[np.where(valid, g, 0)])[0]
+        for h in range(heads):
+            q = rope64(rows_g[qsel, h * 64:(h + 1) * 64], freqs[qsel])
+            k = rope64(rows_g[:, E + h * 64:E + (h + 1) * 64], freqs)
+            v = rows_g[:, 2 * E + h * 64:2 * E + (h + 1) * 64]
+            s = (q @ k.T) * 0.125
+            s -= s.max(axis=1, keepdims=True)
+            p = np.exp(s)
+            o = (p @ v) / p.sum(axis=1, keepdims=True)
+            out[g[qsel], h * 64:(h + 1) * 64] = o
+    sel = np.arange(tokens) if rows is None else np.asarray(rows, np.int64)
+    return out[sel]
 
 
 def vit_block(x: np.ndarray, blk: dict, grid_w: int, grid_h: int, rows=None, threads=None) -> np.ndarray:
-    """One SAM 3 ViT block (src/models/sam3/vision.hpp:152-243) in f64 with
-    Q8_1 staging in front of every quantized linear:
+    """One SAM 3 ViT block (src/models/sam3/vision.hpp:152-243) with GGML's
+    arithmetic for every quantized linear (staged_linear: Q8_1-staged input,
+    f32-decoded weights, f64 dots) and f64 LayerNorm / attention:
       x1 = x + proj(attn(RoPE(qkv(LN1(x)))));  out = x1 + fc2(GELU(fc1(LN2(x1)))).
-    blk holds window, norm1_w/b, norm2_w/b, the decoded f16 weights qkv_w16,
-    proj_w16, fc1_w16, fc2_w16 ([n][k]), the biases and freqs.  x is
-    [tokens][E] f32 in raster order.  Returns the block output for the tokens
-    in `rows` (all when None): K and V cover every token, the rest only `rows`."""
+    blk holds window, norm1_w/b, norm2_w/b, the decoded f32 weights qkv_w,
+    proj_w, fc1_w, fc2_w ([n][k], from dequantize), the biases and freqs.  x
+    is [tokens][E] f32 in raster order; the residual adds are f32 as in GGML.
+    Returns the block output for the tokens in `rows` (all when None): K and V
+    cover every token, the rest only `rows`."""
+    del threads
     x = np.ascontiguousarray(x, dtype=np.float32)
     E = x.shape[1]
     heads = E // 64
     h = layer_norm(x, blk["norm1_w"], blk["norm1_b"])
-    qkv = staged_linear(blk["qkv_w16"], h, blk["qkv_b"], threads=threads)
+    qkv = staged_linear(blk["qkv_w"], h, blk["qkv_b"])
+    pad = staged_linear(blk["qkv_w"], np.zeros((1, E), np.float32), blk["qkv_b"])
     sel = np.arange(x.shape[0]) if rows is None else np.asarray(rows, dtype=np.int64)
-    att = vit_attention(qkv, grid_w, grid_h, heads, 64, blk["window"], blk["freqs"], rows=sel, threads=threads)
-    x1 = (x[sel] + staged_linear(blk["proj_w16"], att, blk["proj_b"], threads=threads)).astype(np.float32)
+    att = attention_np(qkv, grid_w, grid_h, heads, blk["window"], blk["freqs"], rows=sel, pad_qkv=pad)
+    x1 = x[sel] + staged_linear(blk["proj_w"], att, blk["proj_b"])
     h2 = layer_norm(x1, blk["norm2_w"], blk["norm2_b"])
-    f = staged_linear(blk["fc1_w16"], h2, blk["fc1_b"], EPILOGUE_GELU_ERF, threads=threads)
-    return (x1 + staged_linear(blk["fc2_w16"], f, blk["fc2_b"], threads=threads)).astype(np.float32)
+    f = staged_linear(blk["fc1_w"], h2, blk["fc1_b"], EPILOGUE_GELU_ERF)
+    return x1 + staged_linear(blk["fc2_w"], f, blk["fc2_b"])
 
 
 def vit_prefix(image: np.ndarray, patch: int, patch_w: np.ndarray, pos_embed: np.ndarray, ln_w: np.ndarray,

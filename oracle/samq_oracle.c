@@ -962,3 +962,92 @@ int oracle_cpu_linear(int type, const uint8_t* w_rows, int64_t k, int64_t n,
     cpu_weights_free(&w);
     return 0;
 }
+
+/* ------------------------------------------------- CPU flash attention */
+
+#ifdef ORACLE_X86
+#define AVX512_TARGET __attribute__((target("avx512f")))
+AVX512_TARGET static float dot_f32_avx512(const float* a, const float* b, int n) {
+    __m512 acc = _mm512_setzero_ps();
+    int i = 0;
+    for (; i + 16 <= n; i += 16) acc = _mm512_fmadd_ps(_mm512_loadu_ps(a + i), _mm512_loadu_ps(b + i), acc);
+    float s = _mm512_reduce_add_ps(acc);
+    for (; i < n; ++i) s += a[i] * b[i];
+    return s;
+}
+AVX512_TARGET static void mad_f32_avx512(float* y, const float* x, float w, int n) {
+    const __m512 wv = _mm512_set1_ps(w);
+    int i = 0;
+    for (; i + 16 <= n; i += 16)
+        _mm512_storeu_ps(y + i, _mm512_fmadd_ps(_mm512_loadu_ps(x + i), wv, _mm512_loadu_ps(y + i)));
+    for (; i < n; ++i) y[i] += x[i] * w;
+}
+AVX512_TARGET static void scale_f32_avx512(float* y, float w, int n) {
+    const __m512 wv = _mm512_set1_ps(w);
+    int i = 0;
+    for (; i + 16 <= n; i += 16) _mm512_storeu_ps(y + i, _mm512_mul_ps(_mm512_loadu_ps(y + i), wv));
+    for (; i < n; ++i) y[i] *= w;
+}
+#endif
+
+static float dot_f32_scalar(const float* a, const float* b, int n) {
+    float s = 0.0f;
+    for (int i = 0; i < n; ++i) s += a[i] * b[i];
+    return s;
+}
+
+static void flash_row(const float* q, const float* k, int64_t ldk, const float* v, int64_t ldv, int64_t n_kv, int hd,
+                      float scale, float* acc, int wide) {
+    float m = -INFINITY, sum = 0.0f;
+    for (int i = 0; i < hd; ++i) acc[i] = 0.0f;
+    for (int64_t j = 0; j < n_kv; ++j) {
+        const float* kj = k + j * ldk;
+        const float* vj = v + j * ldv;
+#ifdef ORACLE_X86
+        const float s = (wide ? dot_f32_avx512(q, kj, hd) : dot_f32_scalar(q, kj, hd)) * scale;
+#else
+        const float s = dot_f32_scalar(q, kj, hd) * scale;
+#endif
+        float ms = 1.0f, vs = 1.0f;
+        if (s > m) {
+            const float m_old = m;
+            m = s;
+            ms = expf(m_old - m);
+#ifdef ORACLE_X86
+            if (wide) scale_f32_avx512(acc, ms, hd);
+            else
+#endif
+                for (int i = 0; i < hd; ++i) acc[i] *= ms;
+        } else {
+            vs = expf(s - m);
+        }
+#ifdef ORACLE_X86
+        if (wide) mad_f32_avx512(acc, vj, vs, hd);
+        else
+#endif
+            for (int i = 0; i < hd; ++i) acc[i] += vj[i] * vs;
+        sum = sum * ms + vs;
+    }
+    const float inv = sum == 0.0f ? 0.0f : 1.0f / sum;
+    for (int i = 0; i < hd; ++i) acc[i] *= inv;
+    (void)wide;
+}
+
+int oracle_flash_attn_f32(const float* q, int64_t ldq, const float* k, int64_t ldk, const float* v, int64_t ldv,
+                          int64_t n_q, int64_t n_kv, int head_dim, float scale, float* out, int64_t ldo,
+                          int threads) {
+    if (!q || !k || !v || !out || n_q < 0 || n_kv <= 0 || head_dim <= 0 || ldq < head_dim || ldk < head_dim ||
+        ldv < head_dim || ldo < head_dim)
+        return -1;
+    int wide = 0;
+#ifdef ORACLE_X86
+    wide = __builtin_cpu_supports("avx512f") ? 1 : 0;
+#endif
+#ifdef _OPENMP
+#pragma omp parallel for schedule(static) num_threads(threads > 0 ? threads : 1)
+#endif
+    for (int64_t r = 0; r < n_q; ++r)
+        flash_row(q + r * ldq, k, ldk, v, ldv, n_kv, head_dim, scale, out + r * ldo, wide);
+    (void)threads;
+    return 0;
+}

@@ -143,6 +143,18 @@ int oracle_cpu_linear(int type, const uint8_t* w_rows, int64_t k, int64_t n,
 /* 1 when the AVX-512 VNNI kernel is in use on this host. */
 int oracle_cpu_has_vnni(void);
 
+/* Restated GGML CPU flash attention for F32 Q / K / V (the timed CPU baseline's
+ * attention; ggml_flash_attn_ext as sam3_vit_block_forward calls it,
+ * src/models/sam3/vision.hpp:216, no mask): one head, each query row on its
+ * own with an online softmax in f32 -- s = (q . k_j) * scale; when s exceeds
+ * the running maximum M the f32 accumulator and the running sum are rescaled
+ * by expf(M_old - s), otherwise v_j is added with weight expf(s - M); the row
+ * ends divided by the running sum.  q [n_q][ldq], k / v [n_kv][ldk / ldv],
+ * out [n_q][ldo]; OpenMP over the query rows.  Returns 0 on success. */
+int oracle_flash_attn_f32(const float* q, int64_t ldq, const float* k, int64_t ldk, const float* v, int64_t ldv,
+                          int64_t n_q, int64_t n_kv, int head_dim, float scale, float* out, int64_t ldo,
+                          int threads);
+
 #ifdef __cplusplus
 }
 #endif

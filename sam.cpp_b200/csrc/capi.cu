@@ -84,6 +84,12 @@ DeviceState& device_state(int device) {
     return *g_states[device];
 }
 
+DeviceState* existing_device_state(int device) {
+    if (device < 0 || device >= 64) return nullptr;
+    std::lock_guard<std::mutex> lock(g_states_mutex);
+    return g_states[device];
+}
+
 Scratch& scratch_for(DeviceState& state, cudaStream_t stream, size_t bytes) {
     std::lock_guard<std::mutex> lock(state.mutex);
     Scratch& s = state.scratch[stream];
@@ -216,6 +222,8 @@ void release(samq_weights* w) {
     delete w;
 }
 
+}  // namespace
+
 void check_activation_args(int64_t rows, int64_t k, int64_t ld, const void* x, const void* out) {
     require(rows >= 0 && rows <= (int64_t(1) << 31), "rows out of range");
     require(k > 0 && k % 32 == 0 && k <= (int64_t(1) << 20), "width must be a positive multiple of 32");
@@ -224,7 +232,16 @@ void check_activation_args(int64_t rows, int64_t k, int64_t ld, const void* x, c
     require(rows == 0 || aligned16(x), "activation pointer must be 16-byte aligned");
 }
 
-}  // namespace
+void check_linear_args(const samq_weights* w, int64_t m, const float* bias, int epilogue, const float* y,
+                       int64_t ldy) {
+    require(w != nullptr, "null weights");
+    require(m >= 0 && m <= (int64_t(1) << 31), "row count out of range");
+    require(epilogue == SAMQ_EPILOGUE_NONE || epilogue == SAMQ_EPILOGUE_GELU_ERF, "unknown epilogue");
+    require(ldy >= w->n && ldy % 4 == 0, "output row stride must be >= n and a multiple of 4 floats");
+    require(m == 0 || (y != nullptr && aligned16(y)), "output pointer must be 16-byte aligned");
+    (void)bias;
+}
+
 }  // namespace samq
 
 using namespace samq;
@@ -362,16 +379,6 @@ samq_status samq_quantize_mmq_q8_1_v1(const float* x, int64_t rows, int64_t k, i
         device_state(current_device());
         launch_mmq_d4(x, rows, k, ld, static_cast<uint8_t*>(out), static_cast<cudaStream_t>(stream));
     });
-}
-
-static void check_linear_args(const samq_weights* w, int64_t m, const float* bias, int epilogue, const float* y,
-                              int64_t ldy) {
-    require(w != nullptr, "null weights");
-    require(m >= 0 && m <= (int64_t(1) << 31), "row count out of range");
-    require(epilogue == SAMQ_EPILOGUE_NONE || epilogue == SAMQ_EPILOGUE_GELU_ERF, "unknown epilogue");
-    require(ldy >= w->n && ldy % 4 == 0, "output row stride must be >= n and a multiple of 4 floats");
-    require(m == 0 || (y != nullptr && aligned16(y)), "output pointer must be 16-byte aligned");
-    (void)bias;
 }
 
 // K2 over an f16 operand: M <= kStreamMaxRows streams the packed weights
@@ -726,12 +733,25 @@ samq_status samq_query_v1(const samq_weights* w, struct samq_counters_v1* out) {
 samq_status samq_check_v1(int device, void* stream) {
     samq_status found = SAMQ_OK;
     const samq_status rc = guarded([&] {
-        DeviceState& state = device_state(device);
+        int count = 0;
+        check_cuda(cudaGetDeviceCount(&count), "cudaGetDeviceCount");
+        require(device >= 0 && device < count && device < 64, "device index is not visible");
         DeviceGuard guard(device);
         check_cuda(cudaStreamSynchronize(static_cast<cudaStream_t>(stream)), "cudaStreamSynchronize(check)");
+        // The library's status word (only if its device state exists: a caller
+        // that only used the allocation-free path has none, and checking must
+        // not create one) merged with the allocation-free path's own word.
         DeviceStatus host{};
-        check_cuda(cudaMemcpy(&host, state.status, sizeof(host), cudaMemcpyDeviceToHost), "cudaMemcpy(status)");
-        check_cuda(cudaMemset(state.status, 0, sizeof(DeviceStatus)), "cudaMemset(status)");
+        if (DeviceState* state = existing_device_state(device)) {
+            check_cuda(cudaMemcpy(&host, state->status, sizeof(host), cudaMemcpyDeviceToHost), "cudaMemcpy(status)");
+            check_cuda(cudaMemset(state->status, 0, sizeof(DeviceStatus)), "cudaMemset(status)");
+        }
+        DeviceStatus fixed{};
+        if (take_static_status(device, &fixed)) {
+            host.flags |= fixed.flags;
+            host.range_blocks += fixed.range_blocks;
+            if (fixed.flags & kStatusTimeout) host.timeout_site = fixed.timeout_site;
+        }
         if (host.flags & kStatusTimeout) {
             found = SAMQ_ERR_TIMEOUT;
             fail(SAMQ_ERR_TIMEOUT, "a device-side wait timed out at site " + std::to_string(host.timeout_site));

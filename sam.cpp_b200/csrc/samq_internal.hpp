@@ -44,7 +44,20 @@ struct DeviceState {
 };
 
 // Checks the device once and returns its state (throws Error otherwise).
+// The first call on a device allocates its status word.
 DeviceState& device_state(int device);
+// The state of `device` if device_state() has created it, else nullptr
+// (never allocates).
+DeviceState* existing_device_state(int device);
+// Argument checks shared by the linear entry points (throw Error).
+void check_activation_args(int64_t rows, int64_t k, int64_t ld, const void* x, const void* out);
+void check_linear_args(const samq_weights* w, int64_t m, const float* bias, int epilogue, const float* y,
+                       int64_t ldy);
+// Findings of samq_linear_static_v1 on `device` since the last call (its
+// status word is a file-scope device variable, static_scratch.cu); clears
+// them.  Returns false, touching nothing, when that path never ran on the
+// device.  Makes no allocation.
+bool take_static_status(int device, DeviceStatus* out);
 // Scratch of at least `bytes` bytes for work ordered on `stream`.
 Scratch& scratch_for(DeviceState& state, cudaStream_t stream, size_t bytes);
 // Raises `kernel`'s dynamic shared memory limit to `bytes` on state.device the

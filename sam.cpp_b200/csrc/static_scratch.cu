@@ -27,35 +27,75 @@ namespace samq {
 namespace {
 
 constexpr int64_t kStaticOperandElements = SAMQ_STATIC_OPERAND_ELEMENTS;
+constexpr int kMaxDevices = 64;
 
 // Staged activation operand (binary16 bit patterns).  In host code this name
 // is only a stand-in for the device symbol; its device address comes from
 // cudaGetSymbolAddress.
 static __device__ __align__(256) uint16_t g_static_operand[kStaticOperandElements];
+// Findings of this path (range, timeout), read and cleared by samq_check_v1.
+// Zero-initialized when the module loads.
+static __device__ __align__(16) DeviceStatus g_static_status;
+
+// Per-device launch parameters and the two device addresses, filled once per
+// device with that device current.
+struct StaticDevice {
+    bool ready = false;
+    __half* operand = nullptr;
+    DeviceStatus* status = nullptr;
+    DeviceState launch;  // device, sm_count, cc_major; launch.status = status
+};
 
 std::mutex g_static_mutex;
-void* g_static_address[64] = {};
+StaticDevice g_static[kMaxDevices];
 
-// Device address of g_static_operand on `device`, looked up once per device
-// with that device current (the caller's DeviceGuard makes it current).
-__half* static_operand(int device) {
+// Set-up of `device` (the caller's DeviceGuard makes it current): checks the
+// architecture and looks up the device addresses of the two file-scope
+// variables.  Makes no allocation.
+StaticDevice& static_device(int device) {
+    if (device < 0 || device >= kMaxDevices) fail(SAMQ_ERR_INVALID_ARGUMENT, "device index out of range");
     std::lock_guard<std::mutex> lock(g_static_mutex);
-    if (!g_static_address[device]) {
-        void* address = nullptr;
-        check_cuda(cudaGetSymbolAddress(&address, g_static_operand), "cudaGetSymbolAddress(static operand)");
-        if (!address) fail(SAMQ_ERR_CUDA, "static operand has no device address");
-        g_static_address[device] = address;
-    }
-    return static_cast<__half*>(g_static_address[device]);
+    StaticDevice& d = g_static[device];
+    if (d.ready) return d;
+    int sm_count = 0, cc_major = 0, cc_minor = 0;
+    check_cuda(cudaDeviceGetAttribute(&sm_count, cudaDevAttrMultiProcessorCount, device),
+               "cudaDeviceGetAttribute(SM count)");
+    check_cuda(cudaDeviceGetAttribute(&cc_major, cudaDevAttrComputeCapabilityMajor, device),
+               "cudaDeviceGetAttribute(compute capability)");
+    check_cuda(cudaDeviceGetAttribute(&cc_minor, cudaDevAttrComputeCapabilityMinor, device),
+               "cudaDeviceGetAttribute(compute capability)");
+    if (cc_major != 10 || cc_minor != 0) fail(SAMQ_ERR_UNSUPPORTED, "samq kernels are built for sm_100a");
+    void* operand = nullptr;
+    void* status = nullptr;
+    check_cuda(cudaGetSymbolAddress(&operand, g_static_operand), "cudaGetSymbolAddress(static operand)");
+    check_cuda(cudaGetSymbolAddress(&status, g_static_status), "cudaGetSymbolAddress(static status)");
+    if (!operand || !status) fail(SAMQ_ERR_CUDA, "static operand has no device address");
+    d.operand = static_cast<__half*>(operand);
+    d.status = static_cast<DeviceStatus*>(status);
+    d.launch.device = device;
+    d.launch.sm_count = sm_count;
+    d.launch.cc_major = cc_major;
+    d.launch.cc_minor = cc_minor;
+    d.launch.status = d.status;
+    d.ready = true;
+    return d;
 }
-
-void require_arg(bool condition, const char* message) {
-    if (!condition) fail(SAMQ_ERR_INVALID_ARGUMENT, message);
-}
-
-bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 }  // namespace
+
+bool take_static_status(int device, DeviceStatus* out) {
+    DeviceStatus* status = nullptr;
+    {
+        std::lock_guard<std::mutex> lock(g_static_mutex);
+        if (device < 0 || device >= kMaxDevices || !g_static[device].ready) return false;
+        status = g_static[device].status;
+    }
+    DeviceGuard guard(device);
+    check_cuda(cudaMemcpy(out, status, sizeof(DeviceStatus), cudaMemcpyDeviceToHost), "cudaMemcpy(static status)");
+    check_cuda(cudaMemset(status, 0, sizeof(DeviceStatus)), "cudaMemset(static status)");
+    return true;
+}
+
 }  // namespace samq
 
 extern "C" samq_status samq_linear_static_v1(const samq_weights* w, const float* x, int64_t m, int64_t ldx,
@@ -63,32 +103,18 @@ extern "C" samq_status samq_linear_static_v1(const samq_weights* w, const float*
                                               void* stream_ptr) {
     using namespace samq;
     try {
-        require_arg(w != nullptr, "null weights");
-        require_arg(m >= 0, "row count out of range");
-        require_arg(epilogue == SAMQ_EPILOGUE_NONE || epilogue == SAMQ_EPILOGUE_GELU_ERF, "unknown epilogue");
-        require_arg(ldx >= w->k && ldx % 4 == 0, "row stride must be >= width and a multiple of 4 floats");
-        require_arg(ldy >= w->n && ldy % 4 == 0, "output row stride must be >= n and a multiple of 4 floats");
-        require_arg(m <= kStaticOperandElements / w->k,
-                    "m * k exceeds the static operand capacity of SAMQ_STATIC_OPERAND_ELEMENTS "
-                    "(16777216) elements; split the rows across calls");
+        check_linear_args(w, m, bias, epilogue, y, ldy);
+        check_activation_args(m, w->k, ldx, x, y);
+        if (m > kStaticOperandElements / w->k)
+            fail(SAMQ_ERR_INVALID_ARGUMENT,
+                 "m * k exceeds the static operand capacity of SAMQ_STATIC_OPERAND_ELEMENTS "
+                 "(16777216) elements; split the rows across calls");
         if (m > 0) {
-            require_arg(x != nullptr && aligned16(x), "activation pointer must be 16-byte aligned");
-            require_arg(y != nullptr && aligned16(y), "output pointer must be 16-byte aligned");
             DeviceGuard guard(w->device);
-            // Launch parameters without touching the library's device state
-            // (creating that state allocates its status word).
-            DeviceState launch;
-            launch.device = w->device;
-            check_cuda(cudaDeviceGetAttribute(&launch.sm_count, cudaDevAttrMultiProcessorCount, w->device),
-                       "cudaDeviceGetAttribute(SM count)");
-            check_cuda(cudaDeviceGetAttribute(&launch.cc_major, cudaDevAttrComputeCapabilityMajor, w->device),
-                       "cudaDeviceGetAttribute(compute capability)");
-            if (launch.cc_major != 10) fail(SAMQ_ERR_UNSUPPORTED, "samq kernels are built for sm_100a");
-            launch.status = nullptr;  // no findings are recorded on this path; waits stay bounded
-            __half* a = static_operand(w->device);
+            StaticDevice& d = static_device(w->device);
             cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
-            launch_act_f16(x, m, w->k, ldx, a, nullptr, nullptr, stream);
-            launch_gemm_f16(a, w->k, w->operand, m, w->n, w->k, bias, epilogue, y, ldy, launch, stream);
+            launch_act_f16(x, m, w->k, ldx, d.operand, nullptr, d.status, stream);
+            launch_gemm_f16(d.operand, w->k, w->operand, m, w->n, w->k, bias, epilogue, y, ldy, d.launch, stream);
         }
         set_last_error("");
         return SAMQ_OK;

@@ -20,6 +20,7 @@ The fixtures are small .npz files; tests read them on any machine.
 from __future__ import annotations
 
 import argparse
+import os
 import importlib.util
 import json
 import sys
@@ -72,8 +73,12 @@ def activation_matrix(rng, rows, k):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", type=Path, default=Path("/root/reference"))
+    ap.add_argument("--reference", type=Path, default=os.environ.get("SAM_REFERENCE_TREE"),
+                    help="root of the SAM.cpp source tree (or set SAM_REFERENCE_TREE)")
     args = ap.parse_args()
+    if args.reference is None:
+        ap.error("--reference (or SAM_REFERENCE_TREE) must name the SAM.cpp source tree")
+    args.reference = Path(args.reference)
     import gguf
     from gguf import GGMLQuantizationType as T
 

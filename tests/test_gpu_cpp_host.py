@@ -83,7 +83,7 @@ def test_cpp_vit_backbone_on_gpu(tmp_path, oracle):
         w = rng.normal(0, 0.02, (n, k)).astype(np.float32)
         rows = oracle.quantize(t, w)
         writer.add_tensor(f"vit.blocks.0.{gname}.weight", rows.reshape(n, -1), raw_dtype=gguf.GGMLQuantizationType(t))
-        blk[name + "_w16"] = oracle.weight_f16(t, k, n, rows)
+        blk[name + "_w"] = oracle.dequantize(t, rows, n * k).reshape(n, k)
         blk[name + "_b"] = files[name + "_b"] = rng.normal(0, 0.02, n).astype(np.float32)
     writer.write_header_to_file()
     writer.write_kv_data_to_file()

@@ -1,10 +1,12 @@
 """ViT block / backbone prefix parity: samq_vit_block_forward_v1 and
 samq_vit_prefix_v1 against the f64 oracle (oracle.vit_block / vit_prefix).
 
-The block oracle stages every quantized linear's input with the Q8_1 rule and
-uses the decoded f16 weights, as the device path does; the remaining
-differences are f32 accumulation order, f16 Q/K/V/P inside attention, the f32
-LayerNorm and the polynomial erf-GELU.  Since a staged code can flip by one
+The block oracle computes every quantized linear with GGML MMQ's operand
+semantics: the input staged with the Q8_1 rule, times the f32-decoded weights
+(no f16 rounding), f64 dots.  The device path differs by its f16 tensor-core
+operands (the staged values and the weights rounded once to f16, f16 Q/K/V/P
+inside attention), f32 accumulation, the f32 LayerNorm and the polynomial
+erf-GELU.  Since a staged code can flip by one
 when an upstream value moves by an ulp, the bar is on the block's
 contribution (out - x): cosine >= 0.9999 and max error <= 1e-2 of its largest
 magnitude.  The prefix runs the patch convolution on f16 operands (f32
@@ -38,7 +40,7 @@ def make_block(rng, window, positions, qtype=o.Q4_K, fc2_type=o.Q8_0, E=E, MLP=M
     for name, (n, k, t) in {"qkv": (3 * E, E, qtype), "proj": (E, E, qtype), "fc1": (MLP, E, qtype),
                             "fc2": (E, MLP, fc2_type)}.items():
         rows = o.quantize(t, _weights(rng, n, k))
-        host[name + "_w16"] = o.weight_f16(t, k, n, rows)
+        host[name + "_w"] = o.dequantize(t, rows, n * k).reshape(n, k)
         gpu[name] = samq.Weights(t, k, n, rows)
         bias = rng.normal(0.0, 0.02, n).astype(np.float32)
         host[name + "_b"] = bias

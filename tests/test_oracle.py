@@ -201,3 +201,69 @@ def test_kquant_packer_is_close_to_source(oracle):
     for qtype, bound in [(12, 0.12), (13, 0.06), (14, 0.04)]:
         dq = oracle.dequantize(qtype, oracle.quantize(qtype, w), w.size).reshape(w.shape)
         assert np.linalg.norm(dq - w) / np.linalg.norm(w) < bound
+
+
+# ---- ViT window partition / attention restatements ---------------------------
+
+def _iota_grid(channels, width, height):
+    """1, 2, 3, ... in GGML [C, W, H] order (channels fastest) as raster token rows."""
+    return np.arange(1, channels * width * height + 1, dtype=np.float32).reshape(height * width, channels)
+
+
+@pytest.mark.parametrize("shape,golden", [
+    ((2, 3, 2, 2), [1, 2, 3, 4, 7, 8, 9, 10, 5, 6, 0, 0, 11, 12, 0, 0]),
+    ((1, 3, 3, 2), [1, 2, 4, 5, 3, 0, 6, 0, 7, 8, 0, 0, 9, 0, 0, 0]),
+])
+def test_win_part_matches_reference_golden_layouts(oracle, shape, golden):
+    """The handwritten layouts of tests/runtime/ggml/test_window.cpp:44-51
+    (channel order, window order, zero padding) for ggml_win_part."""
+    c, w, h, win = shape
+    x = _iota_grid(c, w, h)
+    parts = oracle.win_part(x, w, h, win)
+    np.testing.assert_array_equal(parts.ravel(), np.asarray(golden, dtype=np.float32))
+    np.testing.assert_array_equal(oracle.win_unpart(parts, w, h, win), x)
+
+
+@pytest.mark.parametrize("shape", [(3, 1, 1, 4), (37, 7, 5, 4), (33, 2, 5, 1), (8, 72, 72, 24)])
+def test_win_part_round_trip(oracle, shape):
+    """The other shapes of test_window.cpp:54-56: win_unpart restores the image
+    exactly, and every non-padding slot holds its own token."""
+    c, w, h, win = shape
+    x = _iota_grid(c, w, h)
+    parts = oracle.win_part(x, w, h, win)
+    nx, ny = -(-w // win), -(-h // win)
+    assert parts.shape == (nx * ny, win * win, c)
+    np.testing.assert_array_equal(oracle.win_unpart(parts, w, h, win), x)
+    idx = oracle.win_part_index(w, h, win)
+    assert np.count_nonzero(idx >= 0) == w * h and np.all(parts[idx < 0] == 0)
+
+
+def test_attention_restatements_agree(oracle):
+    """The numpy attention (used by the block oracle) and the C one
+    (oracle_vit_attention) are independent restatements of the same graph."""
+    rng = np.random.default_rng(3)
+    for grid, heads, window in ((16, 2, 8), (12, 1, 0)):
+        E = heads * 64
+        qkv = rng.normal(0, 1, (grid * grid, 3 * E)).astype(np.float32)
+        freqs = oracle.rope_freqs(window * window if window else grid * grid, seed=grid)
+        a = oracle.attention_np(qkv, grid, grid, heads, window, freqs)
+        b = oracle.vit_attention(qkv, grid, grid, heads, 64, window, freqs)
+        np.testing.assert_allclose(a, b, rtol=0, atol=2e-6)
+        rows = np.array([0, 5, grid * grid - 1])
+        np.testing.assert_array_equal(oracle.attention_np(qkv, grid, grid, heads, window, freqs, rows=rows), a[rows])
+
+
+def test_rope_matches_reference_scalar_formula(oracle):
+    """sam3_apply_rope against the independent scalar complex formula of
+    tests/runtime/ggml/test_rope.cpp:76-93, with its identity and quarter-turn
+    tables: (re cos - im sin, re sin + im cos) within 2e-6 (1 + |expected|)."""
+    rng = np.random.default_rng(0)
+    x = rng.normal(0, 1, (37, 64)).astype(np.float32)
+    for c, s in ((1.0, 0.0), (0.0, 1.0)):
+        f = np.zeros((37, 32, 2), np.float32)
+        f[..., 0], f[..., 1] = c, s
+        out = oracle.rope64(x, f)
+        re, im = x[:, 0::2].astype(np.float64), x[:, 1::2].astype(np.float64)
+        exp_re, exp_im = re * c - im * s, re * s + im * c
+        tol = 2e-6 * (1 + np.maximum(np.abs(exp_re), np.abs(exp_im)))
+        assert np.all(np.abs(out[:, 0::2] - exp_re) <= tol) and np.all(np.abs(out[:, 1::2] - exp_im) <= tol)

@@ -5,11 +5,22 @@ allocator owns the device memory, serving loops that cannot take cudaMalloc's
 device synchronization, hosts that must not run out of memory mid-request) use
 this entry point: it keeps the staged activation operand in a fixed device
 array of the library instead of allocated scratch.  These tests call it
-through the C ABI and compare it with samq_linear_v1 on two calls in a row,
-which also shows that the shared array is rewritten correctly by the second
-call.  The file is named so that pytest collects it last.
+through the C ABI, twice in a row per case (the second call must rewrite the
+shared array correctly), and check it:
+  - against the CPU oracle (f32-decoded weights x decoded Q8_1 activations,
+    f64 dots): cosine >= 0.9999, normalized max error <= 2e-3;
+  - against samq_linear_v1: bit-identical for m > 64 (same kernels on the same
+    operand), within the same tolerance for m <= 64, where samq_linear_v1
+    streams the packed weights with split-K accumulation instead;
+  - that its range findings reach samq_check_v1;
+  - in a fresh process, that calls after the first one leave the device's free
+    memory unchanged.
+The file is named so that pytest collects it last.
 """
-import ctypes
+import subprocess
+import sys
+import textwrap
+from pathlib import Path
 
 import numpy as np
 import pytest
@@ -17,6 +28,7 @@ import pytest
 torch = pytest.importorskip("torch")
 pytestmark = pytest.mark.gpu
 
+ROOT = Path(__file__).resolve().parent.parent
 COS_MIN = 0.9999
 MAX_REL = 2e-3
 
@@ -49,24 +61,42 @@ def metrics(y, ref):
     return cos, float(np.max(np.abs(y64 - r64)) / np.max(np.abs(r64)))
 
 
-def test_static_entry_point_matches_linear_on_two_calls(samq, oracle):
-    rng = np.random.default_rng(2024)
-    cases = [(12, 1024, 768, 300, 1), (8, 4736, 256, 97, 0)]  # (type, k, n, m, epilogue)
-    for qtype, k, n, m, epilogue in cases:
-        rows = oracle.quantize(qtype, weights_matrix(rng, n, k))
-        w = samq.Weights(qtype, k, n, rows)
-        x = torch.from_numpy(rng.normal(0, 1, (m, k)).astype(np.float32)).cuda()
-        bias = torch.from_numpy(rng.normal(0, 0.1, n).astype(np.float32)).cuda()
-        y_static = torch.full((m, n), -3.0, dtype=torch.float32, device="cuda")
-        assert call_static(samq, w, x, m, k, bias, epilogue, y_static, n) == 0, \
-            samq.library().samq_last_error_v1()
-        y_ref = torch.empty((m, n), dtype=torch.float32, device="cuda")
-        samq.linear(w, x, m, k, bias, epilogue, y_ref, n)
-        torch.cuda.synchronize()
-        got, ref = y_static.cpu().numpy(), y_ref.cpu().numpy()
-        cos, rel = metrics(got, ref)
-        assert cos >= COS_MIN and rel <= MAX_REL, (cos, rel)
-        np.testing.assert_array_equal(got, ref)  # same kernels, same operand: identical
+# (type, k, n, m, epilogue): m > 64 takes the same GEMM as samq_linear_v1; m <= 64
+# (1, 32, 64) is where samq_linear_v1 streams packets instead; k = 1056 and 96
+# are multiples of 32 but not of 64 (a partial last K tile).
+CASES = [(12, 1024, 768, 300, 1), (8, 4736, 256, 97, 0), (8, 1056, 384, 64, 1), (14, 512, 256, 1, 0),
+         (8, 96, 128, 32, 0), (13, 768, 200, 65, 1)]
+
+
+@pytest.mark.parametrize("qtype,k,n,m,epilogue", CASES)
+def test_static_entry_point_matches_oracle_and_linear(samq, oracle, qtype, k, n, m, epilogue):
+    rng = np.random.default_rng(2024 + k + m)
+    rows = oracle.quantize(qtype, weights_matrix(rng, n, k))
+    w_dec = oracle.dequantize(qtype, rows, n * k).reshape(n, k)
+    w = samq.Weights(qtype, k, n, rows)
+    bias_h = rng.normal(0, 0.1, n).astype(np.float32)
+    bias = torch.from_numpy(bias_h).cuda()
+    try:
+        for call in range(2):  # two calls in a row through the shared array
+            x_h = rng.normal(0, 1 + call, (m, k)).astype(np.float32)
+            x = torch.from_numpy(x_h).cuda()
+            y_static = torch.full((m, n), -3.0, dtype=torch.float32, device="cuda")
+            assert call_static(samq, w, x, m, k, bias, epilogue, y_static, n) == 0, \
+                samq.library().samq_last_error_v1()
+            y_ref = torch.empty((m, n), dtype=torch.float32, device="cuda")
+            samq.linear(w, x, m, k, bias, epilogue, y_ref, n)
+            samq.check(0)
+            got, lin = y_static.cpu().numpy(), y_ref.cpu().numpy()
+            x_dec = oracle.q8_1_decode(oracle.quantize_q8_1(x_h), m, k)
+            ref = oracle.gemm_f64(w_dec, x_dec, bias=bias_h, epilogue=epilogue)
+            cos, rel = metrics(got, ref)
+            assert cos >= COS_MIN and rel <= MAX_REL, ("oracle", call, cos, rel)
+            if m > 64:
+                np.testing.assert_array_equal(got, lin)  # same kernels, same operand
+            else:
+                cos, rel = metrics(got, lin)
+                assert cos >= COS_MIN and rel <= MAX_REL, ("samq_linear_v1", call, cos, rel)
+    finally:
         w.close()
 
 
@@ -80,3 +110,70 @@ def test_static_entry_point_rejects_oversize(samq, oracle):
     rc = call_static(samq, w, x, m, k, None, 0, y, n)
     assert rc == 1 and b"SAMQ_STATIC_OPERAND_ELEMENTS" in samq.library().samq_last_error_v1()
     w.close()
+
+
+def test_static_entry_point_reports_range_to_check(samq, oracle):
+    """An activation beyond the f16 operand range is recorded in the path's
+    fixed status word and reported (then cleared) by samq_check_v1."""
+    rng = np.random.default_rng(11)
+    k, n, m = 256, 128, 80
+    w = samq.Weights(8, k, n, oracle.quantize(8, weights_matrix(rng, n, k)))
+    x_h = rng.normal(0, 1, (m, k)).astype(np.float32)
+    x_h[7, 3] = 1.0e6
+    x = torch.from_numpy(x_h).cuda()
+    y = torch.empty((m, n), dtype=torch.float32, device="cuda")
+    try:
+        assert call_static(samq, w, x, m, k, None, 0, y, n) == 0
+        stream = torch.cuda.current_stream().cuda_stream
+        assert samq.library().samq_check_v1(0, stream) == 5  # SAMQ_ERR_RANGE
+        x_h[7, 3] = 0.5
+        x.copy_(torch.from_numpy(x_h))
+        assert call_static(samq, w, x, m, k, None, 0, y, n) == 0
+        assert samq.library().samq_check_v1(0, stream) == 0
+    finally:
+        w.close()
+
+
+_NO_ALLOC_SCRIPT = textwrap.dedent("""
+    import sys
+    sys.path[:0] = [{root!r}, {pkg!r}]
+    import numpy as np, torch
+    import samq
+    from oracle import oracle as o
+    samq.init(0)
+    rng = np.random.default_rng(3)
+    lib = samq.library()
+    stream = torch.cuda.current_stream().cuda_stream
+    handles, cases = [], []
+    for qtype, k, n, m in ((12, 1024, 1024, 4096), (8, 4736, 512, 3000), (8, 2048, 256, 48)):
+        w = samq.Weights(qtype, k, n, o.quantize(qtype, rng.normal(0, 0.02, (n, k)).astype(np.float32)))
+        x = torch.randn((m, k), device="cuda")
+        y = torch.empty((m, n), device="cuda")
+        handles.append(w)
+        cases.append((w, x, y, m, k, n))
+    def call(w, x, y, m, k, n):
+        rc = lib.samq_linear_static_v1(w.handle, x.data_ptr(), m, k, None, 0, y.data_ptr(), n, stream)
+        assert rc == 0, lib.samq_last_error_v1()
+    torch.cuda.synchronize()
+    call(*cases[2])  # first call on the device: address look-up
+    torch.cuda.synchronize()
+    free_before = torch.cuda.mem_get_info(0)[0]
+    for _ in range(2):
+        for c in cases:
+            call(*c)
+    torch.cuda.synchronize()
+    assert lib.samq_check_v1(0, stream) == 0, lib.samq_last_error_v1()
+    free_after = torch.cuda.mem_get_info(0)[0]
+    print("free before", free_before, "after", free_after)
+    assert free_after == free_before, (free_before, free_after)
+""")
+
+
+def test_static_entry_point_allocates_nothing_in_fresh_process():
+    """A fresh process: after the first call (which looks up the array's
+    address), calls whose samq_linear_v1 scratch would need up to 27 MB leave
+    the device's free memory exactly unchanged, and so does samq_check_v1."""
+    script = _NO_ALLOC_SCRIPT.format(root=str(ROOT), pkg=str(ROOT / "sam.cpp_b200"))
+    proc = subprocess.run([sys.executable, "-c", script], cwd=str(ROOT), capture_output=True, text=True,
+                          timeout=600)
+    assert proc.returncode == 0, proc.stdout[-2000:] + proc.stderr[-4000:]
