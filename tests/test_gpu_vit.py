@@ -41,6 +41,7 @@ def make_block(rng, window, positions, qtype=o.Q4_K, fc2_type=o.Q8_0, E=E, MLP=M
                             "fc2": (E, MLP, fc2_type)}.items():
         rows = o.quantize(t, _weights(rng, n, k))
         host[name + "_w"] = o.dequantize(t, rows, n * k).reshape(n, k)
+        host[name + "_q"] = (t, rows)
         gpu[name] = samq.Weights(t, k, n, rows)
         bias = rng.normal(0.0, 0.02, n).astype(np.float32)
         host[name + "_b"] = bias
