@@ -302,8 +302,10 @@ def run_reference(args, world, rank):
     print(json.dumps(line), flush=True)
 
 
-def make_backbone(samq, o, torch, device, rank):
-    """Random-init SAM 3 vision backbone on `device` (config 3 statistics)."""
+def make_backbone(samq, o, torch, device, rank, compute=None):
+    """Random-init SAM 3 vision backbone on `device` (config 3 statistics),
+    blocks in the headline compute mode (F16) unless `compute` is given."""
+    compute = samq.COMPUTE_F16 if compute is None else compute
     dev = torch.device("cuda", device)
     blocks, keep = [], []
     base = np.random.default_rng(2024 + rank)
@@ -323,7 +325,7 @@ def make_backbone(samq, o, torch, device, rank):
         window = 0 if i in GLOBAL_BLOCKS else WINDOW
         blocks.append(samq.VitBlock(window, t["norm1_w"], t["norm1_b"], t["qkv"], t["qkv_b"], t["proj"],
                                     t["proj_b"], t["norm2_w"], t["norm2_b"], t["fc1"], t["fc1_b"], t["fc2"],
-                                    t["fc2_b"], freqs_g if window == 0 else freqs_w))
+                                    t["fc2_b"], freqs_g if window == 0 else freqs_w, compute=compute))
         keep.append(t)
     rng = np.random.default_rng(77 + rank)
     prefix = {
@@ -386,10 +388,10 @@ def main():
     feats = torch.empty((M, E), dtype=torch.float32, device="cuda")
     feats_host = torch.empty((M, E), dtype=torch.float32).pin_memory()
 
-    def forward(img=image, out=feats):
+    def forward(img=image, out=feats, blks=blocks, compute=samq.COMPUTE_F16):
         samq.vit_prefix(img, IMAGE, IMAGE, PATCH, prefix["patch_w"], E, prefix["pos"], POS_GRID, prefix["ln_w"],
-                        prefix["ln_b"], out, stream)
-        for blk in blocks:
+                        prefix["ln_b"], out, stream, compute=compute)
+        for blk in blks:
             samq.vit_block_forward(blk, out, GRID, GRID, stream)
 
     for _ in range(args.warmup):
@@ -521,6 +523,11 @@ def main():
     # Config 5's batching: the same backbone over 8 images per GPU per step.
     batch8 = batch_section(samq, torch, stream, args, max_over_ranks, blocks, prefix, world, rank)
     samq.check(local, stream)
+    # The reference's default compute mode (F32 attention and patch columns)
+    # on the same weights: a secondary figure beside the F16-mode headline.
+    f32_blocks = [samq.VitBlock(b.window, *b._keep, compute=samq.COMPUTE_F32) for b in blocks]
+    f32_mode = f32_section(samq, torch, stream, max_over_ranks, forward, f32_blocks, image, feats, world)
+    samq.check(local, stream)
     # Config 5's sharding protocol: 64 images cut into contiguous per-rank ranges.
     sweep = sweep64_section(samq, torch, stream, max_over_ranks, blocks, prefix, world, rank,
                             dist if world > 1 else None)
@@ -541,6 +548,9 @@ def main():
             "metric": METRIC, "value": value, "unit": "images/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": elapsed_ms / args.steps, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "f16", "data": "synthetic",
+            "compute_mode": "F16: the reference's opt-in CudaComputeMode::F16 (f16 tensor-core attention operands, "
+                            "f16 patch columns); quantized linears (Q8_1 staging, f16 operands on tcgen05) are the "
+                            "same in both modes; the default F32 mode is timed in `f32_mode`",
             "config": workload_config(world),
             "roofline": roofline,
             "cpu_baseline": cpu,
@@ -557,6 +567,7 @@ def main():
             "neck": neck,
             "batch8": batch8,
             "sweep64": sweep,
+            "f32_mode": f32_mode,
         }
         print(json.dumps(line), flush=True)
     for w in weights:
@@ -577,7 +588,7 @@ def batch_section(samq, torch, stream, args, max_over_ranks, blocks, prefix, wor
     def fwd():
         for b in range(batch):
             samq.vit_prefix(imgs[b], IMAGE, IMAGE, PATCH, prefix["patch_w"], E, prefix["pos"], POS_GRID,
-                            prefix["ln_w"], prefix["ln_b"], xb[b], stream)
+                            prefix["ln_w"], prefix["ln_b"], xb[b], stream, compute=samq.COMPUTE_F16)
         for blk in blocks:
             samq.vit_block_forward(blk, xb, GRID, GRID, stream, batch=batch)
 
@@ -595,6 +606,24 @@ def batch_section(samq, torch, stream, args, max_over_ranks, blocks, prefix, wor
             "value": steps * batch * world / (ms / 1e3), "unit": "images/s", "batch_per_gpu": batch, "steps": steps,
             "ms_per_step": ms / steps, "features_finite": bool(torch.isfinite(xb).all().item()),
             "gpu_launches": steps * batch * 4 + steps * DEPTH * 7}
+
+
+def f32_section(samq, torch, stream, max_over_ranks, forward, f32_blocks, image, feats, world, steps=10):
+    """Images/s of the same backbone in the reference's default compute mode
+    (SAMQ_COMPUTE_F32: F32 patch columns, f32 qkv and F32-precise attention)."""
+    for _ in range(3):
+        forward(image, feats, f32_blocks, samq.COMPUTE_F32)
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record(stream)
+    for _ in range(steps):
+        forward(image, feats, f32_blocks, samq.COMPUTE_F32)
+    b.record(stream)
+    torch.cuda.synchronize()
+    ms = max_over_ranks(a.elapsed_time(b))
+    return {"metric": "SAM3 vision backbone images/s, compute mode F32 (the reference's default: F32 attention and "
+                      "patch columns)", "value": steps * world / (ms / 1e3), "unit": "images/s", "steps": steps,
+            "ms_per_step": ms / steps, "features_finite": bool(torch.isfinite(feats).all().item())}
 
 
 def sweep64_section(samq, torch, stream, max_over_ranks, blocks, prefix, world, rank, dist, n_images=64, batch=8):
@@ -617,7 +646,7 @@ def sweep64_section(samq, torch, stream, max_over_ranks, blocks, prefix, world, 
         for b0, b1 in own:
             for j in range(b1 - b0):
                 samq.vit_prefix(imgs[b0 - start + j], IMAGE, IMAGE, PATCH, prefix["patch_w"], E, prefix["pos"],
-                                POS_GRID, prefix["ln_w"], prefix["ln_b"], xb[j], stream)
+                                POS_GRID, prefix["ln_w"], prefix["ln_b"], xb[j], stream, compute=samq.COMPUTE_F16)
             for blk in blocks:
                 samq.vit_block_forward(blk, xb, GRID, GRID, stream, batch=b1 - b0)
 
@@ -696,7 +725,8 @@ def neck_section(samq, torch, stream, args, max_over_ranks, pk, steps=10):
             "gpu_launches_per_call": 17, "method": "three-term TF32 split on tcgen05 kind::tf32, segment sums in f32"}
 
 
-PROFILE_EXTRA = ("attention_window", "attention_global", "text_fc2", "neck_conv3x3", "vit_block")
+PROFILE_EXTRA = ("attention_window", "attention_global", "attention_window_f32", "attention_global_f32", "text_fc2",
+                 "neck_conv3x3", "vit_block")
 
 
 def run_profile_case(args):
@@ -730,13 +760,14 @@ def run_profile_case(args):
         torch.cuda.synchronize()
         w.close()
     elif args.profile.startswith("attention"):
-        window = WINDOW if args.profile == "attention_window" else 0
+        window = WINDOW if args.profile.startswith("attention_window") else 0
         rng = np.random.default_rng(3)
         qkv = torch.from_numpy(rng.normal(0, 1, (M, 3 * E)).astype(np.float32)).cuda()
         freqs = torch.from_numpy(o.rope_freqs(WINDOW * WINDOW if window else M)).cuda()
         out = torch.empty((M, E), dtype=torch.float32, device="cuda")
         for _ in range(launches):
-            samq.vit_attention(qkv, 3 * E, GRID, GRID, HEADS, window, freqs, out, E, stream)
+            samq.vit_attention(qkv, 3 * E, GRID, GRID, HEADS, window, freqs, out, E, stream,
+                               compute=samq.COMPUTE_F32 if args.profile.endswith("_f32") else samq.COMPUTE_F16)
     elif args.profile == "text_fc2":
         n, k, m = 1024, 4096, 32
         packed, bias = make_weights(o, n, k, 8, 5)

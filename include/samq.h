@@ -64,6 +64,18 @@ enum {
     SAMQ_EPILOGUE_GELU_ERF = 1 /* ggml_gelu_erf after the bias (src/models/sam3/vision.hpp:234-236) */
 };
 
+/* Arithmetic of the ViT attention and patch embedding: sam::CudaComputeMode
+ * (include/sam/types.hpp:13,21; default F32).  F32 is the reference's default
+ * precise mode (GGML_PREC_F32 attention, F32 convolution columns); F16 is its
+ * opt-in reduced mode (src/runtime/ggml/backends/cuda.hpp:82-92,177-186: f16
+ * Q / K / V / P on the tensor cores, f16 convolution columns).  Quantized
+ * linears compute the same way in both modes, as in the reference (MMQ over
+ * Q8_1-staged activations). */
+enum {
+    SAMQ_COMPUTE_F32 = 0,
+    SAMQ_COMPUTE_F16 = 1
+};
+
 typedef struct samq_weights samq_weights;
 
 /* Replaces the device checks of make_cuda_backend
@@ -162,6 +174,23 @@ samq_status samq_linear_f16_v1(const samq_weights* weights, const void* x_f16, i
  * tensor cores with f32 accumulation and an f32 online softmax. */
 samq_status samq_vit_attention_v1(const float* qkv, int64_t ldq, int grid_w, int grid_h, int heads, int head_dim,
                                   int window, const float* freqs_cis, float* out, int64_t ldo, void* stream);
+/* samq_vit_attention_v1 with the compute mode chosen: SAMQ_COMPUTE_F16 is
+ * exactly samq_vit_attention_v1; SAMQ_COMPUTE_F32 keeps Q, K, V and P in f32
+ * (RoPE with GGML's rounding, f32 products and expf softmax on the FP32 pipe),
+ * the reference's GGML_PREC_F32 attention checked at 1e-5 by
+ * tests/runtime/ggml/test_precision.cpp:68-126. */
+samq_status samq_vit_attention_v2(const float* qkv, int64_t ldq, int grid_w, int grid_h, int heads, int head_dim,
+                                  int window, const float* freqs_cis, float* out, int64_t ldo, int compute,
+                                  void* stream);
+
+/* sam3_apply_rope (src/models/sam3/vision.hpp:113-148) on its own: x and out
+ * are device f32 [head_batches][tokens][head_dim] (GGML [head_dim, N,
+ * heads * B]), freqs_cis [tokens][head_dim / 2][2] (cos, sin); channel pairs
+ * (2i, 2i+1) become (re cos - im sin, re sin + im cos), each product and the
+ * sum rounded to f32 as GGML's mul / sub / add nodes do.  head_dim == 64;
+ * out may equal x. */
+samq_status samq_vit_rope_v1(const float* x, int64_t tokens, int64_t head_batches, int head_dim,
+                             const float* freqs_cis, float* out, void* stream);
 
 /* One SAM 3 ViT block, pre-LN (src/models/sam3/vision.hpp:152-243):
  *   x = x + proj(attn(RoPE(qkv(LN1(x)))))   (windowed or global attention)
@@ -174,7 +203,7 @@ samq_status samq_vit_attention_v1(const float* qkv, int64_t ldq, int grid_w, int
  * qkv E -> 3E, proj E -> E, fc1 E -> MLP, fc2 MLP -> E, with E = 64 * heads
  * and E in {256, 512, 1024}; MLP % 32 == 0. */
 typedef struct samq_vit_block_v1 {
-    uint32_t version;  /* 1 */
+    uint32_t version;  /* 1, or 2 with the compute field */
     int32_t window;    /* 24: windowed blocks (grid divisible by it), 0: global */
     const float* norm1_w;
     const float* norm1_b;
@@ -189,6 +218,11 @@ typedef struct samq_vit_block_v1 {
     const samq_weights* fc2;
     const float* fc2_b;
     const float* freqs_cis;
+    /* version >= 2 only: SAMQ_COMPUTE_F32 (the reference's default) or
+     * SAMQ_COMPUTE_F16.  A version-1 descriptor (which ends before this field)
+     * runs SAMQ_COMPUTE_F16.  In F32 mode the qkv linear's output stays f32 and
+     * the attention is samq_vit_attention_v2's F32 path. */
+    int32_t compute;
 } samq_vit_block_v1;
 
 /* Runs one block in place on the residual stream x, device f32
@@ -213,6 +247,14 @@ samq_status samq_vit_block_forward_batch_v1(const samq_vit_block_v1* block, floa
 samq_status samq_vit_prefix_v1(const float* image, int width, int height, int patch, const float* patch_w,
                                int64_t embed, const float* pos_embed, int pos_grid, const float* ln_w,
                                const float* ln_b, float* x, void* stream);
+/* samq_vit_prefix_v1 with the compute mode chosen: SAMQ_COMPUTE_F16 is
+ * samq_vit_prefix_v1 (f16 convolution columns, as the reference's F16 mode
+ * sets convolution_columns_type, src/runtime/ggml/backends/cuda.hpp:182-185);
+ * SAMQ_COMPUTE_F32 keeps F32 columns and runs the convolution with F32
+ * semantics (the three-term TF32 split of the dense modules below). */
+samq_status samq_vit_prefix_v2(const float* image, int width, int height, int patch, const float* patch_w,
+                               int64_t embed, const float* pos_embed, int pos_grid, const float* ln_w,
+                               const float* ln_b, float* x, int compute, void* stream);
 
 /* ---- Dense (F32 / F16) modules with F32 semantics -------------------------
  * The tensors the reference keeps unquantized (neck convolutions, fusion /

@@ -1,0 +1,281 @@
+// attention_f32.cu -- F32-precise RoPE + windowed / global attention of a SAM 3
+// ViT block (the reference's default CudaComputeMode::F32).
+//
+// The reference's CUDA backend runs ViT attention at GGML_PREC_F32 unless the
+// F16 compute mode is selected (src/runtime/ggml/backends/cuda.hpp:82-92,
+// 156-189): F32 Q, K and V, F32 products (cuBLAS SGEMM in the SAM patch,
+// cmake/patches/ggml-precise-cuda.patch:448-606) and an F32 softmax, checked by
+// a closed-form probe at 1e-5 (tests/runtime/ggml/test_precision.cpp:68-126).
+// Here every operand stays f32 and the products run on the FP32 pipe:
+//   rope_f32_kernel       sam3_apply_rope (src/models/sam3/vision.hpp:100-148)
+//                         with GGML's op sequence and rounding: re*cos and
+//                         im*sin are separate f32 products, then one f32
+//                         subtraction (ggml_mul, ggml_mul, ggml_sub), and
+//                         likewise re*sin + im*cos.
+//   attention_f32_kernel  one CTA per (64 queries, head, group): Q (RoPE'd,
+//                         x 1/8, exact as 1/8 is a power of two) held in
+//                         shared memory, K (RoPE'd) and V staged 64 keys at a
+//                         time, S = Q K^T and O += P V as 4 x 4 register
+//                         tiles per thread over float4 shared-memory loads,
+//                         online softmax with expf, O / l at the end.  The
+//                         output is f32 in raster token order or, in the ViT
+//                         block, the proj linear's Q8_1-staged f16 operand.
+// Window partition / unpartition (ggml_win_part / win_unpart,
+// vision.hpp:170-173,225-227) are the same address maps as in attention.cu.
+// No waits on other CTAs, so nothing here can hang.
+#include <algorithm>
+
+#include "samq_internal.hpp"
+
+namespace samq {
+namespace {
+
+constexpr int kHd = 64;
+constexpr int kTile = 64;       // queries per CTA and keys per step
+constexpr int kPitch = 68;      // shared-memory row pitch (floats): conflict-free float4 columns
+constexpr int kF32Threads = 256;
+constexpr int kF32Smem = 4 * kTile * kPitch * 4;  // Q, K, V^T, P
+
+struct GeometryF32 {
+    int grid_w, grid_h, heads, window;
+    int groups, group_n;
+    int qkv_window_major;  // qkv rows stored window-major (g * group_n + n) instead of raster
+};
+
+__device__ __forceinline__ int raster_token(const GeometryF32& geo, int g, int n) {
+    if (geo.window == 0) return g * geo.group_n + n;
+    const int per_row = geo.grid_w / geo.window;
+    const int wy = g / per_row, wx = g % per_row;
+    const int ly = n / geo.window, lx = n % geo.window;
+    return (wy * geo.window + ly) * geo.grid_w + wx * geo.window + lx;
+}
+
+__device__ __forceinline__ int qkv_row(const GeometryF32& geo, int g, int n) {
+    return geo.qkv_window_major ? g * geo.group_n + n : raster_token(geo, g, n);
+}
+
+// GGML's RoPE arithmetic for the pairs (x0, x1) and (x2, x3) of a float4.
+__device__ __forceinline__ float4 rope4(float4 x, float4 f) {
+    float4 r;
+    r.x = __fsub_rn(__fmul_rn(x.x, f.x), __fmul_rn(x.y, f.y));
+    r.y = __fadd_rn(__fmul_rn(x.x, f.y), __fmul_rn(x.y, f.x));
+    r.z = __fsub_rn(__fmul_rn(x.z, f.z), __fmul_rn(x.w, f.w));
+    r.w = __fadd_rn(__fmul_rn(x.z, f.w), __fmul_rn(x.w, f.z));
+    return r;
+}
+
+__global__ void __launch_bounds__(256) rope_f32_kernel(const float* __restrict__ x, const float* __restrict__ freqs,
+                                                       int64_t tokens, int64_t head_batches, float* __restrict__ out) {
+    const int64_t units = head_batches * tokens * (kHd / 4);
+    for (int64_t u = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; u < units; u += int64_t(gridDim.x) * blockDim.x) {
+        const int64_t c4 = u % (kHd / 4);
+        const int64_t token = (u / (kHd / 4)) % tokens;
+        const float4 v = __ldg(reinterpret_cast<const float4*>(x) + u);
+        const float4 f = __ldg(reinterpret_cast<const float4*>(freqs + (token * (kHd / 2) + c4 * 2) * 2));
+        reinterpret_cast<float4*>(out)[u] = rope4(v, f);
+    }
+}
+
+__device__ __forceinline__ float dot4(float4 a, float4 b, float acc) {
+    acc = fmaf(a.x, b.x, acc);
+    acc = fmaf(a.y, b.y, acc);
+    acc = fmaf(a.z, b.z, acc);
+    return fmaf(a.w, b.w, acc);
+}
+
+template <bool STAGED>
+__global__ void __launch_bounds__(kF32Threads, 2)
+attention_f32_kernel(const float* __restrict__ qkv, int64_t ldq, const float* __restrict__ freqs, GeometryF32 geo,
+                     float* __restrict__ out, __half* __restrict__ out_h, int64_t ldo, DeviceStatus* status) {
+    extern __shared__ float4 smem_f4[];
+    float* qs = reinterpret_cast<float*>(smem_f4);   // [64 queries][kPitch]
+    float* ks = qs + kTile * kPitch;                 // [64 keys][kPitch]
+    float* vt = ks + kTile * kPitch;                 // [64 dims][kPitch]  (V transposed)
+    float* ps = vt + kTile * kPitch;                 // [64 queries][kPitch]
+    const int t = threadIdx.x;
+    const int rq = t >> 4, u = t & 15;               // rows 4rq..4rq+3; keys / dims u + 16j
+    const int q0 = blockIdx.x * kTile, h = blockIdx.y, g = blockIdx.z;
+    const int E = geo.heads * kHd;
+    pdl_wait();
+
+    // Q: RoPE by the query's position in its group, x 1/8 (exact).
+    for (int idx = t; idx < kTile * 16; idx += kF32Threads) {
+        const int r = idx >> 4, c4 = idx & 15, n = q0 + r;
+        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (n < geo.group_n) {
+            const float4 x = __ldg(reinterpret_cast<const float4*>(qkv + int64_t(qkv_row(geo, g, n)) * ldq + h * kHd) + c4);
+            const float4 f = __ldg(reinterpret_cast<const float4*>(freqs + (int64_t(n) * (kHd / 2) + c4 * 2) * 2));
+            v = rope4(x, f);
+            v.x *= 0.125f;
+            v.y *= 0.125f;
+            v.z *= 0.125f;
+            v.w *= 0.125f;
+        }
+        *reinterpret_cast<float4*>(qs + r * kPitch + c4 * 4) = v;
+    }
+
+    float o[4][4], m[4], l[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        m[i] = -INFINITY;
+        l[i] = 0.0f;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) o[i][j] = 0.0f;
+    }
+    const int kblocks = (geo.group_n + kTile - 1) / kTile;
+    for (int kb = 0; kb < kblocks; ++kb) {
+        __syncthreads();  // previous step's K, V^T and P reads are done (and Q is written)
+        for (int idx = t; idx < kTile * 16; idx += kF32Threads) {
+            const int r = idx >> 4, c4 = idx & 15, n = kb * kTile + r;
+            float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (n < geo.group_n) {
+                const float4 x =
+                    __ldg(reinterpret_cast<const float4*>(qkv + int64_t(qkv_row(geo, g, n)) * ldq + E + h * kHd) + c4);
+                const float4 f = __ldg(reinterpret_cast<const float4*>(freqs + (int64_t(n) * (kHd / 2) + c4 * 2) * 2));
+                v = rope4(x, f);
+            }
+            *reinterpret_cast<float4*>(ks + r * kPitch + c4 * 4) = v;
+        }
+        for (int idx = t; idx < kTile * 16; idx += kF32Threads) {
+            const int r = idx & 63, d4 = idx >> 6, n = kb * kTile + r;  // consecutive lanes: consecutive keys
+            float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (n < geo.group_n)
+                v = __ldg(reinterpret_cast<const float4*>(qkv + int64_t(qkv_row(geo, g, n)) * ldq + 2 * E + h * kHd) + d4);
+            vt[(4 * d4 + 0) * kPitch + r] = v.x;
+            vt[(4 * d4 + 1) * kPitch + r] = v.y;
+            vt[(4 * d4 + 2) * kPitch + r] = v.z;
+            vt[(4 * d4 + 3) * kPitch + r] = v.w;
+        }
+        __syncthreads();
+
+        float s[4][4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+#pragma unroll
+            for (int j = 0; j < 4; ++j) s[i][j] = 0.0f;
+#pragma unroll 4
+        for (int d4 = 0; d4 < 16; ++d4) {
+            float4 a[4], b[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) a[i] = *reinterpret_cast<const float4*>(qs + (4 * rq + i) * kPitch + 4 * d4);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) b[j] = *reinterpret_cast<const float4*>(ks + (u + 16 * j) * kPitch + 4 * d4);
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+#pragma unroll
+                for (int j = 0; j < 4; ++j) s[i][j] = dot4(a[i], b[j], s[i][j]);
+        }
+        // Online softmax of the 4 rows; a row's 64 scores sit on 16 neighbouring lanes.
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            float mx = -INFINITY;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                if (kb * kTile + u + 16 * j >= geo.group_n) s[i][j] = -INFINITY;
+                mx = fmaxf(mx, s[i][j]);
+            }
+#pragma unroll
+            for (int off = 1; off < 16; off <<= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+            const float m_new = fmaxf(m[i], mx);
+            const float alpha = expf(m[i] - m_new);
+            float sum = 0.0f;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const float p = expf(s[i][j] - m_new);
+                ps[(4 * rq + i) * kPitch + u + 16 * j] = p;
+                sum += p;
+            }
+#pragma unroll
+            for (int off = 1; off < 16; off <<= 1) sum += __shfl_xor_sync(0xffffffffu, sum, off);
+            l[i] = fmaf(l[i], alpha, sum);
+            m[i] = m_new;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) o[i][j] *= alpha;
+        }
+        __syncthreads();
+#pragma unroll 4
+        for (int k4 = 0; k4 < 16; ++k4) {
+            float4 a[4], b[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) a[i] = *reinterpret_cast<const float4*>(ps + (4 * rq + i) * kPitch + 4 * k4);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) b[j] = *reinterpret_cast<const float4*>(vt + (u + 16 * j) * kPitch + 4 * k4);
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+#pragma unroll
+                for (int j = 0; j < 4; ++j) o[i][j] = dot4(a[i], b[j], o[i][j]);
+        }
+    }
+    pdl_trigger();
+
+    if constexpr (!STAGED) {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const int n = q0 + 4 * rq + i;
+            if (n >= geo.group_n) continue;
+            float* row = out + int64_t(raster_token(geo, g, n)) * ldo + h * kHd;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) row[u + 16 * j] = __fdiv_rn(o[i][j], l[i]);
+        }
+    } else {
+        // O / l through shared memory, then each warp stages whole rows: lane
+        // holds channels 2 lane, 2 lane + 1, so one Q8_1 block is 16 lanes.
+        __syncthreads();
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+#pragma unroll
+            for (int j = 0; j < 4; ++j) ps[(4 * rq + i) * kPitch + u + 16 * j] = __fdiv_rn(o[i][j], l[i]);
+        __syncthreads();
+        const int warp = t >> 5, lane = t & 31;
+        for (int r = warp; r < kTile; r += kF32Threads / 32) {
+            const int n = q0 + r;
+            if (n >= geo.group_n) break;  // warp-uniform
+            const float2 v2 = *reinterpret_cast<const float2*>(ps + r * kPitch + 2 * lane);
+            const float v[2] = {v2.x, v2.y};
+            uint32_t packed[1];
+            const bool bad = stage_q8_1<16, 2>(v, packed);
+            record_range(bad, status);
+            *reinterpret_cast<uint32_t*>(out_h + int64_t(raster_token(geo, g, n)) * ldo + h * kHd + 2 * lane) = packed[0];
+        }
+    }
+}
+
+GeometryF32 make_geometry_f32(int grid_w, int grid_h, int heads, int window, int batch, bool window_major) {
+    GeometryF32 geo{grid_w, grid_h * batch, heads, window, batch, grid_w * grid_h, window_major ? 1 : 0};
+    if (window > 0) {
+        geo.groups = (grid_w / window) * (grid_h * batch / window);
+        geo.group_n = window * window;
+    }
+    return geo;
+}
+
+}  // namespace
+
+void launch_attention_f32(const float* qkv, int64_t ldq, bool qkv_window_major, int grid_w, int grid_h, int heads,
+                          int window, int batch, const float* freqs, float* out, __half* out_h, int64_t ldo,
+                          DeviceState& state, cudaStream_t stream) {
+    const GeometryF32 geo = make_geometry_f32(grid_w, grid_h, heads, window, batch, qkv_window_major);
+    const dim3 grid((geo.group_n + kTile - 1) / kTile, heads, geo.groups);
+    if (out_h) {
+        set_smem_limit_once(state, reinterpret_cast<const void*>(attention_f32_kernel<true>), kF32Smem,
+                            "cudaFuncSetAttribute(attention_f32 smem)");
+        launch_pdl(attention_f32_kernel<true>, grid, dim3(kF32Threads), kF32Smem, stream,
+                   "attention_f32_kernel launch", qkv, ldq, freqs, geo, out, out_h, ldo, state.status);
+    } else {
+        set_smem_limit_once(state, reinterpret_cast<const void*>(attention_f32_kernel<false>), kF32Smem,
+                            "cudaFuncSetAttribute(attention_f32 smem)");
+        launch_pdl(attention_f32_kernel<false>, grid, dim3(kF32Threads), kF32Smem, stream,
+                   "attention_f32_kernel launch", qkv, ldq, freqs, geo, out, out_h, ldo, state.status);
+    }
+}
+
+void launch_rope_f32(const float* x, const float* freqs, int64_t tokens, int64_t head_batches, float* out,
+                     cudaStream_t stream) {
+    const int64_t units = head_batches * tokens * (kHd / 4);
+    if (units == 0) return;
+    const int64_t blocks = std::min<int64_t>((units + 255) / 256, int64_t(148) * 16);
+    rope_f32_kernel<<<static_cast<unsigned>(blocks), 256, 0, stream>>>(x, freqs, tokens, head_batches, out);
+    check_cuda(cudaGetLastError(), "rope_f32_kernel launch");
+}
+
+}  // namespace samq

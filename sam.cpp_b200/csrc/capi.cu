@@ -467,9 +467,10 @@ samq_status samq_linear_f16_v1(const samq_weights* w, const void* x_f16, int64_t
     });
 }
 
-samq_status samq_vit_attention_v1(const float* qkv, int64_t ldq, int grid_w, int grid_h, int heads, int head_dim,
-                                  int window, const float* freqs_cis, float* out, int64_t ldo, void* stream_ptr) {
-    return guarded([&] {
+static void vit_attention(const float* qkv, int64_t ldq, int grid_w, int grid_h, int heads, int head_dim,
+                          int window, const float* freqs_cis, float* out, int64_t ldo, int compute,
+                          void* stream_ptr) {
+    {
         require(head_dim == 64, "head_dim must be 64");
         require(heads > 0 && heads <= 64, "heads out of range");
         require(grid_w > 0 && grid_h > 0 && static_cast<int64_t>(grid_w) * grid_h <= (int64_t(1) << 20),
@@ -484,18 +485,57 @@ samq_status samq_vit_attention_v1(const float* qkv, int64_t ldq, int grid_w, int
         require(ldo >= E && ldo % 4 == 0, "output row stride must be >= heads*64 and a multiple of 4");
         require(qkv && out && freqs_cis && aligned16(qkv) && aligned16(out) && aligned16(freqs_cis),
                 "qkv, freqs_cis and out must be 16-byte aligned device pointers");
+        require(compute == SAMQ_COMPUTE_F32 || compute == SAMQ_COMPUTE_F16, "compute must be SAMQ_COMPUTE_F32 or _F16");
         DeviceState& state = device_state(current_device());
         cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
+        if (compute == SAMQ_COMPUTE_F32) {
+            launch_attention_f32(qkv, ldq, false, grid_w, grid_h, heads, window, 1, freqs_cis, out, nullptr, ldo, state,
+                                 stream);
+            return;
+        }
         Scratch& scratch = scratch_for(state, stream, attention_scratch_bytes(grid_w, grid_h, heads));
         launch_vit_attention(qkv, ldq, grid_w, grid_h, heads, window, freqs_cis, out, ldo, scratch.ptr, state, stream);
+    }
+}
+
+samq_status samq_vit_attention_v1(const float* qkv, int64_t ldq, int grid_w, int grid_h, int heads, int head_dim,
+                                  int window, const float* freqs_cis, float* out, int64_t ldo, void* stream_ptr) {
+    return guarded([&] {
+        vit_attention(qkv, ldq, grid_w, grid_h, heads, head_dim, window, freqs_cis, out, ldo, SAMQ_COMPUTE_F16,
+                      stream_ptr);
+    });
+}
+
+samq_status samq_vit_attention_v2(const float* qkv, int64_t ldq, int grid_w, int grid_h, int heads, int head_dim,
+                                  int window, const float* freqs_cis, float* out, int64_t ldo, int compute,
+                                  void* stream_ptr) {
+    return guarded([&] {
+        vit_attention(qkv, ldq, grid_w, grid_h, heads, head_dim, window, freqs_cis, out, ldo, compute, stream_ptr);
+    });
+}
+
+samq_status samq_vit_rope_v1(const float* x, int64_t tokens, int64_t head_batches, int head_dim,
+                             const float* freqs_cis, float* out, void* stream_ptr) {
+    return guarded([&] {
+        require(head_dim == 64, "head_dim must be 64");
+        require(tokens >= 0 && head_batches >= 0 && tokens <= (int64_t(1) << 24) && head_batches <= (int64_t(1) << 16),
+                "tokens / head_batches out of range");
+        if (tokens == 0 || head_batches == 0) return;
+        require(x && out && freqs_cis && aligned16(x) && aligned16(out) && aligned16(freqs_cis),
+                "x, freqs_cis and out must be 16-byte aligned device pointers");
+        device_state(current_device());
+        launch_rope_f32(x, freqs_cis, tokens, head_batches, out, static_cast<cudaStream_t>(stream_ptr));
     });
 }
 
 static void vit_block_forward(const samq_vit_block_v1* block, float* x, int batch, int grid_w, int grid_h,
                               void* stream_ptr) {
     {
-        require(block != nullptr && block->version == 1, "block descriptor missing or not version 1");
+        require(block != nullptr && (block->version == 1 || block->version == 2),
+                "block descriptor missing or not version 1 / 2");
         const samq_vit_block_v1& b = *block;
+        const int compute = b.version >= 2 ? b.compute : SAMQ_COMPUTE_F16;
+        require(compute == SAMQ_COMPUTE_F32 || compute == SAMQ_COMPUTE_F16, "compute must be SAMQ_COMPUTE_F32 or _F16");
         require(b.qkv && b.proj && b.fc1 && b.fc2, "null weight handle");
         const int64_t E = b.qkv->k, mlp = b.fc1->n;
         require(E == 256 || E == 512 || E == 1024, "embedding width must be 256, 512 or 1024");
@@ -522,9 +562,10 @@ static void vit_block_forward(const samq_vit_block_v1* block, float* x, int batc
         DeviceState& state = device_state(device);
         cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
         const int64_t tokens = static_cast<int64_t>(batch) * grid_w * grid_h;
-        Scratch& scratch = scratch_for(state, stream, vit_block_scratch_bytes(tokens, E, mlp));
+        Scratch& scratch = scratch_for(state, stream, vit_block_scratch_bytes(tokens, E, mlp, compute));
         VitBlockArgs args;
         args.window = window;
+        args.compute = compute;
         args.norm1_w = b.norm1_w;
         args.norm1_b = b.norm1_b;
         args.norm2_w = b.norm2_w;
@@ -553,10 +594,11 @@ samq_status samq_vit_block_forward_batch_v1(const samq_vit_block_v1* block, floa
     return guarded([&] { vit_block_forward(block, x, batch, grid_w, grid_h, stream_ptr); });
 }
 
-samq_status samq_vit_prefix_v1(const float* image, int width, int height, int patch, const float* patch_w,
-                               int64_t embed, const float* pos_embed, int pos_grid, const float* ln_w,
-                               const float* ln_b, float* x, void* stream_ptr) {
-    return guarded([&] {
+static void vit_prefix(const float* image, int width, int height, int patch, const float* patch_w, int64_t embed,
+                       const float* pos_embed, int pos_grid, const float* ln_w, const float* ln_b, float* x,
+                       int compute, void* stream_ptr) {
+    {
+        require(compute == SAMQ_COMPUTE_F32 || compute == SAMQ_COMPUTE_F16, "compute must be SAMQ_COMPUTE_F32 or _F16");
         require(embed == 256 || embed == 512 || embed == 1024, "embedding width must be 256, 512 or 1024");
         require(patch > 0 && patch <= 32 && width > 0 && height > 0 && width % patch == 0 && height % patch == 0,
                 "image sides must be positive multiples of the patch size (patch <= 32)");
@@ -567,9 +609,27 @@ samq_status samq_vit_prefix_v1(const float* image, int width, int height, int pa
         for (const float* p : params) require(p != nullptr && aligned16(p), "arguments must be 16-byte aligned device pointers");
         DeviceState& state = device_state(current_device());
         cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
-        Scratch& scratch = scratch_for(state, stream, vit_prefix_scratch_bytes(tokens, embed, patch));
-        launch_vit_prefix(image, width, height, patch, patch_w, embed, pos_embed, pos_grid, ln_w, ln_b, x, scratch.ptr,
-                          state, stream);
+        Scratch& scratch = scratch_for(state, stream, vit_prefix_scratch_bytes(tokens, embed, patch, compute));
+        launch_vit_prefix(image, width, height, patch, patch_w, embed, pos_embed, pos_grid, ln_w, ln_b, x, compute,
+                          scratch.ptr, state, stream);
+    }
+}
+
+samq_status samq_vit_prefix_v1(const float* image, int width, int height, int patch, const float* patch_w,
+                               int64_t embed, const float* pos_embed, int pos_grid, const float* ln_w,
+                               const float* ln_b, float* x, void* stream_ptr) {
+    return guarded([&] {
+        vit_prefix(image, width, height, patch, patch_w, embed, pos_embed, pos_grid, ln_w, ln_b, x, SAMQ_COMPUTE_F16,
+                   stream_ptr);
+    });
+}
+
+samq_status samq_vit_prefix_v2(const float* image, int width, int height, int patch, const float* patch_w,
+                               int64_t embed, const float* pos_embed, int pos_grid, const float* ln_w,
+                               const float* ln_b, float* x, int compute, void* stream_ptr) {
+    return guarded([&] {
+        vit_prefix(image, width, height, patch, patch_w, embed, pos_embed, pos_grid, ln_w, ln_b, x, compute,
+                   stream_ptr);
     });
 }
 

@@ -167,6 +167,17 @@ void launch_attention_packed(const __half* q, const __half* k, const __half* vt,
                              int window, int batch, float* out, __half* out_h, int64_t ldo, DeviceState& state,
                              cudaStream_t stream);
 
+// attention_f32.cu: F32-precise RoPE + attention (CudaComputeMode::F32).
+// qkv [rows][ldq] f32 (Q | K | V); rows are window-major (g * group_n + n)
+// when qkv_window_major, else raster.  Output f32 raster `out`, or (out_h) the
+// proj linear's Q8_1-staged f16 operand, [tokens][ldo].
+void launch_attention_f32(const float* qkv, int64_t ldq, bool qkv_window_major, int grid_w, int grid_h, int heads,
+                          int window, int batch, const float* freqs, float* out, __half* out_h, int64_t ldo,
+                          DeviceState& state, cudaStream_t stream);
+// sam3_apply_rope on [head_batches][tokens][64] f32 with GGML's rounding.
+void launch_rope_f32(const float* x, const float* freqs, int64_t tokens, int64_t head_batches, float* out,
+                     cudaStream_t stream);
+
 // K2 gemm.cu
 // What the GEMM epilogue writes.  Rows of the output are rows of A.
 enum OutMode : int {
@@ -214,20 +225,21 @@ void launch_linear_stream(const samq_weights* w, const __half* x16, int64_t ldx,
 // vit.cu: the ViT block / backbone prefix around K2 and K3.
 struct VitBlockArgs {
     int window = 0;
+    int compute = SAMQ_COMPUTE_F16;  // SAMQ_COMPUTE_F32: f32 qkv and F32-precise attention
     const float *norm1_w = nullptr, *norm1_b = nullptr, *norm2_w = nullptr, *norm2_b = nullptr;
     const samq_weights *qkv = nullptr, *proj = nullptr, *fc1 = nullptr, *fc2 = nullptr;
     const float *qkv_b = nullptr, *proj_b = nullptr, *fc1_b = nullptr, *fc2_b = nullptr;
     const float* freqs = nullptr;
 };
-size_t vit_block_scratch_bytes(int64_t tokens, int64_t embed, int64_t mlp);
+size_t vit_block_scratch_bytes(int64_t tokens, int64_t embed, int64_t mlp, int compute);
 // x: `batch` images of grid_w x grid_h tokens, image after image.
 void launch_vit_block(const VitBlockArgs& blk, float* x, int batch, int grid_w, int grid_h, void* scratch,
                       DeviceState& state, cudaStream_t stream);
 void launch_ln_stage(const float* x, int64_t rows, int64_t embed, int grid_w, int window, const float* w,
                      const float* b, __half* a, DeviceState& state, cudaStream_t stream);
-size_t vit_prefix_scratch_bytes(int64_t tokens, int64_t embed, int patch);
+size_t vit_prefix_scratch_bytes(int64_t tokens, int64_t embed, int patch, int compute);
 void launch_vit_prefix(const float* image, int width, int height, int patch, const float* patch_w, int64_t embed,
-                       const float* pos, int pos_grid, const float* ln_w, const float* ln_b, float* x,
+                       const float* pos, int pos_grid, const float* ln_w, const float* ln_b, float* x, int compute,
                        void* scratch, DeviceState& state, cudaStream_t stream);
 
 // dense.cu: F32-semantics linears / convolutions (three-term TF32 split).

@@ -162,6 +162,30 @@ __global__ void __launch_bounds__(256) embed_ln_kernel(float* __restrict__ x, in
     for (int i = 0; i < NV; ++i) row[i * 32 + lane] = make_float4(v[i][0], v[i][1], v[i][2], v[i][3]);
 }
 
+// F32 patch columns, a[t][c * P*P + ky * P + kx] = image[c][py*P + ky][px*P + kx]
+// (kp columns per row, kp % 4 == 0), four columns per thread.
+__global__ void __launch_bounds__(256) im2col_f32_kernel(const float* __restrict__ image, int width, int height,
+                                                         int patch, int grid_w, int64_t tokens, int kp,
+                                                         float* __restrict__ a) {
+    pdl_wait();
+    pdl_trigger();
+    const int groups = kp / 4;
+    const int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (idx >= tokens * groups) return;
+    const int64_t t = idx / groups;
+    const int col0 = static_cast<int>(idx - t * groups) * 4;
+    const int py = static_cast<int>(t / grid_w), px = static_cast<int>(t % grid_w);
+    const int pp = patch * patch;
+    float out[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        const int col = col0 + j;
+        const int c = col / pp, rem = col - c * pp, ky = rem / patch, kx = rem - ky * patch;
+        out[j] = __ldg(image + (static_cast<int64_t>(c) * height + py * patch + ky) * width + px * patch + kx);
+    }
+    *reinterpret_cast<float4*>(a + t * kp + col0) = make_float4(out[0], out[1], out[2], out[3]);
+}
+
 // Patch columns: a[t][c * P*P + ky * P + kx] = f16(image[c][py*P + ky][px*P + kx])
 // for token t = py * grid_w + px (ggml_im2col of the stride-P, unpadded patch
 // convolution, ops.hpp sam3_conv_2d), zero in the padding columns kp..ld-1.
@@ -219,9 +243,11 @@ void by_width(int embed, Fn&& fn) {
 
 }  // namespace
 
-size_t vit_block_scratch_bytes(int64_t tokens, int64_t embed, int64_t mlp) {
-    // A1 [T][E] + packed Q, K, V^T 3 [T][E] + fc2 operand [T][MLP], all f16.
-    return static_cast<size_t>(tokens) * (4 * embed + mlp) * sizeof(__half) + 3 * 256;
+size_t vit_block_scratch_bytes(int64_t tokens, int64_t embed, int64_t mlp, int compute) {
+    // A1 [T][E] + packed Q, K, V^T 3 [T][E] + fc2 operand [T][MLP], all f16;
+    // in F32 mode the middle region holds the f32 qkv rows [T][3E] instead.
+    const int64_t middle = compute == SAMQ_COMPUTE_F32 ? 3 * embed * 2 : 3 * embed;
+    return static_cast<size_t>(tokens) * (embed + middle + mlp) * sizeof(__half) + 3 * 256;
 }
 
 void launch_ln_stage(const float* x, int64_t rows, int64_t embed, int grid_w, int window, const float* w,
@@ -241,12 +267,13 @@ void launch_vit_block(const VitBlockArgs& blk, float* x, int batch, int grid_w, 
     // block one attention group per image.
     const int64_t tokens = static_cast<int64_t>(batch) * grid_w * grid_h;
     const int group_n = blk.window > 0 ? blk.window * blk.window : grid_w * grid_h;
+    const bool f32 = blk.compute == SAMQ_COMPUTE_F32;
     auto align = [](uintptr_t p) { return (p + 255) & ~uintptr_t(255); };
     uintptr_t cursor = align(reinterpret_cast<uintptr_t>(scratch));
     __half* a1 = reinterpret_cast<__half*>(cursor);
     cursor = align(cursor + tokens * embed * sizeof(__half));
-    __half* packed = reinterpret_cast<__half*>(cursor);
-    cursor = align(cursor + 3 * tokens * embed * sizeof(__half));
+    __half* packed = reinterpret_cast<__half*>(cursor);  // F16: Q, K, V^T; F32: the f32 qkv rows
+    cursor = align(cursor + (f32 ? 3 * tokens * embed * sizeof(float) : 3 * tokens * embed * sizeof(__half)));
     __half* a3 = reinterpret_cast<__half*>(cursor);
     __half* q = packed;
     __half* k = packed + tokens * embed;
@@ -254,16 +281,31 @@ void launch_vit_block(const VitBlockArgs& blk, float* x, int batch, int grid_w, 
 
     launch_ln_stage(x, tokens, embed, grid_w, blk.window, blk.norm1_w, blk.norm1_b, a1, state, stream);
     Epilogue ep;
-    ep.mode = kOutQkvPack;
-    ep.bias = blk.qkv_b;
-    ep.q = q;
-    ep.k = k;
-    ep.vt = vt;
-    ep.freqs = blk.freqs;
-    ep.heads = heads;
-    ep.group_n = group_n;
-    launch_gemm(a1, embed, blk.qkv->operand, tokens, 3 * embed, embed, ep, state, stream);
-    launch_attention_packed(q, k, vt, grid_w, grid_h, heads, blk.window, batch, nullptr, a1, embed, state, stream);
+    if (f32) {
+        // F32 mode: the qkv linear's f32 output (rows window-major, as LN1
+        // gathered them), then F32-precise RoPE + attention writing the proj
+        // operand.
+        float* qkv32 = reinterpret_cast<float*>(packed);
+        ep.mode = kOutF32;
+        ep.bias = blk.qkv_b;
+        ep.y = qkv32;
+        ep.ldy = 3 * embed;
+        launch_gemm(a1, embed, blk.qkv->operand, tokens, 3 * embed, embed, ep, state, stream);
+        launch_attention_f32(qkv32, 3 * embed, blk.window > 0, grid_w, grid_h, heads, blk.window, batch, blk.freqs,
+                             nullptr, a1, embed, state, stream);
+    } else {
+        ep.mode = kOutQkvPack;
+        ep.bias = blk.qkv_b;
+        ep.q = q;
+        ep.k = k;
+        ep.vt = vt;
+        ep.freqs = blk.freqs;
+        ep.heads = heads;
+        ep.group_n = group_n;
+        launch_gemm(a1, embed, blk.qkv->operand, tokens, 3 * embed, embed, ep, state, stream);
+        launch_attention_packed(q, k, vt, grid_w, grid_h, heads, blk.window, batch, nullptr, a1, embed, state,
+                                stream);
+    }
     ep = Epilogue{};
     ep.mode = kOutF32Residual;
     ep.bias = blk.proj_b;
@@ -290,13 +332,18 @@ void launch_vit_block(const VitBlockArgs& blk, float* x, int batch, int grid_w, 
     launch_gemm(a3, mlp, blk.fc2->operand, tokens, embed, mlp, ep, state, stream);
 }
 
-size_t vit_prefix_scratch_bytes(int64_t tokens, int64_t embed, int patch) {
+size_t vit_prefix_scratch_bytes(int64_t tokens, int64_t embed, int patch, int compute) {
+    if (compute == SAMQ_COMPUTE_F32) {
+        // f32 columns [T][kp], their hi / lo split, and the weight's hi / lo.
+        const int64_t kp = 3 * patch * patch;
+        return static_cast<size_t>(3 * tokens + 2 * embed) * kp * sizeof(float) + 6 * 256;
+    }
     const int64_t ld = (3 * patch * patch + 63) / 64 * 64;
     return static_cast<size_t>(tokens + embed) * ld * sizeof(__half) + 2 * 256;
 }
 
 void launch_vit_prefix(const float* image, int width, int height, int patch, const float* patch_w, int64_t embed,
-                       const float* pos, int pos_grid, const float* ln_w, const float* ln_b, float* x,
+                       const float* pos, int pos_grid, const float* ln_w, const float* ln_b, float* x, int compute,
                        void* scratch, DeviceState& state, cudaStream_t stream) {
     const int grid_w = width / patch, grid_h = height / patch;
     const int64_t tokens = static_cast<int64_t>(grid_w) * grid_h;
@@ -304,6 +351,40 @@ void launch_vit_prefix(const float* image, int width, int height, int patch, con
     const int ld = (kp + 63) / 64 * 64;
     auto align = [](uintptr_t p) { return (p + 255) & ~uintptr_t(255); };
     uintptr_t cursor = align(reinterpret_cast<uintptr_t>(scratch));
+    if (compute == SAMQ_COMPUTE_F32) {
+        // F32 columns (sam3_conv_2d_sk_p0 with F32 im2col, ops.hpp:67-89), the
+        // product with F32 semantics on the dense path (three-term TF32 split).
+        auto take = [&](int64_t floats) {
+            float* p = reinterpret_cast<float*>(cursor);
+            cursor = align(cursor + floats * sizeof(float));
+            return p;
+        };
+        float* cols = take(tokens * kp);
+        float* ch = take(tokens * kp);
+        float* cl = take(tokens * kp);
+        float* wh = take(embed * kp);
+        float* wl = take(embed * kp);
+        launch_pdl(im2col_f32_kernel, dim3(blocks_for(tokens * (kp / 4))), dim3(256), 0, stream,
+                   "im2col_f32_kernel launch", image, width, height, patch, grid_w, tokens, kp, cols);
+        launch_split_rows(cols, tokens, kp, kp, ch, cl, state, stream);
+        launch_split_rows(patch_w, embed, kp, kp, wh, wl, state, stream);
+        samq_dense w;  // a view of the split weight in scratch (not owned)
+        w.device = state.device;
+        w.type = SAMQ_TYPE_F32;
+        w.kind = SAMQ_DENSE_LINEAR;
+        w.cin = kp;
+        w.cout = embed;
+        w.n = embed;
+        w.k = kp;
+        w.hi = wh;
+        w.lo = wl;
+        launch_dense_gemm(ch, cl, w, tokens, 0, 0, nullptr, 0, x, nullptr, embed, state, stream);
+        by_width(static_cast<int>(embed), [&](auto nv) {
+            launch_pdl(embed_ln_kernel<decltype(nv)::value>, dim3(blocks_for(tokens * 32)), dim3(256), 0, stream,
+                       "embed_ln_kernel launch", x, tokens, grid_w, pos, pos_grid, ln_w, ln_b);
+        });
+        return;
+    }
     __half* cols = reinterpret_cast<__half*>(cursor);
     cursor = align(cursor + tokens * ld * sizeof(__half));
     __half* wp = reinterpret_cast<__half*>(cursor);

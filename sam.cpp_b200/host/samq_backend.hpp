@@ -3,8 +3,9 @@
 //
 // Mirrors (paths relative to the SAM.cpp tree):
 //   make_samq_backend     <- make_cuda_backend (src/runtime/ggml/backends/cuda.hpp:156-189):
-//                            same argument meaning (visible CUDA device index) and the same
-//                            failure style (std::runtime_error with a message).
+//                            same argument meaning (visible CUDA device index, compute mode
+//                            with F32 as default) and the same failure style
+//                            (std::runtime_error with a message).
 //   QuantizedLinear       <- one ggml_mul_mat(W_packed, X_f32) node built by
 //                            sam3_channel_projection (src/models/sam3/ops.hpp:40-45) with its
 //                            bias add and optional ggml_gelu_erf (src/models/sam3/vision.hpp:234-238).
@@ -35,6 +36,11 @@ namespace sam::internal {
 
 enum class LinearEpilogue { None = SAMQ_EPILOGUE_NONE, GeluErf = SAMQ_EPILOGUE_GELU_ERF };
 
+// sam::CudaComputeMode (include/sam/types.hpp:13), passed through
+// BackendOptions::cuda_compute: F32 (the default) keeps the ViT attention and
+// the patch-embedding columns in f32; F16 is the opt-in reduced mode.
+enum class CudaComputeMode { F32 = SAMQ_COMPUTE_F32, F16 = SAMQ_COMPUTE_F16 };
+
 inline void samq_require(samq_status status, const char* what) {
     if (status != SAMQ_OK) throw std::runtime_error(std::string(what) + ": " + samq_last_error_v1());
 }
@@ -44,9 +50,10 @@ struct SamqDriver {
     int cuda_device = -1;
     std::string device_name;
     int sm_count = 0;
+    CudaComputeMode compute = CudaComputeMode::F32;
 };
 
-inline SamqDriver make_samq_backend(int device_index) {
+inline SamqDriver make_samq_backend(int device_index, CudaComputeMode compute = CudaComputeMode::F32) {
     if (device_index < 0) throw std::runtime_error("requested CUDA device index is out of range for visible devices");
     struct samq_capabilities_v1 info{};  // "struct": the function of the same name hides the type
     samq_require(samq_capabilities_v1(device_index, &info), "requested samq CUDA device is unavailable");
@@ -55,6 +62,7 @@ inline SamqDriver make_samq_backend(int device_index) {
     driver.cuda_device = device_index;
     driver.device_name = info.name;
     driver.sm_count = info.sm_count;
+    driver.compute = compute;
     return driver;
 }
 
@@ -163,7 +171,8 @@ public:
     void add_block(QuantizedLinear qkv, QuantizedLinear proj, QuantizedLinear fc1, QuantizedLinear fc2,
                    const VitBlockTensors& t) {
         samq_vit_block_v1 b{};
-        b.version = 1;
+        b.version = 2;
+        b.compute = static_cast<int32_t>(driver_.compute);
         b.window = t.window;
         b.norm1_w = t.norm1_w;
         b.norm1_b = t.norm1_b;
@@ -200,10 +209,11 @@ public:
         const int grid_w = width / prefix_.patch, grid_h = height / prefix_.patch;
         const std::int64_t tokens = static_cast<std::int64_t>(grid_w) * grid_h;
         for (int i = 0; i < batch; ++i)
-            samq_require(samq_vit_prefix_v1(images + static_cast<std::int64_t>(i) * 3 * width * height, width, height,
+            samq_require(samq_vit_prefix_v2(images + static_cast<std::int64_t>(i) * 3 * width * height, width, height,
                                             prefix_.patch, prefix_.patch_embed_w, embed_, prefix_.pos_embed,
                                             prefix_.pos_grid, prefix_.ln_pre_w, prefix_.ln_pre_b,
-                                            x + static_cast<std::int64_t>(i) * tokens * embed_, stream),
+                                            x + static_cast<std::int64_t>(i) * tokens * embed_,
+                                            static_cast<int>(driver_.compute), stream),
                          "samq ViT prefix failed");
         for (const samq_vit_block_v1& b : blocks_)
             samq_require(batch == 1 ? samq_vit_block_forward_v1(&b, x, grid_w, grid_h, stream)

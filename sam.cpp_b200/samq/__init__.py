@@ -25,6 +25,7 @@ NAME_TYPES = {v: k for k, v in TYPE_NAMES.items()}
 EPILOGUE_NONE, EPILOGUE_GELU_ERF = 0, 1
 F32, F16 = 0, 1
 DENSE_LINEAR, DENSE_CONV, DENSE_DECONV2X2 = 0, 1, 2
+COMPUTE_F32, COMPUTE_F16 = 0, 1  # sam::CudaComputeMode (default F32)
 BLOCK = {Q8_0: (32, 34), Q4_K: (256, 144), Q5_K: (256, 176), Q6_K: (256, 210)}
 
 STATUS_NAMES = {
@@ -53,7 +54,8 @@ class VitBlockDesc(ctypes.Structure):
     """struct samq_vit_block_v1."""
     _fields_ = [("version", ctypes.c_uint32), ("window", ctypes.c_int32), ("norm1_w", _vp), ("norm1_b", _vp),
                 ("qkv", _vp), ("qkv_b", _vp), ("proj", _vp), ("proj_b", _vp), ("norm2_w", _vp), ("norm2_b", _vp),
-                ("fc1", _vp), ("fc1_b", _vp), ("fc2", _vp), ("fc2_b", _vp), ("freqs_cis", _vp)]
+                ("fc1", _vp), ("fc1_b", _vp), ("fc2", _vp), ("fc2_b", _vp), ("freqs_cis", _vp),
+                ("compute", ctypes.c_int32)]
 
 
 class NeckDesc(ctypes.Structure):
@@ -86,6 +88,9 @@ SIGNATURES = {
     "samq_check_v1": (_i32, [_i32, _vp]),
     "samq_linear_static_v1": (_i32, [_vp, _vp, _i64, _i64, _vp, _i32, _vp, _i64, _vp]),
     "samq_vit_attention_v1": (_i32, [_vp, _i64, _i32, _i32, _i32, _i32, _i32, _vp, _vp, _i64, _vp]),
+    "samq_vit_attention_v2": (_i32, [_vp, _i64, _i32, _i32, _i32, _i32, _i32, _vp, _vp, _i64, _i32, _vp]),
+    "samq_vit_rope_v1": (_i32, [_vp, _i64, _i64, _i32, _vp, _vp, _vp]),
+    "samq_vit_prefix_v2": (_i32, [_vp, _i32, _i32, _i32, _vp, _i64, _vp, _i32, _vp, _vp, _vp, _i32, _vp]),
     "samq_vit_block_forward_v1": (_i32, [ctypes.POINTER(VitBlockDesc), _vp, _i32, _i32, _vp]),
     "samq_vit_block_forward_batch_v1": (_i32, [ctypes.POINTER(VitBlockDesc), _vp, _i32, _i32, _i32, _vp]),
     "samq_vit_prefix_v1": (_i32, [_vp, _i32, _i32, _i32, _vp, _i64, _vp, _i32, _vp, _vp, _vp, _vp]),
@@ -247,10 +252,18 @@ def linear_static(w: Weights, x, m: int, ldx: int, bias, epilogue: int, y, ldy: 
 
 
 def vit_attention(qkv, ldq: int, grid_w: int, grid_h: int, heads: int, window: int, freqs, out, ldo: int,
-                  stream=None, head_dim: int = 64):
-    """samq_vit_attention_v1: RoPE + windowed (window > 0) or global attention."""
-    _check(library().samq_vit_attention_v1(_addr(qkv), ldq, grid_w, grid_h, heads, head_dim, window, _addr(freqs),
-                                           _addr(out), ldo, _stream(stream)))
+                  stream=None, head_dim: int = 64, compute: int = COMPUTE_F32):
+    """samq_vit_attention_v2: RoPE + windowed (window > 0) or global attention,
+    F32-precise (COMPUTE_F32, the reference's default) or on f16 tensor-core
+    operands (COMPUTE_F16)."""
+    _check(library().samq_vit_attention_v2(_addr(qkv), ldq, grid_w, grid_h, heads, head_dim, window, _addr(freqs),
+                                           _addr(out), ldo, compute, _stream(stream)))
+
+
+def vit_rope(x, tokens: int, head_batches: int, freqs, out, stream=None, head_dim: int = 64):
+    """samq_vit_rope_v1: sam3_apply_rope on [head_batches][tokens][64] f32."""
+    _check(library().samq_vit_rope_v1(_addr(x), tokens, head_batches, head_dim, _addr(freqs), _addr(out),
+                                      _stream(stream)))
 
 
 def check(device: int = 0, stream=None):
@@ -262,15 +275,17 @@ class VitBlock:
 
     The f32 parameters are device tensors (kept alive here); the four linears
     are Weights handles.  window is 24 for windowed blocks and 0 for global
-    ones; freqs is [positions][32][2] (cos, sin)."""
+    ones; freqs is [positions][32][2] (cos, sin); compute is COMPUTE_F32 (the
+    reference's default: f32 qkv and F32-precise attention) or COMPUTE_F16."""
 
     def __init__(self, window: int, norm1_w, norm1_b, qkv: Weights, qkv_b, proj: Weights, proj_b, norm2_w, norm2_b,
-                 fc1: Weights, fc1_b, fc2: Weights, fc2_b, freqs):
+                 fc1: Weights, fc1_b, fc2: Weights, fc2_b, freqs, compute: int = COMPUTE_F32):
         self._keep = (norm1_w, norm1_b, qkv, qkv_b, proj, proj_b, norm2_w, norm2_b, fc1, fc1_b, fc2, fc2_b, freqs)
         self.window = window
-        self.desc = VitBlockDesc(1, window, _addr(norm1_w), _addr(norm1_b), qkv.handle, _addr(qkv_b), proj.handle,
+        self.compute = compute
+        self.desc = VitBlockDesc(2, window, _addr(norm1_w), _addr(norm1_b), qkv.handle, _addr(qkv_b), proj.handle,
                                  _addr(proj_b), _addr(norm2_w), _addr(norm2_b), fc1.handle, _addr(fc1_b), fc2.handle,
-                                 _addr(fc2_b), _addr(freqs))
+                                 _addr(fc2_b), _addr(freqs), compute)
 
 
 def vit_block_forward(block: VitBlock, x, grid_w: int, grid_h: int, stream=None, batch: int = 1):
@@ -285,10 +300,11 @@ def vit_block_forward(block: VitBlock, x, grid_w: int, grid_h: int, stream=None,
 
 
 def vit_prefix(image, width: int, height: int, patch: int, patch_w, embed: int, pos_embed, pos_grid: int, ln_w, ln_b,
-               x, stream=None):
-    """samq_vit_prefix_v1: patch embedding + tiled pos_embed + ln_pre into x [tokens][E] f32."""
-    _check(library().samq_vit_prefix_v1(_addr(image), width, height, patch, _addr(patch_w), embed, _addr(pos_embed),
-                                        pos_grid, _addr(ln_w), _addr(ln_b), _addr(x), _stream(stream)))
+               x, stream=None, compute: int = COMPUTE_F32):
+    """samq_vit_prefix_v2: patch embedding + tiled pos_embed + ln_pre into x
+    [tokens][E] f32 (F32 columns with F32 semantics, or f16 columns)."""
+    _check(library().samq_vit_prefix_v2(_addr(image), width, height, patch, _addr(patch_w), embed, _addr(pos_embed),
+                                        pos_grid, _addr(ln_w), _addr(ln_b), _addr(x), compute, _stream(stream)))
 
 
 class Dense:

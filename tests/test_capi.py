@@ -18,7 +18,7 @@ from conftest import PACKAGE, ROOT
 def header_functions():
     text = (ROOT / "include" / "samq.h").read_text()
     text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
-    return sorted(set(re.findall(r"\b(samq_[a-z0-9_]+_v1)\s*\(", text)))
+    return sorted(set(re.findall(r"\b(samq_[a-z0-9_]+_v[0-9]+)\s*\(", text)))
 
 
 @pytest.fixture(scope="module")
@@ -105,6 +105,10 @@ def test_invalid_block_arguments_are_rejected(samq):
     rc = lib.samq_vit_block_forward_batch_v1(None, x, 8, 72, 72, None)
     assert rc == 1 and b"version 1" in lib.samq_last_error_v1()
     desc = samq.VitBlockDesc()
-    desc.version = 2
+    desc.version = 3
     rc = lib.samq_vit_block_forward_batch_v1(ctypes.byref(desc), x, 8, 72, 72, None)
     assert rc == 1 and b"version 1" in lib.samq_last_error_v1()
+    desc.version = 2
+    desc.compute = 7  # neither SAMQ_COMPUTE_F32 nor _F16
+    rc = lib.samq_vit_block_forward_v1(ctypes.byref(desc), x, 72, 72, None)
+    assert rc == 1 and b"compute" in lib.samq_last_error_v1()

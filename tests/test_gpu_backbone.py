@@ -63,7 +63,7 @@ def _stats(got, ref, cpu, base):
             "max_abs": float(np.abs(d).max())}
 
 
-def _run_backbone(grid, seed, sample_rows=None):
+def _run_backbone(grid, seed, sample_rows=None, compute=samq.COMPUTE_F16):
     """Builds 32 random-init blocks, runs the device backbone on one image, the
     oracle block by block on its own previous output, and the reference CPU
     backend's arithmetic the same way.  With sample_rows, the last block is
@@ -76,14 +76,14 @@ def _run_backbone(grid, seed, sample_rows=None):
     t = {k: torch.from_numpy(v).to(dev) for k, v in pre.items()}
     x = torch.empty((grid * grid, E), device=dev)
     samq.vit_prefix(torch.from_numpy(image).to(dev), size, size, PATCH, t["patch_w"], E, t["pos"], POS_GRID,
-                    t["ln_w"], t["ln_b"], x)
+                    t["ln_w"], t["ln_b"], x, compute=compute)
     samq.check(0)
     ref = o.vit_prefix(image, PATCH, pre["patch_w"], pre["pos"], pre["ln_w"], pre["ln_b"])
     cpu, base = ref.copy(), ref.copy()
     history = [("prefix", _stats(x.cpu().numpy(), ref, cpu, base))]
     for i in range(DEPTH):
         window = 0 if i in GLOBAL else 24
-        host, block = make_block(rng, window, grid * grid if window == 0 else 576)
+        host, block = make_block(rng, window, grid * grid if window == 0 else 576, compute=compute)
         samq.vit_block_forward(block, x, grid, grid)
         samq.check(0)
         rows = sample_rows if (i == DEPTH - 1 and sample_rows is not None) else None
@@ -111,10 +111,11 @@ def _check(history):
     assert last["cos"] >= COS_MIN, last
 
 
-def test_backbone_32_blocks_48x48_all_rows():
+@pytest.mark.parametrize("compute", [samq.COMPUTE_F16, samq.COMPUTE_F32])
+def test_backbone_32_blocks_48x48_all_rows(compute):
     """A 672 x 672 image (48 x 48 tokens, 4 windows per windowed block), every
-    token of the final features checked."""
-    _check(_run_backbone(48, seed=1234))
+    token of the final features checked, in both compute modes."""
+    _check(_run_backbone(48, seed=1234, compute=compute))
 
 
 def test_backbone_32_blocks_72x72_sampled_rows():
@@ -123,4 +124,4 @@ def test_backbone_32_blocks_72x72_sampled_rows():
     sampled tokens."""
     rng = np.random.default_rng(77)
     rows = np.sort(rng.choice(72 * 72, 256, replace=False))
-    _check(_run_backbone(72, seed=4321, sample_rows=rows))
+    _check(_run_backbone(72, seed=4321, sample_rows=rows, compute=samq.COMPUTE_F32))

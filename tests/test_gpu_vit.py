@@ -32,7 +32,7 @@ def _weights(rng, n, k):
     return w
 
 
-def make_block(rng, window, positions, qtype=o.Q4_K, fc2_type=o.Q8_0, E=E, MLP=MLP):
+def make_block(rng, window, positions, qtype=o.Q4_K, fc2_type=o.Q8_0, E=E, MLP=MLP, compute=samq.COMPUTE_F16):
     """Random-init block with config-3 statistics: K-quant linears (fc2 Q8_0),
     N(0, 0.02^2) weights with 1% scaled x8, LN gamma 1 + N(0, 0.02^2)."""
     dev = torch.device("cuda")
@@ -55,7 +55,7 @@ def make_block(rng, window, positions, qtype=o.Q4_K, fc2_type=o.Q8_0, E=E, MLP=M
     gpu["freqs"] = torch.from_numpy(host["freqs"]).to(dev)
     block = samq.VitBlock(window, gpu["norm1_w"], gpu["norm1_b"], gpu["qkv"], gpu["qkv_b"], gpu["proj"],
                           gpu["proj_b"], gpu["norm2_w"], gpu["norm2_b"], gpu["fc1"], gpu["fc1_b"], gpu["fc2"],
-                          gpu["fc2_b"], gpu["freqs"])
+                          gpu["fc2_b"], gpu["freqs"], compute=compute)
     return host, block
 
 
@@ -74,11 +74,12 @@ def compare(gpu, ref, x_in):
     return cos, rel
 
 
+@pytest.mark.parametrize("compute", [samq.COMPUTE_F16, samq.COMPUTE_F32])
 @pytest.mark.parametrize("grid,window,seed", [(48, 24, 0), (24, 0, 1), (24, 24, 2)])
-def test_vit_block_parity(grid, window, seed):
+def test_vit_block_parity(grid, window, seed, compute):
     rng = np.random.default_rng(seed)
     positions = window * window if window else grid * grid
-    host, block = make_block(rng, window, positions)
+    host, block = make_block(rng, window, positions, compute=compute)
     x = rng.standard_normal((grid * grid, E)).astype(np.float32)
     out = run_block(block, x, grid)
     ref = o.vit_block(x, host, grid, grid)
@@ -130,8 +131,9 @@ def test_vit_block_other_widths(embed, mlp, grid, window):
     assert cos >= COS_MIN and rel <= DELTA_REL_MAX, (cos, rel)
 
 
+@pytest.mark.parametrize("compute", [samq.COMPUTE_F16, samq.COMPUTE_F32])
 @pytest.mark.parametrize("size,patch,pos_grid", [(1008, 14, 24), (224, 14, 8)])
-def test_vit_prefix_parity(size, patch, pos_grid):
+def test_vit_prefix_parity(size, patch, pos_grid, compute):
     rng = np.random.default_rng(size)
     image = ((rng.random((3, size, size)) - 0.5) / 0.5).astype(np.float32)  # U[0,1] normalized
     patch_w = rng.normal(0.0, 0.02, (E, 3, patch, patch)).astype(np.float32)
@@ -142,13 +144,15 @@ def test_vit_prefix_parity(size, patch, pos_grid):
     dev = torch.device("cuda")
     x = torch.empty((tokens, E), device=dev)
     t = [torch.from_numpy(a).to(dev) for a in (image, patch_w, pos, ln_w, ln_b)]
-    samq.vit_prefix(t[0], size, size, patch, t[1], E, t[2], pos_grid, t[3], t[4], x)
+    samq.vit_prefix(t[0], size, size, patch, t[1], E, t[2], pos_grid, t[3], t[4], x, compute=compute)
     samq.check(0)
     out = x.cpu().numpy()
     ref = o.vit_prefix(image, patch, patch_w, pos, ln_w, ln_b)
     d = (out - ref).astype(np.float64).ravel()
     cos = float(out.ravel().astype(np.float64) @ ref.ravel() / (np.linalg.norm(out) * np.linalg.norm(ref)))
-    assert cos >= 0.99999 and np.abs(d).max() <= 1e-2, (cos, np.abs(d).max())
+    # F16 columns: f16 operands, f32 accumulation; F32: F32 semantics.
+    cos_min, abs_max = (0.99999, 1e-2) if compute == samq.COMPUTE_F16 else (1 - 1e-10, 5e-5)
+    assert cos >= cos_min and np.abs(d).max() <= abs_max, (cos, np.abs(d).max())
 
 
 def test_vit_block_rejects_bad_shapes():
@@ -159,14 +163,15 @@ def test_vit_block_rejects_bad_shapes():
         samq.vit_block_forward(block, x, 50, 50)  # 24 does not divide 50
 
 
+@pytest.mark.parametrize("compute", [samq.COMPUTE_F16, samq.COMPUTE_F32])
 @pytest.mark.parametrize("window,grid", [(24, 48), (0, 24)])
-def test_vit_block_batch_matches_single_images(window, grid):
+def test_vit_block_batch_matches_single_images(window, grid, compute):
     """samq_vit_block_forward_batch_v1 on 3 images (windowed: one grid of
     stacked images; global: one attention group per image) gives each image
     the bits of samq_vit_block_forward_v1 on that image alone."""
     rng = np.random.default_rng(40 + window)
     positions = window * window if window else grid * grid
-    host, block = make_block(rng, window, positions)
+    host, block = make_block(rng, window, positions, compute=compute)
     batch = 3
     xs = rng.standard_normal((batch, grid * grid, E)).astype(np.float32)
     xd = torch.from_numpy(xs).cuda()
