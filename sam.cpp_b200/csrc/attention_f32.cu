@@ -166,6 +166,7 @@ attention_f32_kernel(const float* __restrict__ qkv, int64_t ldq, const float* __
                 for (int j = 0; j < 4; ++j) s[i][j] = dot4(a[i], b[j], s[i][j]);
         }
         // Online softmax of the 4 rows; a row's 64 scores sit on 16 neighbouring lanes.
+        float alpha[4];
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
             float mx = -INFINITY;
@@ -177,7 +178,7 @@ attention_f32_kernel(const float* __restrict__ qkv, int64_t ldq, const float* __
 #pragma unroll
             for (int off = 1; off < 16; off <<= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
             const float m_new = fmaxf(m[i], mx);
-            const float alpha = expf(m[i] - m_new);
+            alpha[i] = expf(m[i] - m_new);
             float sum = 0.0f;
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
@@ -187,12 +188,19 @@ attention_f32_kernel(const float* __restrict__ qkv, int64_t ldq, const float* __
             }
 #pragma unroll
             for (int off = 1; off < 16; off <<= 1) sum += __shfl_xor_sync(0xffffffffu, sum, off);
-            l[i] = fmaf(l[i], alpha, sum);
+            l[i] = fmaf(l[i], alpha[i], sum);
             m[i] = m_new;
-#pragma unroll
-            for (int j = 0; j < 4; ++j) o[i][j] *= alpha;
         }
         __syncthreads();
+        // This tile's P V in fresh accumulators, added to the running O once:
+        // a long sequential sum over thousands of keys would let f32 rounding
+        // grow with the key count (the reference's closed-form probe at 5184
+        // keys needs the blocked sum to stay within 1e-5).
+        float ot[4][4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+#pragma unroll
+            for (int j = 0; j < 4; ++j) ot[i][j] = 0.0f;
 #pragma unroll 4
         for (int k4 = 0; k4 < 16; ++k4) {
             float4 a[4], b[4];
@@ -203,8 +211,12 @@ attention_f32_kernel(const float* __restrict__ qkv, int64_t ldq, const float* __
 #pragma unroll
             for (int i = 0; i < 4; ++i)
 #pragma unroll
-                for (int j = 0; j < 4; ++j) o[i][j] = dot4(a[i], b[j], o[i][j]);
+                for (int j = 0; j < 4; ++j) ot[i][j] = dot4(a[i], b[j], ot[i][j]);
         }
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+#pragma unroll
+            for (int j = 0; j < 4; ++j) o[i][j] = fmaf(o[i][j], alpha[i], ot[i][j]);
     }
     pdl_trigger();
 

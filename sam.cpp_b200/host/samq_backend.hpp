@@ -30,6 +30,7 @@
 #include <vector>
 
 #include "gguf_reader.hpp"
+#include "weight_policy.hpp"
 #include "samq.h"
 
 namespace sam::internal {
@@ -134,6 +135,20 @@ inline QuantizedLinear load_quantized_linear(const SamqDriver& driver, samq_io::
     if (t.dimensions.size() != 2) throw std::runtime_error("GGUF linear weight must be 2-D: " + name);
     const std::vector<std::uint8_t> bytes = reader.tensor_bytes(t);
     return QuantizedLinear(driver, t.type, t.dimensions[0], t.dimensions[1], bytes.data(), bytes.size(), stream);
+}
+
+// The same, after checking the tensor's stored type against the checkpoint's
+// weight-precision policy (samq_policy::inspect_weight_policy, the reference's
+// inspect_weights): a tensor stored with another type than its profile
+// assigns (for example a K-quant fc2 that is not the Q8_0 fallback) is
+// rejected before any device memory is touched.
+inline QuantizedLinear load_quantized_linear(const SamqDriver& driver, samq_io::GgufReader& reader,
+                                             const samq_policy::WeightPolicy& policy, const std::string& name,
+                                             cudaStream_t stream = nullptr) {
+    const samq_io::GgufTensor& t = reader.tensor(name);
+    if (t.type != policy.expected_type(t.name, t.dimensions))
+        throw std::runtime_error("incompatible SAM 3 tensor precision: " + name);
+    return load_quantized_linear(driver, reader, name, stream);
 }
 
 // Device pointers to one ViT block's F32 tensors (src/models/sam3/tensors.hpp:108-126).
