@@ -256,6 +256,59 @@ samq_status samq_vit_prefix_v2(const float* image, int width, int height, int pa
                                int64_t embed, const float* pos_embed, int pos_grid, const float* ln_w,
                                const float* ln_b, float* x, int compute, void* stream);
 
+/* ---- Text encoder and general attention ------------------------------------
+ * The SAM 3 text encoder (src/models/sam3/text_encoder.hpp:68-180):
+ *   x = token_embed[ids] + pos_embed                       (samq_token_embed_v1)
+ *   24 x pre-LN block with a causal mask                   (samq_text_block_forward_v1)
+ *   features = resizer(LN_final(x))                        (samq_layer_norm_v1 + samq_linear_v1)
+ * The block's linears are quantized weight handles (Q8_0 in the reference's
+ * full-linear and mixed profiles) and stage their inputs to Q8_1 like every
+ * quantized linear here; its attention keeps F32 operands (the reference runs
+ * masked attention at GGML_PREC_F32 in both compute modes,
+ * src/runtime/ggml/backends/cuda.hpp:86-91). */
+typedef struct samq_text_block_v1 {
+    uint32_t version;  /* 1 */
+    const float* norm1_w;   /* text.blocks.N.ln_1.weight [E] */
+    const float* norm1_b;
+    const samq_weights* in_proj;   /* attn.in_proj.weight, E -> 3E (Q | K | V, heads of 64) */
+    const float* in_proj_b;
+    const samq_weights* out_proj;  /* attn.out_proj.weight, E -> E */
+    const float* out_proj_b;
+    const float* norm2_w;   /* ln_2 */
+    const float* norm2_b;
+    const samq_weights* fc1;       /* mlp.fc1.weight, E -> MLP, erf-GELU after the bias */
+    const float* fc1_b;
+    const samq_weights* fc2;       /* mlp.fc2.weight, MLP -> E */
+    const float* fc2_b;
+} samq_text_block_v1;
+
+/* One block in place on x, device f32 [tokens][E] (E = 64 * heads). */
+samq_status samq_text_block_forward_v1(const samq_text_block_v1* block, float* x, int tokens, void* stream);
+
+/* ggml_get_rows + ggml_add: out[i] = table[ids[i]] + pos[i] (pos may be NULL).
+ * table is device f32 [vocab][width], ids HOST int32 [count] (each checked to
+ * lie in [0, vocab); the reference's tokenizer validates ids before this node,
+ * src/models/sam3/tokenizer.hpp:103-118), pos / out device f32 [count][width]. */
+samq_status samq_token_embed_v1(const float* table, int64_t vocab, int width, const int32_t* ids, int count,
+                                const float* pos, float* out, void* stream);
+
+/* sam3_layer_norm in f32 (ggml_norm with eps, then * w + b; b may be NULL),
+ * rows of `width` values: x [rows][ldx] -> out [rows][ldo] (may alias). */
+samq_status samq_layer_norm_v1(const float* x, int64_t rows, int width, int64_t ldx, const float* w, const float* b,
+                               float eps, float* out, int64_t ldo, void* stream);
+
+/* ggml_flash_attn_ext at GGML_PREC_F32 for the fusion / decoder / text
+ * attentions: per head h, out = softmax(scale Q_h K_h^T + bias) V_h with F32
+ * operands.  q [lq][ldq], k and v [lk][ldk / ldv], out [lq][ldo], head h at
+ * columns h*head_dim (head_dim 32 or 64, all strides multiples of 4 floats,
+ * pointers 16-byte aligned).  bias (nullable) is additive,
+ * bias[h * bias_h + q * bias_q + k] (a key padding mask: bias_h = bias_q = 0,
+ * -INFINITY at masked keys); causal != 0 masks keys k > q.  A query whose
+ * keys are all masked gets 0. */
+samq_status samq_attention_v1(const float* q, int64_t ldq, const float* k, int64_t ldk, const float* v, int64_t ldv,
+                              int lq, int lk, int heads, int head_dim, float scale, int causal, const float* bias,
+                              int64_t bias_h, int64_t bias_q, float* out, int64_t ldo, void* stream);
+
 /* ---- Dense (F32 / F16) modules with F32 semantics -------------------------
  * The tensors the reference keeps unquantized (neck convolutions, fusion /
  * decoder / mask-head linears in the F32 profiles: "only ViT linear weights

@@ -530,3 +530,57 @@ def neck(x: np.ndarray, layers: dict) -> list:
     s3 = conv2d_nhwc(s3, *L["s3_conv1x1"])
     s3 = conv2d_nhwc(s3, *L["s3_conv3x3"])
     return [s0, s1, s2, s3]
+
+
+# ---- text encoder / general attention (f64) ----------------------------------
+
+def attention_gen(q: np.ndarray, k: np.ndarray, v: np.ndarray, heads: int, head_dim: int, scale: float,
+                  causal: bool = False, bias=None) -> np.ndarray:
+    """ggml_flash_attn_ext semantics in f64: per head h, softmax(scale Q_h K_h^T
+    + bias_h) V_h; q [lq][>= heads*hd], k / v [lk][...]; bias broadcastable to
+    [heads][lq][lk] (additive, -inf masks); causal masks keys k > q.  A query
+    with every key masked gets 0."""
+    q, k, v = (np.asarray(a, np.float64) for a in (q, k, v))
+    lq, lk = q.shape[0], k.shape[0]
+    out = np.zeros((lq, heads * head_dim), np.float64)
+    b = None if bias is None else np.broadcast_to(np.asarray(bias, np.float64), (heads, lq, lk))
+    for h in range(heads):
+        sl = slice(h * head_dim, (h + 1) * head_dim)
+        s = (q[:, sl] @ k[:, sl].T) * scale
+        if b is not None:
+            s = s + b[h]
+        if causal:
+            s = np.where(np.arange(lk)[None, :] > np.arange(lq)[:, None], -np.inf, s)
+        mx = s.max(axis=1, keepdims=True)
+        mx = np.where(np.isfinite(mx), mx, 0.0)
+        p = np.exp(s - mx)
+        den = p.sum(axis=1, keepdims=True)
+        out[:, sl] = np.where(den > 0, (p @ v[:, sl]) / np.where(den > 0, den, 1.0), 0.0)
+    return out.astype(np.float32)
+
+
+def text_block(x: np.ndarray, blk: dict) -> np.ndarray:
+    """One SAM 3 text-encoder block (src/models/sam3/text_encoder.hpp:68-150):
+    x1 = x + out_proj(attn_causal(in_proj(LN1(x)))); out = x1 + fc2(GELU(fc1(LN2(x1)))),
+    every quantized linear with MMQ operand semantics (staged_linear), attention
+    in f64 with the causal mask and scale 1/8 (heads of 64)."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    E = x.shape[1]
+    heads = E // 64
+    h = layer_norm(x, blk["norm1_w"], blk["norm1_b"])
+    qkv = staged_linear(blk["in_proj_w"], h, blk["in_proj_b"])
+    att = attention_gen(qkv[:, :E], qkv[:, E:2 * E], qkv[:, 2 * E:], heads, 64, 0.125, causal=True)
+    x1 = x + staged_linear(blk["out_proj_w"], att, blk["out_proj_b"])
+    h2 = layer_norm(x1, blk["norm2_w"], blk["norm2_b"])
+    f = staged_linear(blk["fc1_w"], h2, blk["fc1_b"], EPILOGUE_GELU_ERF)
+    return x1 + staged_linear(blk["fc2_w"], f, blk["fc2_b"])
+
+
+def text_encoder(ids, token_embed: np.ndarray, pos_embed: np.ndarray, blocks: list, ln_w, ln_b, resizer_w,
+                 resizer_b) -> np.ndarray:
+    """sam3_build_text_encoder_graph (text_encoder.hpp:151-180): token rows +
+    pos_embed, the blocks, the final LayerNorm and the quantized resizer."""
+    x = (np.asarray(token_embed, np.float32)[np.asarray(ids)] + np.asarray(pos_embed, np.float32)).astype(np.float32)
+    for blk in blocks:
+        x = text_block(x, blk)
+    return staged_linear(resizer_w, layer_norm(x, ln_w, ln_b), resizer_b)

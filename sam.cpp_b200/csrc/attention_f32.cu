@@ -252,6 +252,158 @@ attention_f32_kernel(const float* __restrict__ qkv, int64_t ldq, const float* __
     }
 }
 
+// ---- general attention (text encoder, fusion / decoder attention) ----------
+//
+// softmax(scale * Q K^T + bias) V per head with F32 operands, GGML
+// flash_attn_ext semantics at GGML_PREC_F32: Q [lq][ldq], K [lk][ldk],
+// V [lk][ldv] with head h at columns h*HD .. h*HD + HD - 1; out [lq][ldo] the
+// same.  The mask is additive: bias[h * bias_h + q * bias_q + k] (a per-key
+// padding mask has bias_h = bias_q = 0; box relative-position biases vary with
+// both), and `causal` masks keys k > q (the text encoder's triangular mask).
+// A row whose keys are all masked yields 0.  One CTA per (64 queries, head);
+// the 4 x 4 register tiles and the per-tile blocked P V sums of the ViT kernel.
+struct AttnGenArgs {
+    const float* q;
+    const float* k;
+    const float* v;
+    const float* bias;
+    float* out;
+    int64_t ldq, ldk, ldv, ldo, bias_h, bias_q;
+    int lq, lk, causal;
+    float scale;
+};
+
+template <int HD>
+__global__ void __launch_bounds__(kF32Threads, 2) attention_gen_kernel(AttnGenArgs a) {
+    constexpr int kP = HD + 4;    // Q / K row pitch (floats)
+    constexpr int kJ = HD / 16;   // output channels per thread
+    extern __shared__ float4 smem_f4[];
+    float* qs = reinterpret_cast<float*>(smem_f4);  // [64][kP]
+    float* ks = qs + kTile * kP;                    // [64][kP]
+    float* vt = ks + kTile * kP;                    // [HD][kPitch]
+    float* ps = vt + HD * kPitch;                   // [64][kPitch]
+    const int t = threadIdx.x;
+    const int rq = t >> 4, u = t & 15;
+    const int q0 = blockIdx.x * kTile, h = blockIdx.y;
+    pdl_wait();
+    for (int idx = t; idx < kTile * (HD / 4); idx += kF32Threads) {
+        const int r = idx / (HD / 4), c4 = idx % (HD / 4), n = q0 + r;
+        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (n < a.lq) v = __ldg(reinterpret_cast<const float4*>(a.q + int64_t(n) * a.ldq + h * HD) + c4);
+        *reinterpret_cast<float4*>(qs + r * kP + c4 * 4) = v;
+    }
+    float o[4][kJ], m[4], l[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        m[i] = -INFINITY;
+        l[i] = 0.0f;
+#pragma unroll
+        for (int j = 0; j < kJ; ++j) o[i][j] = 0.0f;
+    }
+    int kend = a.lk;
+    if (a.causal) kend = min(kend, q0 + kTile);
+    const int kblocks = (kend + kTile - 1) / kTile;
+    for (int kb = 0; kb < kblocks; ++kb) {
+        __syncthreads();
+        for (int idx = t; idx < kTile * (HD / 4); idx += kF32Threads) {
+            const int r = idx / (HD / 4), c4 = idx % (HD / 4), n = kb * kTile + r;
+            float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (n < a.lk) v = __ldg(reinterpret_cast<const float4*>(a.k + int64_t(n) * a.ldk + h * HD) + c4);
+            *reinterpret_cast<float4*>(ks + r * kP + c4 * 4) = v;
+        }
+        for (int idx = t; idx < kTile * (HD / 4); idx += kF32Threads) {
+            const int r = idx & 63, d4 = idx >> 6, n = kb * kTile + r;
+            float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (n < a.lk) v = __ldg(reinterpret_cast<const float4*>(a.v + int64_t(n) * a.ldv + h * HD) + d4);
+            vt[(4 * d4 + 0) * kPitch + r] = v.x;
+            vt[(4 * d4 + 1) * kPitch + r] = v.y;
+            vt[(4 * d4 + 2) * kPitch + r] = v.z;
+            vt[(4 * d4 + 3) * kPitch + r] = v.w;
+        }
+        __syncthreads();
+        float s[4][4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+#pragma unroll
+            for (int j = 0; j < 4; ++j) s[i][j] = 0.0f;
+#pragma unroll
+        for (int d4 = 0; d4 < HD / 4; ++d4) {
+            float4 qa[4], kb4[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) qa[i] = *reinterpret_cast<const float4*>(qs + (4 * rq + i) * kP + 4 * d4);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) kb4[j] = *reinterpret_cast<const float4*>(ks + (u + 16 * j) * kP + 4 * d4);
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+#pragma unroll
+                for (int j = 0; j < 4; ++j) s[i][j] = dot4(qa[i], kb4[j], s[i][j]);
+        }
+        float alpha[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const int qn = q0 + 4 * rq + i;
+            float mx = -INFINITY;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const int kn = kb * kTile + u + 16 * j;
+                float sv = s[i][j] * a.scale;
+                if (kn >= a.lk || (a.causal && kn > qn)) sv = -INFINITY;
+                else if (a.bias && qn < a.lq) sv += __ldg(a.bias + h * a.bias_h + int64_t(qn) * a.bias_q + kn);
+                s[i][j] = sv;
+                mx = fmaxf(mx, sv);
+            }
+#pragma unroll
+            for (int off = 1; off < 16; off <<= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+            const float m_new = fmaxf(m[i], mx);
+            // All keys so far masked: keep the row empty (no NaN from -inf - -inf).
+            const float m_use = m_new == -INFINITY ? 0.0f : m_new;
+            alpha[i] = expf(m[i] - m_use);
+            float sum = 0.0f;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const float p = expf(s[i][j] - m_use);
+                ps[(4 * rq + i) * kPitch + u + 16 * j] = p;
+                sum += p;
+            }
+#pragma unroll
+            for (int off = 1; off < 16; off <<= 1) sum += __shfl_xor_sync(0xffffffffu, sum, off);
+            l[i] = fmaf(l[i], alpha[i], sum);
+            m[i] = m_new;
+        }
+        __syncthreads();
+        float ot[4][kJ];
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+#pragma unroll
+            for (int j = 0; j < kJ; ++j) ot[i][j] = 0.0f;
+#pragma unroll 4
+        for (int k4 = 0; k4 < 16; ++k4) {
+            float4 pa[4], vb[kJ];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) pa[i] = *reinterpret_cast<const float4*>(ps + (4 * rq + i) * kPitch + 4 * k4);
+#pragma unroll
+            for (int j = 0; j < kJ; ++j) vb[j] = *reinterpret_cast<const float4*>(vt + (u + 16 * j) * kPitch + 4 * k4);
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+#pragma unroll
+                for (int j = 0; j < kJ; ++j) ot[i][j] = dot4(pa[i], vb[j], ot[i][j]);
+        }
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+#pragma unroll
+            for (int j = 0; j < kJ; ++j) o[i][j] = fmaf(o[i][j], alpha[i], ot[i][j]);
+    }
+    pdl_trigger();
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const int n = q0 + 4 * rq + i;
+        if (n >= a.lq) continue;
+        float* row = a.out + int64_t(n) * a.ldo + h * HD;
+#pragma unroll
+        for (int j = 0; j < kJ; ++j) row[u + 16 * j] = l[i] > 0.0f ? __fdiv_rn(o[i][j], l[i]) : 0.0f;
+    }
+}
+
 GeometryF32 make_geometry_f32(int grid_w, int grid_h, int heads, int window, int batch, bool window_major) {
     GeometryF32 geo{grid_w, grid_h * batch, heads, window, batch, grid_w * grid_h, window_major ? 1 : 0};
     if (window > 0) {
@@ -278,6 +430,26 @@ void launch_attention_f32(const float* qkv, int64_t ldq, bool qkv_window_major, 
                             "cudaFuncSetAttribute(attention_f32 smem)");
         launch_pdl(attention_f32_kernel<false>, grid, dim3(kF32Threads), kF32Smem, stream,
                    "attention_f32_kernel launch", qkv, ldq, freqs, geo, out, out_h, ldo, state.status);
+    }
+}
+
+void launch_attention_gen(const float* q, int64_t ldq, const float* k, int64_t ldk, const float* v, int64_t ldv,
+                          int lq, int lk, int heads, int head_dim, float scale, int causal, const float* bias,
+                          int64_t bias_h, int64_t bias_q, float* out, int64_t ldo, DeviceState& state,
+                          cudaStream_t stream) {
+    if (lq == 0) return;
+    AttnGenArgs a{q, k, v, bias, out, ldq, ldk, ldv, ldo, bias_h, bias_q, lq, lk, causal, scale};
+    const dim3 grid((lq + kTile - 1) / kTile, heads);
+    if (head_dim == 64) {
+        constexpr int smem = (2 * kTile * 68 + 64 * kPitch + kTile * kPitch) * 4;
+        set_smem_limit_once(state, reinterpret_cast<const void*>(attention_gen_kernel<64>), smem,
+                            "cudaFuncSetAttribute(attention_gen smem)");
+        launch_pdl(attention_gen_kernel<64>, grid, dim3(kF32Threads), smem, stream, "attention_gen_kernel launch", a);
+    } else {
+        constexpr int smem = (2 * kTile * 36 + 32 * kPitch + kTile * kPitch) * 4;
+        set_smem_limit_once(state, reinterpret_cast<const void*>(attention_gen_kernel<32>), smem,
+                            "cudaFuncSetAttribute(attention_gen smem)");
+        launch_pdl(attention_gen_kernel<32>, grid, dim3(kF32Threads), smem, stream, "attention_gen_kernel launch", a);
     }
 }
 

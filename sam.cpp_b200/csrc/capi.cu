@@ -633,6 +633,96 @@ samq_status samq_vit_prefix_v2(const float* image, int width, int height, int pa
     });
 }
 
+samq_status samq_text_block_forward_v1(const samq_text_block_v1* block, float* x, int tokens, void* stream_ptr) {
+    return guarded([&] {
+        require(block != nullptr && block->version == 1, "text block descriptor missing or not version 1");
+        const samq_text_block_v1& b = *block;
+        require(b.in_proj && b.out_proj && b.fc1 && b.fc2, "null weight handle");
+        const int64_t E = b.in_proj->k, mlp = b.fc1->n;
+        require(E % 64 == 0 && E <= 4096 && b.in_proj->n == 3 * E && b.out_proj->k == E && b.out_proj->n == E &&
+                    b.fc1->k == E && b.fc2->k == mlp && b.fc2->n == E,
+                "linear shapes must be in_proj E->3E, out_proj E->E, fc1 E->MLP, fc2 MLP->E (E % 64 == 0)");
+        require(mlp % 32 == 0, "MLP width must be a multiple of 32");
+        require(tokens > 0 && tokens <= 4096, "token count out of range");
+        const float* params[] = {b.norm1_w, b.norm1_b, b.in_proj_b, b.out_proj_b, b.norm2_w, b.norm2_b,
+                                 b.fc1_b, b.fc2_b, x};
+        for (const float* p : params) require(p != nullptr && aligned16(p), "parameters must be 16-byte aligned device pointers");
+        const int device = current_device();
+        for (const samq_weights* w : {b.in_proj, b.out_proj, b.fc1, b.fc2})
+            require(w->device == device, "weight handle belongs to another device");
+        DeviceState& state = device_state(device);
+        cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
+        TextBlockArgs args;
+        args.norm1_w = b.norm1_w;
+        args.norm1_b = b.norm1_b;
+        args.norm2_w = b.norm2_w;
+        args.norm2_b = b.norm2_b;
+        args.in_proj = b.in_proj;
+        args.out_proj = b.out_proj;
+        args.fc1 = b.fc1;
+        args.fc2 = b.fc2;
+        args.in_proj_b = b.in_proj_b;
+        args.out_proj_b = b.out_proj_b;
+        args.fc1_b = b.fc1_b;
+        args.fc2_b = b.fc2_b;
+        Scratch& scratch = scratch_for(state, stream, text_block_scratch_bytes(args, tokens, state.sm_count));
+        launch_text_block(args, x, tokens, scratch.ptr, state, stream);
+        for (const samq_weights* w : {b.in_proj, b.out_proj, b.fc1, b.fc2})
+            const_cast<samq_weights*>(w)->launches.fetch_add(1);
+    });
+}
+
+samq_status samq_token_embed_v1(const float* table, int64_t vocab, int width, const int32_t* ids, int count,
+                                const float* pos, float* out, void* stream_ptr) {
+    return guarded([&] {
+        require(vocab > 0 && width > 0 && width <= (1 << 20) && count >= 0 && count <= (1 << 20),
+                "embedding sizes out of range");
+        if (count == 0) return;
+        require(table && ids && out, "null pointer");
+        for (int i = 0; i < count; ++i)
+            require(ids[i] >= 0 && ids[i] < vocab, "token id outside the vocabulary");
+        DeviceState& state = device_state(current_device());
+        cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
+        Scratch& scratch = scratch_for(state, stream, static_cast<size_t>(count) * sizeof(int32_t) + 256);
+        check_cuda(cudaMemcpyAsync(scratch.ptr, ids, static_cast<size_t>(count) * sizeof(int32_t),
+                                   cudaMemcpyHostToDevice, stream),
+                   "cudaMemcpyAsync(token ids)");
+        launch_embed_rows(table, static_cast<const int32_t*>(scratch.ptr), pos, count, width, out, stream);
+        // The host ids may be reused by the caller as soon as this returns.
+        check_cuda(cudaStreamSynchronize(stream), "cudaStreamSynchronize(token ids)");
+    });
+}
+
+samq_status samq_layer_norm_v1(const float* x, int64_t rows, int width, int64_t ldx, const float* w, const float* b,
+                               float eps, float* out, int64_t ldo, void* stream_ptr) {
+    return guarded([&] {
+        require(rows >= 0 && width > 0 && ldx >= width && ldo >= width, "layer norm sizes out of range");
+        require(eps > 0.0f, "eps must be positive");
+        if (rows == 0) return;
+        require(x && w && out, "null pointer");
+        device_state(current_device());
+        launch_layer_norm_f32(x, rows, width, ldx, w, b, out, ldo, eps, static_cast<cudaStream_t>(stream_ptr));
+    });
+}
+
+samq_status samq_attention_v1(const float* q, int64_t ldq, const float* k, int64_t ldk, const float* v, int64_t ldv,
+                              int lq, int lk, int heads, int head_dim, float scale, int causal, const float* bias,
+                              int64_t bias_h, int64_t bias_q, float* out, int64_t ldo, void* stream_ptr) {
+    return guarded([&] {
+        require(head_dim == 32 || head_dim == 64, "head_dim must be 32 or 64");
+        require(heads > 0 && heads <= 256 && lq >= 0 && lk > 0 && lq <= (1 << 22) && lk <= (1 << 22),
+                "attention sizes out of range");
+        const int64_t E = int64_t(heads) * head_dim;
+        require(ldq >= E && ldk >= E && ldv >= E && ldo >= E && ldq % 4 == 0 && ldk % 4 == 0 && ldv % 4 == 0,
+                "row strides must cover heads * head_dim and be multiples of 4 floats");
+        if (lq == 0) return;
+        require(q && k && v && out && aligned16(q) && aligned16(k) && aligned16(v), "q, k, v must be 16-byte aligned");
+        DeviceState& state = device_state(current_device());
+        launch_attention_gen(q, ldq, k, ldk, v, ldv, lq, lk, heads, head_dim, scale, causal, bias, bias_h, bias_q,
+                             out, ldo, state, static_cast<cudaStream_t>(stream_ptr));
+    });
+}
+
 samq_status samq_dense_create_v1(int device, int type, int kind, int kw, int kh, int64_t cin, int64_t cout,
                                  const void* data, size_t bytes, void* stream_ptr, samq_dense** out) {
     return guarded([&] {

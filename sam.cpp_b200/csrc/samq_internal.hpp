@@ -174,6 +174,13 @@ void launch_attention_packed(const __half* q, const __half* k, const __half* vt,
 void launch_attention_f32(const float* qkv, int64_t ldq, bool qkv_window_major, int grid_w, int grid_h, int heads,
                           int window, int batch, const float* freqs, float* out, __half* out_h, int64_t ldo,
                           DeviceState& state, cudaStream_t stream);
+// General F32 attention (attention_f32.cu): Q [lq][ldq], K / V [lk][ld],
+// head h at columns h*head_dim (head_dim 32 or 64), additive bias
+// bias[h*bias_h + q*bias_q + k] (nullable), causal mask, out [lq][ldo].
+void launch_attention_gen(const float* q, int64_t ldq, const float* k, int64_t ldk, const float* v, int64_t ldv,
+                          int lq, int lk, int heads, int head_dim, float scale, int causal, const float* bias,
+                          int64_t bias_h, int64_t bias_q, float* out, int64_t ldo, DeviceState& state,
+                          cudaStream_t stream);
 // sam3_apply_rope on [head_batches][tokens][64] f32 with GGML's rounding.
 void launch_rope_f32(const float* x, const float* freqs, int64_t tokens, int64_t head_batches, float* out,
                      cudaStream_t stream);
@@ -241,6 +248,24 @@ size_t vit_prefix_scratch_bytes(int64_t tokens, int64_t embed, int patch, int co
 void launch_vit_prefix(const float* image, int width, int height, int patch, const float* patch_w, int64_t embed,
                        const float* pos, int pos_grid, const float* ln_w, const float* ln_b, float* x, int compute,
                        void* scratch, DeviceState& state, cudaStream_t stream);
+
+// text.cu: the text encoder's pieces.
+struct TextBlockArgs {
+    const float *norm1_w = nullptr, *norm1_b = nullptr, *norm2_w = nullptr, *norm2_b = nullptr;
+    const samq_weights *in_proj = nullptr, *out_proj = nullptr, *fc1 = nullptr, *fc2 = nullptr;
+    const float *in_proj_b = nullptr, *out_proj_b = nullptr, *fc1_b = nullptr, *fc2_b = nullptr;
+};
+size_t text_block_scratch_bytes(const TextBlockArgs& blk, int64_t tokens, int sms);
+void launch_text_block(const TextBlockArgs& blk, float* x, int64_t tokens, void* scratch, DeviceState& state,
+                       cudaStream_t stream);
+void launch_layer_norm_f32(const float* x, int64_t rows, int width, int64_t ldx, const float* w, const float* b,
+                           float* out, int64_t ldo, float eps, cudaStream_t stream);
+void launch_add_rows(float* x, int64_t ldx, const float* y, int64_t ldy, int64_t rows, int width, cudaStream_t stream);
+void launch_embed_rows(const float* table, const int32_t* ids, const float* pos, int count, int width, float* out,
+                       cudaStream_t stream);
+void linear_from_staged(const samq_weights* w, const __half* a, int64_t lda, int64_t m, const float* bias,
+                        int epilogue, float* y, int64_t ldy, float* partials, DeviceState& state,
+                        cudaStream_t stream);
 
 // dense.cu: F32-semantics linears / convolutions (three-term TF32 split).
 void launch_dense_prep(const void* src, int type, int kind, int ks, int64_t cin, int64_t cout, int64_t n, int64_t k,

@@ -58,6 +58,13 @@ class VitBlockDesc(ctypes.Structure):
                 ("compute", ctypes.c_int32)]
 
 
+class TextBlockDesc(ctypes.Structure):
+    """struct samq_text_block_v1."""
+    _fields_ = [("version", ctypes.c_uint32), ("norm1_w", _vp), ("norm1_b", _vp), ("in_proj", _vp),
+                ("in_proj_b", _vp), ("out_proj", _vp), ("out_proj_b", _vp), ("norm2_w", _vp), ("norm2_b", _vp),
+                ("fc1", _vp), ("fc1_b", _vp), ("fc2", _vp), ("fc2_b", _vp)]
+
+
 class NeckDesc(ctypes.Structure):
     """struct samq_neck_v1: (weights, bias) pairs in the order of NECK_LAYERS."""
     _fields_ = [("version", ctypes.c_uint32)] + [
@@ -94,6 +101,11 @@ SIGNATURES = {
     "samq_vit_block_forward_v1": (_i32, [ctypes.POINTER(VitBlockDesc), _vp, _i32, _i32, _vp]),
     "samq_vit_block_forward_batch_v1": (_i32, [ctypes.POINTER(VitBlockDesc), _vp, _i32, _i32, _i32, _vp]),
     "samq_vit_prefix_v1": (_i32, [_vp, _i32, _i32, _i32, _vp, _i64, _vp, _i32, _vp, _vp, _vp, _vp]),
+    "samq_text_block_forward_v1": (_i32, [ctypes.POINTER(TextBlockDesc), _vp, _i32, _vp]),
+    "samq_token_embed_v1": (_i32, [_vp, _i64, _i32, _vp, _i32, _vp, _vp, _vp]),
+    "samq_layer_norm_v1": (_i32, [_vp, _i64, _i32, _i64, _vp, _vp, ctypes.c_float, _vp, _i64, _vp]),
+    "samq_attention_v1": (_i32, [_vp, _i64, _vp, _i64, _vp, _i64, _i32, _i32, _i32, _i32, ctypes.c_float, _i32, _vp,
+                                 _i64, _i64, _vp, _i64, _vp]),
     "samq_dense_create_v1": (_i32, [_i32, _i32, _i32, _i32, _i32, _i64, _i64, _vp, _sz, _vp, ctypes.POINTER(_vp)]),
     "samq_dense_destroy_v1": (_i32, [_vp]),
     "samq_dense_linear_v1": (_i32, [_vp, _vp, _i64, _i64, _vp, _i32, _vp, _i64, _vp]),
@@ -305,6 +317,45 @@ def vit_prefix(image, width: int, height: int, patch: int, patch_w, embed: int, 
     [tokens][E] f32 (F32 columns with F32 semantics, or f16 columns)."""
     _check(library().samq_vit_prefix_v2(_addr(image), width, height, patch, _addr(patch_w), embed, _addr(pos_embed),
                                         pos_grid, _addr(ln_w), _addr(ln_b), _addr(x), compute, _stream(stream)))
+
+
+class TextBlock:
+    """One text-encoder block's device parameters (samq_text_block_v1): f32
+    device tensors and four Weights handles (kept alive here)."""
+
+    def __init__(self, norm1_w, norm1_b, in_proj: Weights, in_proj_b, out_proj: Weights, out_proj_b, norm2_w, norm2_b,
+                 fc1: Weights, fc1_b, fc2: Weights, fc2_b):
+        self._keep = (norm1_w, norm1_b, in_proj, in_proj_b, out_proj, out_proj_b, norm2_w, norm2_b, fc1, fc1_b, fc2,
+                      fc2_b)
+        self.desc = TextBlockDesc(1, _addr(norm1_w), _addr(norm1_b), in_proj.handle, _addr(in_proj_b),
+                                  out_proj.handle, _addr(out_proj_b), _addr(norm2_w), _addr(norm2_b), fc1.handle,
+                                  _addr(fc1_b), fc2.handle, _addr(fc2_b))
+
+
+def text_block_forward(block: TextBlock, x, tokens: int, stream=None):
+    """samq_text_block_forward_v1: one causal pre-LN block in place on x [tokens][E]."""
+    _check(library().samq_text_block_forward_v1(ctypes.byref(block.desc), _addr(x), tokens, _stream(stream)))
+
+
+def token_embed(table, vocab: int, width: int, ids, pos, out, stream=None):
+    """samq_token_embed_v1: out = table[ids] + pos; ids is a host sequence of ints."""
+    arr = (ctypes.c_int32 * len(ids))(*[int(i) for i in ids])
+    _check(library().samq_token_embed_v1(_addr(table), vocab, width, arr, len(ids), _addr(pos), _addr(out),
+                                         _stream(stream)))
+
+
+def layer_norm(x, rows: int, width: int, ldx: int, w, b, out, ldo: int, eps: float = 1e-5, stream=None):
+    """samq_layer_norm_v1: f32 LayerNorm of rows."""
+    _check(library().samq_layer_norm_v1(_addr(x), rows, width, ldx, _addr(w), _addr(b), eps, _addr(out), ldo,
+                                        _stream(stream)))
+
+
+def attention(q, ldq: int, k, ldk: int, v, ldv: int, lq: int, lk: int, heads: int, head_dim: int, scale: float, out,
+              ldo: int, causal: bool = False, bias=None, bias_h: int = 0, bias_q: int = 0, stream=None):
+    """samq_attention_v1: F32 multi-head attention with an optional causal or additive mask."""
+    _check(library().samq_attention_v1(_addr(q), ldq, _addr(k), ldk, _addr(v), ldv, lq, lk, heads, head_dim, scale,
+                                       1 if causal else 0, _addr(bias), bias_h, bias_q, _addr(out), ldo,
+                                       _stream(stream)))
 
 
 class Dense:

@@ -1,0 +1,196 @@
+"""Text encoder and general F32 attention on the device against the f64 oracle.
+
+samq_attention_v1 (the fusion / decoder / text attention) is pinned to the
+reference's closed-form precision probe, case for case
+(tests/runtime/ggml/test_precision.cpp:68-160: head dims 32 and 64, 1 to 257
+queries over 128 to 5184 keys, the masked-sparse variant), at its 1e-5 bar,
+and checked against oracle.attention_gen on random inputs with causal, key
+padding and per-(head, query, key) masks.
+
+samq_text_block_forward_v1 and the whole encoder (token embedding, 24 blocks,
+final LayerNorm, resizer; src/models/sam3/text_encoder.hpp:68-180) are checked
+against oracle.text_block / text_encoder with the config-4 shapes (width 1024,
+16 heads, MLP 4096, 32 tokens, Q8_0 linears).  One block: the contribution's
+cosine >= 0.9999 and max error <= 1e-2 of its largest magnitude (the ViT
+block's bar; Q8_1 re-staging makes single codes flip).  Whole encoder: the
+resized features' normalized L2 to the oracle <= 1.25 x that of the
+reference's CPU-backend arithmetic (Q8_0 activation packing) from the same
+oracle, and <= 0.02 -- the drift argument of the backbone test.
+"""
+import numpy as np
+import pytest
+import torch
+
+import samq
+from oracle import oracle as o
+
+pytestmark = pytest.mark.gpu
+E, HEADS, MLP, L, VOCAB, OUT = 1024, 16, 4096, 32, 49408, 256
+
+
+def _dev(a):
+    return torch.from_numpy(np.ascontiguousarray(a)).cuda()
+
+
+def _run_attention(q, k, v, heads, hd, scale, causal=False, bias=None, bias_h=0, bias_q=0):
+    lq, lk = q.shape[0], k.shape[0]
+    out = torch.full((lq, heads * hd), -7.0, device="cuda")
+    samq.attention(_dev(q), q.shape[1], _dev(k), k.shape[1], _dev(v), v.shape[1], lq, lk, heads, hd, scale, out,
+                   heads * hd, causal=causal, bias=None if bias is None else _dev(bias), bias_h=bias_h,
+                   bias_q=bias_q)
+    samq.check(0)
+    return out.cpu().numpy()
+
+
+@pytest.mark.parametrize("dims,queries,keys,masked", [
+    (64, 1, 128, False), (32, 1, 130, False), (64, 33, 130, False), (32, 7, 130, True), (64, 33, 130, True),
+    (32, 129, 5184, False), (64, 257, 576, False)])
+def test_precision_probe_reference_cases(dims, queries, keys, masked):
+    """test_precision.cpp:68-126 with its cases (:152-159): Q = 1.0003 +
+    (query % 7) 1e-5, K = +-0.0625 and V = +-1 on the first / second half of
+    the keys; masked_sparse adds -inf on keys 0..3, which shifts the result by
+    0.5 log((keys/2 - 4) / (keys - keys/2)).  Bar: 1e-5."""
+    scale = np.float32(1.0 / np.sqrt(np.float32(dims)))
+    q = np.repeat((np.float32(1.0003) + (np.arange(queries) % 7).astype(np.float32) * np.float32(0.00001))[:, None],
+                  dims, axis=1).astype(np.float32)
+    half = np.arange(keys) < keys // 2
+    k = np.repeat(np.where(half, np.float32(0.0625), np.float32(-0.0625))[:, None], dims, axis=1).astype(np.float32)
+    v = np.repeat(np.where(half, np.float32(1.0), np.float32(-1.0))[:, None], dims, axis=1).astype(np.float32)
+    bias = None
+    shift = 0.0
+    if masked:
+        bias = np.where(np.arange(keys) < 4, -np.inf, 0.0).astype(np.float32)
+        shift = 0.5 * np.log((keys // 2 - 4) / (keys - keys // 2))
+    got = _run_attention(q, k, v, 1, dims, float(scale), bias=bias).astype(np.float64)
+    expected = np.tanh(dims * 0.0625 * float(scale) * q.astype(np.float64) + shift)
+    assert np.all(np.isfinite(got)) and np.abs(got - expected).max() <= 1e-5, np.abs(got - expected).max()
+
+
+@pytest.mark.parametrize("lq,lk,heads,hd,mode", [
+    (32, 32, 16, 64, "causal"), (200, 5184, 8, 32, "rpb"), (5184, 33, 8, 32, "padding"), (201, 201, 8, 32, "none"),
+    (70, 45, 3, 64, "rpb")])
+def test_attention_parity_random(lq, lk, heads, hd, mode):
+    """Random Q / K / V with each mask form against oracle.attention_gen:
+    cosine >= 1 - 1e-10 and normalized max error <= 1e-5 (F32 level)."""
+    rng = np.random.default_rng(lq + lk + heads)
+    q = rng.normal(0, 1, (lq, heads * hd)).astype(np.float32)
+    k = rng.normal(0, 1, (lk, heads * hd)).astype(np.float32)
+    v = rng.normal(0, 1, (lk, heads * hd)).astype(np.float32)
+    scale = float(1.0 / np.sqrt(hd))
+    bias, bias_h, bias_q, causal = None, 0, 0, mode == "causal"
+    if mode == "rpb":
+        bias = rng.normal(0, 2, (heads, lq, lk)).astype(np.float32)
+        bias_h, bias_q = lq * lk, lk
+    elif mode == "padding":
+        bias = np.where(np.arange(lk) >= lk - 7, -np.inf, 0.0).astype(np.float32)
+    got = _run_attention(q, k, v, heads, hd, scale, causal=causal, bias=bias, bias_h=bias_h, bias_q=bias_q)
+    ref = o.attention_gen(q, k, v, heads, hd, scale, causal=causal, bias=bias)
+    g, r = got.astype(np.float64).ravel(), ref.astype(np.float64).ravel()
+    cos = float(g @ r / (np.linalg.norm(g) * np.linalg.norm(r)))
+    rel = float(np.abs(g - r).max() / np.abs(r).max())
+    assert cos >= 1 - 1e-10 and rel <= 1e-5, (cos, rel)
+
+
+def _weights(rng, n, k):
+    w = rng.normal(0.0, 0.02, (n, k)).astype(np.float32)
+    w[rng.random(w.shape) < 0.01] *= 8.0
+    return w
+
+
+def make_text_block(rng, qtype=o.Q8_0):
+    """Random-init text block (config-4 statistics: Q8_0 linears, N(0, 0.02^2)
+    weights with 1% x8, LN gamma 1 + N(0, 0.02^2))."""
+    host, dev = {}, {}
+    for name, (n, k) in {"in_proj": (3 * E, E), "out_proj": (E, E), "fc1": (MLP, E), "fc2": (E, MLP)}.items():
+        rows = o.quantize(qtype, _weights(rng, n, k))
+        host[name + "_w"] = o.dequantize(qtype, rows, n * k).reshape(n, k)
+        host[name + "_q"] = (qtype, rows)
+        dev[name] = samq.Weights(qtype, k, n, rows)
+        host[name + "_b"] = rng.normal(0.0, 0.02, n).astype(np.float32)
+        dev[name + "_b"] = _dev(host[name + "_b"])
+    for name in ("norm1", "norm2"):
+        host[name + "_w"] = (1.0 + rng.normal(0.0, 0.02, E)).astype(np.float32)
+        host[name + "_b"] = rng.normal(0.0, 0.02, E).astype(np.float32)
+        dev[name + "_w"], dev[name + "_b"] = _dev(host[name + "_w"]), _dev(host[name + "_b"])
+    block = samq.TextBlock(dev["norm1_w"], dev["norm1_b"], dev["in_proj"], dev["in_proj_b"], dev["out_proj"],
+                           dev["out_proj_b"], dev["norm2_w"], dev["norm2_b"], dev["fc1"], dev["fc1_b"], dev["fc2"],
+                           dev["fc2_b"])
+    return host, block
+
+
+def test_text_block_parity():
+    rng = np.random.default_rng(31)
+    host, block = make_text_block(rng)
+    x = rng.standard_normal((L, E)).astype(np.float32)
+    xd = _dev(x)
+    samq.text_block_forward(block, xd, L)
+    samq.check(0)
+    got = xd.cpu().numpy().astype(np.float64)
+    ref = o.text_block(x, host).astype(np.float64)
+    dg, dr = (got - x).ravel(), (ref - x).ravel()
+    cos = float(dg @ dr / (np.linalg.norm(dg) * np.linalg.norm(dr)))
+    rel = float(np.abs(dg - dr).max() / np.abs(dr).max())
+    assert cos >= 0.9999 and rel <= 1e-2, (cos, rel)
+
+
+def _cpu_path_block(x, blk):
+    """The block with the reference CPU backend's linears (Q8_0 packing, integer dots)."""
+    keep = o.staged_linear
+
+    def linear(w, v, bias=None, epilogue=o.EPILOGUE_NONE):
+        name = next(n for n in ("in_proj", "out_proj", "fc1", "fc2") if blk[n + "_w"] is w)
+        return o.cpu_path_linear(blk, name, v, bias, epilogue)
+    o.staged_linear = linear
+    try:
+        return o.text_block(x, blk)
+    finally:
+        o.staged_linear = keep
+
+
+def test_text_encoder_parity():
+    """Token embedding + 24 blocks + final LayerNorm + resizer at config-4
+    shapes, the API-valid token form [49406, 30 ids, 49407]
+    (src/models/sam3/tokenizer.hpp:103-118)."""
+    rng = np.random.default_rng(4)
+    ids = np.concatenate([[49406], rng.integers(1, 49405, L - 2), [49407]]).astype(np.int32)
+    table = (rng.normal(0, 0.02, (VOCAB, E))).astype(np.float32)
+    pos = rng.normal(0, 0.01, (L, E)).astype(np.float32)
+    ln_w = (1 + rng.normal(0, 0.02, E)).astype(np.float32)
+    ln_b = rng.normal(0, 0.02, E).astype(np.float32)
+    res_rows = o.quantize(o.Q8_0, _weights(rng, OUT, E))
+    res_w = o.dequantize(o.Q8_0, res_rows, OUT * E).reshape(OUT, E)
+    res_b = rng.normal(0, 0.02, OUT).astype(np.float32)
+    x = torch.empty((L, E), device="cuda")
+    samq.token_embed(_dev(table), VOCAB, E, ids, _dev(pos), x)
+    hosts = []
+    for _ in range(24):
+        host, block = make_text_block(rng)
+        samq.text_block_forward(block, x, L)
+        hosts.append(host)
+        for held in block._keep:
+            if isinstance(held, samq.Weights):
+                held.close()
+    normed = torch.empty_like(x)
+    samq.layer_norm(x, L, E, E, _dev(ln_w), _dev(ln_b), normed, E)
+    res = samq.Weights(o.Q8_0, E, OUT, res_rows)
+    feats = torch.empty((L, OUT), device="cuda")
+    samq.linear(res, normed, L, E, _dev(res_b), samq.EPILOGUE_NONE, feats, OUT)
+    samq.check(0)
+    got = feats.cpu().numpy()
+    ref = o.text_encoder(ids, table, pos, hosts, ln_w, ln_b, res_w, res_b)
+    xc = (table[ids] + pos).astype(np.float32)
+    for blk in hosts:
+        xc = _cpu_path_block(xc, blk)
+    cpu = o.cpu_path_linear({"res_w": res_w, "res_q": (o.Q8_0, res_rows)}, "res", o.layer_norm(xc, ln_w, ln_b), res_b)
+    nl2 = float(np.linalg.norm(got - ref) / np.linalg.norm(ref))
+    cpu_nl2 = float(np.linalg.norm(cpu - ref) / np.linalg.norm(ref))
+    print(f"text encoder: nl2 {nl2:.5f}, reference CPU path {cpu_nl2:.5f}")
+    assert nl2 <= 0.02 and nl2 <= 1.25 * cpu_nl2 + 1e-4, (nl2, cpu_nl2)
+    res.close()
+
+
+def test_token_embed_rejects_out_of_vocabulary():
+    table = torch.zeros((10, 8), device="cuda")
+    out = torch.empty((2, 8), device="cuda")
+    with pytest.raises(samq.SamqError):
+        samq.token_embed(table, 10, 8, [3, 10], None, out)
