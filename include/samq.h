@@ -309,6 +309,40 @@ samq_status samq_attention_v1(const float* q, int64_t ldq, const float* k, int64
                               int lq, int lk, int heads, int head_dim, float scale, int causal, const float* bias,
                               int64_t bias_h, int64_t bias_q, float* out, int64_t ldo, void* stream);
 
+/* ---- Fusion encoder -----------------------------------------------------------
+ * A linear of the fusion / decoder modules is either a quantized weight handle
+ * (the full-linear Q8_0 profiles) or a dense F32 / F16 handle of kind
+ * SAMQ_DENSE_LINEAR (the mixed profile's fusion=f32, decoder=f32): exactly one
+ * of the two is non-NULL. */
+struct samq_dense;
+typedef struct samq_linear_ref_v1 {
+    const samq_weights* quantized;
+    const struct samq_dense* dense;
+    const float* bias;  /* [n] or NULL */
+} samq_linear_ref_v1;
+
+/* One fusion-encoder layer (src/models/sam3/fusion_encoder.hpp:38-150), tensor
+ * names fenc.layers.N.* (src/models/sam3/tensors.hpp:218-243), width D:
+ *   x = x + sa.out_proj(attn(Q, K from LN1(x) + pos; V from LN1(x)))
+ *   x = x + ca.out_proj(attn(Q from LN2(x); K, V from prompt; + prompt_bias))
+ *   x = x + linear2(ReLU(linear1(LN3(x))))
+ * in_proj weights are [3D][D] (Q | K | V rows, D % 128 == 0); heads of D / heads
+ * channels (32 or 64), attention with F32 operands. */
+typedef struct samq_fusion_layer_v1 {
+    uint32_t version;  /* 1 */
+    int32_t heads;     /* 8 in SAM 3 */
+    const float *norm1_w, *norm1_b, *norm2_w, *norm2_b, *norm3_w, *norm3_b;
+    samq_linear_ref_v1 sa_in_proj, sa_out_proj, ca_in_proj, ca_out_proj, linear1, linear2;
+} samq_fusion_layer_v1;
+
+/* x: device f32 [tokens][D] image tokens (in place), pos [tokens][D] their
+ * positional encoding, prompt [prompt_tokens][D] the prompt tokens (text
+ * features and the geometry token), prompt_bias [prompt_tokens] additive key
+ * bias (0 or a large negative value at padding tokens; NULL: none). */
+samq_status samq_fusion_layer_forward_v1(const samq_fusion_layer_v1* layer, float* x, const float* pos, int tokens,
+                                         const float* prompt, const float* prompt_bias, int prompt_tokens,
+                                         void* stream);
+
 /* ---- Dense (F32 / F16) modules with F32 semantics -------------------------
  * The tensors the reference keeps unquantized (neck convolutions, fusion /
  * decoder / mask-head linears in the F32 profiles: "only ViT linear weights

@@ -584,3 +584,40 @@ def text_encoder(ids, token_embed: np.ndarray, pos_embed: np.ndarray, blocks: li
     for blk in blocks:
         x = text_block(x, blk)
     return staged_linear(resizer_w, layer_norm(x, ln_w, ln_b), resizer_b)
+
+
+def module_linear(lin: dict, x: np.ndarray, rows=None, epilogue=EPILOGUE_NONE) -> np.ndarray:
+    """A linear of the fusion / decoder modules: lin = {"w": f32 [n][k] (the
+    decoded weight), "b": [n] or None, "quantized": bool}.  Quantized: MMQ
+    operand semantics (staged_linear); dense: the F32 product in f64.  `rows`
+    selects a row slice of the weight (the in_proj views)."""
+    w = lin["w"] if rows is None else lin["w"][rows]
+    b = None if lin["b"] is None else (lin["b"] if rows is None else lin["b"][rows])
+    if lin["quantized"]:
+        return staged_linear(w, x, b, epilogue)
+    return dense_linear(x, w, b, gelu=epilogue == EPILOGUE_GELU_ERF).astype(np.float32)
+
+
+def fusion_layer(x: np.ndarray, pos: np.ndarray, prompt: np.ndarray, prompt_bias, ly: dict, heads: int) -> np.ndarray:
+    """sam3_fenc_layer_forward (src/models/sam3/fusion_encoder.hpp:38-150) with
+    f64 LayerNorm / attention; ly holds norm{1,2,3}_{w,b} and the module_linear
+    dicts sa_in_proj, sa_out_proj, ca_in_proj, ca_out_proj, linear1, linear2."""
+    x = np.asarray(x, np.float32)
+    D = x.shape[1]
+    hd = D // heads
+    scale = 1.0 / np.sqrt(hd)
+    h = layer_norm(x, ly["norm1_w"], ly["norm1_b"])
+    qk_in = (h + np.asarray(pos, np.float32)).astype(np.float32)
+    qk = module_linear(ly["sa_in_proj"], qk_in, slice(0, 2 * D))
+    v = module_linear(ly["sa_in_proj"], h, slice(2 * D, 3 * D))
+    att = attention_gen(qk[:, :D], qk[:, D:], v, heads, hd, scale)
+    x = x + module_linear(ly["sa_out_proj"], att)
+    h = layer_norm(x, ly["norm2_w"], ly["norm2_b"])
+    q = module_linear(ly["ca_in_proj"], h, slice(0, D))
+    kv = module_linear(ly["ca_in_proj"], np.asarray(prompt, np.float32), slice(D, 3 * D))
+    bias = None if prompt_bias is None else np.asarray(prompt_bias, np.float32)[None, None, :]
+    att = attention_gen(q, kv[:, :D], kv[:, D:], heads, hd, scale, bias=bias)
+    x = x + module_linear(ly["ca_out_proj"], att)
+    h = layer_norm(x, ly["norm3_w"], ly["norm3_b"])
+    f = np.maximum(module_linear(ly["linear1"], h), 0.0).astype(np.float32)
+    return x + module_linear(ly["linear2"], f)

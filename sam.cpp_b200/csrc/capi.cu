@@ -723,6 +723,46 @@ samq_status samq_attention_v1(const float* q, int64_t ldq, const float* k, int64
     });
 }
 
+static void check_linear_ref(const samq_linear_ref_v1& l, int64_t k, int64_t n, int device, const char* what) {
+    const std::string name(what);
+    require((l.quantized != nullptr) != (l.dense != nullptr), (name + ": exactly one of quantized / dense").c_str());
+    if (l.dense) require(l.dense->kind == SAMQ_DENSE_LINEAR, (name + ": dense handle is not a LINEAR").c_str());
+    require(linear_in(l) == k && linear_out(l) == n, (name + ": unexpected shape").c_str());
+    require((l.quantized ? l.quantized->device : l.dense->device) == device, (name + ": handle on another device").c_str());
+    require(l.bias == nullptr || aligned16(l.bias), (name + ": bias must be 16-byte aligned").c_str());
+}
+
+samq_status samq_fusion_layer_forward_v1(const samq_fusion_layer_v1* layer, float* x, const float* pos, int tokens,
+                                         const float* prompt, const float* prompt_bias, int prompt_tokens,
+                                         void* stream_ptr) {
+    return guarded([&] {
+        require(layer != nullptr && layer->version == 1, "fusion layer descriptor missing or not version 1");
+        const samq_fusion_layer_v1& ly = *layer;
+        require(ly.sa_in_proj.quantized || ly.sa_in_proj.dense, "sa_in_proj missing");
+        const int64_t D = linear_in(ly.sa_in_proj);
+        require(D % 128 == 0 && D <= 4096 && ly.heads > 0 && D % ly.heads == 0 &&
+                    (D / ly.heads == 32 || D / ly.heads == 64),
+                "width must be a multiple of 128 with heads of 32 or 64 channels");
+        const int device = current_device();
+        require(ly.linear1.quantized || ly.linear1.dense, "linear1 missing");
+        const int64_t F = linear_out(ly.linear1);
+        check_linear_ref(ly.sa_in_proj, D, 3 * D, device, "sa_in_proj");
+        check_linear_ref(ly.sa_out_proj, D, D, device, "sa_out_proj");
+        check_linear_ref(ly.ca_in_proj, D, 3 * D, device, "ca_in_proj");
+        check_linear_ref(ly.ca_out_proj, D, D, device, "ca_out_proj");
+        check_linear_ref(ly.linear1, D, F, device, "linear1");
+        check_linear_ref(ly.linear2, F, D, device, "linear2");
+        require(F % 32 == 0, "FFN width must be a multiple of 32");
+        require(tokens > 0 && tokens <= (1 << 22) && prompt_tokens > 0 && prompt_tokens <= 4096, "token counts out of range");
+        const float* params[] = {ly.norm1_w, ly.norm1_b, ly.norm2_w, ly.norm2_b, ly.norm3_w, ly.norm3_b, x, pos, prompt};
+        for (const float* p : params) require(p != nullptr && aligned16(p), "parameters must be 16-byte aligned device pointers");
+        DeviceState& state = device_state(device);
+        cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
+        Scratch& scratch = scratch_for(state, stream, fusion_layer_scratch_bytes(ly, tokens, prompt_tokens, state.sm_count));
+        launch_fusion_layer(ly, x, pos, tokens, prompt, prompt_bias, prompt_tokens, scratch.ptr, state, stream);
+    });
+}
+
 samq_status samq_dense_create_v1(int device, int type, int kind, int kw, int kh, int64_t cin, int64_t cout,
                                  const void* data, size_t bytes, void* stream_ptr, samq_dense** out) {
     return guarded([&] {

@@ -267,6 +267,19 @@ void linear_from_staged(const samq_weights* w, const __half* a, int64_t lda, int
                         int epilogue, float* y, int64_t ldy, float* partials, DeviceState& state,
                         cudaStream_t stream);
 
+// fusion.cu: fusion-encoder layer and the linear helper of the F32 modules.
+void launch_add2(const float* a, const float* b, float* out, int64_t rows, int width, cudaStream_t stream);
+void launch_relu(float* x, int64_t count, cudaStream_t stream);
+int64_t linear_in(const samq_linear_ref_v1& l);
+int64_t linear_out(const samq_linear_ref_v1& l);
+size_t linear_scratch_bytes(const samq_linear_ref_v1& l, int64_t m, int sms);
+void apply_linear(const samq_linear_ref_v1& l, int64_t row0, int64_t rows, const float* x, int64_t ldx, int64_t m,
+                  int epilogue, float* y, int64_t ldy, void* scratch, DeviceState& state, cudaStream_t stream);
+size_t fusion_layer_scratch_bytes(const samq_fusion_layer_v1& ly, int64_t tokens, int64_t prompt_tokens, int sms);
+void launch_fusion_layer(const samq_fusion_layer_v1& ly, float* x, const float* pos, int64_t tokens,
+                         const float* prompt, const float* prompt_bias, int64_t prompt_tokens, void* scratch,
+                         DeviceState& state, cudaStream_t stream);
+
 // dense.cu: F32-semantics linears / convolutions (three-term TF32 split).
 void launch_dense_prep(const void* src, int type, int kind, int ks, int64_t cin, int64_t cout, int64_t n, int64_t k,
                        float* hi, float* lo, DeviceState& state, cudaStream_t stream);

@@ -65,6 +65,18 @@ class TextBlockDesc(ctypes.Structure):
                 ("fc1", _vp), ("fc1_b", _vp), ("fc2", _vp), ("fc2_b", _vp)]
 
 
+class LinearRef(ctypes.Structure):
+    """struct samq_linear_ref_v1."""
+    _fields_ = [("quantized", _vp), ("dense", _vp), ("bias", _vp)]
+
+
+class FusionLayerDesc(ctypes.Structure):
+    """struct samq_fusion_layer_v1."""
+    _fields_ = [("version", ctypes.c_uint32), ("heads", ctypes.c_int32)] + \
+        [(n, _vp) for n in ("norm1_w", "norm1_b", "norm2_w", "norm2_b", "norm3_w", "norm3_b")] + \
+        [(n, LinearRef) for n in ("sa_in_proj", "sa_out_proj", "ca_in_proj", "ca_out_proj", "linear1", "linear2")]
+
+
 class NeckDesc(ctypes.Structure):
     """struct samq_neck_v1: (weights, bias) pairs in the order of NECK_LAYERS."""
     _fields_ = [("version", ctypes.c_uint32)] + [
@@ -106,6 +118,7 @@ SIGNATURES = {
     "samq_layer_norm_v1": (_i32, [_vp, _i64, _i32, _i64, _vp, _vp, ctypes.c_float, _vp, _i64, _vp]),
     "samq_attention_v1": (_i32, [_vp, _i64, _vp, _i64, _vp, _i64, _i32, _i32, _i32, _i32, ctypes.c_float, _i32, _vp,
                                  _i64, _i64, _vp, _i64, _vp]),
+    "samq_fusion_layer_forward_v1": (_i32, [ctypes.POINTER(FusionLayerDesc), _vp, _vp, _i32, _vp, _vp, _i32, _vp]),
     "samq_dense_create_v1": (_i32, [_i32, _i32, _i32, _i32, _i32, _i64, _i64, _vp, _sz, _vp, ctypes.POINTER(_vp)]),
     "samq_dense_destroy_v1": (_i32, [_vp]),
     "samq_dense_linear_v1": (_i32, [_vp, _vp, _i64, _i64, _vp, _i32, _vp, _i64, _vp]),
@@ -356,6 +369,34 @@ def attention(q, ldq: int, k, ldk: int, v, ldv: int, lq: int, lk: int, heads: in
     _check(library().samq_attention_v1(_addr(q), ldq, _addr(k), ldk, _addr(v), ldv, lq, lk, heads, head_dim, scale,
                                        1 if causal else 0, _addr(bias), bias_h, bias_q, _addr(out), ldo,
                                        _stream(stream)))
+
+
+def linear_ref(weights, bias) -> LinearRef:
+    """A samq_linear_ref_v1 for a Weights (quantized) or Dense handle."""
+    if isinstance(weights, Weights):
+        return LinearRef(weights.handle, None, _addr(bias))
+    return LinearRef(None, weights.handle, _addr(bias))
+
+
+class FusionLayer:
+    """One fusion-encoder layer (samq_fusion_layer_v1); `linears` maps
+    sa_in_proj, sa_out_proj, ca_in_proj, ca_out_proj, linear1, linear2 to
+    (Weights or Dense, bias device tensor); norms to device tensors."""
+
+    def __init__(self, heads: int, norms: dict, linears: dict):
+        self._keep = (norms, linears)
+        fields = [1, heads] + [_addr(norms[n]) for n in ("norm1_w", "norm1_b", "norm2_w", "norm2_b", "norm3_w",
+                                                         "norm3_b")]
+        fields += [linear_ref(*linears[n]) for n in ("sa_in_proj", "sa_out_proj", "ca_in_proj", "ca_out_proj",
+                                                     "linear1", "linear2")]
+        self.desc = FusionLayerDesc(*fields)
+
+
+def fusion_layer_forward(layer: FusionLayer, x, pos, tokens: int, prompt, prompt_bias, prompt_tokens: int,
+                         stream=None):
+    """samq_fusion_layer_forward_v1 in place on x [tokens][D]."""
+    _check(library().samq_fusion_layer_forward_v1(ctypes.byref(layer.desc), _addr(x), _addr(pos), tokens,
+                                                  _addr(prompt), _addr(prompt_bias), prompt_tokens, _stream(stream)))
 
 
 class Dense:
