@@ -343,6 +343,51 @@ samq_status samq_fusion_layer_forward_v1(const samq_fusion_layer_v1* layer, floa
                                          const float* prompt, const float* prompt_bias, int prompt_tokens,
                                          void* stream);
 
+/* ---- DETR decoder, scoring and presence head ----------------------------------
+ * src/models/sam3/detector.hpp:67-713, tensor names ddec.*, scoring.*
+ * (src/models/sam3/tensors.hpp:245-351).  One layer's weights (post-norm
+ * sublayers in this order): self-attention -> norm2, text cross-attention ->
+ * norm_ca_text, image cross-attention with the box relative-position bias ->
+ * norm1, ReLU FFN -> norm3.  in_proj weights are [3D][D] (Q | K | V rows). */
+typedef struct samq_decoder_layer_v1 {
+    samq_linear_ref_v1 sa_in_proj, sa_out_proj, ca_text_in_proj, ca_text_out_proj, ca_in_proj, ca_out_proj,
+        linear1, linear2;
+    const float *norm1_w, *norm1_b, *norm2_w, *norm2_b, *norm_ca_text_w, *norm_ca_text_b, *norm3_w, *norm3_b;
+} samq_decoder_layer_v1;
+
+typedef struct samq_decoder_v1 {
+    uint32_t version;  /* 1 */
+    int32_t heads;     /* 8 */
+    int32_t layers;    /* 6 */
+    int32_t queries;   /* 200 */
+    const samq_decoder_layer_v1* layer;  /* [layers], host memory */
+    const float* query_embed;       /* ddec.query_embed.weight [queries][D] */
+    const float* presence_token;    /* ddec.presence_token.weight [D] */
+    const float* reference_points;  /* ddec.reference_points.weight [queries][4], f32 */
+    samq_linear_ref_v1 ref_point_head[2];  /* 512 -> D (ReLU) -> D */
+    samq_linear_ref_v1 bbox_embed[3];      /* D -> D (ReLU) -> D (ReLU) -> 4 */
+    const float *rpb_x0_w, *rpb_x0_b, *rpb_y0_w, *rpb_y0_b;  /* boxRPB layers.0: [256][2], [256] f32 */
+    samq_linear_ref_v1 rpb_x1, rpb_y1;     /* boxRPB layers.1: 256 -> heads */
+    const float *norm_w, *norm_b;          /* ddec.norm */
+    const float *presence_norm_w, *presence_norm_b;  /* ddec.presence_token_out_norm */
+    samq_linear_ref_v1 presence_head[3];   /* D -> D (ReLU) -> D (ReLU) -> 1 */
+    samq_linear_ref_v1 prompt_mlp[2];      /* scoring.prompt_mlp: D -> FFN (ReLU) -> D */
+    const float *prompt_mlp_norm_w, *prompt_mlp_norm_b;
+    samq_linear_ref_v1 prompt_proj, hs_proj;  /* D -> D */
+} samq_decoder_v1;
+
+/* enc, enc_pos: device f32 [grid * grid][D] (the fusion output and the image
+ * positional encoding); prompt [prompt_tokens][D], prompt_bias [prompt_tokens]
+ * (additive key bias), prompt_valid [prompt_tokens] (the scoring pool weights,
+ * T / n_valid at valid tokens and 0 at padding, execution.hpp:160-175).
+ * Outputs (device): queries_out [queries + 1][D] (the presence query, then the
+ * normalized object queries: the mask head's input), boxes [queries][4]
+ * (cx, cy, w, h in [0, 1]), scores [queries], presence [1] (raw logit). */
+samq_status samq_decoder_forward_v1(const samq_decoder_v1* decoder, const float* enc, const float* enc_pos, int grid,
+                                    const float* prompt, const float* prompt_bias, const float* prompt_valid,
+                                    int prompt_tokens, float* queries_out, float* boxes, float* scores,
+                                    float* presence, void* stream);
+
 /* ---- Dense (F32 / F16) modules with F32 semantics -------------------------
  * The tensors the reference keeps unquantized (neck convolutions, fusion /
  * decoder / mask-head linears in the F32 profiles: "only ViT linear weights

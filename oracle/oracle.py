@@ -621,3 +621,134 @@ def fusion_layer(x: np.ndarray, pos: np.ndarray, prompt: np.ndarray, prompt_bias
     h = layer_norm(x, ly["norm3_w"], ly["norm3_b"])
     f = np.maximum(module_linear(ly["linear1"], h), 0.0).astype(np.float32)
     return x + module_linear(ly["linear2"], f)
+
+
+# ---- DETR decoder + scoring (src/models/sam3/detector.hpp) -------------------
+
+def sine_dim_t() -> np.ndarray:
+    """The 64 angle multipliers execution.hpp:223-226 uploads: 2 pi / 10000^(2i/128), f32."""
+    i = np.arange(64, dtype=np.float32)
+    return (np.float32(2.0) * np.float32(np.pi) / np.power(np.float32(10000.0), np.float32(2.0) * i / np.float32(128.0))
+            ).astype(np.float32)
+
+
+def sine_pos_embed_4d(ref: np.ndarray) -> np.ndarray:
+    """sam3_build_sine_pos_embed_4d (detector.hpp:67-104): ref [NQ][4]
+    (cx, cy, w, h); coordinates in the order cy, cx, w, h, each as 64
+    (sin, cos) pairs of ref * dim_t -> [NQ][512] (f64)."""
+    ref = np.asarray(ref, np.float32)
+    parts = []
+    for ci in (1, 0, 2, 3):
+        a = (ref[:, ci:ci + 1] * sine_dim_t()[None, :]).astype(np.float64)  # the f32 product GGML forms
+        pair = np.stack([np.sin(a), np.cos(a)], axis=-1).reshape(ref.shape[0], 128)
+        parts.append(pair)
+    return np.concatenate(parts, axis=1)
+
+
+def box_rpb(ref: np.ndarray, grid: int, x0_w, x0_b, x1: dict, y0_w, y0_b, y1: dict, heads: int) -> np.ndarray:
+    """sam3_compute_box_rpb (detector.hpp:160-305): the additive image
+    cross-attention bias [heads][NQ + 1][grid * grid] (row 0, the presence
+    token, zero).  Deltas coord - edge with coord = i / grid, log transform
+    sign(8d) log2(|8d| + 1) / 3, per axis MLP Linear(2 -> 256) + ReLU, Linear(256 -> heads),
+    outer sum over (h, w) with key index h * grid + w."""
+    ref = np.asarray(ref, np.float64)
+    nq = ref.shape[0]
+    coords = (np.arange(grid, dtype=np.float32) / np.float32(grid)).astype(np.float64)
+    cx, cy, w, h = ref[:, 0], ref[:, 1], ref[:, 2], ref[:, 3]
+
+    def logt(d):
+        d8 = 8.0 * d
+        return np.sign(d8) * np.log2(np.abs(d8) + 1.0) / 3.0
+
+    def mlp(lo, hi, w0, b0, l1):
+        d = np.stack([logt(coords[None, :] - lo[:, None]), logt(coords[None, :] - hi[:, None])], axis=-1)  # [NQ][G][2]
+        hdn = np.maximum(d @ np.asarray(w0, np.float64).T + np.asarray(b0, np.float64), 0.0)
+        flat = hdn.reshape(nq * grid, -1).astype(np.float32)
+        return module_linear(l1, flat).astype(np.float64).reshape(nq, grid, heads)
+
+    rx = mlp(cx - 0.5 * w, cx + 0.5 * w, x0_w, x0_b, x1)
+    ry = mlp(cy - 0.5 * h, cy + 0.5 * h, y0_w, y0_b, y1)
+    bias = np.zeros((heads, nq + 1, grid * grid), np.float64)
+    # key h * grid + w: ry[q][h] + rx[q][w]
+    bias[:, 1:, :] = (ry.transpose(2, 0, 1)[:, :, :, None] + rx.transpose(2, 0, 1)[:, :, None, :]).reshape(
+        heads, nq, grid * grid)
+    return bias.astype(np.float32)
+
+
+def inverse_sigmoid(x):
+    x = np.clip(x, 0.0, 1.0)
+    return np.log(np.clip(x, 1e-3, 1.0)) - np.log(np.clip(1.0 - x, 1e-3, 1.0))
+
+
+def sigmoid(x):
+    return 1.0 / (1.0 + np.exp(-np.asarray(x, np.float64)))
+
+
+def mlp_chain(lins: list, x, relu_last=False):
+    for j, lin in enumerate(lins):
+        x = module_linear(lin, np.asarray(x, np.float32))
+        if j < len(lins) - 1 or relu_last:
+            x = np.maximum(x, 0.0)
+    return np.asarray(x, np.float32)
+
+
+def decoder_layer(q, qpos, enc, enc_pos, text, text_bias, rpb, ly: dict, heads: int):
+    """sam3_ddec_layer_forward (detector.hpp:307-478): post-norm self-attention
+    (norm2), text cross-attention (norm_ca_text), image cross-attention with
+    the box bias (norm1), ReLU FFN (norm3)."""
+    D = q.shape[1]
+    hd = D // heads
+    scale = 1.0 / np.sqrt(hd)
+    qin = (q + qpos).astype(np.float32)
+    qk = module_linear(ly["sa_in_proj"], qin, slice(0, 2 * D))
+    v = module_linear(ly["sa_in_proj"], q, slice(2 * D, 3 * D))
+    att = attention_gen(qk[:, :D], qk[:, D:], v, heads, hd, scale)
+    q = layer_norm(q + module_linear(ly["sa_out_proj"], att), ly["norm2_w"], ly["norm2_b"])
+    qin = (q + qpos).astype(np.float32)
+    qq = module_linear(ly["ca_text_in_proj"], qin, slice(0, D))
+    kv = module_linear(ly["ca_text_in_proj"], text, slice(D, 3 * D))
+    tb = None if text_bias is None else np.asarray(text_bias, np.float32)[None, None, :]
+    att = attention_gen(qq, kv[:, :D], kv[:, D:], heads, hd, scale, bias=tb)
+    q = layer_norm(q + module_linear(ly["ca_text_out_proj"], att), ly["norm_ca_text_w"], ly["norm_ca_text_b"])
+    qin = (q + qpos).astype(np.float32)
+    kin = (np.asarray(enc, np.float32) + np.asarray(enc_pos, np.float32)).astype(np.float32)
+    qq = module_linear(ly["ca_in_proj"], qin, slice(0, D))
+    kk = module_linear(ly["ca_in_proj"], kin, slice(D, 2 * D))
+    vv = module_linear(ly["ca_in_proj"], enc, slice(2 * D, 3 * D))
+    att = attention_gen(qq, kk, vv, heads, hd, scale, bias=rpb)
+    q = layer_norm(q + module_linear(ly["ca_out_proj"], att), ly["norm1_w"], ly["norm1_b"])
+    f = np.maximum(module_linear(ly["linear1"], q), 0.0).astype(np.float32)
+    return layer_norm(q + module_linear(ly["linear2"], f), ly["norm3_w"], ly["norm3_b"])
+
+
+def decoder(enc, enc_pos, text, text_bias, text_valid, dec: dict, grid: int, heads: int):
+    """sam3_build_ddec_graph + sam3_dot_product_scoring (detector.hpp:507-713):
+    returns (queries_for_seg [NQ + 1][D], boxes [NQ][4], scores [NQ], presence logit)."""
+    qe = np.asarray(dec["query_embed"], np.float32)
+    nq, D = qe.shape
+    q = np.concatenate([np.asarray(dec["presence_token"], np.float32).reshape(1, D), qe], axis=0)
+    ref = sigmoid(np.asarray(dec["reference_points"], np.float32)).astype(np.float32)
+    last_presence = q[:1]
+    for ly in dec["layers"]:
+        sine = sine_pos_embed_4d(ref).astype(np.float32)
+        qpos = np.zeros((nq + 1, D), np.float32)
+        qpos[1:] = mlp_chain(dec["ref_point_head"], sine)
+        rpb = box_rpb(ref, grid, dec["rpb_x0_w"], dec["rpb_x0_b"], dec["rpb_x1"], dec["rpb_y0_w"], dec["rpb_y0_b"],
+                      dec["rpb_y1"], heads)
+        q = decoder_layer(q, qpos, enc, enc_pos, text, text_bias, rpb, ly, heads)
+        last_presence = q[:1]
+        normed = layer_norm(q[1:], dec["norm_w"], dec["norm_b"])
+        bd = mlp_chain(dec["bbox_embed"], normed).astype(np.float64)
+        ref = sigmoid(inverse_sigmoid(ref.astype(np.float64)) + bd).astype(np.float32)
+    obj = layer_norm(q[1:], dec["norm_w"], dec["norm_b"])
+    text = np.asarray(text, np.float32)
+    tm = mlp_chain(dec["prompt_mlp"], text)
+    tm = layer_norm(tm + text, dec["prompt_mlp_norm_w"], dec["prompt_mlp_norm_b"])
+    valid = np.asarray(text_valid, np.float64)
+    pooled = ((tm.astype(np.float64) * valid[:, None]).sum(axis=0) / tm.shape[0]).astype(np.float32)[None, :]
+    pp = module_linear(dec["prompt_proj"], pooled).astype(np.float64)
+    hs = module_linear(dec["hs_proj"], obj).astype(np.float64)
+    scores = np.clip((hs @ pp[0]) / np.sqrt(D), -12.0, 12.0).astype(np.float32)
+    pres = layer_norm(last_presence, dec["presence_norm_w"], dec["presence_norm_b"])
+    presence = float(mlp_chain(dec["presence_head"], pres)[0, 0])
+    return np.concatenate([last_presence, obj], axis=0), ref, scores, presence

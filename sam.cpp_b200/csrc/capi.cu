@@ -763,6 +763,71 @@ samq_status samq_fusion_layer_forward_v1(const samq_fusion_layer_v1* layer, floa
     });
 }
 
+samq_status samq_decoder_forward_v1(const samq_decoder_v1* decoder, const float* enc, const float* enc_pos, int grid,
+                                    const float* prompt, const float* prompt_bias, const float* prompt_valid,
+                                    int prompt_tokens, float* queries_out, float* boxes, float* scores,
+                                    float* presence, void* stream_ptr) {
+    return guarded([&] {
+        require(decoder != nullptr && decoder->version == 1, "decoder descriptor missing or not version 1");
+        const samq_decoder_v1& d = *decoder;
+        require(d.layers > 0 && d.layers <= 64 && d.layer != nullptr && d.queries > 0 && d.queries <= 4096,
+                "decoder layer / query counts out of range");
+        require(d.layer[0].sa_in_proj.quantized || d.layer[0].sa_in_proj.dense, "sa_in_proj missing");
+        const int64_t D = linear_in(d.layer[0].sa_in_proj);
+        require(D % 128 == 0 && d.heads > 0 && d.heads <= 16 && D % d.heads == 0 &&
+                    (D / d.heads == 32 || D / d.heads == 64),
+                "width must be a multiple of 128 with at most 16 heads of 32 or 64 channels");
+        const int device = current_device();
+        require(d.layer[0].linear1.quantized || d.layer[0].linear1.dense, "linear1 missing");
+        const int64_t F = linear_out(d.layer[0].linear1);
+        for (int i = 0; i < d.layers; ++i) {
+            const samq_decoder_layer_v1& ly = d.layer[i];
+            check_linear_ref(ly.sa_in_proj, D, 3 * D, device, "sa_in_proj");
+            check_linear_ref(ly.sa_out_proj, D, D, device, "sa_out_proj");
+            check_linear_ref(ly.ca_text_in_proj, D, 3 * D, device, "ca_text_in_proj");
+            check_linear_ref(ly.ca_text_out_proj, D, D, device, "ca_text_out_proj");
+            check_linear_ref(ly.ca_in_proj, D, 3 * D, device, "ca_in_proj");
+            check_linear_ref(ly.ca_out_proj, D, D, device, "ca_out_proj");
+            check_linear_ref(ly.linear1, D, F, device, "linear1");
+            check_linear_ref(ly.linear2, F, D, device, "linear2");
+            const float* norms[] = {ly.norm1_w, ly.norm1_b, ly.norm2_w, ly.norm2_b, ly.norm_ca_text_w,
+                                    ly.norm_ca_text_b, ly.norm3_w, ly.norm3_b};
+            for (const float* p : norms) require(p != nullptr, "decoder norm missing");
+        }
+        check_linear_ref(d.ref_point_head[0], 512, D, device, "ref_point_head.0");
+        check_linear_ref(d.ref_point_head[1], D, D, device, "ref_point_head.1");
+        check_linear_ref(d.bbox_embed[0], D, D, device, "bbox_embed.0");
+        check_linear_ref(d.bbox_embed[1], D, D, device, "bbox_embed.1");
+        check_linear_ref(d.bbox_embed[2], D, 4, device, "bbox_embed.2");
+        check_linear_ref(d.rpb_x1, 256, d.heads, device, "boxRPB_embed_x.1");
+        check_linear_ref(d.rpb_y1, 256, d.heads, device, "boxRPB_embed_y.1");
+        check_linear_ref(d.presence_head[0], D, D, device, "presence_token_head.0");
+        check_linear_ref(d.presence_head[1], D, D, device, "presence_token_head.1");
+        check_linear_ref(d.presence_head[2], D, 1, device, "presence_token_head.2");
+        require(d.prompt_mlp[0].quantized || d.prompt_mlp[0].dense, "prompt_mlp missing");
+        const int64_t Fp = linear_out(d.prompt_mlp[0]);
+        check_linear_ref(d.prompt_mlp[0], D, Fp, device, "prompt_mlp.0");
+        check_linear_ref(d.prompt_mlp[1], Fp, D, device, "prompt_mlp.1");
+        check_linear_ref(d.prompt_proj, D, D, device, "prompt_proj");
+        check_linear_ref(d.hs_proj, D, D, device, "hs_proj");
+        require(grid > 0 && grid <= 256 && prompt_tokens > 0 && prompt_tokens <= 4096, "grid / prompt out of range");
+        const float* params[] = {d.query_embed, d.presence_token, d.reference_points, d.rpb_x0_w, d.rpb_x0_b,
+                                 d.rpb_y0_w, d.rpb_y0_b, d.norm_w, d.norm_b, d.presence_norm_w, d.presence_norm_b,
+                                 d.prompt_mlp_norm_w, d.prompt_mlp_norm_b, enc, enc_pos, prompt, queries_out, boxes,
+                                 scores, presence};
+        for (const float* p : params) require(p != nullptr, "decoder parameter or buffer missing");
+        require(aligned16(enc) && aligned16(enc_pos) && aligned16(prompt) && aligned16(queries_out),
+                "activations must be 16-byte aligned");
+        DeviceState& state = device_state(device);
+        cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
+        const int64_t tokens = int64_t(grid) * grid;
+        Scratch& scratch =
+            scratch_for(state, stream, decoder_scratch_bytes(d, tokens, prompt_tokens, grid, state.sm_count));
+        launch_decoder(d, enc, enc_pos, tokens, grid, prompt, prompt_bias, prompt_valid, prompt_tokens, queries_out,
+                       boxes, scores, presence, scratch.ptr, state, stream);
+    });
+}
+
 samq_status samq_dense_create_v1(int device, int type, int kind, int kw, int kh, int64_t cin, int64_t cout,
                                  const void* data, size_t bytes, void* stream_ptr, samq_dense** out) {
     return guarded([&] {

@@ -280,6 +280,13 @@ void launch_fusion_layer(const samq_fusion_layer_v1& ly, float* x, const float* 
                          const float* prompt, const float* prompt_bias, int64_t prompt_tokens, void* scratch,
                          DeviceState& state, cudaStream_t stream);
 
+// decoder.cu: the DETR decoder, scoring and presence head.
+size_t decoder_scratch_bytes(const samq_decoder_v1& dec, int64_t enc_tokens, int64_t prompt_tokens, int grid, int sms);
+void launch_decoder(const samq_decoder_v1& dec, const float* enc, const float* enc_pos, int64_t enc_tokens, int grid,
+                    const float* prompt, const float* prompt_bias, const float* prompt_valid, int64_t prompt_tokens,
+                    float* queries_out, float* boxes, float* scores, float* presence, void* scratch,
+                    DeviceState& state, cudaStream_t stream);
+
 // dense.cu: F32-semantics linears / convolutions (three-term TF32 split).
 void launch_dense_prep(const void* src, int type, int kind, int ks, int64_t cin, int64_t cout, int64_t n, int64_t k,
                        float* hi, float* lo, DeviceState& state, cudaStream_t stream);

@@ -77,6 +77,30 @@ class FusionLayerDesc(ctypes.Structure):
         [(n, LinearRef) for n in ("sa_in_proj", "sa_out_proj", "ca_in_proj", "ca_out_proj", "linear1", "linear2")]
 
 
+DECODER_LAYER_LINEARS = ("sa_in_proj", "sa_out_proj", "ca_text_in_proj", "ca_text_out_proj", "ca_in_proj",
+                         "ca_out_proj", "linear1", "linear2")
+DECODER_LAYER_NORMS = ("norm1_w", "norm1_b", "norm2_w", "norm2_b", "norm_ca_text_w", "norm_ca_text_b", "norm3_w",
+                       "norm3_b")
+
+
+class DecoderLayerDesc(ctypes.Structure):
+    """struct samq_decoder_layer_v1."""
+    _fields_ = [(n, LinearRef) for n in DECODER_LAYER_LINEARS] + [(n, _vp) for n in DECODER_LAYER_NORMS]
+
+
+class DecoderDesc(ctypes.Structure):
+    """struct samq_decoder_v1."""
+    _fields_ = [("version", ctypes.c_uint32), ("heads", ctypes.c_int32), ("layers", ctypes.c_int32),
+                ("queries", ctypes.c_int32), ("layer", ctypes.POINTER(DecoderLayerDesc)),
+                ("query_embed", _vp), ("presence_token", _vp), ("reference_points", _vp),
+                ("ref_point_head", LinearRef * 2), ("bbox_embed", LinearRef * 3),
+                ("rpb_x0_w", _vp), ("rpb_x0_b", _vp), ("rpb_y0_w", _vp), ("rpb_y0_b", _vp),
+                ("rpb_x1", LinearRef), ("rpb_y1", LinearRef), ("norm_w", _vp), ("norm_b", _vp),
+                ("presence_norm_w", _vp), ("presence_norm_b", _vp), ("presence_head", LinearRef * 3),
+                ("prompt_mlp", LinearRef * 2), ("prompt_mlp_norm_w", _vp), ("prompt_mlp_norm_b", _vp),
+                ("prompt_proj", LinearRef), ("hs_proj", LinearRef)]
+
+
 class NeckDesc(ctypes.Structure):
     """struct samq_neck_v1: (weights, bias) pairs in the order of NECK_LAYERS."""
     _fields_ = [("version", ctypes.c_uint32)] + [
@@ -119,6 +143,8 @@ SIGNATURES = {
     "samq_attention_v1": (_i32, [_vp, _i64, _vp, _i64, _vp, _i64, _i32, _i32, _i32, _i32, ctypes.c_float, _i32, _vp,
                                  _i64, _i64, _vp, _i64, _vp]),
     "samq_fusion_layer_forward_v1": (_i32, [ctypes.POINTER(FusionLayerDesc), _vp, _vp, _i32, _vp, _vp, _i32, _vp]),
+    "samq_decoder_forward_v1": (_i32, [ctypes.POINTER(DecoderDesc), _vp, _vp, _i32, _vp, _vp, _vp, _i32, _vp, _vp,
+                                       _vp, _vp, _vp]),
     "samq_dense_create_v1": (_i32, [_i32, _i32, _i32, _i32, _i32, _i64, _i64, _vp, _sz, _vp, ctypes.POINTER(_vp)]),
     "samq_dense_destroy_v1": (_i32, [_vp]),
     "samq_dense_linear_v1": (_i32, [_vp, _vp, _i64, _i64, _vp, _i32, _vp, _i64, _vp]),
@@ -397,6 +423,46 @@ def fusion_layer_forward(layer: FusionLayer, x, pos, tokens: int, prompt, prompt
     """samq_fusion_layer_forward_v1 in place on x [tokens][D]."""
     _check(library().samq_fusion_layer_forward_v1(ctypes.byref(layer.desc), _addr(x), _addr(pos), tokens,
                                                   _addr(prompt), _addr(prompt_bias), prompt_tokens, _stream(stream)))
+
+
+class Decoder:
+    """The DETR decoder with scoring and presence head (samq_decoder_v1).
+    `layers`: per layer a dict of DECODER_LAYER_LINEARS -> (Weights or Dense,
+    bias) and DECODER_LAYER_NORMS -> device tensors.  `params`: device tensors
+    query_embed, presence_token, reference_points, rpb_x0_w / b, rpb_y0_w / b,
+    norm_w / b, presence_norm_w / b, prompt_mlp_norm_w / b; `heads_linears`:
+    ref_point_head, bbox_embed, presence_head, prompt_mlp (lists of (handle,
+    bias)), rpb_x1, rpb_y1, prompt_proj, hs_proj ((handle, bias))."""
+
+    def __init__(self, heads: int, queries: int, layers: list, params: dict, heads_linears: dict):
+        self._keep = (layers, params, heads_linears)
+        arr = (DecoderLayerDesc * len(layers))()
+        for i, ly in enumerate(layers):
+            arr[i] = DecoderLayerDesc(*([linear_ref(*ly[n]) for n in DECODER_LAYER_LINEARS] +
+                                        [_addr(ly[n]) for n in DECODER_LAYER_NORMS]))
+        self._layers = arr
+        d = DecoderDesc()
+        d.version, d.heads, d.layers, d.queries = 1, heads, len(layers), queries
+        d.layer = ctypes.cast(arr, ctypes.POINTER(DecoderLayerDesc))
+        for n in ("query_embed", "presence_token", "reference_points", "rpb_x0_w", "rpb_x0_b", "rpb_y0_w", "rpb_y0_b",
+                  "norm_w", "norm_b", "presence_norm_w", "presence_norm_b", "prompt_mlp_norm_w", "prompt_mlp_norm_b"):
+            setattr(d, n, _addr(params[n]))
+        for n in ("ref_point_head", "bbox_embed", "presence_head", "prompt_mlp"):
+            field = getattr(d, n)
+            for j, pair in enumerate(heads_linears[n]):
+                field[j] = linear_ref(*pair)
+        for n in ("rpb_x1", "rpb_y1", "prompt_proj", "hs_proj"):
+            setattr(d, n, linear_ref(*heads_linears[n]))
+        self.desc = d
+
+
+def decoder_forward(decoder: Decoder, enc, enc_pos, grid: int, prompt, prompt_bias, prompt_valid, prompt_tokens: int,
+                    queries_out, boxes, scores, presence, stream=None):
+    """samq_decoder_forward_v1."""
+    _check(library().samq_decoder_forward_v1(ctypes.byref(decoder.desc), _addr(enc), _addr(enc_pos), grid,
+                                             _addr(prompt), _addr(prompt_bias), _addr(prompt_valid), prompt_tokens,
+                                             _addr(queries_out), _addr(boxes), _addr(scores), _addr(presence),
+                                             _stream(stream)))
 
 
 class Dense:
