@@ -388,6 +388,64 @@ samq_status samq_decoder_forward_v1(const samq_decoder_v1* decoder, const float*
                                     int prompt_tokens, float* queries_out, float* boxes, float* scores,
                                     float* presence, void* stream);
 
+/* ---- Geometry encoder (text-only prompt form) ---------------------------------
+ * src/models/sam3/prompt_encoder.hpp:44-160, tensor names geom.*
+ * (src/models/sam3/tensors.hpp:357-410): the learned CLS token through
+ * final_proj and norm, `layers` pre-norm layers (self-attention over the
+ * token, cross-attention to the image with keys image + pos, ReLU FFN),
+ * encode_norm.  The result is the geometry prompt token appended after the
+ * text tokens (src/models/sam3/execution.hpp:157-175). */
+typedef struct samq_geometry_layer_v1 {
+    samq_linear_ref_v1 sa_in_proj, sa_out_proj, ca_in_proj, ca_out_proj, linear1, linear2;
+    const float *norm1_w, *norm1_b, *norm2_w, *norm2_b, *norm3_w, *norm3_b;
+} samq_geometry_layer_v1;
+
+typedef struct samq_geometry_encoder_v1 {
+    uint32_t version;  /* 1 */
+    int32_t heads;     /* 8 */
+    int32_t layers;    /* 3 */
+    const samq_geometry_layer_v1* layer;  /* [layers], host memory */
+    const float* cls_token;               /* geom.cls_embed.weight [D], device */
+    samq_linear_ref_v1 final_proj;        /* D -> D */
+    const float *norm_w, *norm_b, *encode_norm_w, *encode_norm_b;
+} samq_geometry_encoder_v1;
+
+/* image, pos: device f32 [tokens][D] (the 1x neck map and the image positional
+ * encoding); out: device f32 [D]. */
+samq_status samq_geometry_encoder_forward_v1(const samq_geometry_encoder_v1* encoder, const float* image,
+                                             const float* pos, int tokens, float* out, void* stream);
+
+/* ---- Segmentation head ----------------------------------------------------------
+ * src/models/sam3/mask_decoder.hpp:57-202, tensor names seg.*
+ * (src/models/sam3/tensors.hpp:405-442).  Convolutions are samq_dense handles
+ * (CONV, 3x3 for conv[i], 1x1 for instance); products have F32 semantics. */
+typedef struct samq_seg_head_v1 {
+    uint32_t version;  /* 1 */
+    int32_t heads;     /* 8 */
+    const float *cross_attn_norm_w, *cross_attn_norm_b;
+    samq_linear_ref_v1 ca_in_proj, ca_out_proj;  /* seg.cross_attend_prompt */
+    const struct samq_dense* conv[2];            /* seg.pixel_decoder.conv_layers.{0,1} */
+    const float* conv_b[2];
+    const float* norm_w[2];                      /* seg.pixel_decoder.norms.{0,1} (GroupNorm 8) */
+    const float* norm_b[2];
+    const struct samq_dense* instance;           /* seg.instance_seg_head (1x1) */
+    const float* instance_b;
+    samq_linear_ref_v1 mask_embed[3];            /* seg.mask_predictor.mask_embed.layers.{0,1,2} */
+} samq_seg_head_v1;
+
+/* enc: the fusion output [grid^2][D]; fpn1 [(2 grid)^2][D], fpn0
+ * [(4 grid)^2][D] (the neck's 2x and 4x maps, NHWC); queries [nq][D] (the
+ * decoder's object queries); prompt [prompt_tokens][D] with key bias
+ * prompt_bias; mask_logits [nq][(4 grid)^2] raw logits.  All device. */
+samq_status samq_seg_head_forward_v1(const samq_seg_head_v1* head, const float* enc, int grid, const float* fpn0,
+                                     const float* fpn1, const float* queries, int nq, const float* prompt,
+                                     const float* prompt_bias, int prompt_tokens, float* mask_logits, void* stream);
+
+/* The image positional encoding sam3_sinusoidal_pe_2d
+ * (src/models/sam3/vision.hpp:39-75), computed on the host in f32 as the
+ * reference does: out [h * w][d] host floats. */
+samq_status samq_sine_pe_2d_v1(int h, int w, int d, float* out);
+
 /* ---- Dense (F32 / F16) modules with F32 semantics -------------------------
  * The tensors the reference keeps unquantized (neck convolutions, fusion /
  * decoder / mask-head linears in the F32 profiles: "only ViT linear weights

@@ -752,3 +752,103 @@ def decoder(enc, enc_pos, text, text_bias, text_valid, dec: dict, grid: int, hea
     pres = layer_norm(last_presence, dec["presence_norm_w"], dec["presence_norm_b"])
     presence = float(mlp_chain(dec["presence_head"], pres)[0, 0])
     return np.concatenate([last_presence, obj], axis=0), ref, scores, presence
+
+
+# ---- image positional encoding, geometry encoder, segmentation head -----------
+
+def sine_pe_2d(h: int, w: int, d: int) -> np.ndarray:
+    """sam3_sinusoidal_pe_2d (src/models/sam3/vision.hpp:39-75), the image
+    positional encoding, [h * w][d] f32 rows (token y * w + x): channel i < d/2
+    is the y encoding, channel d/2 + i the x encoding; pos = (p + 1) / n * 2 pi,
+    dim_t = 10000^((i & ~1) / (d/2)), sin at even i, cos at odd i.  Evaluated
+    in f64 from the f32 arguments the reference forms."""
+    half = d // 2
+    i = np.arange(half)
+    dim_t = np.power(np.float32(10000.0), (i & ~1).astype(np.float32) / np.float32(half)).astype(np.float32)
+    scale = np.float32(2.0 * np.pi)
+    py = ((np.arange(h, dtype=np.float32) + 1) / np.float32(h) * scale).astype(np.float32)
+    px = ((np.arange(w, dtype=np.float32) + 1) / np.float32(w) * scale).astype(np.float32)
+    ay = (py[:, None] / dim_t[None, :]).astype(np.float32).astype(np.float64)  # [h][half]
+    ax = (px[:, None] / dim_t[None, :]).astype(np.float32).astype(np.float64)  # [w][half]
+    even = (i % 2 == 0)[None, :]
+    vy = np.where(even, np.sin(ay), np.cos(ay))
+    vx = np.where(even, np.sin(ax), np.cos(ax))
+    out = np.empty((h, w, d), np.float64)
+    out[:, :, :half] = vy[:, None, :]
+    out[:, :, half:] = vx[None, :, :]
+    return out.reshape(h * w, d).astype(np.float32)
+
+
+def geometry_encoder(image: np.ndarray, pos: np.ndarray, ge: dict, heads: int = 8) -> np.ndarray:
+    """sam3_build_geom_enc_graph (src/models/sam3/prompt_encoder.hpp:44-160)
+    for a text-only prompt: the learned CLS token through final_proj and norm,
+    three pre-norm layers (self-attention over the single token, cross-attention
+    to the image with keys image + pos, ReLU FFN), then encode_norm.  Returns
+    the geometry prompt token [1][D] f32."""
+    cls = np.asarray(ge["cls"], np.float32).reshape(1, -1)
+    D = cls.shape[1]
+    hd = D // heads
+    scale = 1.0 / np.sqrt(hd)
+    x = layer_norm(module_linear(ge["final_proj"], cls), ge["norm_w"], ge["norm_b"])
+    kin = (np.asarray(image, np.float32) + np.asarray(pos, np.float32)).astype(np.float32)
+    for ly in ge["layers"]:
+        xn = layer_norm(x, ly["norm1_w"], ly["norm1_b"])
+        qkv = module_linear(ly["sa_in_proj"], xn)
+        att = attention_gen(qkv[:, :D], qkv[:, D:2 * D], qkv[:, 2 * D:], heads, hd, scale)
+        x = (x.astype(np.float64) + module_linear(ly["sa_out_proj"], att)).astype(np.float32)
+        xn = layer_norm(x, ly["norm2_w"], ly["norm2_b"])
+        q = module_linear(ly["ca_in_proj"], xn, slice(0, D))
+        k = module_linear(ly["ca_in_proj"], kin, slice(D, 2 * D))
+        v = module_linear(ly["ca_in_proj"], image, slice(2 * D, 3 * D))
+        att = attention_gen(q, k, v, heads, hd, scale)
+        x = (x.astype(np.float64) + module_linear(ly["ca_out_proj"], att)).astype(np.float32)
+        xn = layer_norm(x, ly["norm3_w"], ly["norm3_b"])
+        f = np.maximum(module_linear(ly["linear1"], xn), 0.0).astype(np.float32)
+        x = (x.astype(np.float64) + module_linear(ly["linear2"], f)).astype(np.float32)
+    return layer_norm(x, ge["encode_norm_w"], ge["encode_norm_b"])
+
+
+def group_norm_nhwc(x: np.ndarray, groups: int, w, b, eps: float = 1e-5) -> np.ndarray:
+    """ggml_group_norm(groups, eps) of an NHWC map followed by the per-channel
+    affine (src/models/sam3/mask_decoder.hpp:75-83): statistics over all pixels
+    and the C / groups channels of a group, f64."""
+    x = np.asarray(x, np.float64)
+    H, W, C = x.shape
+    g = x.reshape(H * W, groups, C // groups)
+    mean = g.mean(axis=(0, 2), keepdims=True)
+    var = ((g - mean) ** 2).mean(axis=(0, 2), keepdims=True)
+    y = ((g - mean) / np.sqrt(var + eps)).reshape(H, W, C)
+    return y * np.asarray(w, np.float64) + np.asarray(b, np.float64)
+
+
+def upsample2x_nhwc(x: np.ndarray) -> np.ndarray:
+    """ggml_upscale(x, 2, NEAREST): out[y][x] = in[y / 2][x / 2]."""
+    return np.repeat(np.repeat(np.asarray(x), 2, axis=0), 2, axis=1)
+
+
+def seg_head(enc: np.ndarray, fpn0: np.ndarray, fpn1: np.ndarray, queries: np.ndarray, prompt: np.ndarray,
+             prompt_bias, sh: dict, grid: int, heads: int = 8) -> np.ndarray:
+    """sam3_build_seg_head_graph + sam3_pixel_decoder
+    (src/models/sam3/mask_decoder.hpp:57-202): prompt cross-attention on the
+    fusion output (residual, no positions), pixel decoder over (fusion output,
+    fpn1, fpn0) with nearest 2x upsampling, 3x3 conv, GroupNorm(8) and ReLU,
+    the 1x1 instance head, the 3-layer mask-embedding MLP on the object queries
+    and the einsum: mask logits [Q][(4 grid)^2] (f64)."""
+    enc = np.asarray(enc, np.float32)
+    D = enc.shape[1]
+    hd = D // heads
+    ln = layer_norm(enc, sh["cross_attn_norm_w"], sh["cross_attn_norm_b"])
+    q = module_linear(sh["ca_in_proj"], ln, slice(0, D))
+    kv = module_linear(sh["ca_in_proj"], prompt, slice(D, 3 * D))
+    tb = None if prompt_bias is None else np.asarray(prompt_bias, np.float32)[None, None, :]
+    att = attention_gen(q, kv[:, :D], kv[:, D:], heads, hd, 1.0 / np.sqrt(hd), bias=tb)
+    enc = (enc.astype(np.float64) + module_linear(sh["ca_out_proj"], att)).astype(np.float32)
+    prev = enc.reshape(grid, grid, D)
+    for i, fpn in enumerate((fpn1, fpn0)):
+        size = grid * (2 << i)
+        merged = (np.asarray(fpn, np.float32).reshape(size, size, D) + upsample2x_nhwc(prev)).astype(np.float32)
+        y = conv2d_nhwc(merged, sh["conv_w"][i], sh["conv_b"][i])
+        prev = np.maximum(group_norm_nhwc(y, 8, sh["norm_w"][i], sh["norm_b"][i]), 0.0).astype(np.float32)
+    pe = conv2d_nhwc(prev, sh["instance_w"], sh["instance_b"], stride=1, pad=0).reshape(-1, D)
+    me = mlp_chain(sh["mask_embed"], queries).astype(np.float64)
+    return me @ pe.T

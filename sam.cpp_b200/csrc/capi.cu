@@ -828,6 +828,108 @@ samq_status samq_decoder_forward_v1(const samq_decoder_v1* decoder, const float*
     });
 }
 
+samq_status samq_geometry_encoder_forward_v1(const samq_geometry_encoder_v1* encoder, const float* image,
+                                             const float* pos, int tokens, float* out, void* stream_ptr) {
+    return guarded([&] {
+        require(encoder != nullptr && encoder->version == 1, "geometry encoder descriptor missing or not version 1");
+        const samq_geometry_encoder_v1& g = *encoder;
+        require(g.layers > 0 && g.layers <= 16 && g.layer != nullptr, "geometry layer count out of range");
+        require(g.final_proj.quantized || g.final_proj.dense, "final_proj missing");
+        const int64_t D = linear_in(g.final_proj);
+        require(D % 128 == 0 && D <= 4096 && g.heads > 0 && D % g.heads == 0 &&
+                    (D / g.heads == 32 || D / g.heads == 64),
+                "width must be a multiple of 128 with heads of 32 or 64 channels");
+        const int device = current_device();
+        check_linear_ref(g.final_proj, D, D, device, "final_proj");
+        require(g.layer[0].linear1.quantized || g.layer[0].linear1.dense, "linear1 missing");
+        const int64_t F = linear_out(g.layer[0].linear1);
+        for (int i = 0; i < g.layers; ++i) {
+            const samq_geometry_layer_v1& ly = g.layer[i];
+            check_linear_ref(ly.sa_in_proj, D, 3 * D, device, "sa_in_proj");
+            check_linear_ref(ly.sa_out_proj, D, D, device, "sa_out_proj");
+            check_linear_ref(ly.ca_in_proj, D, 3 * D, device, "ca_in_proj");
+            check_linear_ref(ly.ca_out_proj, D, D, device, "ca_out_proj");
+            check_linear_ref(ly.linear1, D, F, device, "linear1");
+            check_linear_ref(ly.linear2, F, D, device, "linear2");
+            const float* norms[] = {ly.norm1_w, ly.norm1_b, ly.norm2_w, ly.norm2_b, ly.norm3_w, ly.norm3_b};
+            for (const float* p : norms) require(p != nullptr, "geometry norm missing");
+        }
+        const float* params[] = {g.cls_token, g.norm_w, g.norm_b, g.encode_norm_w, g.encode_norm_b, image, pos, out};
+        for (const float* p : params) require(p != nullptr, "geometry parameter or buffer missing");
+        require(tokens > 0 && tokens <= (1 << 22), "token count out of range");
+        require(aligned16(image) && aligned16(pos) && aligned16(g.cls_token), "inputs must be 16-byte aligned");
+        DeviceState& state = device_state(device);
+        cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
+        Scratch& scratch = scratch_for(state, stream, geometry_scratch_bytes(g, tokens, state.sm_count));
+        launch_geometry_encoder(g, image, pos, tokens, out, scratch.ptr, state, stream);
+    });
+}
+
+samq_status samq_seg_head_forward_v1(const samq_seg_head_v1* head, const float* enc, int grid, const float* fpn0,
+                                     const float* fpn1, const float* queries, int nq, const float* prompt,
+                                     const float* prompt_bias, int prompt_tokens, float* mask_logits,
+                                     void* stream_ptr) {
+    return guarded([&] {
+        require(head != nullptr && head->version == 1, "segmentation head descriptor missing or not version 1");
+        const samq_seg_head_v1& h = *head;
+        require(h.ca_in_proj.quantized || h.ca_in_proj.dense, "ca_in_proj missing");
+        const int64_t D = linear_in(h.ca_in_proj);
+        require((D == 128 || D == 256 || D == 512 || D == 1024) && h.heads > 0 && D % h.heads == 0 &&
+                    (D / h.heads == 32 || D / h.heads == 64),
+                "width must be 128, 256, 512 or 1024 with heads of 32 or 64 channels");
+        const int device = current_device();
+        check_linear_ref(h.ca_in_proj, D, 3 * D, device, "cross_attend_prompt.in_proj");
+        check_linear_ref(h.ca_out_proj, D, D, device, "cross_attend_prompt.out_proj");
+        for (int j = 0; j < 3; ++j) check_linear_ref(h.mask_embed[j], D, D, device, "mask_embed");
+        for (int i = 0; i < 2; ++i) {
+            const samq_dense* c = h.conv[i];
+            require(c != nullptr && c->kind == SAMQ_DENSE_CONV && c->ks == 3 && c->cin == D && c->cout == D &&
+                        c->device == device,
+                    "pixel decoder convolutions must be 3x3 D -> D on this device");
+            require(h.norm_w[i] != nullptr && h.norm_b[i] != nullptr, "pixel decoder norm missing");
+        }
+        const samq_dense* ins = h.instance;
+        require(ins != nullptr && (ins->kind == SAMQ_DENSE_CONV || ins->kind == SAMQ_DENSE_LINEAR) && ins->ks == 1 &&
+                    ins->cin == D && ins->cout == D && ins->device == device,
+                "instance head must be a 1x1 D -> D convolution on this device");
+        require(h.cross_attn_norm_w && h.cross_attn_norm_b, "cross_attn_norm missing");
+        require(grid > 0 && grid <= 128 && nq > 0 && nq <= 4096 && prompt_tokens > 0 && prompt_tokens <= 4096,
+                "grid / query / prompt count out of range");
+        const float* bufs[] = {enc, fpn0, fpn1, queries, prompt, mask_logits};
+        for (const float* p : bufs) require(p != nullptr, "segmentation head buffer missing");
+        require(aligned16(enc) && aligned16(fpn0) && aligned16(fpn1) && aligned16(queries) && aligned16(prompt) &&
+                    aligned16(mask_logits),
+                "buffers must be 16-byte aligned");
+        DeviceState& state = device_state(device);
+        cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
+        Scratch& scratch =
+            scratch_for(state, stream, seg_head_scratch_bytes(h, grid, nq, prompt_tokens, state.sm_count));
+        launch_seg_head(h, enc, grid, fpn0, fpn1, queries, nq, prompt, prompt_bias, prompt_tokens, mask_logits,
+                        scratch.ptr, state, stream);
+    });
+}
+
+samq_status samq_sine_pe_2d_v1(int h, int w, int d, float* out) {
+    return guarded([&] {
+        require(h > 0 && w > 0 && h <= 4096 && w <= 4096 && d > 0 && d % 2 == 0 && d <= 8192 && out != nullptr,
+                "positional encoding size out of range");
+        const int half = d / 2;
+        const float scale = 2.0f * 3.14159265358979323846f;
+        for (int y = 0; y < h; ++y) {
+            const float py = (static_cast<float>(y + 1) / static_cast<float>(h)) * scale;
+            for (int x = 0; x < w; ++x) {
+                const float px = (static_cast<float>(x + 1) / static_cast<float>(w)) * scale;
+                float* row = out + (static_cast<int64_t>(y) * w + x) * d;
+                for (int i = 0; i < half; ++i) {
+                    const float dim_t = powf(10000.0f, static_cast<float>(i & ~1) / static_cast<float>(half));
+                    row[i] = (i % 2 == 0) ? sinf(py / dim_t) : cosf(py / dim_t);
+                    row[half + i] = (i % 2 == 0) ? sinf(px / dim_t) : cosf(px / dim_t);
+                }
+            }
+        }
+    });
+}
+
 samq_status samq_dense_create_v1(int device, int type, int kind, int kw, int kh, int64_t cin, int64_t cout,
                                  const void* data, size_t bytes, void* stream_ptr, samq_dense** out) {
     return guarded([&] {

@@ -87,18 +87,6 @@ __device__ __forceinline__ void tc_mma_tf32(uint32_t tmem_d, uint64_t adesc, uin
         : "memory");
 }
 
-// Round to TF32 (10 stored mantissa bits), nearest, ties away from zero.
-__device__ __forceinline__ float rna_tf32(float x) {
-    uint32_t r;
-    asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
-    return __uint_as_float(r);
-}
-
-__device__ __forceinline__ void split_tf32(float x, float& hi, float& lo) {
-    hi = rna_tf32(x);
-    lo = rna_tf32(x - hi);
-}
-
 // ggml_gelu_erf in f32: 0.5 x (1 + erf(x / sqrt 2)).
 __device__ __forceinline__ float gelu_erf_f32(float x) { return 0.5f * x * (1.0f + erff(x * 0.70710678118654752f)); }
 

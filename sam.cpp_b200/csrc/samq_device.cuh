@@ -16,6 +16,20 @@ enum : uint32_t {
     kStatusLayout = 4u,   // dynamic shared memory base too poorly aligned for the kernel's layout
 };
 
+// Round to TF32 (10 stored mantissa bits), nearest, ties away from zero.
+__device__ __forceinline__ float rna_tf32(float x) {
+    uint32_t r;
+    asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+    return __uint_as_float(r);
+}
+
+// The F32-semantics GEMM operand split: hi = rna_tf32(x), lo = rna_tf32(x - hi)
+// (x - hi is exact in f32).
+__device__ __forceinline__ void split_tf32(float x, float& hi, float& lo) {
+    hi = rna_tf32(x);
+    lo = rna_tf32(x - hi);
+}
+
 struct DeviceStatus {
     uint32_t flags;       // OR of kStatus*
     uint32_t timeout_site;

@@ -287,6 +287,15 @@ void launch_decoder(const samq_decoder_v1& dec, const float* enc, const float* e
                     float* queries_out, float* boxes, float* scores, float* presence, void* scratch,
                     DeviceState& state, cudaStream_t stream);
 
+// seg.cu: the segmentation head and the geometry encoder.
+size_t seg_head_scratch_bytes(const samq_seg_head_v1& sh, int grid, int64_t queries, int64_t prompt_tokens, int sms);
+void launch_seg_head(const samq_seg_head_v1& sh, const float* enc, int grid, const float* fpn0, const float* fpn1,
+                     const float* queries, int64_t nq, const float* prompt, const float* prompt_bias,
+                     int64_t prompt_tokens, float* logits, void* scratch, DeviceState& state, cudaStream_t stream);
+size_t geometry_scratch_bytes(const samq_geometry_encoder_v1& ge, int64_t tokens, int sms);
+void launch_geometry_encoder(const samq_geometry_encoder_v1& ge, const float* image, const float* pos, int64_t tokens,
+                             float* out, void* scratch, DeviceState& state, cudaStream_t stream);
+
 // dense.cu: F32-semantics linears / convolutions (three-term TF32 split).
 void launch_dense_prep(const void* src, int type, int kind, int ks, int64_t cin, int64_t cout, int64_t n, int64_t k,
                        float* hi, float* lo, DeviceState& state, cudaStream_t stream);

@@ -101,6 +101,30 @@ class DecoderDesc(ctypes.Structure):
                 ("prompt_proj", LinearRef), ("hs_proj", LinearRef)]
 
 
+GEOMETRY_LAYER_LINEARS = ("sa_in_proj", "sa_out_proj", "ca_in_proj", "ca_out_proj", "linear1", "linear2")
+GEOMETRY_LAYER_NORMS = ("norm1_w", "norm1_b", "norm2_w", "norm2_b", "norm3_w", "norm3_b")
+
+
+class GeometryLayerDesc(ctypes.Structure):
+    """struct samq_geometry_layer_v1."""
+    _fields_ = [(n, LinearRef) for n in GEOMETRY_LAYER_LINEARS] + [(n, _vp) for n in GEOMETRY_LAYER_NORMS]
+
+
+class GeometryEncoderDesc(ctypes.Structure):
+    """struct samq_geometry_encoder_v1."""
+    _fields_ = [("version", ctypes.c_uint32), ("heads", ctypes.c_int32), ("layers", ctypes.c_int32),
+                ("layer", ctypes.POINTER(GeometryLayerDesc)), ("cls_token", _vp), ("final_proj", LinearRef),
+                ("norm_w", _vp), ("norm_b", _vp), ("encode_norm_w", _vp), ("encode_norm_b", _vp)]
+
+
+class SegHeadDesc(ctypes.Structure):
+    """struct samq_seg_head_v1."""
+    _fields_ = [("version", ctypes.c_uint32), ("heads", ctypes.c_int32), ("cross_attn_norm_w", _vp),
+                ("cross_attn_norm_b", _vp), ("ca_in_proj", LinearRef), ("ca_out_proj", LinearRef),
+                ("conv", _vp * 2), ("conv_b", _vp * 2), ("norm_w", _vp * 2), ("norm_b", _vp * 2),
+                ("instance", _vp), ("instance_b", _vp), ("mask_embed", LinearRef * 3)]
+
+
 class NeckDesc(ctypes.Structure):
     """struct samq_neck_v1: (weights, bias) pairs in the order of NECK_LAYERS."""
     _fields_ = [("version", ctypes.c_uint32)] + [
@@ -145,6 +169,10 @@ SIGNATURES = {
     "samq_fusion_layer_forward_v1": (_i32, [ctypes.POINTER(FusionLayerDesc), _vp, _vp, _i32, _vp, _vp, _i32, _vp]),
     "samq_decoder_forward_v1": (_i32, [ctypes.POINTER(DecoderDesc), _vp, _vp, _i32, _vp, _vp, _vp, _i32, _vp, _vp,
                                        _vp, _vp, _vp]),
+    "samq_geometry_encoder_forward_v1": (_i32, [ctypes.POINTER(GeometryEncoderDesc), _vp, _vp, _i32, _vp, _vp]),
+    "samq_seg_head_forward_v1": (_i32, [ctypes.POINTER(SegHeadDesc), _vp, _i32, _vp, _vp, _vp, _i32, _vp, _vp, _i32,
+                                        _vp, _vp]),
+    "samq_sine_pe_2d_v1": (_i32, [_i32, _i32, _i32, _vp]),
     "samq_dense_create_v1": (_i32, [_i32, _i32, _i32, _i32, _i32, _i64, _i64, _vp, _sz, _vp, ctypes.POINTER(_vp)]),
     "samq_dense_destroy_v1": (_i32, [_vp]),
     "samq_dense_linear_v1": (_i32, [_vp, _vp, _i64, _i64, _vp, _i32, _vp, _i64, _vp]),
@@ -463,6 +491,70 @@ def decoder_forward(decoder: Decoder, enc, enc_pos, grid: int, prompt, prompt_bi
                                              _addr(prompt), _addr(prompt_bias), _addr(prompt_valid), prompt_tokens,
                                              _addr(queries_out), _addr(boxes), _addr(scores), _addr(presence),
                                              _stream(stream)))
+
+
+class GeometryEncoder:
+    """The text-only-prompt geometry encoder (samq_geometry_encoder_v1).
+    `layers`: per layer a dict of GEOMETRY_LAYER_LINEARS -> (Weights or Dense,
+    bias) and GEOMETRY_LAYER_NORMS -> device tensors; `params`: cls_token,
+    norm_w / b, encode_norm_w / b device tensors; final_proj: (handle, bias)."""
+
+    def __init__(self, heads: int, layers: list, params: dict, final_proj):
+        self._keep = (layers, params, final_proj)
+        arr = (GeometryLayerDesc * len(layers))()
+        for i, ly in enumerate(layers):
+            arr[i] = GeometryLayerDesc(*([linear_ref(*ly[n]) for n in GEOMETRY_LAYER_LINEARS] +
+                                         [_addr(ly[n]) for n in GEOMETRY_LAYER_NORMS]))
+        self._layers = arr
+        self.desc = GeometryEncoderDesc(1, heads, len(layers), ctypes.cast(arr, ctypes.POINTER(GeometryLayerDesc)),
+                                        _addr(params["cls_token"]), linear_ref(*final_proj), _addr(params["norm_w"]),
+                                        _addr(params["norm_b"]), _addr(params["encode_norm_w"]),
+                                        _addr(params["encode_norm_b"]))
+
+
+def geometry_encoder_forward(encoder: GeometryEncoder, image, pos, tokens: int, out, stream=None):
+    """samq_geometry_encoder_forward_v1: out [D] = the geometry prompt token."""
+    _check(library().samq_geometry_encoder_forward_v1(ctypes.byref(encoder.desc), _addr(image), _addr(pos), tokens,
+                                                      _addr(out), _stream(stream)))
+
+
+class SegHead:
+    """The segmentation head (samq_seg_head_v1): `params` holds device tensors
+    cross_attn_norm_w / b, conv_b, norm_w, norm_b (pairs) and instance_b;
+    convs: two 3x3 Dense CONV handles; instance: 1x1 Dense CONV; ca_in_proj,
+    ca_out_proj: (handle, bias); mask_embed: three (handle, bias)."""
+
+    def __init__(self, heads: int, params: dict, convs, instance, ca_in_proj, ca_out_proj, mask_embed):
+        self._keep = (params, convs, instance, ca_in_proj, ca_out_proj, mask_embed)
+        d = SegHeadDesc()
+        d.version, d.heads = 1, heads
+        d.cross_attn_norm_w, d.cross_attn_norm_b = _addr(params["cross_attn_norm_w"]), _addr(params["cross_attn_norm_b"])
+        d.ca_in_proj, d.ca_out_proj = linear_ref(*ca_in_proj), linear_ref(*ca_out_proj)
+        for i in range(2):
+            d.conv[i] = convs[i].handle
+            d.conv_b[i] = _addr(params["conv_b"][i])
+            d.norm_w[i] = _addr(params["norm_w"][i])
+            d.norm_b[i] = _addr(params["norm_b"][i])
+        d.instance, d.instance_b = instance.handle, _addr(params["instance_b"])
+        for j in range(3):
+            d.mask_embed[j] = linear_ref(*mask_embed[j])
+        self.desc = d
+
+
+def seg_head_forward(head: SegHead, enc, grid: int, fpn0, fpn1, queries, nq: int, prompt, prompt_bias,
+                     prompt_tokens: int, mask_logits, stream=None):
+    """samq_seg_head_forward_v1: mask_logits [nq][(4 grid)^2]."""
+    _check(library().samq_seg_head_forward_v1(ctypes.byref(head.desc), _addr(enc), grid, _addr(fpn0), _addr(fpn1),
+                                              _addr(queries), nq, _addr(prompt), _addr(prompt_bias), prompt_tokens,
+                                              _addr(mask_logits), _stream(stream)))
+
+
+def sine_pe_2d(h: int, w: int, d: int):
+    """samq_sine_pe_2d_v1: the image positional encoding [h * w][d] (host f32 numpy)."""
+    import numpy as np
+    out = np.empty((h * w, d), np.float32)
+    _check(library().samq_sine_pe_2d_v1(h, w, d, out.ctypes.data))
+    return out
 
 
 class Dense:

@@ -112,3 +112,45 @@ def test_invalid_block_arguments_are_rejected(samq):
     desc.compute = 7  # neither SAMQ_COMPUTE_F32 nor _F16
     rc = lib.samq_vit_block_forward_v1(ctypes.byref(desc), x, 72, 72, None)
     assert rc == 1 and b"compute" in lib.samq_last_error_v1()
+
+
+def test_module_descriptors_are_checked_before_device_work(samq):
+    """The fusion, decoder, geometry and segmentation entries reject a missing
+    or wrongly versioned descriptor without touching a device."""
+    lib = samq.library()
+    x = ctypes.c_void_p(16)
+    assert lib.samq_fusion_layer_forward_v1(None, x, x, 16, x, None, 1, None) == 1
+    assert b"version 1" in lib.samq_last_error_v1()
+    assert lib.samq_decoder_forward_v1(None, x, x, 8, x, None, None, 1, x, x, x, x, None) == 1
+    assert b"version 1" in lib.samq_last_error_v1()
+    dec = samq.DecoderDesc()
+    dec.version = 2
+    assert lib.samq_decoder_forward_v1(ctypes.byref(dec), x, x, 8, x, None, None, 1, x, x, x, x, None) == 1
+    assert lib.samq_geometry_encoder_forward_v1(None, x, x, 16, x, None) == 1
+    assert b"version 1" in lib.samq_last_error_v1()
+    geo = samq.GeometryEncoderDesc()
+    geo.version = 1
+    geo.layers = 0
+    assert lib.samq_geometry_encoder_forward_v1(ctypes.byref(geo), x, x, 16, x, None) == 1
+    assert b"layer count" in lib.samq_last_error_v1()
+    assert lib.samq_seg_head_forward_v1(None, x, 8, x, x, x, 4, x, None, 1, x, None) == 1
+    assert b"version 1" in lib.samq_last_error_v1()
+
+
+def test_sine_pe_2d_host(samq):
+    """samq_sine_pe_2d_v1 (host f32, the reference's own arithmetic) against
+    the oracle's f64 evaluation of the same f32 arguments, and its layout:
+    y encoding in the first half, x in the second, sin at even channels."""
+    import sys
+    sys.path.insert(0, str(ROOT))
+    from oracle import oracle as o
+    pe = samq.sine_pe_2d(72, 72, 256)
+    ref = o.sine_pe_2d(72, 72, 256)
+    assert np.abs(pe.astype(np.float64) - ref).max() <= 1e-6
+    assert abs(float(pe[0, 0]) - np.sin(2 * np.pi / 72)) <= 1e-6 and abs(float(pe[0, 1]) - np.cos(2 * np.pi / 72)) <= 1e-6
+    assert np.array_equal(pe[5 * 72 + 3, :128], pe[5 * 72 + 40, :128])  # y half depends on the row only
+    assert np.array_equal(pe[3 * 72 + 9, 128:], pe[60 * 72 + 9, 128:])  # x half on the column only
+    pe2 = samq.sine_pe_2d(24, 36, 64)
+    assert np.abs(pe2.astype(np.float64) - o.sine_pe_2d(24, 36, 64)).max() <= 1e-6
+    with pytest.raises(samq.SamqError):
+        samq.sine_pe_2d(0, 4, 8)
