@@ -586,13 +586,37 @@ def text_encoder(ids, token_embed: np.ndarray, pos_embed: np.ndarray, blocks: li
     return staged_linear(resizer_w, layer_norm(x, ln_w, ln_b), resizer_b)
 
 
+_EXACT_OPERANDS = [False]
+
+
+class exact_operands:
+    """Context in which module_linear evaluates quantized linears over the
+    device GEMM's exact f16 operands (weight_f16 of the packed rows, act_f16 of
+    the activations: lin["w16"] must be present) instead of GGML MMQ's decoded
+    operands.  The distance between the two is the operand precision of the
+    f16 tensor-core path; the device is held tightly to this mode."""
+
+    def __enter__(self):
+        _EXACT_OPERANDS[0] = True
+        return self
+
+    def __exit__(self, *exc):
+        _EXACT_OPERANDS[0] = False
+        return False
+
+
 def module_linear(lin: dict, x: np.ndarray, rows=None, epilogue=EPILOGUE_NONE) -> np.ndarray:
     """A linear of the fusion / decoder modules: lin = {"w": f32 [n][k] (the
-    decoded weight), "b": [n] or None, "quantized": bool}.  Quantized: MMQ
-    operand semantics (staged_linear); dense: the F32 product in f64.  `rows`
-    selects a row slice of the weight (the in_proj views)."""
+    decoded weight), "b": [n] or None, "quantized": bool, optionally "w16": the
+    f16 device operand}.  Quantized: MMQ operand semantics (staged_linear), or
+    the exact-operand product inside `exact_operands()`; dense: the F32 product
+    in f64.  `rows` selects a row slice of the weight (the in_proj views)."""
     w = lin["w"] if rows is None else lin["w"][rows]
     b = None if lin["b"] is None else (lin["b"] if rows is None else lin["b"][rows])
+    if lin["quantized"] and _EXACT_OPERANDS[0]:
+        w16 = lin["w16"] if rows is None else lin["w16"][rows]
+        return gemm_f64(np.ascontiguousarray(w16), act_f16(np.asarray(x, np.float32)), bias=b,
+                        epilogue=epilogue).astype(np.float32)
     if lin["quantized"]:
         return staged_linear(w, x, b, epilogue)
     return dense_linear(x, w, b, gelu=epilogue == EPILOGUE_GELU_ERF).astype(np.float32)

@@ -6,9 +6,13 @@
 and the 72 x 72 grid (mask logits at 288 x 288).
 
 F32 linears: F32 semantics end to end, max error <= 1e-4 of the output's
-largest magnitude.  Q8_0 linears: the device's distance from the oracle may be
-at most 2x the oracle's own drift under one ulp of noise on its image input
-plus a 1e-3 floor (relative to the largest magnitude), as for the decoder.
+largest magnitude.  Q8_0 linears: the quantized GEMM multiplies f16 operands
+(the decoded weight and the decoded Q8_1 activation, each rounded to f16), so
+it is held to the oracle evaluated over those exact operands
+(oracle.exact_operands): at most 2x that oracle's drift under one ulp of noise
+on the image input plus 1e-3 (relative to the largest magnitude).  Against
+GGML MMQ's decoded-operand semantics its distance may exceed the exact-operand
+oracle's own distance from them by at most 1e-3.
 """
 import numpy as np
 import pytest
@@ -32,9 +36,11 @@ def _linear(rng, n, k, quantized, scale=1.0):
         rows = o.quantize(o.Q8_0, w)
         handle = samq.Weights(o.Q8_0, k, n, rows)
         w = o.dequantize(o.Q8_0, rows, n * k).reshape(n, k)
+        w16 = o.weight_f16(o.Q8_0, k, n, rows)
     else:
         handle = samq.Dense(samq.DENSE_LINEAR, w)
-    return {"w": w, "b": b, "quantized": quantized}, (handle, _dev(b))
+        w16 = None
+    return {"w": w, "b": b, "quantized": quantized, "w16": w16}, (handle, _dev(b))
 
 
 def _norm(rng):
@@ -91,9 +97,13 @@ def test_geometry_encoder(quantized):
     if not quantized:
         assert err <= 1e-4, err
         return
-    drift = _rel(o.geometry_encoder(_noisy(image), pos, host, HEADS)[0], ref)
-    print("geometry", err, drift)
-    assert err <= 2.0 * drift + 1e-3, (err, drift)
+    with o.exact_operands():
+        exact = o.geometry_encoder(image, pos, host, HEADS)[0]
+        drift = _rel(o.geometry_encoder(_noisy(image), pos, host, HEADS)[0], exact)
+    err_exact, operand = _rel(got, exact), _rel(exact, ref)
+    print("geometry", err, err_exact, drift, operand)
+    assert err_exact <= 2.0 * drift + 1e-3, (err_exact, drift)
+    assert err <= operand + 1e-3, (err, operand)
 
 
 def make_seg_head(rng, quantized):
@@ -170,7 +180,10 @@ def test_seg_head_q8_0_linears(grid):
     enc, fpn0, fpn1, queries, prompt, bias = seg_inputs(rng, grid)
     got = run_seg(head, grid, enc, fpn0, fpn1, queries, prompt, bias)
     ref = o.seg_head(enc, fpn0, fpn1, queries, prompt, bias, host, grid, HEADS)
-    drift = _rel(o.seg_head(_noisy(enc), fpn0, fpn1, queries, prompt, bias, host, grid, HEADS), ref)
-    err = _rel(got, ref)
-    print("seg q8_0", grid, err, drift)
-    assert err <= 2.0 * drift + 1e-3, (err, drift)
+    with o.exact_operands():
+        exact = o.seg_head(enc, fpn0, fpn1, queries, prompt, bias, host, grid, HEADS)
+        drift = _rel(o.seg_head(_noisy(enc), fpn0, fpn1, queries, prompt, bias, host, grid, HEADS), exact)
+    err, err_exact, operand = _rel(got, ref), _rel(got, exact), _rel(exact, ref)
+    print("seg q8_0", grid, err, err_exact, drift, operand)
+    assert err_exact <= 2.0 * drift + 1e-3, (err_exact, drift)
+    assert err <= operand + 1e-3, (err, operand)
