@@ -441,6 +441,12 @@ samq_status samq_seg_head_forward_v1(const samq_seg_head_v1* head, const float* 
                                      const float* fpn1, const float* queries, int nq, const float* prompt,
                                      const float* prompt_bias, int prompt_tokens, float* mask_logits, void* stream);
 
+/* Host GGUF row quantizer (the role of tools/quantize/quantize_rows.cpp:210,
+ * ggml_quantize_chunk): n rows of k f32 values (host) -> n packed rows (host,
+ * bytes = n * row bytes).  Q8_0 is the reference converter's quantizer
+ * (gguf-py); the K-quants use a min / max encoder per sub-block. */
+samq_status samq_quantize_rows_v1(int type, int64_t k, int64_t n, const float* src, void* dst, size_t bytes);
+
 /* The image positional encoding sam3_sinusoidal_pe_2d
  * (src/models/sam3/vision.hpp:39-75), computed on the host in f32 as the
  * reference does: out [h * w][d] host floats. */

@@ -273,14 +273,23 @@ def layer_norm(x: np.ndarray, w: np.ndarray, b: np.ndarray, eps: float = 1e-5) -
     return (c / np.sqrt(var + eps) * np.asarray(w, np.float64) + np.asarray(b, np.float64)).astype(np.float32)
 
 
+_EXACT_OPERANDS = [False]
+
+
 def staged_linear(w: np.ndarray, x: np.ndarray, bias=None, epilogue=EPILOGUE_NONE) -> np.ndarray:
     """A quantized linear with GGML MMQ's operand semantics: x is staged to
     Q8_1 (quantize_q8_1 restated) and the product runs over the DECODED
     operands, d_x * q_x for the activations and the weight's f32 dequantized
     values (w = dequantize(...), [n][k] f32, no f16 rounding), in f64; then
-    bias and erf-GELU, rounded to f32 (the reference's F32 output tensor)."""
+    bias and erf-GELU, rounded to f32 (the reference's F32 output tensor).
+    Inside `exact_operands()` both operands are first rounded to f16 as the
+    device's tensor-core operands are (act_f16, and the f16 rounding of the
+    decoded weight that weight_f16 produces)."""
     x = np.ascontiguousarray(x, dtype=np.float32)
     m, k = x.shape
+    if _EXACT_OPERANDS[0]:
+        w16 = np.ascontiguousarray(np.asarray(w, np.float32).astype(np.float16))
+        return gemm_f64(w16, act_f16(x), bias=bias, epilogue=epilogue)
     xd = q8_1_decode(quantize_q8_1(x), m, k).astype(np.float64)
     y = xd @ np.asarray(w, np.float64).T
     if bias is not None:
@@ -586,15 +595,12 @@ def text_encoder(ids, token_embed: np.ndarray, pos_embed: np.ndarray, blocks: li
     return staged_linear(resizer_w, layer_norm(x, ln_w, ln_b), resizer_b)
 
 
-_EXACT_OPERANDS = [False]
-
-
 class exact_operands:
-    """Context in which module_linear evaluates quantized linears over the
-    device GEMM's exact f16 operands (weight_f16 of the packed rows, act_f16 of
-    the activations: lin["w16"] must be present) instead of GGML MMQ's decoded
-    operands.  The distance between the two is the operand precision of the
-    f16 tensor-core path; the device is held tightly to this mode."""
+    """Context in which every quantized linear (staged_linear, and through it
+    module_linear, vit_block, text_block ...) runs over the device GEMM's
+    exact f16 operands instead of GGML MMQ's decoded operands.  The distance
+    between the two is the operand precision of the f16 tensor-core path; the
+    device is held tightly to this mode."""
 
     def __enter__(self):
         _EXACT_OPERANDS[0] = True
@@ -607,16 +613,11 @@ class exact_operands:
 
 def module_linear(lin: dict, x: np.ndarray, rows=None, epilogue=EPILOGUE_NONE) -> np.ndarray:
     """A linear of the fusion / decoder modules: lin = {"w": f32 [n][k] (the
-    decoded weight), "b": [n] or None, "quantized": bool, optionally "w16": the
-    f16 device operand}.  Quantized: MMQ operand semantics (staged_linear), or
-    the exact-operand product inside `exact_operands()`; dense: the F32 product
-    in f64.  `rows` selects a row slice of the weight (the in_proj views)."""
+    decoded weight), "b": [n] or None, "quantized": bool}.  Quantized: MMQ
+    operand semantics (staged_linear); dense: the F32 product in f64.  `rows`
+    selects a row slice of the weight (the in_proj views)."""
     w = lin["w"] if rows is None else lin["w"][rows]
     b = None if lin["b"] is None else (lin["b"] if rows is None else lin["b"][rows])
-    if lin["quantized"] and _EXACT_OPERANDS[0]:
-        w16 = lin["w16"] if rows is None else lin["w16"][rows]
-        return gemm_f64(np.ascontiguousarray(w16), act_f16(np.asarray(x, np.float32)), bias=b,
-                        epilogue=epilogue).astype(np.float32)
     if lin["quantized"]:
         return staged_linear(w, x, b, epilogue)
     return dense_linear(x, w, b, gelu=epilogue == EPILOGUE_GELU_ERF).astype(np.float32)

@@ -909,6 +909,18 @@ samq_status samq_seg_head_forward_v1(const samq_seg_head_v1* head, const float* 
     });
 }
 
+samq_status samq_quantize_rows_v1(int type, int64_t k, int64_t n, const float* src, void* dst, size_t bytes) {
+    return guarded([&] {
+        require(supported_type(type), "weight type must be Q8_0, Q4_K, Q5_K or Q6_K");
+        require(n > 0 && n <= (int64_t(1) << 24), "row count out of range");
+        const int64_t rb = row_bytes(type, k);
+        require(rb > 0 && k <= (int64_t(1) << 20), "width is not a whole number of blocks");
+        require(src != nullptr && dst != nullptr && bytes == static_cast<size_t>(rb * n),
+                "output size differs from n packed rows");
+        quantize_rows(type, k, n, src, static_cast<uint8_t*>(dst));
+    });
+}
+
 samq_status samq_sine_pe_2d_v1(int h, int w, int d, float* out) {
     return guarded([&] {
         require(h > 0 && w > 0 && h <= 4096 && w <= 4096 && d > 0 && d % 2 == 0 && d <= 8192 && out != nullptr,

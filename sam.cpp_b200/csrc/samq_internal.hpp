@@ -144,6 +144,8 @@ void launch_mmq_d4(const float* x, int64_t rows, int64_t k, int64_t ld, uint8_t*
 int64_t packet_code_bytes(int type);
 int64_t packet_bytes(int type);
 int64_t row_bytes(int type, int64_t k);
+// rows.cu: host GGUF row quantizer (Q8_0 as gguf-py; K-quants min / max).
+void quantize_rows(int type, int64_t k, int64_t n, const float* src, uint8_t* out);
 void launch_gguf_to_packets(int type, int64_t k, int64_t n, const uint8_t* rows, uint8_t* packets,
                             uint32_t* bad_scales, cudaStream_t stream);
 void launch_packets_to_gguf(int type, int64_t k, int64_t n, const uint8_t* packets, uint8_t* rows,

@@ -173,6 +173,7 @@ SIGNATURES = {
     "samq_seg_head_forward_v1": (_i32, [ctypes.POINTER(SegHeadDesc), _vp, _i32, _vp, _vp, _vp, _i32, _vp, _vp, _i32,
                                         _vp, _vp]),
     "samq_sine_pe_2d_v1": (_i32, [_i32, _i32, _i32, _vp]),
+    "samq_quantize_rows_v1": (_i32, [_i32, _i64, _i64, _vp, _vp, _sz]),
     "samq_dense_create_v1": (_i32, [_i32, _i32, _i32, _i32, _i32, _i64, _i64, _vp, _sz, _vp, ctypes.POINTER(_vp)]),
     "samq_dense_destroy_v1": (_i32, [_vp]),
     "samq_dense_linear_v1": (_i32, [_vp, _vp, _i64, _i64, _vp, _i32, _vp, _i64, _vp]),
@@ -547,6 +548,16 @@ def seg_head_forward(head: SegHead, enc, grid: int, fpn0, fpn1, queries, nq: int
     _check(library().samq_seg_head_forward_v1(ctypes.byref(head.desc), _addr(enc), grid, _addr(fpn0), _addr(fpn1),
                                               _addr(queries), nq, _addr(prompt), _addr(prompt_bias), prompt_tokens,
                                               _addr(mask_logits), _stream(stream)))
+
+
+def quantize_rows(qtype: int, w):
+    """samq_quantize_rows_v1: f32 [n][k] (numpy) -> packed GGUF rows (uint8, host)."""
+    import numpy as np
+    w = np.ascontiguousarray(w, dtype=np.float32)
+    n, k = w.shape
+    out = np.empty(n * row_bytes(qtype, k), np.uint8)
+    _check(library().samq_quantize_rows_v1(qtype, k, n, w.ctypes.data, out.ctypes.data, out.nbytes))
+    return out
 
 
 def sine_pe_2d(h: int, w: int, d: int):

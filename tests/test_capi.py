@@ -154,3 +154,31 @@ def test_sine_pe_2d_host(samq):
     assert np.abs(pe2.astype(np.float64) - o.sine_pe_2d(24, 36, 64)).max() <= 1e-6
     with pytest.raises(samq.SamqError):
         samq.sine_pe_2d(0, 4, 8)
+
+
+@pytest.mark.parametrize("qtype", [8, 12, 13, 14])
+def test_quantize_rows_host(samq, qtype):
+    """samq_quantize_rows_v1: Q8_0 bit-exact with the oracle's restatement of
+    the reference converter's quantizer; every format decodes (oracle
+    dequantizer, pinned to gguf-py) to within its step of the source."""
+    import sys
+    sys.path.insert(0, str(ROOT))
+    from oracle import oracle as o
+    rng = np.random.default_rng(qtype)
+    n, k = 7, 512
+    w = rng.normal(0, 0.02, (n, k)).astype(np.float32)
+    w[rng.random(w.shape) < 0.01] *= 8.0
+    w[3] = 0.0  # an all-zero row
+    rows = samq.quantize_rows(qtype, w)
+    assert rows.nbytes == n * samq.row_bytes(qtype, k)
+    if qtype == 8:
+        assert np.array_equal(rows, o.quantize(8, w).ravel())
+    dec = o.dequantize(qtype, rows, n * k).reshape(n, k)
+    assert np.all(dec[3] == 0.0)
+    # the decoded error is no worse than that of the oracle's own packer for the format
+    ref = o.dequantize(qtype, o.quantize(qtype, w), n * k).reshape(n, k)
+    err, ref_err = np.linalg.norm(dec - w), np.linalg.norm(ref - w)
+    assert err <= 1.05 * ref_err + 1e-9, (err, ref_err)
+    assert err <= {8: 0.01, 12: 0.12, 13: 0.06, 14: 0.04}[qtype] * np.linalg.norm(w)
+    with pytest.raises(samq.SamqError):
+        samq.quantize_rows(qtype, np.full((1, 256), np.nan, np.float32))

@@ -37,11 +37,9 @@ def _linear(rng, n, k, quantized, scale=1.0):
         rows = o.quantize(o.Q8_0, w)
         handle = samq.Weights(o.Q8_0, k, n, rows)
         w = o.dequantize(o.Q8_0, rows, n * k).reshape(n, k)
-        w16 = o.weight_f16(o.Q8_0, k, n, rows)
     else:
         handle = samq.Dense(samq.DENSE_LINEAR, w)
-        w16 = None
-    return {"w": w, "b": b, "quantized": quantized, "w16": w16}, (handle, _dev(b))
+    return {"w": w, "b": b, "quantized": quantized}, (handle, _dev(b))
 
 
 def _norm(rng):
