@@ -80,13 +80,16 @@ def step_ops(m=M):
     return sum(2.0 * m * n * k for _, n, k, *_ in LINEARS)
 
 
-def make_weights(oracle_mod, n, k, qtype, seed):
+def make_weights(quantize, n, k, qtype, seed):
+    """Config-2 statistics: N(0, 0.02^2) with 1% of entries x8; `quantize`
+    packs them (samq.quantize_rows on the GPU arm, the oracle's packer in the
+    CPU baseline)."""
     rng = np.random.default_rng(seed)
     w = rng.normal(0.0, 0.02, (n, k)).astype(np.float32)
     mask = rng.random(w.shape) < 0.01
     w[mask] *= 8
     bias = rng.normal(0.0, 0.02, n).astype(np.float32)
-    return oracle_mod.quantize(qtype, w), bias
+    return quantize(qtype, w), bias
 
 
 def peaks():
@@ -222,7 +225,7 @@ class CpuBackbone:
         self.o = oracle_mod
         self.threads = oracle_mod.default_threads()
         self.rows, self.qrows = rows, qrows
-        self.weights = [make_weights(oracle_mod, n, k, qtype, seed) for _, n, k, qtype, _, seed in LINEARS]
+        self.weights = [make_weights(oracle_mod.quantize, n, k, qtype, seed) for _, n, k, qtype, _, seed in LINEARS]
         rng = np.random.default_rng(11)
         self.x = {name: rng.normal(0, 1, (rows, k)).astype(np.float32) for name, n, k, *_ in LINEARS}
         self.y = {name: np.empty((rows, n), np.float32) for name, n, *_ in LINEARS}
@@ -302,22 +305,23 @@ def run_reference(args, world, rank):
     print(json.dumps(line), flush=True)
 
 
-def make_backbone(samq, o, torch, device, rank, compute=None):
+def make_backbone(samq, torch, device, rank, compute=None):
     """Random-init SAM 3 vision backbone on `device` (config 3 statistics),
     blocks in the headline compute mode (F16) unless `compute` is given."""
+    from samq.synthetic import rope_freqs
     compute = samq.COMPUTE_F16 if compute is None else compute
     dev = torch.device("cuda", device)
     blocks, keep = [], []
     base = np.random.default_rng(2024 + rank)
-    freqs_w = torch.from_numpy(o.rope_freqs(WINDOW * WINDOW, seed=1)).to(dev)
-    freqs_g = torch.from_numpy(o.rope_freqs(M, seed=2)).to(dev)
+    freqs_w = torch.from_numpy(rope_freqs(WINDOW * WINDOW, seed=1)).to(dev)
+    freqs_g = torch.from_numpy(rope_freqs(M, seed=2)).to(dev)
     for i in range(DEPTH):
         rng = np.random.default_rng(base.integers(1 << 62))
         t = {}
         for name, n, k, qtype in (("qkv", 3 * E, E, 12), ("proj", E, E, 12), ("fc1", MLP, E, 12), ("fc2", E, MLP, 8)):
             w = rng.standard_normal((n, k), dtype=np.float32) * np.float32(0.02)
             w[rng.random((n, k), dtype=np.float32) < 0.01] *= 8
-            t[name] = samq.Weights(qtype, k, n, o.quantize(qtype, w), device=device)
+            t[name] = samq.Weights(qtype, k, n, samq.quantize_rows(qtype, w), device=device)
             t[name + "_b"] = torch.from_numpy(rng.normal(0, 0.02, n).astype(np.float32)).to(dev)
         for name in ("norm1", "norm2"):
             t[name + "_w"] = torch.from_numpy((1 + rng.normal(0, 0.02, E)).astype(np.float32)).to(dev)
@@ -366,7 +370,6 @@ def main():
     import torch
     import torch.distributed as dist
     import samq
-    from oracle import oracle as o
 
     torch.cuda.set_device(local)
     if world > 1:
@@ -381,7 +384,7 @@ def main():
         return shard_max(ms, dist if world > 1 else None, torch.device("cuda", local))
 
     # ---- backbone (config 3): one image per step per GPU ------------------
-    blocks, prefix, keep = make_backbone(samq, o, torch, local, rank)
+    blocks, prefix, keep = make_backbone(samq, torch, local, rank)
     rng = np.random.default_rng(500 + rank)
     image_host = torch.from_numpy(((rng.random((3, IMAGE, IMAGE), dtype=np.float32) - 0.5) / 0.5)).pin_memory()
     image = image_host.cuda()
@@ -468,7 +471,7 @@ def main():
     # ---- q-GEMM (config 2): the four block linears from f32 ----------------
     weights, biases, xs, ys = [], [], [], []
     for name, n, k, qtype, epi, seed in LINEARS:
-        packed, bias = make_weights(o, n, k, qtype, seed + 4 * rank)
+        packed, bias = make_weights(samq.quantize_rows, n, k, qtype, seed + 4 * rank)
         weights.append(samq.Weights(qtype, k, n, packed, device=local))
         biases.append(torch.from_numpy(bias).cuda())
         xs.append(torch.from_numpy(np.random.default_rng(1000 + seed + 17 * rank).normal(0, 1, (M, k))
@@ -533,8 +536,14 @@ def main():
                             dist if world > 1 else None)
     samq.check(local, stream)
 
+    # Configs 4 and 5 through the whole image path (samq.sam3.Sam3Image).
+    image_path = image_path_section(samq, torch, stream, max_over_ranks, world, rank, local,
+                                    dist if world > 1 else None)
+    samq.check(local, stream)
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        from oracle import oracle as o
         cb = CpuBackbone(o)
         cb.step()
         samples, t0 = [], time.perf_counter()
@@ -568,6 +577,7 @@ def main():
             "batch8": batch8,
             "sweep64": sweep,
             "f32_mode": f32_mode,
+            "image_path": image_path,
         }
         print(json.dumps(line), flush=True)
     for w in weights:
@@ -667,6 +677,99 @@ def sweep64_section(samq, torch, stream, max_over_ranks, blocks, prefix, world, 
             "gpu_launches": (end - start) * 4 + len(own) * DEPTH * 7}
 
 
+def image_path_section(samq, torch, stream, max_over_ranks, world, rank, local, dist, steps=4):
+    """The whole SAM 3 image path through samq.sam3.Sam3Image, random-init
+    models written by samq.synthetic, both in the headline F16 compute mode:
+
+    config4: the full-linear Q8_0 model, one 1008 x 1008 image and its 32-token
+      prompt per step: encode_image (ViT, neck, geometry token), encode_text,
+      predict (fusion, decoder + scoring, segmentation head with 200 x 288 x
+      288 mask logits); per-stage device times from CUDA events.
+    config5: the mixed model (vision Q4_K, text Q8_0, fusion / decoder F32),
+      64 distinct images sharded contiguously over the ranks, per-GPU batches
+      of 8 (the 32 blocks batched, neck / geometry / predict per image), one
+      fixed prompt encoded once; images/s = 64 / (max over ranks of the
+      device time)."""
+    from samq import synthetic
+    from samq.sam3 import Sam3Image
+    from samq.shard import batches, image_range
+    hp = synthetic.Hparams()
+    out = {}
+    t0 = time.perf_counter()
+    model = Sam3Image(synthetic.sam3_tensors(hp, "q8_0", seed=40 + rank), hp, compute=samq.COMPUTE_F16,
+                      device=local)
+    build_s = time.perf_counter() - t0
+    pixels = torch.from_numpy(synthetic.image(hp, 400 + rank)).to("cuda")
+    ids = synthetic.token_ids(hp, 401)
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
+    stage_ms = np.zeros(3)
+    for step in range(2 + steps):
+        ev[0].record(stream)
+        feats = model.encode_image(pixels, stream)
+        ev[1].record(stream)
+        text = model.encode_text(ids, stream)
+        ev[2].record(stream)
+        pred = model.predict(feats, ids, text, stream)
+        ev[3].record(stream)
+        torch.cuda.synchronize()
+        if step >= 2:
+            stage_ms += [ev[i].elapsed_time(ev[i + 1]) for i in range(3)]
+    stage_ms /= steps
+    total = max_over_ranks(float(stage_ms.sum()))
+    out["config4"] = {"metric": "SAM3 full-component Q8_0 text-prompted segmentation images/s (1008x1008, "
+                                "batch 1, text encoded per image)", "value": 1e3 / total * world,
+                      "unit": "images/s", "ms_per_image": total, "steps": steps,
+                      "stage_ms": {"encode_image": stage_ms[0], "encode_text": stage_ms[1],
+                                   "predict": stage_ms[2]},
+                      "mask_logits": list(pred.mask_logits.shape),
+                      "outputs_finite": bool(torch.isfinite(pred.mask_logits).all().item()
+                                             and torch.isfinite(pred.boxes).all().item()),
+                      "model_build_s": build_s}
+    model.close()
+    del model, feats, text, pred
+    torch.cuda.empty_cache()
+
+    t0 = time.perf_counter()
+    model = Sam3Image(synthetic.sam3_tensors(hp, "mixed", seed=50), hp, compute=samq.COMPUTE_F16, device=local)
+    build_s = time.perf_counter() - t0
+    ids = synthetic.token_ids(hp, 501)
+    text = model.encode_text(ids, stream)
+    n_images, batch = 64, 8
+    start, end = image_range(n_images, world, rank)
+    own = batches(start, end, batch)
+    imgs = torch.empty((end - start, 3, hp.img_size, hp.img_size), device="cuda")
+    for i in range(start, end):
+        imgs[i - start].copy_(torch.from_numpy(synthetic.image(hp, 10_000 + i)))
+    finite = [True]
+
+    def run():
+        for b0, b1 in own:
+            for f in model.encode_images(imgs[b0 - start:b1 - start], stream):
+                pred = model.predict(f, ids, text, stream)
+            finite[0] = finite[0] and bool(torch.isfinite(pred.mask_logits[:, :64]).all().item())
+
+    run()
+    torch.cuda.synchronize()
+    if dist is not None:
+        dist.barrier()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record(stream)
+    run()
+    b.record(stream)
+    torch.cuda.synchronize()
+    ms = max_over_ranks(a.elapsed_time(b))
+    out["config5"] = {"metric": "SAM3 mixed-allocation image path images/s (vision Q4_K, text Q8_0, fusion / "
+                                "decoder F32), 64 images sharded contiguously, per-GPU batches of 8",
+                      "value": n_images / (ms / 1e3), "unit": "images/s", "scaling": "strong", "ms": ms,
+                      "images": n_images, "images_this_rank": end - start, "batch_per_gpu": batch,
+                      "prompt": "one fixed 32-token prompt, encoded once outside the timed region",
+                      "outputs_finite": finite[0], "model_build_s": build_s}
+    model.close()
+    del model, imgs
+    torch.cuda.empty_cache()
+    return out
+
+
 NECK_MID, NECK_D = 512, 256
 
 
@@ -733,7 +836,7 @@ def run_profile_case(args):
     """One kernel's case launched alone, for ncu (-k regex:<kernel>)."""
     import torch
     import samq
-    from oracle import oracle as o
+    from samq.synthetic import rope_freqs
     torch.cuda.set_device(0)
     samq.init(0)
     stream = torch.cuda.current_stream()
@@ -742,7 +845,7 @@ def run_profile_case(args):
         # One windowed ViT block (block 0 of the backbone) on a 72 x 72 grid,
         # every launch of it: the LayerNorm-staging, GEMM and attention
         # kernels in their in-block modes.
-        blocks, _, keep = make_backbone(samq, o, torch, 0, 0)
+        blocks, _, keep = make_backbone(samq, torch, 0, 0)
         x = torch.from_numpy(np.random.default_rng(3).normal(0, 1, (M, E)).astype(np.float32)).cuda()
         for _ in range(launches):
             samq.vit_block_forward(blocks[0], x, GRID, GRID, stream)
@@ -763,14 +866,14 @@ def run_profile_case(args):
         window = WINDOW if args.profile.startswith("attention_window") else 0
         rng = np.random.default_rng(3)
         qkv = torch.from_numpy(rng.normal(0, 1, (M, 3 * E)).astype(np.float32)).cuda()
-        freqs = torch.from_numpy(o.rope_freqs(WINDOW * WINDOW if window else M)).cuda()
+        freqs = torch.from_numpy(rope_freqs(WINDOW * WINDOW if window else M)).cuda()
         out = torch.empty((M, E), dtype=torch.float32, device="cuda")
         for _ in range(launches):
             samq.vit_attention(qkv, 3 * E, GRID, GRID, HEADS, window, freqs, out, E, stream,
                                compute=samq.COMPUTE_F32 if args.profile.endswith("_f32") else samq.COMPUTE_F16)
     elif args.profile == "text_fc2":
         n, k, m = 1024, 4096, 32
-        packed, bias = make_weights(o, n, k, 8, 5)
+        packed, bias = make_weights(samq.quantize_rows, n, k, 8, 5)
         w = samq.Weights(8, k, n, packed)
         x = torch.from_numpy(np.random.default_rng(5).normal(0, 1, (m, k)).astype(np.float32)).cuda()
         a16 = torch.empty((m, k), dtype=torch.float16, device="cuda")
@@ -787,7 +890,7 @@ def run_profile_case(args):
         print(json.dumps({"profile_case": args.profile, "launches": launches}))
         return
     name, n, k, qtype, epi, seed = next(l for l in LINEARS if l[0] == args.profile)
-    packed, bias = make_weights(o, n, k, qtype, seed)
+    packed, bias = make_weights(samq.quantize_rows, n, k, qtype, seed)
     w = samq.Weights(qtype, k, n, packed)
     x = torch.from_numpy(np.random.default_rng(seed).normal(0, 1, (M, k)).astype(np.float32)).cuda()
     a16 = torch.empty((M, k), dtype=torch.float16, device="cuda")

@@ -245,6 +245,30 @@ class Sam3Image:
         geometry_encoder_forward(self.geometry, maps[2], position, grid * grid, geometry, stream=stream)
         return ImageFeatures(maps[:3], position, geometry, grid)
 
+    def encode_images(self, pixels, stream=None) -> list:
+        """encode_image over a batch [B][3][S][S] (device): the 32 blocks run
+        batched (samq_vit_block_forward_batch_v1, weights read once per block
+        for the whole batch), the neck and geometry token per image."""
+        torch, hp = self.torch, self.hp
+        size, grid, E, D = hp.img_size, hp.grid, hp.embed, hp.neck_dim
+        batch = pixels.shape[0]
+        x = torch.empty((batch, grid * grid, E), device=self.dev)
+        for b in range(batch):
+            vit_prefix(pixels[b], size, size, hp.patch, self.patch_w, E, self.pos_embed, hp.pos_grid, self.ln_pre[0],
+                       self.ln_pre[1], x[b], stream=stream, compute=self.compute)
+        for blk in self.blocks:
+            vit_block_forward(blk, x, grid, grid, stream=stream, batch=batch)
+        position = self.position(grid)
+        out = []
+        for b in range(batch):
+            maps = [torch.empty(((grid * s) ** 2 // 4, D), device=self.dev) for s in (8, 4, 2)]
+            maps.append(torch.empty(((grid // 2) ** 2, D), device=self.dev))
+            neck_forward(self.neck, x[b], grid, grid, maps, stream=stream)
+            geometry = torch.empty(D, device=self.dev)
+            geometry_encoder_forward(self.geometry, maps[2], position, grid * grid, geometry, stream=stream)
+            out.append(ImageFeatures(maps[:3], position, geometry, grid))
+        return out
+
     def encode_text(self, ids, stream=None):
         """execution.hpp:126-153: [ctx][256] text features."""
         torch, hp = self.torch, self.hp
