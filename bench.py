@@ -516,8 +516,8 @@ def main():
                                for i in range(len(LINEARS))},
                 "measured_on": "the 4 block-linear shapes at M=5184 (f32 epilogue, fused bias / GELU): 20 "
                                "launches each, every launch alone between two CUDA events on the launching "
-                               "stream after a 256 MB write that flushes L2; achieved = sum 2MNK / sum of the "
-                               "average launch times"}
+                               "stream after a 256 MB read that flushes L2 (clean lines, no write-back in the "
+                               "timed launch); achieved = sum 2MNK / sum of the average launch times"}
 
     # The SimpleFPN neck (F32 semantics, dense.cu) on this image's 72 x 72 ViT
     # output: a secondary figure beside the quantized backbone.
@@ -909,10 +909,14 @@ def gemm_only_durations(samq, weights, xs, ys, biases, stream, reps=20):
     """Average device time of one GEMM launch per shape: the f16 A operand is
     staged once (samq_stage_f16_v1); then each of `reps` launches of
     samq_linear_f16_v1 (the tcgen05 GEMM kernel alone) is timed between two
-    CUDA events on the launching stream, after a 256 MB write (twice the L2)
-    so that it starts with its operands in HBM."""
+    CUDA events on the launching stream, after a 256 MB read (twice the L2)
+    so that it starts with its operands in HBM.  The flush reads rather than
+    writes: a write leaves L2 full of dirty lines whose write-back to HBM
+    would run during the timed launch and charge it for traffic that is not
+    its own."""
     import torch
-    flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+    flush = torch.ones(64 << 20, dtype=torch.float32, device="cuda")
+    sink = torch.zeros((), dtype=torch.float32, device="cuda")
     out = []
     for i, (name, n, k, qtype, epi, _) in enumerate(LINEARS):
         m = xs[i].shape[0]
@@ -922,7 +926,7 @@ def gemm_only_durations(samq, weights, xs, ys, biases, stream, reps=20):
             samq.linear_f16(weights[i], a16, m, k, biases[i], epi, ys[i], n, stream)
         events = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(reps)]
         for a, b in events:
-            flush.fill_(1)
+            torch.sum(flush, dim=0, out=sink)
             a.record(stream)
             samq.linear_f16(weights[i], a16, m, k, biases[i], epi, ys[i], n, stream)
             b.record(stream)
