@@ -284,27 +284,31 @@ class Sam3Image:
         linear(self.resizer[0], normed, L, T, self.resizer[1], EPILOGUE_NONE, out, hp.neck_dim, stream=stream)
         return out
 
-    def prepare_prompt(self, features: ImageFeatures, ids, text) -> Prompt:
-        """execution.hpp:157-175: tokens = [text; geometry], bias 0 / -1e9 at
-        padding ids, pooling weights (T + 1) / n_valid at valid tokens."""
-        torch, hp = self.torch, self.hp
-        L = hp.ctx
+    def prompt_masks(self, ids):
+        """The host half of prepare_prompt (execution.hpp:157-175): key bias 0 /
+        -1e9 at padding ids, pooling weights (T + 1) / n_valid at valid tokens,
+        the geometry token (last) valid; uploaded as device tensors."""
+        torch, L = self.torch, self.hp.ctx
         ids = np.asarray(ids)
-        tokens = torch.cat([text, features.geometry.view(1, -1)], dim=0).contiguous()
         valid_count = 1 + int(np.count_nonzero(ids[:L]))
         scale = np.float32(L + 1) / np.float32(valid_count)
-        bias = np.where(ids[:L] != 0, 0.0, -1.0e9).astype(np.float32)
-        validity = np.where(ids[:L] != 0, scale, 0.0).astype(np.float32)
-        bias = np.append(bias, np.float32(0.0))
-        validity = np.append(validity, scale).astype(np.float32)
-        return Prompt(tokens, torch.from_numpy(bias).to(self.dev), torch.from_numpy(validity).to(self.dev))
+        bias = np.append(np.where(ids[:L] != 0, 0.0, -1.0e9), 0.0).astype(np.float32)
+        validity = np.append(np.where(ids[:L] != 0, scale, 0.0), scale).astype(np.float32)
+        return torch.from_numpy(bias).to(self.dev), torch.from_numpy(validity).to(self.dev)
 
-    def predict(self, features: ImageFeatures, ids, text, stream=None) -> Prediction:
+    def prepare_prompt(self, features: ImageFeatures, ids, text, masks=None) -> Prompt:
+        """execution.hpp:157-175: tokens = [text; geometry] with prompt_masks."""
+        bias, validity = self.prompt_masks(ids) if masks is None else masks
+        tokens = self.torch.cat([text, features.geometry.view(1, -1)], dim=0).contiguous()
+        return Prompt(tokens, bias, validity)
+
+    def predict(self, features: ImageFeatures, ids, text, stream=None, masks=None) -> Prediction:
         """execution.hpp:241-324 (predict_joint): fusion -> decoder + scoring ->
-        segmentation head."""
+        segmentation head.  With `masks` (prompt_masks(ids), computed once per
+        prompt) it issues device work only, so it can be captured in a graph."""
         torch, hp = self.torch, self.hp
         grid, D, Q = features.grid, hp.neck_dim, hp.queries
-        prompt = self.prepare_prompt(features, ids, text)
+        prompt = self.prepare_prompt(features, ids, text, masks)
         P = prompt.tokens.shape[0]
         fused = features.neck[2].clone()
         for layer in self.fusion:
@@ -320,3 +324,39 @@ class Sam3Image:
         seg_head_forward(self.seg, fused, grid, features.neck[0], features.neck[1], queries[1:], Q, prompt.tokens,
                          prompt.bias, P, masks, stream=stream)
         return Prediction(fused, queries, boxes, scores, presence, masks)
+
+
+class ImagePathGraph:
+    """encode_image + predict for one prompt, captured once as a CUDA graph.
+
+    The image path issues ~400 kernel launches per image, most of them small
+    (the decoder and fusion layers run on 201 queries / 33 prompt tokens), so
+    on the host it is launch-bound; a graph replays the whole sequence with
+    one launch.  Usage: copy the normalised pixels into `pixels`, call
+    `replay()`; the results are in `prediction` (device tensors reused by
+    every replay).  The library's per-stream scratch is sized by a warm-up
+    run on the capture stream before capture, so no allocation happens while
+    capturing; the text features and the prompt masks are computed outside."""
+
+    def __init__(self, model: Sam3Image, ids, text):
+        torch, hp = model.torch, model.hp
+        self.model, self.torch = model, torch
+        self.stream = torch.cuda.Stream(device=model.dev)
+        self.pixels = torch.zeros((3, hp.img_size, hp.img_size), device=model.dev)
+        self.text = text
+        self.masks = model.prompt_masks(ids)
+        self.ids = np.asarray(ids)
+        self.stream.wait_stream(torch.cuda.current_stream(model.dev))
+        with torch.cuda.stream(self.stream):
+            self._run()
+        self.stream.synchronize()
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph, stream=self.stream):
+            self.features, self.prediction = self._run()
+
+    def _run(self):
+        feats = self.model.encode_image(self.pixels)
+        return feats, self.model.predict(feats, self.ids, self.text, masks=self.masks)
+
+    def replay(self):
+        self.graph.replay()

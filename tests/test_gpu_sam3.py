@@ -288,3 +288,24 @@ def test_end_to_end_from_pixels(case):
         return oracle_heads(m, HP, nneck, ntxt, ids)
     drift = _noise_drift(rerun, ref, 21)
     _check(r, drift, 0.15)
+
+
+def test_image_path_graph_matches_eager(case):
+    """ImagePathGraph (encode_image + predict captured as one CUDA graph)
+    replays the same kernels in the same order: identical bits to the eager
+    calls, on two different images through the same graph."""
+    from samq.sam3 import ImagePathGraph
+    tensors, model, pixels, ids, m = case
+    text = model.encode_text(ids)
+    graph = ImagePathGraph(model, ids, text)
+    for seed in (12, 14):
+        img = torch.from_numpy(synthetic.image(HP, seed)).cuda()
+        feats = model.encode_image(img)
+        eager = model.predict(feats, ids, text)
+        graph.pixels.copy_(img)
+        graph.replay()
+        torch.cuda.synchronize()
+        samq.check(0)
+        for name in ("mask_logits", "boxes", "class_logits", "presence_logit", "queries"):
+            a, b = getattr(eager, name), getattr(graph.prediction, name)
+            assert torch.equal(a, b), (seed, name, float((a - b).abs().max()))
