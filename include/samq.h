@@ -441,6 +441,24 @@ samq_status samq_seg_head_forward_v1(const samq_seg_head_v1* head, const float* 
                                      const float* fpn1, const float* queries, int nq, const float* prompt,
                                      const float* prompt_bias, int prompt_tokens, float* mask_logits, void* stream);
 
+/* ---- Quantized linear with GGML MMQ's exact arithmetic -------------------------
+ * Y = sum_b d_w[n][b] d_x[m][b] (q_w . q_x)_b + bias over 32-value blocks: the
+ * integer block dots exact on the tensor cores, the per-block rescale in f32
+ * (GGML CUDA mul_mat_q over Q8_0 weights and MMQ-D4 staged activations,
+ * verify_q8_mmq_dots.py:54-105).  No activation range limit beyond finiteness.
+ * The codes are held as f16 (tcgen05 kind::f16) or int8 (kind::i8). */
+enum { SAMQ_MMQ_CODES_F16 = 0, SAMQ_MMQ_CODES_I8 = 1 };
+typedef struct samq_mmq_weights samq_mmq_weights;
+
+/* Q8_0 GGUF rows (n rows of k values, k % 128 == 0) -> device codes + scales. */
+samq_status samq_mmq_weights_create_v1(int device, int type, int variant, int64_t k, int64_t n, const void* gguf_rows,
+                                       size_t bytes, void* stream, samq_mmq_weights** out);
+samq_status samq_mmq_weights_destroy_v1(samq_mmq_weights* weights);
+/* x [m][ldx] f32 (device) staged with the MMQ-D4 rule, then the exact GEMM;
+ * epilogue SAMQ_EPILOGUE_NONE or _GELU_ERF; y [m][ldy] f32. */
+samq_status samq_linear_mmq_v1(const samq_mmq_weights* weights, const float* x, int64_t m, int64_t ldx,
+                               const float* bias, int epilogue, float* y, int64_t ldy, void* stream);
+
 /* Host GGUF row quantizer (the role of tools/quantize/quantize_rows.cpp:210,
  * ggml_quantize_chunk): n rows of k f32 values (host) -> n packed rows (host,
  * bytes = n * row bytes).  Q8_0 is the reference converter's quantizer

@@ -909,6 +909,80 @@ samq_status samq_seg_head_forward_v1(const samq_seg_head_v1* head, const float* 
     });
 }
 
+samq_status samq_mmq_weights_create_v1(int device, int type, int variant, int64_t k, int64_t n, const void* gguf_rows,
+                                       size_t bytes, void* stream_ptr, samq_mmq_weights** out) {
+    return guarded([&] {
+        require(out != nullptr, "null output handle");
+        *out = nullptr;
+        require(type == SAMQ_TYPE_Q8_0, "the exact MMQ path takes Q8_0 weights");
+        require(variant == SAMQ_MMQ_CODES_F16 || variant == SAMQ_MMQ_CODES_I8, "unknown code variant");
+        require(k > 0 && k % 128 == 0 && k <= (int64_t(1) << 20), "width must be a positive multiple of 128");
+        require(n > 0 && n <= (int64_t(1) << 24), "row count out of range");
+        require(gguf_rows != nullptr && bytes == static_cast<size_t>(row_bytes(type, k) * n),
+                "GGUF payload size differs from n rows");
+        DeviceState& state = device_state(device);
+        (void)state;
+        DeviceGuard guard(device);
+        cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
+        auto* w = new samq_mmq_weights;
+        std::unique_ptr<samq_mmq_weights, void (*)(samq_mmq_weights*)> hold(w, [](samq_mmq_weights* p) {
+            if (p->codes) cudaFree(p->codes);
+            if (p->scales) cudaFree(p->scales);
+            delete p;
+        });
+        w->device = device;
+        w->variant = variant;
+        w->k = k;
+        w->n = n;
+        void* staging = nullptr;
+        check_cuda(cudaMalloc(&staging, bytes), "cudaMalloc(mmq staging)");
+        struct Free {
+            void* p;
+            ~Free() { cudaFree(p); }
+        } free_staging{staging};
+        check_cuda(cudaMalloc(&w->codes, static_cast<size_t>(n * k) * mmq_code_bytes(variant)), "cudaMalloc(codes)");
+        check_cuda(cudaMalloc(reinterpret_cast<void**>(&w->scales), static_cast<size_t>(n * (k / 32)) * sizeof(float)),
+                   "cudaMalloc(scales)");
+        check_cuda(cudaMemcpyAsync(staging, gguf_rows, bytes, cudaMemcpyHostToDevice, stream), "cudaMemcpyAsync(rows)");
+        launch_mmq_weights(variant, static_cast<const uint8_t*>(staging), n, k, w->codes, w->scales, stream);
+        check_cuda(cudaStreamSynchronize(stream), "cudaStreamSynchronize(mmq weights)");
+        *out = hold.release();
+    });
+}
+
+samq_status samq_mmq_weights_destroy_v1(samq_mmq_weights* w) {
+    return guarded([&] {
+        if (!w) return;
+        DeviceGuard guard(w->device);
+        if (w->codes) cudaFree(w->codes);
+        if (w->scales) cudaFree(w->scales);
+        delete w;
+    });
+}
+
+samq_status samq_linear_mmq_v1(const samq_mmq_weights* w, const float* x, int64_t m, int64_t ldx, const float* bias,
+                               int epilogue, float* y, int64_t ldy, void* stream_ptr) {
+    return guarded([&] {
+        require(w != nullptr && w->codes != nullptr, "null weights");
+        require(m > 0 && m <= (int64_t(1) << 24), "row count out of range");
+        require(ldx >= w->k && ldx % 4 == 0 && ldy >= w->n && ldy % 4 == 0, "leading dimensions");
+        require(x && y && aligned16(x) && aligned16(y), "x and y must be 16-byte aligned device pointers");
+        require(epilogue == SAMQ_EPILOGUE_NONE || epilogue == SAMQ_EPILOGUE_GELU_ERF, "unknown epilogue");
+        const int device = current_device();
+        require(w->device == device, "weights belong to another device");
+        DeviceState& state = device_state(device);
+        cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
+        const size_t code_bytes = static_cast<size_t>(m * w->k) * mmq_code_bytes(w->variant);
+        const size_t scale_bytes = static_cast<size_t>(m * (w->k / 32)) * sizeof(float);
+        Scratch& scratch = scratch_for(state, stream, code_bytes + scale_bytes + 512);
+        uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(scratch.ptr) + 255) & ~uintptr_t(255));
+        float* dx = reinterpret_cast<float*>(base + ((code_bytes + 255) & ~size_t(255)));
+        launch_mmq_stage(w->variant, x, m, w->k, ldx, base, dx, state.status, stream);
+        launch_mmq_gemm(w->variant, base, dx, w->codes, w->scales, m, w->n, w->k, bias,
+                        epilogue == SAMQ_EPILOGUE_GELU_ERF ? 1 : 0, y, ldy, state, stream);
+    });
+}
+
 samq_status samq_quantize_rows_v1(int type, int64_t k, int64_t n, const float* src, void* dst, size_t bytes) {
     return guarded([&] {
         require(supported_type(type), "weight type must be Q8_0, Q4_K, Q5_K or Q6_K");

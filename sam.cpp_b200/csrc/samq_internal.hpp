@@ -130,6 +130,15 @@ struct samq_dense {
     float* lo = nullptr;
 };
 
+// Weights of the exact MMQ path: codes [n][k] (f16 or int8), scales [k / 32][n].
+struct samq_mmq_weights {
+    int device = -1;
+    int variant = 0;
+    int64_t k = 0, n = 0;
+    void* codes = nullptr;
+    float* scales = nullptr;
+};
+
 // ---- launchers implemented in the .cu files -------------------------------
 namespace samq {
 
@@ -288,6 +297,16 @@ void launch_decoder(const samq_decoder_v1& dec, const float* enc, const float* e
                     const float* prompt, const float* prompt_bias, const float* prompt_valid, int64_t prompt_tokens,
                     float* queries_out, float* boxes, float* scores, float* presence, void* scratch,
                     DeviceState& state, cudaStream_t stream);
+
+// gemm_mmq.cu: quantized linear with GGML MMQ's exact arithmetic.
+size_t mmq_code_bytes(int variant);
+void launch_mmq_weights(int variant, const uint8_t* rows, int64_t n, int64_t k, void* codes, float* scales,
+                        cudaStream_t stream);
+void launch_mmq_stage(int variant, const float* x, int64_t rows, int64_t k, int64_t ld, void* codes, float* scales,
+                      DeviceStatus* status, cudaStream_t stream);
+void launch_mmq_gemm(int variant, const void* a_codes, const float* dx, const void* b_codes, const float* dw,
+                     int64_t m, int64_t n, int64_t k, const float* bias, int gelu, float* y, int64_t ldy,
+                     DeviceState& state, cudaStream_t stream);
 
 // seg.cu: the segmentation head and the geometry encoder.
 size_t seg_head_scratch_bytes(const samq_seg_head_v1& sh, int grid, int64_t queries, int64_t prompt_tokens, int sms);

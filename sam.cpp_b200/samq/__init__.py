@@ -174,6 +174,9 @@ SIGNATURES = {
                                         _vp, _vp]),
     "samq_sine_pe_2d_v1": (_i32, [_i32, _i32, _i32, _vp]),
     "samq_quantize_rows_v1": (_i32, [_i32, _i64, _i64, _vp, _vp, _sz]),
+    "samq_mmq_weights_create_v1": (_i32, [_i32, _i32, _i32, _i64, _i64, _vp, _sz, _vp, ctypes.POINTER(_vp)]),
+    "samq_mmq_weights_destroy_v1": (_i32, [_vp]),
+    "samq_linear_mmq_v1": (_i32, [_vp, _vp, _i64, _i64, _vp, _i32, _vp, _i64, _vp]),
     "samq_dense_create_v1": (_i32, [_i32, _i32, _i32, _i32, _i32, _i64, _i64, _vp, _sz, _vp, ctypes.POINTER(_vp)]),
     "samq_dense_destroy_v1": (_i32, [_vp]),
     "samq_dense_linear_v1": (_i32, [_vp, _vp, _i64, _i64, _vp, _i32, _vp, _i64, _vp]),
@@ -558,6 +561,41 @@ def quantize_rows(qtype: int, w):
     out = np.empty(n * row_bytes(qtype, k), np.uint8)
     _check(library().samq_quantize_rows_v1(qtype, k, n, w.ctypes.data, out.ctypes.data, out.nbytes))
     return out
+
+
+MMQ_CODES_F16, MMQ_CODES_I8 = 0, 1
+
+
+class MmqWeights:
+    """Q8_0 weights for the exact MMQ path (samq_mmq_weights*): integer codes
+    held as f16 (variant MMQ_CODES_F16) or int8 (MMQ_CODES_I8) plus f32 block
+    scales."""
+
+    def __init__(self, qtype: int, k: int, n: int, gguf_rows, variant: int = MMQ_CODES_F16, device: int = 0,
+                 stream=None):
+        import numpy as np
+        rows = np.ascontiguousarray(gguf_rows, dtype=np.uint8).reshape(-1)
+        handle = ctypes.c_void_p()
+        _check(library().samq_mmq_weights_create_v1(device, qtype, variant, k, n, rows.ctypes.data, rows.nbytes,
+                                                    _stream(stream), ctypes.byref(handle)))
+        self.handle, self.k, self.n, self.variant, self.device = handle, k, n, variant, device
+
+    def close(self):
+        if self.handle:
+            _check(library().samq_mmq_weights_destroy_v1(self.handle))
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+def linear_mmq(w: MmqWeights, x, m: int, ldx: int, bias, epilogue: int, y, ldy: int, stream=None):
+    """samq_linear_mmq_v1: y = epilogue(x W^T + bias) with GGML MMQ's exact arithmetic."""
+    _check(library().samq_linear_mmq_v1(w.handle, _addr(x), m, ldx, _addr(bias), epilogue, _addr(y), ldy,
+                                        _stream(stream)))
 
 
 def sine_pe_2d(h: int, w: int, d: int):
