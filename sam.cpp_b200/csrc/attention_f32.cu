@@ -271,6 +271,11 @@ struct AttnGenArgs {
     int64_t ldq, ldk, ldv, ldo, bias_h, bias_q;
     int lq, lk, causal;
     float scale;
+    // Key split (few queries, many keys): CTA z covers keys [z kps, (z + 1) kps)
+    // and writes its unnormalized output and (max, sum) to part
+    // [splits][heads][lq][HD + 2]; attention_combine_kernel merges them.
+    float* part;
+    int kps;
 };
 
 template <int HD>
@@ -302,8 +307,13 @@ __global__ void __launch_bounds__(kF32Threads, 2) attention_gen_kernel(AttnGenAr
     }
     int kend = a.lk;
     if (a.causal) kend = min(kend, q0 + kTile);
+    int kb_begin = 0;
+    if (a.part != nullptr) {
+        kb_begin = static_cast<int>(blockIdx.z) * (a.kps / kTile);
+        kend = min(kend, static_cast<int>(blockIdx.z + 1) * a.kps);
+    }
     const int kblocks = (kend + kTile - 1) / kTile;
-    for (int kb = 0; kb < kblocks; ++kb) {
+    for (int kb = kb_begin; kb < kblocks; ++kb) {
         __syncthreads();
         for (int idx = t; idx < kTile * (HD / 4); idx += kF32Threads) {
             const int r = idx / (HD / 4), c4 = idx % (HD / 4), n = kb * kTile + r;
@@ -398,10 +408,66 @@ __global__ void __launch_bounds__(kF32Threads, 2) attention_gen_kernel(AttnGenAr
     for (int i = 0; i < 4; ++i) {
         const int n = q0 + 4 * rq + i;
         if (n >= a.lq) continue;
+        if (a.part != nullptr) {
+            float* row = a.part + ((int64_t(blockIdx.z) * gridDim.y + h) * a.lq + n) * (HD + 2);
+#pragma unroll
+            for (int j = 0; j < kJ; ++j) row[u + 16 * j] = o[i][j];
+            if (u == 0) {
+                row[HD] = m[i];
+                row[HD + 1] = l[i];
+            }
+            continue;
+        }
         float* row = a.out + int64_t(n) * a.ldo + h * HD;
 #pragma unroll
         for (int j = 0; j < kJ; ++j) row[u + 16 * j] = l[i] > 0.0f ? __fdiv_rn(o[i][j], l[i]) : 0.0f;
     }
+}
+
+// Merges the key splits of attention_gen_kernel: one warp per (head, query),
+// M = max_s m_s, L = sum_s l_s e^(m_s - M), out = sum_s o_s e^(m_s - M) / L
+// (0 for a row whose keys are all masked), the online softmax's own rescale.
+template <int HD>
+__global__ void __launch_bounds__(256) attention_combine_kernel(const float* __restrict__ part, int splits, int heads,
+                                                                int lq, float* __restrict__ out, int64_t ldo) {
+    pdl_wait();
+    pdl_trigger();
+    const int lane = threadIdx.x & 31;
+    const int64_t row = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+    if (row >= int64_t(heads) * lq) return;
+    const int h = static_cast<int>(row / lq), n = static_cast<int>(row % lq);
+    const int64_t split_stride = int64_t(heads) * lq * (HD + 2);
+    const float* base = part + row * (HD + 2);
+    float mx = -INFINITY;
+    for (int s = 0; s < splits; ++s) mx = fmaxf(mx, base[s * split_stride + HD]);
+    const float m_use = mx == -INFINITY ? 0.0f : mx;
+    constexpr int kC = HD / 32;
+    float acc[kC], sum = 0.0f;
+#pragma unroll
+    for (int c = 0; c < kC; ++c) acc[c] = 0.0f;
+    for (int s = 0; s < splits; ++s) {
+        const float* p = base + s * split_stride;
+        const float w = expf(p[HD] - m_use);
+        sum = fmaf(p[HD + 1], w, sum);
+#pragma unroll
+        for (int c = 0; c < kC; ++c) acc[c] = fmaf(p[lane + 32 * c], w, acc[c]);
+    }
+    float* dst = out + int64_t(n) * ldo + h * HD;
+#pragma unroll
+    for (int c = 0; c < kC; ++c) dst[lane + 32 * c] = sum > 0.0f ? __fdiv_rn(acc[c], sum) : 0.0f;
+}
+
+// Key splits for lq queries x lk keys over `heads`: enough CTAs for two per SM
+// when the query tiles alone do not fill the GPU, at least 2 key tiles each.
+int key_splits(int lq, int lk, int heads, int causal, int sms) {
+    if (causal) return 1;
+    const int ctas = (lq + kTile - 1) / kTile * heads;
+    const int tiles = (lk + kTile - 1) / kTile;
+    if (ctas >= sms || tiles < 4) return 1;
+    int splits = std::min({(2 * sms + ctas - 1) / ctas, tiles / 2, 64});
+    if (splits < 2) return 1;
+    const int per = (tiles + splits - 1) / splits;
+    return (tiles + per - 1) / per;
 }
 
 GeometryF32 make_geometry_f32(int grid_w, int grid_h, int heads, int window, int batch, bool window_major) {
@@ -433,23 +499,45 @@ void launch_attention_f32(const float* qkv, int64_t ldq, bool qkv_window_major, 
     }
 }
 
+size_t attention_partial_floats(int lq, int lk, int heads, int head_dim, int causal, int sms) {
+    const int splits = key_splits(lq, lk, heads, causal, sms);
+    return splits > 1 ? static_cast<size_t>(splits) * heads * lq * (head_dim + 2) : 0;
+}
+
 void launch_attention_gen(const float* q, int64_t ldq, const float* k, int64_t ldk, const float* v, int64_t ldv,
                           int lq, int lk, int heads, int head_dim, float scale, int causal, const float* bias,
                           int64_t bias_h, int64_t bias_q, float* out, int64_t ldo, DeviceState& state,
-                          cudaStream_t stream) {
+                          cudaStream_t stream, float* partials, size_t partial_floats) {
     if (lq == 0) return;
-    AttnGenArgs a{q, k, v, bias, out, ldq, ldk, ldv, ldo, bias_h, bias_q, lq, lk, causal, scale};
-    const dim3 grid((lq + kTile - 1) / kTile, heads);
+    AttnGenArgs a{q, k, v, bias, out, ldq, ldk, ldv, ldo, bias_h, bias_q, lq, lk, causal, scale, nullptr, 0};
+    int splits = key_splits(lq, lk, heads, causal, state.sm_count);
+    if (partials == nullptr || partial_floats < attention_partial_floats(lq, lk, heads, head_dim, causal, state.sm_count))
+        splits = 1;
+    if (splits > 1) {
+        const int tiles = (lk + kTile - 1) / kTile;
+        a.kps = (tiles + splits - 1) / splits * kTile;
+        a.part = partials;
+    }
+    const dim3 grid((lq + kTile - 1) / kTile, heads, splits);
+    const unsigned combine_blocks = static_cast<unsigned>((int64_t(heads) * lq * 32 + 255) / 256);
     if (head_dim == 64) {
         constexpr int smem = (2 * kTile * 68 + 64 * kPitch + kTile * kPitch) * 4;
         set_smem_limit_once(state, reinterpret_cast<const void*>(attention_gen_kernel<64>), smem,
                             "cudaFuncSetAttribute(attention_gen smem)");
         launch_pdl(attention_gen_kernel<64>, grid, dim3(kF32Threads), smem, stream, "attention_gen_kernel launch", a);
+        if (splits > 1)
+            launch_pdl(attention_combine_kernel<64>, dim3(combine_blocks), dim3(256), 0, stream,
+                       "attention_combine_kernel launch", static_cast<const float*>(partials), splits, heads, lq, out,
+                       ldo);
     } else {
         constexpr int smem = (2 * kTile * 36 + 32 * kPitch + kTile * kPitch) * 4;
         set_smem_limit_once(state, reinterpret_cast<const void*>(attention_gen_kernel<32>), smem,
                             "cudaFuncSetAttribute(attention_gen smem)");
         launch_pdl(attention_gen_kernel<32>, grid, dim3(kF32Threads), smem, stream, "attention_gen_kernel launch", a);
+        if (splits > 1)
+            launch_pdl(attention_combine_kernel<32>, dim3(combine_blocks), dim3(256), 0, stream,
+                       "attention_combine_kernel launch", static_cast<const float*>(partials), splits, heads, lq, out,
+                       ldo);
     }
 }
 

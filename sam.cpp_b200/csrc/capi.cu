@@ -718,8 +718,12 @@ samq_status samq_attention_v1(const float* q, int64_t ldq, const float* k, int64
         if (lq == 0) return;
         require(q && k && v && out && aligned16(q) && aligned16(k) && aligned16(v), "q, k, v must be 16-byte aligned");
         DeviceState& state = device_state(current_device());
+        cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
+        const size_t part = attention_partial_floats(lq, lk, heads, head_dim, causal, state.sm_count);
+        float* partials = nullptr;
+        if (part > 0) partials = static_cast<float*>(scratch_for(state, stream, part * sizeof(float)).ptr);
         launch_attention_gen(q, ldq, k, ldk, v, ldv, lq, lk, heads, head_dim, scale, causal, bias, bias_h, bias_q,
-                             out, ldo, state, static_cast<cudaStream_t>(stream_ptr));
+                             out, ldo, state, stream, partials, part);
     });
 }
 

@@ -141,6 +141,15 @@ __global__ void __launch_bounds__(256) dot_score_kernel(const float* __restrict_
 
 }  // namespace
 
+// Key-split partials of the decoder's attentions (self over nq + 1 queries,
+// image cross-attention over enc_tokens keys), one buffer reused by both.
+size_t decoder_attention_partials(const samq_decoder_v1& dec, int64_t enc_tokens, int sms) {
+    const int64_t D = linear_in(dec.layer[0].sa_in_proj);
+    const int heads = dec.heads, hd = static_cast<int>(D / heads), nq1 = dec.queries + 1;
+    return std::max(attention_partial_floats(nq1, nq1, heads, hd, 0, sms),
+                    attention_partial_floats(nq1, static_cast<int>(enc_tokens), heads, hd, 0, sms));
+}
+
 size_t decoder_scratch_bytes(const samq_decoder_v1& dec, int64_t enc_tokens, int64_t prompt_tokens, int grid,
                              int sms) {
     const int64_t D = linear_in(dec.layer[0].sa_in_proj), nq = dec.queries, F = linear_out(dec.layer[0].linear1);
@@ -164,7 +173,8 @@ size_t decoder_scratch_bytes(const samq_decoder_v1& dec, int64_t enc_tokens, int
     const size_t floats = static_cast<size_t>(nq + 1) * D * 8 + (nq + 1) * F + nq * 512 + nq * 4 * 2 +
                           static_cast<size_t>(enc_tokens) * D * 3 + prompt_tokens * (2 * D + Fp) +
                           static_cast<size_t>(nq) * grid * (hidden + 16) * 2 +
-                          static_cast<size_t>(heads) * (nq + 1) * grid * grid + D * 4 + nq * 2;
+                          static_cast<size_t>(heads) * (nq + 1) * grid * grid + D * 4 + nq * 2 +
+                          decoder_attention_partials(dec, enc_tokens, sms);
     return floats * sizeof(float) + linear + 40 * 256;
 }
 
@@ -206,6 +216,8 @@ void launch_decoder(const samq_decoder_v1& dec, const float* enc, const float* e
     float* bias = take(int64_t(heads) * nq1 * grid * grid);
     float* pooled = take(D * 4);
     float* hsp = take(nq * D);
+    const size_t part_floats = decoder_attention_partials(dec, enc_tokens, state.sm_count);
+    float* part = take(static_cast<int64_t>(part_floats));
     void* lin = reinterpret_cast<void*>(cursor);
     auto linear = [&](const samq_linear_ref_v1& l, int64_t row0, int64_t rows, const float* x, int64_t ldx, int64_t m,
                       float* out, int64_t ldo) {
@@ -252,7 +264,7 @@ void launch_decoder(const samq_decoder_v1& dec, const float* enc, const float* e
         linear(ly.sa_in_proj, 0, 2 * D, qin, D, nq1, qk, 2 * D);
         linear(ly.sa_in_proj, 2 * D, D, q, D, nq1, v, D);
         launch_attention_gen(qk, 2 * D, qk + D, 2 * D, v, D, nq1, nq1, heads, hd, scale, 0, nullptr, 0, 0, att, D,
-                             state, stream);
+                             state, stream, part, part_floats);
         linear(ly.sa_out_proj, 0, D, att, D, nq1, y, D);
         launch_add_rows(q, D, y, D, nq1, static_cast<int>(D), stream);
         launch_layer_norm_f32(q, nq1, static_cast<int>(D), D, ly.norm2_w, ly.norm2_b, q, D, 1e-5f, stream);
@@ -272,7 +284,7 @@ void launch_decoder(const samq_decoder_v1& dec, const float* enc, const float* e
         linear(ly.ca_in_proj, D, D, kin, D, enc_tokens, kimg, D);
         linear(ly.ca_in_proj, 2 * D, D, enc, D, enc_tokens, vimg, D);
         launch_attention_gen(qk, D, kimg, D, vimg, D, nq1, static_cast<int>(enc_tokens), heads, hd, scale, 0, bias,
-                             int64_t(nq1) * grid * grid, int64_t(grid) * grid, att, D, state, stream);
+                             int64_t(nq1) * grid * grid, int64_t(grid) * grid, att, D, state, stream, part, part_floats);
         linear(ly.ca_out_proj, 0, D, att, D, nq1, y, D);
         launch_add_rows(q, D, y, D, nq1, static_cast<int>(D), stream);
         launch_layer_norm_f32(q, nq1, static_cast<int>(D), D, ly.norm1_w, ly.norm1_b, q, D, 1e-5f, stream);

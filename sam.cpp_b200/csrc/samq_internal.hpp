@@ -188,10 +188,13 @@ void launch_attention_f32(const float* qkv, int64_t ldq, bool qkv_window_major, 
 // General F32 attention (attention_f32.cu): Q [lq][ldq], K / V [lk][ld],
 // head h at columns h*head_dim (head_dim 32 or 64), additive bias
 // bias[h*bias_h + q*bias_q + k] (nullable), causal mask, out [lq][ldo].
+// With few query tiles and many keys the keys are split over CTAs when the
+// caller provides `partials` of attention_partial_floats(...) floats.
+size_t attention_partial_floats(int lq, int lk, int heads, int head_dim, int causal, int sms);
 void launch_attention_gen(const float* q, int64_t ldq, const float* k, int64_t ldk, const float* v, int64_t ldv,
                           int lq, int lk, int heads, int head_dim, float scale, int causal, const float* bias,
                           int64_t bias_h, int64_t bias_q, float* out, int64_t ldo, DeviceState& state,
-                          cudaStream_t stream);
+                          cudaStream_t stream, float* partials = nullptr, size_t partial_floats = 0);
 // sam3_apply_rope on [head_batches][tokens][64] f32 with GGML's rounding.
 void launch_rope_f32(const float* x, const float* freqs, int64_t tokens, int64_t head_batches, float* out,
                      cudaStream_t stream);

@@ -304,8 +304,10 @@ size_t geometry_scratch_bytes(const samq_geometry_encoder_v1& ge, int64_t tokens
             linear = std::max(linear, linear_scratch_bytes(*l, 1, sms));
         linear = std::max(linear, linear_scratch_bytes(ly.ca_in_proj, tokens, sms));
     }
-    // x, xn, qkv(3D), att, y, ffn(F) for the token; kin, k, v [T][D]
-    const size_t floats = static_cast<size_t>(D) * 7 + F + static_cast<size_t>(tokens) * D * 3;
+    // x, xn, qkv(3D), att, y, ffn(F) for the token; kin, k, v [T][D]; key-split partials
+    const size_t floats = static_cast<size_t>(D) * 7 + F + static_cast<size_t>(tokens) * D * 3 +
+                          attention_partial_floats(1, static_cast<int>(tokens), ge.heads,
+                                                   static_cast<int>(D / ge.heads), 0, sms);
     return floats * sizeof(float) + linear + 16 * 256;
 }
 
@@ -330,6 +332,8 @@ void launch_geometry_encoder(const samq_geometry_encoder_v1& ge, const float* im
     float* kin = take(tokens * D);
     float* k = take(tokens * D);
     float* v = take(tokens * D);
+    const size_t part_floats = attention_partial_floats(1, static_cast<int>(tokens), heads, hd, 0, state.sm_count);
+    float* part = take(static_cast<int64_t>(part_floats));
     void* lin = reinterpret_cast<void*>(cursor);
     auto linear = [&](const samq_linear_ref_v1& l, int64_t row0, int64_t rows, const float* in, int64_t m,
                       float* o) { apply_linear(l, row0, rows, in, D, m, SAMQ_EPILOGUE_NONE, o, rows, lin, state, stream); };
@@ -352,7 +356,7 @@ void launch_geometry_encoder(const samq_geometry_encoder_v1& ge, const float* im
         linear(ly.ca_in_proj, D, D, kin, tokens, k);
         linear(ly.ca_in_proj, 2 * D, D, image, tokens, v);
         launch_attention_gen(qkv, D, k, D, v, D, 1, static_cast<int>(tokens), heads, hd, scale, 0, nullptr, 0, 0, att,
-                             D, state, stream);
+                             D, state, stream, part, part_floats);
         linear(ly.ca_out_proj, 0, D, att, 1, y);
         launch_add_rows(x, D, y, D, 1, static_cast<int>(D), stream);
         // ReLU FFN.

@@ -73,10 +73,12 @@ def test_precision_probe_reference_cases(dims, queries, keys, masked):
 
 @pytest.mark.parametrize("lq,lk,heads,hd,mode", [
     (32, 32, 16, 64, "causal"), (200, 5184, 8, 32, "rpb"), (5184, 33, 8, 32, "padding"), (201, 201, 8, 32, "none"),
-    (70, 45, 3, 64, "rpb")])
+    (70, 45, 3, 64, "rpb"), (1, 5184, 8, 32, "none"), (3, 700, 16, 64, "padding"), (40, 512, 4, 32, "tailmask")])
 def test_attention_parity_random(lq, lk, heads, hd, mode):
     """Random Q / K / V with each mask form against oracle.attention_gen:
-    cosine >= 1 - 1e-10 and normalized max error <= 1e-5 (F32 level)."""
+    cosine >= 1 - 1e-10 and normalized max error <= 1e-5 (F32 level).  The
+    few-query cases run with the keys split over CTAs and merged; "tailmask"
+    masks every key from 100 on, so whole key splits are empty."""
     rng = np.random.default_rng(lq + lk + heads)
     q = rng.normal(0, 1, (lq, heads * hd)).astype(np.float32)
     k = rng.normal(0, 1, (lk, heads * hd)).astype(np.float32)
@@ -88,6 +90,8 @@ def test_attention_parity_random(lq, lk, heads, hd, mode):
         bias_h, bias_q = lq * lk, lk
     elif mode == "padding":
         bias = np.where(np.arange(lk) >= lk - 7, -np.inf, 0.0).astype(np.float32)
+    elif mode == "tailmask":
+        bias = np.where(np.arange(lk) >= 100, -np.inf, 0.0).astype(np.float32)
     got = _run_attention(q, k, v, heads, hd, scale, causal=causal, bias=bias, bias_h=bias_h, bias_q=bias_q)
     ref = o.attention_gen(q, k, v, heads, hd, scale, causal=causal, bias=bias)
     g, r = got.astype(np.float64).ravel(), ref.astype(np.float64).ravel()
