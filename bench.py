@@ -519,6 +519,11 @@ def main():
                                "stream after a 256 MB read that flushes L2 (clean lines, no write-back in the "
                                "timed launch); achieved = sum 2MNK / sum of the average launch times"}
 
+    # The exact-MMQ-arithmetic GEMM (gemm_mmq.cu) beside K2 on the same four
+    # shapes with Q8_0 weights: integer codes on kind::f16 and on kind::i8.
+    mmq = mmq_section(samq, torch, stream, max_over_ranks, xs, ys, biases, rank, args.warmup, world, pk)
+    samq.check(local, stream)
+
     # The SimpleFPN neck (F32 semantics, dense.cu) on this image's 72 x 72 ViT
     # output: a secondary figure beside the quantized backbone.
     neck = neck_section(samq, torch, stream, args, max_over_ranks, pk)
@@ -578,6 +583,7 @@ def main():
             "sweep64": sweep,
             "f32_mode": f32_mode,
             "image_path": image_path,
+            "mmq": mmq,
         }
         print(json.dumps(line), flush=True)
     for w in weights:
@@ -675,6 +681,44 @@ def sweep64_section(samq, torch, stream, max_over_ranks, blocks, prefix, world, 
             "scaling": "strong", "images": n_images, "images_this_rank": end - start, "batch_per_gpu": batch,
             "ms": ms, "features_finite": bool(torch.isfinite(xb).all().item()),
             "gpu_launches": (end - start) * 4 + len(own) * DEPTH * 7}
+
+
+def mmq_section(samq, torch, stream, max_over_ranks, xs, ys, biases, rank, warmup, world, pk, reps=100):
+    """samq_linear_mmq_v1 (GGML MMQ's exact arithmetic: MMQ-D4 staging + the
+    per-block-rescaled integer GEMM) on the four ViT-block shapes at M = 5184
+    with Q8_0 weights, both code variants, each call timed back to back (D4
+    staging included, as `qgemm` includes K1).  The int8 variant is quoted
+    against the nominal dense int8 peak (4.5 POPS; no measured int8 figure
+    exists for this pool), both against the measured bf16 burst."""
+    out = {}
+    for variant, name in ((samq.MMQ_CODES_F16, "codes_f16_kind_f16"), (samq.MMQ_CODES_I8, "codes_i8_kind_i8")):
+        per, total_ms = {}, 0.0
+        for i, (lname, n, k, qtype, epi, seed) in enumerate(LINEARS):
+            packed, _ = make_weights(samq.quantize_rows, n, k, 8, seed + 4 * rank)
+            w = samq.MmqWeights(8, k, n, packed, variant=variant)
+            for _ in range(warmup):
+                samq.linear_mmq(w, xs[i], M, k, biases[i], epi, ys[i], n, stream)
+            torch.cuda.synchronize()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(stream)
+            for _ in range(reps):
+                samq.linear_mmq(w, xs[i], M, k, biases[i], epi, ys[i], n, stream)
+            b.record(stream)
+            torch.cuda.synchronize()
+            ms = max_over_ranks(a.elapsed_time(b) / reps)
+            total_ms += ms
+            tops = 2.0 * M * n * k / (ms / 1e3) / 1e12
+            per[lname] = {"us": ms * 1e3, "tops": tops, "frac_bf16_burst": tops / pk["bf16_tflops"]}
+            if variant == samq.MMQ_CODES_I8:
+                per[lname]["frac_int8_nominal"] = tops / 4500.0
+            w.close()
+        ops = step_ops()
+        out[name] = {"tops_four_linears": ops / (total_ms / 1e3) / 1e12 * world, "ms_four_linears": total_ms,
+                     "per_linear": per}
+    out["what"] = ("exact GGML MMQ arithmetic: integer codes on the tensor cores, one TMEM slot per 32-value block, "
+                   "f32 per-block rescale in the epilogue (2 f32 operations per output per block); compare "
+                   "`qgemm` (K2, f16 decoded operands, same shapes, K1 included)")
+    return out
 
 
 def image_path_section(samq, torch, stream, max_over_ranks, world, rank, local, dist, steps=4):
