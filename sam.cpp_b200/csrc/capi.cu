@@ -921,7 +921,7 @@ samq_status samq_mmq_weights_create_v1(int device, int type, int variant, int64_
         require(type == SAMQ_TYPE_Q8_0, "the exact MMQ path takes Q8_0 weights");
         require(variant == SAMQ_MMQ_CODES_F16 || variant == SAMQ_MMQ_CODES_I8, "unknown code variant");
         require(k > 0 && k % 128 == 0 && k <= (int64_t(1) << 20), "width must be a positive multiple of 128");
-        require(n > 0 && n <= (int64_t(1) << 24), "row count out of range");
+        require(n > 0 && n % 2 == 0 && n <= (int64_t(1) << 24), "row count must be even and in range");
         require(gguf_rows != nullptr && bytes == static_cast<size_t>(row_bytes(type, k) * n),
                 "GGUF payload size differs from n rows");
         DeviceState& state = device_state(device);

@@ -18,9 +18,13 @@
 //   CODES_I8   the codes as int8: tcgen05.mma kind::i8, K = 32, one MMA per
 //              block, s32 accumulator, converted by the epilogue.
 // Every block's accumulator has to be drained and rescaled: 2 f32 operations
-// per output value per block (a packed f32x2 multiply and fused add), so the
-// epilogue, not the tensor core, sets the pace.  This is the trade the f16
-// path avoids; the kernel measures it.
+// per output value per block, 256 FMA-pipe cycles per 128 x 128 block on an
+// SM against 128 tensor cycles for the f16 MMAs (64 for int8), so the
+// epilogue, not the tensor core, sets the pace.  Measured on B200 at the
+// ViT-block shapes: ~0.2 of K2's speed for both variants alike (instruction
+// issue bound, tensor pipe ~4% active): the int8 rate cannot be used behind
+// a per-block drain, which is why K2 folds the scales into f16 operands.
+// This path is the exact-arithmetic option (and has no activation range limit).
 //
 // Persistent, warp-specialised, one CTA per SM, 320 threads:
 //   warp 0   TMA producer: 128-row A code tiles and 128-row B code tiles,
@@ -41,9 +45,17 @@ namespace {
 
 constexpr int QM = 128, QN = 128;
 constexpr int kSlots = 4;
-constexpr int kQEpiWarps = 8;
+constexpr int kQEpiWarps = 8;                  // two per TMEM lane quarter
+constexpr int kQCols = QN / (kQEpiWarps / 4);  // columns of a tile per epilogue warp
 constexpr int kQThreads = 64 + 32 * kQEpiWarps;
 constexpr int kQOutChunk = 32 * 32 * 4;
+// Per epilogue warp, a ring of kScaleDepth blocks' scales (64 weight scales of
+// its columns, 32 activation scales of its rows) filled by cp.async
+// kScaleDepth - 1 blocks ahead of use, so no global load latency sits on a
+// block's path.
+constexpr int kScaleDepth = 4;
+constexpr int kScaleEntry = kQCols + 32;       // weight scales of its columns, activation scales of its rows
+constexpr int kScaleRing = kScaleDepth * kScaleEntry * 4;
 constexpr uint32_t kQTmemCols = kSlots * QN;
 
 template <int VARIANT>
@@ -54,11 +66,12 @@ struct MmqShape {
     static constexpr int k_mma = 32 / elem;               // K of one MMA instruction
     static constexpr int mma_per_block = 32 / k_mma;
     static constexpr int tile_bytes = QM * 128;           // A or B tile of one stage
-    static constexpr int stages = 6;
+    static constexpr int stages = 5;
     static constexpr int a_off = 0;
     static constexpr int b_off = stages * tile_bytes;
     static constexpr int out_off = b_off + stages * tile_bytes;
-    static constexpr int bar_off = out_off + kQEpiWarps * kQOutChunk;
+    static constexpr int scale_off = out_off + kQEpiWarps * kQOutChunk;
+    static constexpr int bar_off = scale_off + kQEpiWarps * kScaleRing;
     static constexpr int bar_bytes = (2 * stages + 2 * kSlots + 1) * 8 + 8;
     static constexpr int total = bar_off + bar_bytes + 1024;
 };
@@ -70,6 +83,22 @@ __host__ __device__ constexpr uint32_t idesc_codes(int variant, int m, int n) {
                ? (2u << 4) | (1u << 7) | (1u << 10) | (static_cast<uint32_t>(n >> 3) << 17) |
                      (static_cast<uint32_t>(m >> 4) << 24)
                : (1u << 4) | (static_cast<uint32_t>(n >> 3) << 17) | (static_cast<uint32_t>(m >> 4) << 24);
+}
+
+__device__ __forceinline__ void cp_async_8(void* smem_dst, const void* src, bool valid) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 8, %2;" ::"r"(smem_u32(smem_dst)), "l"(src),
+                 "r"(valid ? 8 : 0)
+                 : "memory");
+}
+__device__ __forceinline__ void cp_async_4(void* smem_dst, const void* src, bool valid) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(smem_u32(smem_dst)), "l"(src),
+                 "r"(valid ? 4 : 0)
+                 : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
 }
 
 __device__ __forceinline__ void tc_mma_codes(int variant, uint32_t tmem_d, uint64_t adesc, uint64_t bdesc,
@@ -84,24 +113,6 @@ __device__ __forceinline__ void tc_mma_codes(int variant, uint32_t tmem_d, uint6
     } else {
         tc_mma_f16(tmem_d, adesc, bdesc, idesc, accumulate);
     }
-}
-
-// acc += t * s for two f32 pairs (packed f32x2 FMA on sm_100).
-__device__ __forceinline__ void fma2(float& a0, float& a1, float t0, float t1, float s0, float s1) {
-    uint64_t acc, t, s;
-    asm("mov.b64 %0, {%1, %2};" : "=l"(acc) : "f"(a0), "f"(a1));
-    asm("mov.b64 %0, {%1, %2};" : "=l"(t) : "f"(t0), "f"(t1));
-    asm("mov.b64 %0, {%1, %2};" : "=l"(s) : "f"(s0), "f"(s1));
-    asm("fma.rn.f32x2 %0, %1, %2, %0;" : "+l"(acc) : "l"(t), "l"(s));
-    asm("mov.b64 {%0, %1}, %2;" : "=f"(a0), "=f"(a1) : "l"(acc));
-}
-
-__device__ __forceinline__ void mul2(float& r0, float& r1, float a0, float a1, float b) {
-    uint64_t r, a, bb;
-    asm("mov.b64 %0, {%1, %2};" : "=l"(a) : "f"(a0), "f"(a1));
-    asm("mov.b64 %0, {%1, %1};" : "=l"(bb) : "f"(b));
-    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(bb));
-    asm("mov.b64 {%0, %1}, %2;" : "=f"(r0), "=f"(r1) : "l"(r));
 }
 
 struct MmqArgs {
@@ -233,74 +244,84 @@ gemm_mmq_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant
         }
     } else {
         const int quarter = warp & 3;
-        const int half = (warp - 2) >> 2;  // columns 64 * half .. + 63 of the tile
+        const int part = (warp - 2) >> 2;  // columns kQCols * part .. of the tile
         uint8_t* stage_buf = sout + (warp - 2) * kQOutChunk;
+        float* ring = reinterpret_cast<float*>(smem + S::scale_off + (warp - 2) * kScaleRing);
+        // Block g of this warp's stream (its tiles' blocks in order) -> ring
+        // entry g % kScaleDepth: 64 weight scales, then 32 activation scales.
+        const int my_tiles = blockIdx.x < tiles ? (tiles - 1 - blockIdx.x) / gridDim.x + 1 : 0;
+        const uint32_t total_blocks = static_cast<uint32_t>(my_tiles) * nblocks;
+        auto prefetch = [&](uint32_t gb) {
+            if (gb < total_blocks) {
+                const int t = blockIdx.x + static_cast<int>(gb / nblocks) * gridDim.x;
+                const int b = static_cast<int>(gb % nblocks);
+                const int tm = t / n_tiles, tn = t % n_tiles;
+                const int r = tm * QM + quarter * 32 + lane;
+                float* e = ring + (gb % kScaleDepth) * kScaleEntry;
+                if (kQCols == 64) {
+                    const int c = tn * QN + part * 64 + 2 * lane;
+                    cp_async_8(e + 2 * lane, args.dw + static_cast<int64_t>(b) * n + (c + 1 < n ? c : 0), c + 1 < n);
+                } else {
+                    const int c = tn * QN + part * kQCols + lane;
+                    cp_async_4(e + lane, args.dw + static_cast<int64_t>(b) * n + (c < n ? c : 0), c < n);
+                }
+                cp_async_4(e + kQCols + lane, args.dx + static_cast<int64_t>(b) * m + (r < m ? r : 0), r < m);
+            }
+            cp_async_commit();  // an empty group keeps the wait count uniform
+        };
+        // n is even for Q8_0 rows of whole blocks (n % 2 == 0 is checked by the host).
+        for (uint32_t gb = 0; gb < kScaleDepth - 1; ++gb) prefetch(gb);
         uint32_t g = 0;
         bool ok = true;
         for (int tile = blockIdx.x; tile < tiles && ok; tile += gridDim.x) {
             const int mt = tile / n_tiles, nt = tile % n_tiles;
             const int row0 = mt * QM + quarter * 32;
-            const int row = row0 + lane;
-            const int col_base = nt * QN + half * 64;
-            float acc[64];
+            const int col_base = nt * QN + part * kQCols;
+            float acc[kQCols];
 #pragma unroll
-            for (int i = 0; i < 64; ++i) acc[i] = 0.0f;
+            for (int i = 0; i < kQCols; ++i) acc[i] = 0.0f;
             for (int b = 0; b < nblocks; ++b, ++g) {
                 const int slot = static_cast<int>(g % kSlots);
-                // The row's activation scale and the 64 columns' weight scales
-                // of this block, issued before the wait for the slot.
-                const float dx = row < m ? __ldg(args.dx + static_cast<int64_t>(b) * m + row) : 0.0f;
-                const float* dwp = args.dw + static_cast<int64_t>(b) * n + col_base;
+                prefetch(g + kScaleDepth - 1);
+                cp_async_wait<kScaleDepth - 1>();
+                __syncwarp();
+                const float* e = ring + (g % kScaleDepth) * kScaleEntry;
+                const float dx = e[kQCols + lane];
                 // Warp-uniform wait: tcgen05.ld is warp-collective.
                 if (!__all_sync(0xffffffffu, mbar_wait(&slot_full[slot], (g / kSlots) & 1u, status, 66))) {
                     ok = false;
                     break;
                 }
                 tc_fence_after();
-                uint32_t t0[32], t1[32];
+                uint32_t t[kQCols];
                 const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) +
-                                       static_cast<uint32_t>(slot * QN + half * 64);
-                tc_ld_32x32b_x32(taddr, t0);
-                tc_ld_32x32b_x32(taddr + 32, t1);
+                                       static_cast<uint32_t>(slot * QN + part * kQCols);
+#pragma unroll
+                for (int h = 0; h < kQCols / 32; ++h)
+                    tc_ld_32x32b_x32(taddr + 32 * h, *reinterpret_cast<uint32_t(*)[32]>(t + 32 * h));
                 tc_wait_ld();
                 tc_fence_before();
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&slot_empty[slot]);
 #pragma unroll
-                for (int c4 = 0; c4 < 16; ++c4) {
+                for (int c4 = 0; c4 < kQCols / 4; ++c4) {
                     const int c = c4 * 4;
-                    float4 w = make_float4(0.f, 0.f, 0.f, 0.f);
-                    if (col_base + c + 3 < n) {
-                        w = __ldg(reinterpret_cast<const float4*>(dwp + c));
-                    } else {
-                        if (col_base + c < n) w.x = __ldg(dwp + c);
-                        if (col_base + c + 1 < n) w.y = __ldg(dwp + c + 1);
-                        if (col_base + c + 2 < n) w.z = __ldg(dwp + c + 2);
+                    const float4 w = *reinterpret_cast<const float4*>(e + c);
+                    const uint32_t* src = t + c;
+                    const float ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {
+                        const float v = VARIANT == SAMQ_MMQ_CODES_I8 ? static_cast<float>(static_cast<int32_t>(src[j]))
+                                                                     : __uint_as_float(src[j]);
+                        acc[c + j] = fmaf(v, ws[j] * dx, acc[c + j]);
                     }
-                    float s0, s1, s2, s3;
-                    mul2(s0, s1, w.x, w.y, dx);
-                    mul2(s2, s3, w.z, w.w, dx);
-                    const uint32_t* src = c < 32 ? t0 + c : t1 + (c - 32);
-                    float v0, v1, v2, v3;
-                    if (VARIANT == SAMQ_MMQ_CODES_I8) {
-                        v0 = static_cast<float>(static_cast<int32_t>(src[0]));
-                        v1 = static_cast<float>(static_cast<int32_t>(src[1]));
-                        v2 = static_cast<float>(static_cast<int32_t>(src[2]));
-                        v3 = static_cast<float>(static_cast<int32_t>(src[3]));
-                    } else {
-                        v0 = __uint_as_float(src[0]);
-                        v1 = __uint_as_float(src[1]);
-                        v2 = __uint_as_float(src[2]);
-                        v3 = __uint_as_float(src[3]);
-                    }
-                    fma2(acc[c], acc[c + 1], v0, v1, s0, s1);
-                    fma2(acc[c + 2], acc[c + 3], v2, v3, s2, s3);
                 }
+                __syncwarp();  // the ring entry is rewritten kScaleDepth - 1 blocks later
             }
             if (!ok) break;
             // Tile done: bias (+ erf-GELU), 32 x 32 chunks through shared memory, TMA store.
 #pragma unroll
-            for (int chunk = 0; chunk < 2; ++chunk) {
+            for (int chunk = 0; chunk < kQCols / 32; ++chunk) {
                 const int col0 = col_base + chunk * 32;
                 if (col0 >= n) break;
                 const float bias_lane = (args.bias != nullptr && col0 + lane < n) ? __ldg(args.bias + col0 + lane) : 0.0f;
@@ -326,6 +347,7 @@ gemm_mmq_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant
                 }
             }
         }
+        cp_async_wait<0>();
         if (lane == 0) bulk_wait_group_read<0>();
         __syncwarp();
     }
