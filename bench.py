@@ -894,7 +894,7 @@ def neck_section(samq, torch, stream, args, max_over_ranks, pk, steps=10):
 
 
 PROFILE_EXTRA = ("attention_window", "attention_global", "attention_window_f32", "attention_global_f32", "text_fc2",
-                 "neck_conv3x3", "vit_block")
+                 "neck_conv3x3", "vit_block", "mmq_qkv")
 
 
 def run_profile_case(args):
@@ -936,6 +936,19 @@ def run_profile_case(args):
         for _ in range(launches):
             samq.vit_attention(qkv, 3 * E, GRID, GRID, HEADS, window, freqs, out, E, stream,
                                compute=samq.COMPUTE_F32 if args.profile.endswith("_f32") else samq.COMPUTE_F16)
+    elif args.profile == "mmq_qkv":
+        # The exact-MMQ-arithmetic GEMM (samq_linear_mmq_v1, f16 codes) at the
+        # qkv shape: D4 staging + gemm_mmq_kernel per launch.
+        n, k = 3 * E, E
+        packed, bias = make_weights(samq.quantize_rows, n, k, 8, 0)
+        w = samq.MmqWeights(8, k, n, packed)
+        x = torch.from_numpy(np.random.default_rng(0).normal(0, 1, (M, k)).astype(np.float32)).cuda()
+        y = torch.empty((M, n), dtype=torch.float32, device="cuda")
+        b = torch.from_numpy(bias).cuda()
+        for _ in range(launches):
+            samq.linear_mmq(w, x, M, k, b, 0, y, n, stream)
+        torch.cuda.synchronize()
+        w.close()
     elif args.profile == "text_fc2":
         n, k, m = 1024, 4096, 32
         packed, bias = make_weights(samq.quantize_rows, n, k, 8, 5)
