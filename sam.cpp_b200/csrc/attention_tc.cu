@@ -1,0 +1,397 @@
+// attention_tc.cu -- F32-precise attention on the sm_100a tensor cores for
+// large query and key counts: softmax(Q K^T * scale) V per head, no mask
+// (the fusion encoder's self-attention over the image tokens,
+// src/models/sam3/fusion_encoder.hpp:60-90, kept at F32 precision by the
+// reference in both CUDA compute modes, src/runtime/ggml/backends/cuda.hpp:86-91).
+//
+// F32 accuracy from TF32 MMAs (the split of dense.cu): every operand x is
+// split once into hi = rna_tf32(x) and lo = rna_tf32(x - hi), and each product
+// is hi*hi + hi*lo + lo*hi.  The hi*hi terms and the two correction terms
+// accumulate in separate TMEM regions and are added in registers with f32
+// round-to-nearest (the tensor core's accumulation rounds toward zero per MMA).
+//   S = Q K^T:  M = 128 queries, N = 64 keys, K = head dim (32 / 64)
+//   O = P V:    M = 128 queries, N = head dim, K = 64 keys
+// The online softmax runs in f32 registers of the softmax warps (one query row
+// per thread, read from TMEM); P goes to shared memory as its hi / lo split.
+// Per 64-key tile the output O_t is a fresh accumulator and the softmax warps
+// add it as o = o * alpha + O_t (the blocked sum of the SIMT kernel).
+//
+// One CTA per (128 queries, head), 288 threads:
+//   warps 0-3  loaders: Q once, then K and V^T tiles (hi / lo, 128-byte swizzle)
+//   warp 4     TMEM owner and MMA issuer (S_j is issued ahead of P_{j-1} V_{j-1})
+//   warps 5-8  softmax (TMEM lane quarter = warp % 4)
+// No TMA multicast; every mbarrier wait is bounded (kStatusTimeout on expiry).
+#include <algorithm>
+#include <cmath>
+
+#include "samq_internal.hpp"
+
+namespace samq {
+namespace {
+
+constexpr int kQ = 128;          // queries per CTA
+constexpr int kKeys = 64;        // keys per tile
+constexpr int kTcThreads = 288;
+
+__host__ __device__ constexpr uint32_t idesc_tf32_mn(int m, int n) {
+    return (1u << 4) | (2u << 7) | (2u << 10) | (static_cast<uint32_t>(n >> 3) << 17) |
+           (static_cast<uint32_t>(m >> 4) << 24);
+}
+
+__device__ __forceinline__ void mma_tf32(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                         uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+template <int HD>
+struct TcLayout {
+    static constexpr int stages = HD == 32 ? 2 : 1;
+    static constexpr int chunks = HD / 32;                    // 128-byte swizzle rows along the head dim
+    static constexpr int q_bytes = chunks * kQ * 128;         // one of hi / lo
+    static constexpr int k_bytes = chunks * kKeys * 128;      // K tile [64 keys][HD], one of hi / lo
+    static constexpr int v_bytes = 2 * HD * 128;              // V^T tile [HD][64 keys], one of hi / lo
+    static constexpr int p_bytes = 2 * kQ * 128;              // P [128][64 keys], one of hi / lo
+    static constexpr int q_off = 0;
+    static constexpr int k_off = q_off + 2 * q_bytes;
+    static constexpr int v_off = k_off + stages * 2 * k_bytes;
+    static constexpr int p_off = v_off + stages * 2 * v_bytes;
+    static constexpr int bar_off = p_off + 2 * p_bytes;
+    static constexpr int bars = 1 + 2 * stages + 2 * 2 + 1 + 2 * 2 + 1;
+    static constexpr int total = bar_off + bars * 8 + 16 + 1024;
+    // TMEM columns: S (hi*hi, corrections) x 2 buffers, then O likewise.
+    __host__ __device__ static constexpr uint32_t s_col(int b) { return static_cast<uint32_t>(b * 2 * kKeys); }
+    __host__ __device__ static constexpr uint32_t o_col(int b) { return static_cast<uint32_t>(4 * kKeys + b * 2 * HD); }
+};
+
+// Byte offset of element (row, k) of a K-major operand tile stored as
+// 128-byte-swizzled chunks of 32 f32 along k, `rows` rows per chunk.
+__device__ __forceinline__ uint32_t sw_off(int row, int k, int rows) {
+    const int chunk = k >> 5, kin = k & 31;
+    return static_cast<uint32_t>(chunk * rows * 128 + row * 128 + ((((kin >> 2) ^ (row & 7)) << 4) | ((kin & 3) << 2)));
+}
+
+struct TcArgs {
+    const float* q;
+    const float* k;
+    const float* v;
+    float* out;
+    int64_t ldq, ldk, ldv, ldo;
+    int lq, lk;
+    float scale;
+    DeviceStatus* status;
+};
+
+// Softmax warps: wait for P_j V_j (O buffer j % 2), add it as
+// o = o * alpha + (hi*hi + corrections), release the buffer.
+template <int HD, class L>
+__device__ __forceinline__ bool take_o(float (&o)[HD], float alpha, int j, uint64_t* o_full, uint64_t* o_empty,
+                                       uint32_t tmem_lane, int lane, DeviceStatus* status) {
+    const int b = j & 1;
+    if (!__all_sync(0xffffffffu, mbar_wait(&o_full[b], (j >> 1) & 1u, status, 88))) return false;
+    tc_fence_after();
+#pragma unroll
+    for (int c0 = 0; c0 < HD; c0 += 32) {
+        uint32_t oh[32], oc[32];
+        tc_ld_32x32b_x32(tmem_lane + L::o_col(b) + c0, oh);
+        tc_ld_32x32b_x32(tmem_lane + L::o_col(b) + HD + c0, oc);
+        tc_wait_ld();
+#pragma unroll
+        for (int c = 0; c < 32; ++c) o[c0 + c] = fmaf(o[c0 + c], alpha, __uint_as_float(oh[c]) + __uint_as_float(oc[c]));
+    }
+    tc_fence_before();
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&o_empty[b]);
+    return true;
+}
+
+template <int HD>
+__global__ void __launch_bounds__(kTcThreads, 1) attention_tc_kernel(const TcArgs a) {
+    using L = TcLayout<HD>;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::bar_off);
+    uint64_t* q_full = bars;
+    uint64_t* kv_full = q_full + 1;
+    uint64_t* kv_empty = kv_full + L::stages;
+    uint64_t* s_full = kv_empty + L::stages;
+    uint64_t* s_empty = s_full + 2;
+    uint64_t* p_full = s_empty + 2;
+    uint64_t* o_full = p_full + 1;
+    uint64_t* o_empty = o_full + 2;
+    uint64_t* drain = o_empty + 2;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+    DeviceStatus* status = a.status;
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int q0 = blockIdx.x * kQ, h = blockIdx.y;
+    const int tiles = (a.lk + kKeys - 1) / kKeys;
+
+    if (threadIdx.x == 0) {
+        mbar_init(q_full, 4);
+        for (int s = 0; s < L::stages; ++s) {
+            mbar_init(&kv_full[s], 4);
+            mbar_init(&kv_empty[s], 1);
+        }
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&s_full[b], 1);
+            mbar_init(&s_empty[b], 4);
+            mbar_init(&o_full[b], 1);
+            mbar_init(&o_empty[b], 4);
+        }
+        mbar_init(p_full, 4);
+        mbar_init(drain, 1);
+        fence_barrier_init();
+    }
+    if (warp == 4) tmem_alloc(tmem_slot, 512);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+    pdl_wait();
+
+    if (warp < 4) {
+        // ---- loaders ---------------------------------------------------------
+        const int t = threadIdx.x;  // 0..127
+        uint8_t* qh = smem + L::q_off;
+        uint8_t* ql = qh + L::q_bytes;
+        for (int idx = t; idx < kQ * (HD / 4); idx += 128) {
+            const int r = idx / (HD / 4), d4 = idx % (HD / 4), n = q0 + r;
+            float4 x = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (n < a.lq) x = __ldg(reinterpret_cast<const float4*>(a.q + int64_t(n) * a.ldq + h * HD) + d4);
+            float4 hi, lo;
+            split_tf32(x.x, hi.x, lo.x);
+            split_tf32(x.y, hi.y, lo.y);
+            split_tf32(x.z, hi.z, lo.z);
+            split_tf32(x.w, hi.w, lo.w);
+            const uint32_t off = sw_off(r, 4 * d4, kQ);
+            *reinterpret_cast<float4*>(qh + off) = hi;
+            *reinterpret_cast<float4*>(ql + off) = lo;
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(q_full);
+        for (int j = 0; j < tiles; ++j) {
+            const int s = j % L::stages;
+            if (!__all_sync(0xffffffffu, mbar_wait(&kv_empty[s], ((j / L::stages) & 1u) ^ 1u, status, 81))) break;
+            uint8_t* kh = smem + L::k_off + s * 2 * L::k_bytes;
+            uint8_t* kl = kh + L::k_bytes;
+            uint8_t* vh = smem + L::v_off + s * 2 * L::v_bytes;
+            uint8_t* vl = vh + L::v_bytes;
+            const int key0 = j * kKeys;
+            for (int idx = t; idx < kKeys * (HD / 4); idx += 128) {
+                const int r = idx / (HD / 4), d4 = idx % (HD / 4), n = key0 + r;
+                float4 x = make_float4(0.f, 0.f, 0.f, 0.f);
+                if (n < a.lk) x = __ldg(reinterpret_cast<const float4*>(a.k + int64_t(n) * a.ldk + h * HD) + d4);
+                float4 hi, lo;
+                split_tf32(x.x, hi.x, lo.x);
+                split_tf32(x.y, hi.y, lo.y);
+                split_tf32(x.z, hi.z, lo.z);
+                split_tf32(x.w, hi.w, lo.w);
+                const uint32_t off = sw_off(r, 4 * d4, kKeys);
+                *reinterpret_cast<float4*>(kh + off) = hi;
+                *reinterpret_cast<float4*>(kl + off) = lo;
+            }
+            // V^T: row = channel d, k index = key; lanes run along the keys.
+            for (int idx = t; idx < kKeys * (HD / 4); idx += 128) {
+                const int r = idx % kKeys, d4 = idx / kKeys, n = key0 + r;
+                float4 x = make_float4(0.f, 0.f, 0.f, 0.f);
+                if (n < a.lk) x = __ldg(reinterpret_cast<const float4*>(a.v + int64_t(n) * a.ldv + h * HD) + d4);
+                const float xs[4] = {x.x, x.y, x.z, x.w};
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    float hi, lo;
+                    split_tf32(xs[i], hi, lo);
+                    const uint32_t off = sw_off(4 * d4 + i, r, HD);
+                    *reinterpret_cast<float*>(vh + off) = hi;
+                    *reinterpret_cast<float*>(vl + off) = lo;
+                }
+            }
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&kv_full[s]);
+        }
+    } else if (warp == 4) {
+        // ---- MMA issuer --------------------------------------------------------
+        if (lane == 0) {
+            constexpr uint32_t id_s = idesc_tf32_mn(kQ, kKeys);
+            constexpr uint32_t id_o = idesc_tf32_mn(kQ, HD);
+            const uint32_t qh = smem_u32(smem + L::q_off), ql = qh + L::q_bytes;
+            const uint32_t ph = smem_u32(smem + L::p_off), pl = ph + L::p_bytes;
+            bool ok = mbar_wait(q_full, 0, status, 82);
+            auto issue_s = [&](int j) -> bool {
+                const int s = j % L::stages, b = j & 1;
+                if (!mbar_wait(&kv_full[s], (j / L::stages) & 1u, status, 83)) return false;
+                if (!mbar_wait(&s_empty[b], ((j >> 1) & 1u) ^ 1u, status, 84)) return false;
+                tc_fence_after();
+                const uint32_t kh = smem_u32(smem + L::k_off + s * 2 * L::k_bytes), kl = kh + L::k_bytes;
+                const uint32_t dh = tmem_base + L::s_col(b), dc = dh + kKeys;
+#pragma unroll
+                for (int t = 0; t < HD / 8; ++t) {
+                    const uint32_t qo = (t >> 2) * kQ * 128 + (t & 3) * 32, ko = (t >> 2) * kKeys * 128 + (t & 3) * 32;
+                    mma_tf32(dh, smem_desc_sw128(qh + qo), smem_desc_sw128(kh + ko), id_s, t != 0 ? 1u : 0u);
+                    mma_tf32(dc, smem_desc_sw128(qh + qo), smem_desc_sw128(kl + ko), id_s, t != 0 ? 1u : 0u);
+                    mma_tf32(dc, smem_desc_sw128(ql + qo), smem_desc_sw128(kh + ko), id_s, 1u);
+                }
+                tc_commit(&s_full[b]);
+                return true;
+            };
+            auto issue_o = [&](int j) -> bool {
+                const int s = j % L::stages, b = j & 1;
+                if (!mbar_wait(p_full, j & 1u, status, 85)) return false;
+                if (!mbar_wait(&o_empty[b], ((j >> 1) & 1u) ^ 1u, status, 86)) return false;
+                tc_fence_after();
+                const uint32_t vh = smem_u32(smem + L::v_off + s * 2 * L::v_bytes), vl = vh + L::v_bytes;
+                const uint32_t dh = tmem_base + L::o_col(b), dc = dh + HD;
+#pragma unroll
+                for (int t = 0; t < kKeys / 8; ++t) {
+                    const uint32_t po = (t >> 2) * kQ * 128 + (t & 3) * 32, vo = (t >> 2) * HD * 128 + (t & 3) * 32;
+                    mma_tf32(dh, smem_desc_sw128(ph + po), smem_desc_sw128(vh + vo), id_o, t != 0 ? 1u : 0u);
+                    mma_tf32(dc, smem_desc_sw128(ph + po), smem_desc_sw128(vl + vo), id_o, t != 0 ? 1u : 0u);
+                    mma_tf32(dc, smem_desc_sw128(pl + po), smem_desc_sw128(vh + vo), id_o, 1u);
+                }
+                tc_commit(&o_full[b]);
+                tc_commit(&kv_empty[s]);
+                return true;
+            };
+            if (ok && tiles > 0) ok = issue_s(0);
+            for (int j = 0; j < tiles && ok; ++j) {
+                if (L::stages >= 2) {
+                    // S_{j+1} ahead of P_j V_j: the softmax of tile j + 1 overlaps P_j V_j.
+                    if (j + 1 < tiles && !issue_s(j + 1)) break;
+                    ok = issue_o(j);
+                } else {
+                    // One K / V stage: it holds tile j until P_j V_j is done.
+                    ok = issue_o(j);
+                    if (ok && j + 1 < tiles) ok = issue_s(j + 1);
+                }
+            }
+            tc_commit(drain);
+            mbar_wait(drain, 0, status, 87);
+        }
+    } else {
+        // ---- softmax -----------------------------------------------------------
+        const int quarter = warp & 3;
+        const int row = quarter * 32 + lane;  // query q0 + row
+        uint8_t* sph = smem + L::p_off;
+        uint8_t* spl = sph + L::p_bytes;
+        const uint32_t lane_addr = static_cast<uint32_t>(quarter * 32) << 16;
+        float o[HD], m = -INFINITY, l = 0.0f, alpha_prev = 1.0f;
+#pragma unroll
+        for (int c = 0; c < HD; ++c) o[c] = 0.0f;
+        bool ok = true;
+        for (int j = 0; j < tiles && ok; ++j) {
+            const int b = j & 1;
+            if (!__all_sync(0xffffffffu, mbar_wait(&s_full[b], (j >> 1) & 1u, status, 89))) {
+                ok = false;
+                break;
+            }
+            tc_fence_after();
+            float sv[kKeys];
+#pragma unroll
+            for (int c0 = 0; c0 < kKeys; c0 += 32) {
+                uint32_t sh[32], sc[32];
+                tc_ld_32x32b_x32(tmem_base + lane_addr + L::s_col(b) + c0, sh);
+                tc_ld_32x32b_x32(tmem_base + lane_addr + L::s_col(b) + kKeys + c0, sc);
+                tc_wait_ld();
+#pragma unroll
+                for (int c = 0; c < 32; ++c) sv[c0 + c] = (__uint_as_float(sh[c]) + __uint_as_float(sc[c])) * a.scale;
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&s_empty[b]);
+            const int key0 = j * kKeys;
+            float mx = m;
+#pragma unroll
+            for (int c = 0; c < kKeys; ++c) {
+                if (key0 + c >= a.lk) sv[c] = -INFINITY;
+                mx = fmaxf(mx, sv[c]);
+            }
+            const float m_use = mx == -INFINITY ? 0.0f : mx;
+            const float alpha = expf(m - m_use);
+            float sum = 0.0f;
+#pragma unroll
+            for (int c = 0; c < kKeys; ++c) {
+                sv[c] = expf(sv[c] - m_use);
+                sum += sv[c];
+            }
+            l = fmaf(l, alpha, sum);
+            m = mx;
+            // P buffer is free once P_{j-1} V_{j-1} completed (o_full of j - 1).
+            if (j > 0 && !take_o<HD, L>(o, alpha_prev, j - 1, o_full, o_empty, tmem_base + lane_addr, lane, status)) {
+                ok = false;
+                break;
+            }
+            alpha_prev = alpha;
+#pragma unroll
+            for (int c4 = 0; c4 < kKeys / 4; ++c4) {
+                float4 hi, lo;
+                split_tf32(sv[4 * c4], hi.x, lo.x);
+                split_tf32(sv[4 * c4 + 1], hi.y, lo.y);
+                split_tf32(sv[4 * c4 + 2], hi.z, lo.z);
+                split_tf32(sv[4 * c4 + 3], hi.w, lo.w);
+                const uint32_t off = sw_off(row, 4 * c4, kQ);
+                *reinterpret_cast<float4*>(sph + off) = hi;
+                *reinterpret_cast<float4*>(spl + off) = lo;
+            }
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(p_full);
+        }
+        if (ok && tiles > 0)
+            ok = take_o<HD, L>(o, alpha_prev, tiles - 1, o_full, o_empty, tmem_base + lane_addr, lane, status);
+        pdl_trigger();
+        const int n = q0 + row;
+        if (ok && n < a.lq) {
+            float* dst = a.out + int64_t(n) * a.ldo + h * HD;
+#pragma unroll
+            for (int c4 = 0; c4 < HD / 4; ++c4) {
+                float4 r4;
+                r4.x = l > 0.0f ? __fdiv_rn(o[4 * c4], l) : 0.0f;
+                r4.y = l > 0.0f ? __fdiv_rn(o[4 * c4 + 1], l) : 0.0f;
+                r4.z = l > 0.0f ? __fdiv_rn(o[4 * c4 + 2], l) : 0.0f;
+                r4.w = l > 0.0f ? __fdiv_rn(o[4 * c4 + 3], l) : 0.0f;
+                reinterpret_cast<float4*>(dst)[c4] = r4;
+            }
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 4) {
+        tc_fence_after();
+        tmem_dealloc(tmem_base, 512);
+    }
+}
+
+}  // namespace
+
+bool attention_tc_eligible(int lq, int lk, int head_dim, int causal, const float* bias, int64_t ldo) {
+    return (head_dim == 32 || head_dim == 64) && !causal && bias == nullptr && lq >= 1024 && lk >= 256 &&
+           ldo % 4 == 0;
+}
+
+void launch_attention_tc(const float* q, int64_t ldq, const float* k, int64_t ldk, const float* v, int64_t ldv,
+                         int lq, int lk, int heads, int head_dim, float scale, float* out, int64_t ldo,
+                         DeviceState& state, cudaStream_t stream) {
+    TcArgs a{q, k, v, out, ldq, ldk, ldv, ldo, lq, lk, scale, state.status};
+    const dim3 grid((lq + kQ - 1) / kQ, heads);
+    if (head_dim == 64) {
+        using L = TcLayout<64>;
+        static_assert(L::total <= 232448, "shared memory budget");
+        set_smem_limit_once(state, reinterpret_cast<const void*>(attention_tc_kernel<64>), L::total,
+                            "cudaFuncSetAttribute(attention_tc smem)");
+        launch_pdl(attention_tc_kernel<64>, grid, dim3(kTcThreads), L::total, stream, "attention_tc_kernel launch", a);
+    } else {
+        using L = TcLayout<32>;
+        static_assert(L::total <= 232448, "shared memory budget");
+        set_smem_limit_once(state, reinterpret_cast<const void*>(attention_tc_kernel<32>), L::total,
+                            "cudaFuncSetAttribute(attention_tc smem)");
+        launch_pdl(attention_tc_kernel<32>, grid, dim3(kTcThreads), L::total, stream, "attention_tc_kernel launch", a);
+    }
+}
+
+}  // namespace samq

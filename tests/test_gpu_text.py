@@ -73,12 +73,15 @@ def test_precision_probe_reference_cases(dims, queries, keys, masked):
 
 @pytest.mark.parametrize("lq,lk,heads,hd,mode", [
     (32, 32, 16, 64, "causal"), (200, 5184, 8, 32, "rpb"), (5184, 33, 8, 32, "padding"), (201, 201, 8, 32, "none"),
-    (70, 45, 3, 64, "rpb"), (1, 5184, 8, 32, "none"), (3, 700, 16, 64, "padding"), (40, 512, 4, 32, "tailmask")])
+    (70, 45, 3, 64, "rpb"), (1, 5184, 8, 32, "none"), (3, 700, 16, 64, "padding"), (40, 512, 4, 32, "tailmask"),
+    (5184, 5184, 8, 32, "none"), (1100, 300, 4, 64, "none"), (1030, 1029, 2, 32, "none"), (2048, 2048, 16, 64, "none")])
 def test_attention_parity_random(lq, lk, heads, hd, mode):
     """Random Q / K / V with each mask form against oracle.attention_gen:
     cosine >= 1 - 1e-10 and normalized max error <= 1e-5 (F32 level).  The
     few-query cases run with the keys split over CTAs and merged; "tailmask"
-    masks every key from 100 on, so whole key splits are empty."""
+    masks every key from 100 on, so whole key splits are empty.  The unmasked
+    cases with >= 1024 queries run on the tensor cores (attention_tc.cu,
+    three-term TF32), ragged in both queries and keys."""
     rng = np.random.default_rng(lq + lk + heads)
     q = rng.normal(0, 1, (lq, heads * hd)).astype(np.float32)
     k = rng.normal(0, 1, (lk, heads * hd)).astype(np.float32)
