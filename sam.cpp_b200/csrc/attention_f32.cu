@@ -509,7 +509,7 @@ void launch_attention_gen(const float* q, int64_t ldq, const float* k, int64_t l
                           int64_t bias_h, int64_t bias_q, float* out, int64_t ldo, DeviceState& state,
                           cudaStream_t stream, float* partials, size_t partial_floats) {
     if (lq == 0) return;
-    if (attention_tc_eligible(lq, lk, head_dim, causal, bias, ldo)) {
+    if (attention_tc_eligible(lq, lk, head_dim, causal, bias, out, ldo)) {
         launch_attention_tc(q, ldq, k, ldk, v, ldv, lq, lk, heads, head_dim, scale, out, ldo, state, stream);
         return;
     }

@@ -369,9 +369,10 @@ __global__ void __launch_bounds__(kTcThreads, 1) attention_tc_kernel(const TcArg
 
 }  // namespace
 
-bool attention_tc_eligible(int lq, int lk, int head_dim, int causal, const float* bias, int64_t ldo) {
+bool attention_tc_eligible(int lq, int lk, int head_dim, int causal, const float* bias, const float* out,
+                           int64_t ldo) {
     return (head_dim == 32 || head_dim == 64) && !causal && bias == nullptr && lq >= 1024 && lk >= 256 &&
-           ldo % 4 == 0;
+           ldo % 4 == 0 && (reinterpret_cast<uintptr_t>(out) & 15u) == 0;
 }
 
 void launch_attention_tc(const float* q, int64_t ldq, const float* k, int64_t ldk, const float* v, int64_t ldv,

@@ -193,7 +193,8 @@ void launch_attention_f32(const float* qkv, int64_t ldq, bool qkv_window_major, 
 size_t attention_partial_floats(int lq, int lk, int heads, int head_dim, int causal, int sms);
 // attention_tc.cu: the same attention on the tensor cores (three-term TF32),
 // for many queries and keys without a mask.
-bool attention_tc_eligible(int lq, int lk, int head_dim, int causal, const float* bias, int64_t ldo);
+bool attention_tc_eligible(int lq, int lk, int head_dim, int causal, const float* bias, const float* out,
+                           int64_t ldo);
 void launch_attention_tc(const float* q, int64_t ldq, const float* k, int64_t ldk, const float* v, int64_t ldv,
                          int lq, int lk, int heads, int head_dim, float scale, float* out, int64_t ldo,
                          DeviceState& state, cudaStream_t stream);
