@@ -894,7 +894,7 @@ def neck_section(samq, torch, stream, args, max_over_ranks, pk, steps=10):
 
 
 PROFILE_EXTRA = ("attention_window", "attention_global", "attention_window_f32", "attention_global_f32", "text_fc2",
-                 "neck_conv3x3", "vit_block", "mmq_qkv")
+                 "neck_conv3x3", "vit_block", "mmq_qkv", "attention_fusion")
 
 
 def run_profile_case(args):
@@ -936,6 +936,18 @@ def run_profile_case(args):
         for _ in range(launches):
             samq.vit_attention(qkv, 3 * E, GRID, GRID, HEADS, window, freqs, out, E, stream,
                                compute=samq.COMPUTE_F32 if args.profile.endswith("_f32") else samq.COMPUTE_F16)
+    elif args.profile == "attention_fusion":
+        # The fusion encoder's self-attention: 5184 x 5184 tokens, 8 heads of
+        # 32, no mask (samq_attention_v1 -> the tensor-core F32 kernel).
+        T, H, hd = M, 8, 32
+        D = H * hd
+        rng = np.random.default_rng(3)
+        qkv = torch.from_numpy(rng.normal(0, 1, (T, 3 * D)).astype(np.float32)).cuda()
+        out = torch.empty((T, D), dtype=torch.float32, device="cuda")
+        for _ in range(launches):
+            samq.attention(qkv, 3 * D, qkv[:, D:], 3 * D, qkv[:, 2 * D:], 3 * D, T, T, H, hd, float(1 / np.sqrt(hd)),
+                           out, D, stream=stream)
+        torch.cuda.synchronize()
     elif args.profile == "mmq_qkv":
         # The exact-MMQ-arithmetic GEMM (samq_linear_mmq_v1, f16 codes) at the
         # qkv shape: D4 staging + gemm_mmq_kernel per launch.
