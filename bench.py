@@ -894,7 +894,7 @@ def neck_section(samq, torch, stream, args, max_over_ranks, pk, steps=10):
 
 
 PROFILE_EXTRA = ("attention_window", "attention_global", "attention_window_f32", "attention_global_f32", "text_fc2",
-                 "neck_conv3x3", "vit_block", "mmq_qkv", "attention_fusion")
+                 "neck_conv3x3", "vit_block", "mmq_qkv", "fusion_self_attention")
 
 
 def run_profile_case(args):
@@ -936,7 +936,7 @@ def run_profile_case(args):
         for _ in range(launches):
             samq.vit_attention(qkv, 3 * E, GRID, GRID, HEADS, window, freqs, out, E, stream,
                                compute=samq.COMPUTE_F32 if args.profile.endswith("_f32") else samq.COMPUTE_F16)
-    elif args.profile == "attention_fusion":
+    elif args.profile == "fusion_self_attention":
         # The fusion encoder's self-attention: 5184 x 5184 tokens, 8 heads of
         # 32, no mask (samq_attention_v1 -> the tensor-core F32 kernel).
         T, H, hd = M, 8, 32
