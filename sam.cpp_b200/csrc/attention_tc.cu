@@ -16,10 +16,11 @@
 // Per 64-key tile the output O_t is a fresh accumulator and the softmax warps
 // add it as o = o * alpha + O_t (the blocked sum of the SIMT kernel).
 //
-// One CTA per (128 queries, head), 288 threads:
-//   warps 0-3  loaders: Q once, then K and V^T tiles (hi / lo, 128-byte swizzle)
-//   warp 4     TMEM owner and MMA issuer (S_j is issued ahead of P_{j-1} V_{j-1})
-//   warps 5-8  softmax (TMEM lane quarter = warp % 4)
+// One CTA per (128 queries, head), 224 threads (7 warps, so no SM
+// sub-partition holds more than two and every thread may use 255 registers):
+//   warps 0-1  loaders: Q once, then K and V^T tiles (hi / lo, 128-byte swizzle)
+//   warp 2     TMEM owner and MMA issuer (S_j is issued ahead of P_{j-1} V_{j-1})
+//   warps 3-6  softmax (TMEM lane quarter = warp % 4)
 // No TMA multicast; every mbarrier wait is bounded (kStatusTimeout on expiry).
 #include <algorithm>
 #include <cmath>
@@ -31,7 +32,9 @@ namespace {
 
 constexpr int kQ = 128;          // queries per CTA
 constexpr int kKeys = 64;        // keys per tile
-constexpr int kTcThreads = 288;
+constexpr int kLoaders = 2;     // loader warps
+constexpr int kMmaWarp = kLoaders;
+constexpr int kTcThreads = 32 * (kLoaders + 1 + 4);  // 7 warps: at most 2 per SM sub-partition
 
 __host__ __device__ constexpr uint32_t idesc_tf32_mn(int m, int n) {
     return (1u << 4) | (2u << 7) | (2u << 10) | (static_cast<uint32_t>(n >> 3) << 17) |
@@ -132,9 +135,9 @@ __global__ void __launch_bounds__(kTcThreads, 1) attention_tc_kernel(const TcArg
     const int tiles = (a.lk + kKeys - 1) / kKeys;
 
     if (threadIdx.x == 0) {
-        mbar_init(q_full, 4);
+        mbar_init(q_full, kLoaders);
         for (int s = 0; s < L::stages; ++s) {
-            mbar_init(&kv_full[s], 4);
+            mbar_init(&kv_full[s], kLoaders);
             mbar_init(&kv_empty[s], 1);
         }
         for (int b = 0; b < 2; ++b) {
@@ -147,66 +150,87 @@ __global__ void __launch_bounds__(kTcThreads, 1) attention_tc_kernel(const TcArg
         mbar_init(drain, 1);
         fence_barrier_init();
     }
-    if (warp == 4) tmem_alloc(tmem_slot, 512);
+    if (warp == kMmaWarp) tmem_alloc(tmem_slot, 512);
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
     pdl_wait();
 
-    if (warp < 4) {
+    if (warp < kLoaders) {
         // ---- loaders ---------------------------------------------------------
-        const int t = threadIdx.x;  // 0..127
+        const int t = threadIdx.x;  // 0 .. 32 kLoaders - 1
         uint8_t* qh = smem + L::q_off;
         uint8_t* ql = qh + L::q_bytes;
-        for (int idx = t; idx < kQ * (HD / 4); idx += 128) {
-            const int r = idx / (HD / 4), d4 = idx % (HD / 4), n = q0 + r;
-            float4 x = make_float4(0.f, 0.f, 0.f, 0.f);
-            if (n < a.lq) x = __ldg(reinterpret_cast<const float4*>(a.q + int64_t(n) * a.ldq + h * HD) + d4);
-            float4 hi, lo;
-            split_tf32(x.x, hi.x, lo.x);
-            split_tf32(x.y, hi.y, lo.y);
-            split_tf32(x.z, hi.z, lo.z);
-            split_tf32(x.w, hi.w, lo.w);
-            const uint32_t off = sw_off(r, 4 * d4, kQ);
-            *reinterpret_cast<float4*>(qh + off) = hi;
-            *reinterpret_cast<float4*>(ql + off) = lo;
+        // Every load of a tile is issued before any of them is used, so a
+        // tile costs one global latency, not one per float4.
+        constexpr int kLt = 32 * kLoaders;
+        constexpr int kQLoads = kQ * (HD / 4) / kLt, kKvLoads = kKeys * (HD / 4) / kLt;
+        {
+            float4 x[kQLoads];
+#pragma unroll
+            for (int i = 0; i < kQLoads; ++i) {
+                const int idx = t + kLt * i, r = idx / (HD / 4), d4 = idx % (HD / 4), n = q0 + r;
+                x[i] = n < a.lq ? __ldg(reinterpret_cast<const float4*>(a.q + int64_t(n) * a.ldq + h * HD) + d4)
+                                : make_float4(0.f, 0.f, 0.f, 0.f);
+            }
+#pragma unroll
+            for (int i = 0; i < kQLoads; ++i) {
+                const int idx = t + kLt * i, r = idx / (HD / 4), d4 = idx % (HD / 4);
+                float4 hi, lo;
+                split_tf32(x[i].x, hi.x, lo.x);
+                split_tf32(x[i].y, hi.y, lo.y);
+                split_tf32(x[i].z, hi.z, lo.z);
+                split_tf32(x[i].w, hi.w, lo.w);
+                const uint32_t off = sw_off(r, 4 * d4, kQ);
+                *reinterpret_cast<float4*>(qh + off) = hi;
+                *reinterpret_cast<float4*>(ql + off) = lo;
+            }
         }
         fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) mbar_arrive(q_full);
         for (int j = 0; j < tiles; ++j) {
             const int s = j % L::stages;
+            const int key0 = j * kKeys;
+            float4 xk[kKvLoads], xv[kKvLoads];
+#pragma unroll
+            for (int i = 0; i < kKvLoads; ++i) {
+                const int idx = t + kLt * i;
+                const int rk = idx / (HD / 4), dk = idx % (HD / 4), nk = key0 + rk;
+                const int rv = idx % kKeys, dv = idx / kKeys, nv = key0 + rv;
+                xk[i] = nk < a.lk ? __ldg(reinterpret_cast<const float4*>(a.k + int64_t(nk) * a.ldk + h * HD) + dk)
+                                  : make_float4(0.f, 0.f, 0.f, 0.f);
+                xv[i] = nv < a.lk ? __ldg(reinterpret_cast<const float4*>(a.v + int64_t(nv) * a.ldv + h * HD) + dv)
+                                  : make_float4(0.f, 0.f, 0.f, 0.f);
+            }
             if (!__all_sync(0xffffffffu, mbar_wait(&kv_empty[s], ((j / L::stages) & 1u) ^ 1u, status, 81))) break;
             uint8_t* kh = smem + L::k_off + s * 2 * L::k_bytes;
             uint8_t* kl = kh + L::k_bytes;
             uint8_t* vh = smem + L::v_off + s * 2 * L::v_bytes;
             uint8_t* vl = vh + L::v_bytes;
-            const int key0 = j * kKeys;
-            for (int idx = t; idx < kKeys * (HD / 4); idx += 128) {
-                const int r = idx / (HD / 4), d4 = idx % (HD / 4), n = key0 + r;
-                float4 x = make_float4(0.f, 0.f, 0.f, 0.f);
-                if (n < a.lk) x = __ldg(reinterpret_cast<const float4*>(a.k + int64_t(n) * a.ldk + h * HD) + d4);
+#pragma unroll
+            for (int i = 0; i < kKvLoads; ++i) {
+                const int idx = t + kLt * i, r = idx / (HD / 4), d4 = idx % (HD / 4);
                 float4 hi, lo;
-                split_tf32(x.x, hi.x, lo.x);
-                split_tf32(x.y, hi.y, lo.y);
-                split_tf32(x.z, hi.z, lo.z);
-                split_tf32(x.w, hi.w, lo.w);
+                split_tf32(xk[i].x, hi.x, lo.x);
+                split_tf32(xk[i].y, hi.y, lo.y);
+                split_tf32(xk[i].z, hi.z, lo.z);
+                split_tf32(xk[i].w, hi.w, lo.w);
                 const uint32_t off = sw_off(r, 4 * d4, kKeys);
                 *reinterpret_cast<float4*>(kh + off) = hi;
                 *reinterpret_cast<float4*>(kl + off) = lo;
             }
             // V^T: row = channel d, k index = key; lanes run along the keys.
-            for (int idx = t; idx < kKeys * (HD / 4); idx += 128) {
-                const int r = idx % kKeys, d4 = idx / kKeys, n = key0 + r;
-                float4 x = make_float4(0.f, 0.f, 0.f, 0.f);
-                if (n < a.lk) x = __ldg(reinterpret_cast<const float4*>(a.v + int64_t(n) * a.ldv + h * HD) + d4);
-                const float xs[4] = {x.x, x.y, x.z, x.w};
 #pragma unroll
-                for (int i = 0; i < 4; ++i) {
+            for (int i = 0; i < kKvLoads; ++i) {
+                const int idx = t + kLt * i, r = idx % kKeys, d4 = idx / kKeys;
+                const float xs[4] = {xv[i].x, xv[i].y, xv[i].z, xv[i].w};
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
                     float hi, lo;
-                    split_tf32(xs[i], hi, lo);
-                    const uint32_t off = sw_off(4 * d4 + i, r, HD);
+                    split_tf32(xs[e], hi, lo);
+                    const uint32_t off = sw_off(4 * d4 + e, r, HD);
                     *reinterpret_cast<float*>(vh + off) = hi;
                     *reinterpret_cast<float*>(vl + off) = lo;
                 }
@@ -215,7 +239,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) attention_tc_kernel(const TcArg
             __syncwarp();
             if (lane == 0) mbar_arrive(&kv_full[s]);
         }
-    } else if (warp == 4) {
+    } else if (warp == kMmaWarp) {
         // ---- MMA issuer --------------------------------------------------------
         if (lane == 0) {
             constexpr uint32_t id_s = idesc_tf32_mn(kQ, kKeys);
@@ -361,7 +385,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) attention_tc_kernel(const TcArg
     }
     tc_fence_before();
     __syncthreads();
-    if (warp == 4) {
+    if (warp == kMmaWarp) {
         tc_fence_after();
         tmem_dealloc(tmem_base, 512);
     }
