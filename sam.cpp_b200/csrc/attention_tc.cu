@@ -54,6 +54,7 @@ __device__ __forceinline__ void mma_tf32(uint32_t tmem_d, uint64_t adesc, uint64
 template <int HD>
 struct TcLayout {
     static constexpr int stages = HD == 32 ? 2 : 1;
+    static constexpr int p_bufs = HD == 32 ? 2 : 1;           // P double-buffered where shared memory allows
     static constexpr int chunks = HD / 32;                    // 128-byte swizzle rows along the head dim
     static constexpr int q_bytes = chunks * kQ * 128;         // one of hi / lo
     static constexpr int k_bytes = chunks * kKeys * 128;      // K tile [64 keys][HD], one of hi / lo
@@ -63,8 +64,8 @@ struct TcLayout {
     static constexpr int k_off = q_off + 2 * q_bytes;
     static constexpr int v_off = k_off + stages * 2 * k_bytes;
     static constexpr int p_off = v_off + stages * 2 * v_bytes;
-    static constexpr int bar_off = p_off + 2 * p_bytes;
-    static constexpr int bars = 1 + 2 * stages + 2 * 2 + 1 + 2 * 2 + 1;
+    static constexpr int bar_off = p_off + p_bufs * 2 * p_bytes;
+    static constexpr int bars = 1 + 2 * stages + 2 * 2 + p_bufs + 2 * 2 + 1;
     static constexpr int total = bar_off + bars * 8 + 16 + 1024;
     // TMEM columns: S (hi*hi, corrections) x 2 buffers, then O likewise.
     __host__ __device__ static constexpr uint32_t s_col(int b) { return static_cast<uint32_t>(b * 2 * kKeys); }
@@ -95,7 +96,7 @@ template <int HD, class L>
 __device__ __forceinline__ bool take_o(float (&o)[HD], float alpha, int j, uint64_t* o_full, uint64_t* o_empty,
                                        uint32_t tmem_lane, int lane, DeviceStatus* status) {
     const int b = j & 1;
-    if (!__all_sync(0xffffffffu, mbar_wait(&o_full[b], (j >> 1) & 1u, status, 88))) return false;
+    if (!__all_sync(0xffffffffu, mbar_poll(&o_full[b], (j >> 1) & 1u, status, 88))) return false;
     tc_fence_after();
 #pragma unroll
     for (int c0 = 0; c0 < HD; c0 += 32) {
@@ -124,7 +125,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) attention_tc_kernel(const TcArg
     uint64_t* s_full = kv_empty + L::stages;
     uint64_t* s_empty = s_full + 2;
     uint64_t* p_full = s_empty + 2;
-    uint64_t* o_full = p_full + 1;
+    uint64_t* o_full = p_full + L::p_bufs;
     uint64_t* o_empty = o_full + 2;
     uint64_t* drain = o_empty + 2;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
@@ -146,7 +147,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) attention_tc_kernel(const TcArg
             mbar_init(&o_full[b], 1);
             mbar_init(&o_empty[b], 4);
         }
-        mbar_init(p_full, 4);
+        for (int b = 0; b < L::p_bufs; ++b) mbar_init(&p_full[b], 4);
         mbar_init(drain, 1);
         fence_barrier_init();
     }
@@ -204,7 +205,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) attention_tc_kernel(const TcArg
                 xv[i] = nv < a.lk ? __ldg(reinterpret_cast<const float4*>(a.v + int64_t(nv) * a.ldv + h * HD) + dv)
                                   : make_float4(0.f, 0.f, 0.f, 0.f);
             }
-            if (!__all_sync(0xffffffffu, mbar_wait(&kv_empty[s], ((j / L::stages) & 1u) ^ 1u, status, 81))) break;
+            if (!__all_sync(0xffffffffu, mbar_poll(&kv_empty[s], ((j / L::stages) & 1u) ^ 1u, status, 81))) break;
             uint8_t* kh = smem + L::k_off + s * 2 * L::k_bytes;
             uint8_t* kl = kh + L::k_bytes;
             uint8_t* vh = smem + L::v_off + s * 2 * L::v_bytes;
@@ -245,12 +246,11 @@ __global__ void __launch_bounds__(kTcThreads, 1) attention_tc_kernel(const TcArg
             constexpr uint32_t id_s = idesc_tf32_mn(kQ, kKeys);
             constexpr uint32_t id_o = idesc_tf32_mn(kQ, HD);
             const uint32_t qh = smem_u32(smem + L::q_off), ql = qh + L::q_bytes;
-            const uint32_t ph = smem_u32(smem + L::p_off), pl = ph + L::p_bytes;
             bool ok = mbar_wait(q_full, 0, status, 82);
             auto issue_s = [&](int j) -> bool {
                 const int s = j % L::stages, b = j & 1;
-                if (!mbar_wait(&kv_full[s], (j / L::stages) & 1u, status, 83)) return false;
-                if (!mbar_wait(&s_empty[b], ((j >> 1) & 1u) ^ 1u, status, 84)) return false;
+                if (!mbar_poll(&kv_full[s], (j / L::stages) & 1u, status, 83)) return false;
+                if (!mbar_poll(&s_empty[b], ((j >> 1) & 1u) ^ 1u, status, 84)) return false;
                 tc_fence_after();
                 const uint32_t kh = smem_u32(smem + L::k_off + s * 2 * L::k_bytes), kl = kh + L::k_bytes;
                 const uint32_t dh = tmem_base + L::s_col(b), dc = dh + kKeys;
@@ -265,11 +265,12 @@ __global__ void __launch_bounds__(kTcThreads, 1) attention_tc_kernel(const TcArg
                 return true;
             };
             auto issue_o = [&](int j) -> bool {
-                const int s = j % L::stages, b = j & 1;
-                if (!mbar_wait(p_full, j & 1u, status, 85)) return false;
-                if (!mbar_wait(&o_empty[b], ((j >> 1) & 1u) ^ 1u, status, 86)) return false;
+                const int s = j % L::stages, b = j & 1, pb = j % L::p_bufs;
+                if (!mbar_poll(&p_full[pb], (j / L::p_bufs) & 1u, status, 85)) return false;
+                if (!mbar_poll(&o_empty[b], ((j >> 1) & 1u) ^ 1u, status, 86)) return false;
                 tc_fence_after();
                 const uint32_t vh = smem_u32(smem + L::v_off + s * 2 * L::v_bytes), vl = vh + L::v_bytes;
+                const uint32_t ph = smem_u32(smem + L::p_off + pb * 2 * L::p_bytes), pl = ph + L::p_bytes;
                 const uint32_t dh = tmem_base + L::o_col(b), dc = dh + HD;
 #pragma unroll
                 for (int t = 0; t < kKeys / 8; ++t) {
@@ -301,8 +302,6 @@ __global__ void __launch_bounds__(kTcThreads, 1) attention_tc_kernel(const TcArg
         // ---- softmax -----------------------------------------------------------
         const int quarter = warp & 3;
         const int row = quarter * 32 + lane;  // query q0 + row
-        uint8_t* sph = smem + L::p_off;
-        uint8_t* spl = sph + L::p_bytes;
         const uint32_t lane_addr = static_cast<uint32_t>(quarter * 32) << 16;
         float o[HD], m = -INFINITY, l = 0.0f, alpha_prev = 1.0f;
 #pragma unroll
@@ -310,7 +309,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) attention_tc_kernel(const TcArg
         bool ok = true;
         for (int j = 0; j < tiles && ok; ++j) {
             const int b = j & 1;
-            if (!__all_sync(0xffffffffu, mbar_wait(&s_full[b], (j >> 1) & 1u, status, 89))) {
+            if (!__all_sync(0xffffffffu, mbar_poll(&s_full[b], (j >> 1) & 1u, status, 89))) {
                 ok = false;
                 break;
             }
@@ -345,12 +344,18 @@ __global__ void __launch_bounds__(kTcThreads, 1) attention_tc_kernel(const TcArg
             }
             l = fmaf(l, alpha, sum);
             m = mx;
-            // P buffer is free once P_{j-1} V_{j-1} completed (o_full of j - 1).
-            if (j > 0 && !take_o<HD, L>(o, alpha_prev, j - 1, o_full, o_empty, tmem_base + lane_addr, lane, status)) {
-                ok = false;
-                break;
+            // P buffer j % p_bufs is free once P V of its previous tile is done:
+            // with one buffer that is tile j - 1 (taken here, before the write),
+            // with two it is j - 2 (taken in the previous iteration).
+            if (L::p_bufs == 1 && j > 0) {
+                if (!take_o<HD, L>(o, alpha_prev, j - 1, o_full, o_empty, tmem_base + lane_addr, lane, status)) {
+                    ok = false;
+                    break;
+                }
+                alpha_prev = alpha;
             }
-            alpha_prev = alpha;
+            uint8_t* sph = smem + L::p_off + (j % L::p_bufs) * 2 * L::p_bytes;
+            uint8_t* spl = sph + L::p_bytes;
 #pragma unroll
             for (int c4 = 0; c4 < kKeys / 4; ++c4) {
                 float4 hi, lo;
@@ -364,7 +369,15 @@ __global__ void __launch_bounds__(kTcThreads, 1) attention_tc_kernel(const TcArg
             }
             fence_proxy_async_smem();
             __syncwarp();
-            if (lane == 0) mbar_arrive(p_full);
+            if (lane == 0) mbar_arrive(&p_full[j % L::p_bufs]);
+            if (L::p_bufs == 2) {
+                if (j > 0 &&
+                    !take_o<HD, L>(o, alpha_prev, j - 1, o_full, o_empty, tmem_base + lane_addr, lane, status)) {
+                    ok = false;
+                    break;
+                }
+                alpha_prev = alpha;
+            }
         }
         if (ok && tiles > 0)
             ok = take_o<HD, L>(o, alpha_prev, tiles - 1, o_full, o_empty, tmem_base + lane_addr, lane, status);

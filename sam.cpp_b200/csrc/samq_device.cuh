@@ -84,6 +84,37 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
     return done != 0;
 }
 
+// One probe of the phase that returns at once (no suspend hint).
+__device__ __forceinline__ bool mbar_test_wait(uint64_t* bar, uint32_t parity) {
+    uint32_t done;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(done)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return done != 0;
+}
+
+// Bounded polling wait (test_wait, %globaltimer checked every 64 probes): for
+// short pipeline hand-offs where a suspended thread's wake-up would cost more
+// than the step it waits for.
+__device__ __forceinline__ bool mbar_poll(uint64_t* bar, uint32_t parity, DeviceStatus* status, uint32_t site) {
+    if (mbar_test_wait(bar, parity)) return true;
+    const uint64_t start = global_timer_ns();
+    for (uint32_t spin = 1;; ++spin) {
+        if (mbar_test_wait(bar, parity)) return true;
+        if ((spin & 63u) == 0 && global_timer_ns() - start > kWaitTimeoutNs) {
+            if (status) {
+                atomicOr(&status->flags, kStatusTimeout);
+                atomicExch(&status->timeout_site, site);
+            }
+            return false;
+        }
+    }
+}
+
 // Bounded wait for the phase with parity `parity`.  Returns false (and records
 // the site) when the wait is abandoned.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, DeviceStatus* status, uint32_t site) {
