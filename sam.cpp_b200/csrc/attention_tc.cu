@@ -86,7 +86,7 @@ struct TcArgs {
     float* out;
     int64_t ldq, ldk, ldv, ldo;
     int lq, lk;
-    float scale;
+    float scale_log2e;  // softmax scale x log2(e)
     DeviceStatus* status;
 };
 
@@ -314,7 +314,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) attention_tc_kernel(const TcArg
                 break;
             }
             tc_fence_after();
-            float sv[kKeys];
+            float sv[kKeys];  // raw scores Q . K (scale applied in the exponent)
 #pragma unroll
             for (int c0 = 0; c0 < kKeys; c0 += 32) {
                 uint32_t sh[32], sc[32];
@@ -322,24 +322,29 @@ __global__ void __launch_bounds__(kTcThreads, 1) attention_tc_kernel(const TcArg
                 tc_ld_32x32b_x32(tmem_base + lane_addr + L::s_col(b) + kKeys + c0, sc);
                 tc_wait_ld();
 #pragma unroll
-                for (int c = 0; c < 32; ++c) sv[c0 + c] = (__uint_as_float(sh[c]) + __uint_as_float(sc[c])) * a.scale;
+                for (int c = 0; c < 32; ++c) sv[c0 + c] = __uint_as_float(sh[c]) + __uint_as_float(sc[c]);
             }
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&s_empty[b]);
             const int key0 = j * kKeys;
+            if (key0 + kKeys > a.lk) {
+#pragma unroll
+                for (int c = 0; c < kKeys; ++c)
+                    if (key0 + c >= a.lk) sv[c] = -INFINITY;
+            }
             float mx = m;
 #pragma unroll
-            for (int c = 0; c < kKeys; ++c) {
-                if (key0 + c >= a.lk) sv[c] = -INFINITY;
-                mx = fmaxf(mx, sv[c]);
-            }
+            for (int c = 0; c < kKeys; ++c) mx = fmaxf(mx, sv[c]);
+            // exp(scale (s - m)) = 2^(s c - m c), c = scale log2(e): one FMA and the
+            // MUFU exponential (relative error ~2^-22) per score.
             const float m_use = mx == -INFINITY ? 0.0f : mx;
-            const float alpha = expf(m - m_use);
+            const float mc = m_use * a.scale_log2e;
+            const float alpha = ex2_mufu(fmaf(m, a.scale_log2e, -mc));
             float sum = 0.0f;
 #pragma unroll
             for (int c = 0; c < kKeys; ++c) {
-                sv[c] = expf(sv[c] - m_use);
+                sv[c] = ex2_mufu(fmaf(sv[c], a.scale_log2e, -mc));
                 sum += sv[c];
             }
             l = fmaf(l, alpha, sum);
@@ -415,7 +420,7 @@ bool attention_tc_eligible(int lq, int lk, int head_dim, int causal, const float
 void launch_attention_tc(const float* q, int64_t ldq, const float* k, int64_t ldk, const float* v, int64_t ldv,
                          int lq, int lk, int heads, int head_dim, float scale, float* out, int64_t ldo,
                          DeviceState& state, cudaStream_t stream) {
-    TcArgs a{q, k, v, out, ldq, ldk, ldv, ldo, lq, lk, scale, state.status};
+    TcArgs a{q, k, v, out, ldq, ldk, ldv, ldo, lq, lk, scale * 1.4426950408889634f, state.status};
     const dim3 grid((lq + kQ - 1) / kQ, heads);
     if (head_dim == 64) {
         using L = TcLayout<64>;
