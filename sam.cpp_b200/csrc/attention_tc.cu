@@ -55,6 +55,8 @@ template <int HD>
 struct TcLayout {
     static constexpr int stages = HD == 32 ? 2 : 1;
     static constexpr int p_bufs = HD == 32 ? 2 : 1;           // P double-buffered where shared memory allows
+    static constexpr int s_bufs = HD == 32 ? 2 : 1;           // S buffers in TMEM (3 accumulators each)
+    static constexpr int o_bufs = 1;                          // O buffers in TMEM (3 accumulators each)
     static constexpr int chunks = HD / 32;                    // 128-byte swizzle rows along the head dim
     static constexpr int q_bytes = chunks * kQ * 128;         // one of hi / lo
     static constexpr int k_bytes = chunks * kKeys * 128;      // K tile [64 keys][HD], one of hi / lo
@@ -65,11 +67,15 @@ struct TcLayout {
     static constexpr int v_off = k_off + stages * 2 * k_bytes;
     static constexpr int p_off = v_off + stages * 2 * v_bytes;
     static constexpr int bar_off = p_off + p_bufs * 2 * p_bytes;
-    static constexpr int bars = 1 + 2 * stages + 2 * 2 + p_bufs + 2 * 2 + 1;
+    static constexpr int bars = 1 + 2 * stages + 2 * s_bufs + p_bufs + 2 * o_bufs + 1;
     static constexpr int total = bar_off + bars * 8 + 16 + 1024;
-    // TMEM columns: S (hi*hi, corrections) x 2 buffers, then O likewise.
-    __host__ __device__ static constexpr uint32_t s_col(int b) { return static_cast<uint32_t>(b * 2 * kKeys); }
-    __host__ __device__ static constexpr uint32_t o_col(int b) { return static_cast<uint32_t>(4 * kKeys + b * 2 * HD); }
+    // TMEM columns: S buffers of three accumulators (hi*hi, hi*lo, lo*hi: three
+    // independent MMA chains instead of one long one), then O likewise.
+    __host__ __device__ static constexpr uint32_t s_col(int b) { return static_cast<uint32_t>(b * 3 * kKeys); }
+    __host__ __device__ static constexpr uint32_t o_col(int b) {
+        return static_cast<uint32_t>(s_bufs * 3 * kKeys + b * 3 * HD);
+    }
+    static_assert(s_bufs * 3 * kKeys + o_bufs * 3 * HD <= 512, "TMEM columns");
 };
 
 // Byte offset of element (row, k) of a K-major operand tile stored as
@@ -95,17 +101,20 @@ struct TcArgs {
 template <int HD, class L>
 __device__ __forceinline__ bool take_o(float (&o)[HD], float alpha, int j, uint64_t* o_full, uint64_t* o_empty,
                                        uint32_t tmem_lane, int lane, DeviceStatus* status) {
-    const int b = j & 1;
-    if (!__all_sync(0xffffffffu, mbar_poll(&o_full[b], (j >> 1) & 1u, status, 88))) return false;
+    const int b = j % L::o_bufs;
+    if (!__all_sync(0xffffffffu, mbar_poll(&o_full[b], (j / L::o_bufs) & 1u, status, 88))) return false;
     tc_fence_after();
 #pragma unroll
     for (int c0 = 0; c0 < HD; c0 += 32) {
-        uint32_t oh[32], oc[32];
-        tc_ld_32x32b_x32(tmem_lane + L::o_col(b) + c0, oh);
-        tc_ld_32x32b_x32(tmem_lane + L::o_col(b) + HD + c0, oc);
+        uint32_t o0[32], o1[32], o2[32];
+        tc_ld_32x32b_x32(tmem_lane + L::o_col(b) + c0, o0);
+        tc_ld_32x32b_x32(tmem_lane + L::o_col(b) + HD + c0, o1);
+        tc_ld_32x32b_x32(tmem_lane + L::o_col(b) + 2 * HD + c0, o2);
         tc_wait_ld();
 #pragma unroll
-        for (int c = 0; c < 32; ++c) o[c0 + c] = fmaf(o[c0 + c], alpha, __uint_as_float(oh[c]) + __uint_as_float(oc[c]));
+        for (int c = 0; c < 32; ++c)
+            o[c0 + c] = fmaf(o[c0 + c], alpha,
+                             __uint_as_float(o0[c]) + (__uint_as_float(o1[c]) + __uint_as_float(o2[c])));
     }
     tc_fence_before();
     __syncwarp();
@@ -123,11 +132,11 @@ __global__ void __launch_bounds__(kTcThreads, 1) attention_tc_kernel(const TcArg
     uint64_t* kv_full = q_full + 1;
     uint64_t* kv_empty = kv_full + L::stages;
     uint64_t* s_full = kv_empty + L::stages;
-    uint64_t* s_empty = s_full + 2;
-    uint64_t* p_full = s_empty + 2;
+    uint64_t* s_empty = s_full + L::s_bufs;
+    uint64_t* p_full = s_empty + L::s_bufs;
     uint64_t* o_full = p_full + L::p_bufs;
-    uint64_t* o_empty = o_full + 2;
-    uint64_t* drain = o_empty + 2;
+    uint64_t* o_empty = o_full + L::o_bufs;
+    uint64_t* drain = o_empty + L::o_bufs;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
     DeviceStatus* status = a.status;
 
@@ -141,9 +150,11 @@ __global__ void __launch_bounds__(kTcThreads, 1) attention_tc_kernel(const TcArg
             mbar_init(&kv_full[s], kLoaders);
             mbar_init(&kv_empty[s], 1);
         }
-        for (int b = 0; b < 2; ++b) {
+        for (int b = 0; b < L::s_bufs; ++b) {
             mbar_init(&s_full[b], 1);
             mbar_init(&s_empty[b], 4);
+        }
+        for (int b = 0; b < L::o_bufs; ++b) {
             mbar_init(&o_full[b], 1);
             mbar_init(&o_empty[b], 4);
         }
@@ -248,36 +259,38 @@ __global__ void __launch_bounds__(kTcThreads, 1) attention_tc_kernel(const TcArg
             const uint32_t qh = smem_u32(smem + L::q_off), ql = qh + L::q_bytes;
             bool ok = mbar_wait(q_full, 0, status, 82);
             auto issue_s = [&](int j) -> bool {
-                const int s = j % L::stages, b = j & 1;
+                const int s = j % L::stages, b = j % L::s_bufs;
                 if (!mbar_poll(&kv_full[s], (j / L::stages) & 1u, status, 83)) return false;
-                if (!mbar_poll(&s_empty[b], ((j >> 1) & 1u) ^ 1u, status, 84)) return false;
+                if (!mbar_poll(&s_empty[b], ((j / L::s_bufs) & 1u) ^ 1u, status, 84)) return false;
                 tc_fence_after();
                 const uint32_t kh = smem_u32(smem + L::k_off + s * 2 * L::k_bytes), kl = kh + L::k_bytes;
-                const uint32_t dh = tmem_base + L::s_col(b), dc = dh + kKeys;
+                const uint32_t d0 = tmem_base + L::s_col(b), d1 = d0 + kKeys, d2 = d0 + 2 * kKeys;
 #pragma unroll
                 for (int t = 0; t < HD / 8; ++t) {
                     const uint32_t qo = (t >> 2) * kQ * 128 + (t & 3) * 32, ko = (t >> 2) * kKeys * 128 + (t & 3) * 32;
-                    mma_tf32(dh, smem_desc_sw128(qh + qo), smem_desc_sw128(kh + ko), id_s, t != 0 ? 1u : 0u);
-                    mma_tf32(dc, smem_desc_sw128(qh + qo), smem_desc_sw128(kl + ko), id_s, t != 0 ? 1u : 0u);
-                    mma_tf32(dc, smem_desc_sw128(ql + qo), smem_desc_sw128(kh + ko), id_s, 1u);
+                    const uint32_t acc = t != 0 ? 1u : 0u;
+                    mma_tf32(d0, smem_desc_sw128(qh + qo), smem_desc_sw128(kh + ko), id_s, acc);
+                    mma_tf32(d1, smem_desc_sw128(qh + qo), smem_desc_sw128(kl + ko), id_s, acc);
+                    mma_tf32(d2, smem_desc_sw128(ql + qo), smem_desc_sw128(kh + ko), id_s, acc);
                 }
                 tc_commit(&s_full[b]);
                 return true;
             };
             auto issue_o = [&](int j) -> bool {
-                const int s = j % L::stages, b = j & 1, pb = j % L::p_bufs;
+                const int s = j % L::stages, b = j % L::o_bufs, pb = j % L::p_bufs;
                 if (!mbar_poll(&p_full[pb], (j / L::p_bufs) & 1u, status, 85)) return false;
-                if (!mbar_poll(&o_empty[b], ((j >> 1) & 1u) ^ 1u, status, 86)) return false;
+                if (!mbar_poll(&o_empty[b], ((j / L::o_bufs) & 1u) ^ 1u, status, 86)) return false;
                 tc_fence_after();
                 const uint32_t vh = smem_u32(smem + L::v_off + s * 2 * L::v_bytes), vl = vh + L::v_bytes;
                 const uint32_t ph = smem_u32(smem + L::p_off + pb * 2 * L::p_bytes), pl = ph + L::p_bytes;
-                const uint32_t dh = tmem_base + L::o_col(b), dc = dh + HD;
+                const uint32_t d0 = tmem_base + L::o_col(b), d1 = d0 + HD, d2 = d0 + 2 * HD;
 #pragma unroll
                 for (int t = 0; t < kKeys / 8; ++t) {
                     const uint32_t po = (t >> 2) * kQ * 128 + (t & 3) * 32, vo = (t >> 2) * HD * 128 + (t & 3) * 32;
-                    mma_tf32(dh, smem_desc_sw128(ph + po), smem_desc_sw128(vh + vo), id_o, t != 0 ? 1u : 0u);
-                    mma_tf32(dc, smem_desc_sw128(ph + po), smem_desc_sw128(vl + vo), id_o, t != 0 ? 1u : 0u);
-                    mma_tf32(dc, smem_desc_sw128(pl + po), smem_desc_sw128(vh + vo), id_o, 1u);
+                    const uint32_t acc = t != 0 ? 1u : 0u;
+                    mma_tf32(d0, smem_desc_sw128(ph + po), smem_desc_sw128(vh + vo), id_o, acc);
+                    mma_tf32(d1, smem_desc_sw128(ph + po), smem_desc_sw128(vl + vo), id_o, acc);
+                    mma_tf32(d2, smem_desc_sw128(pl + po), smem_desc_sw128(vh + vo), id_o, acc);
                 }
                 tc_commit(&o_full[b]);
                 tc_commit(&kv_empty[s]);
@@ -308,8 +321,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) attention_tc_kernel(const TcArg
         for (int c = 0; c < HD; ++c) o[c] = 0.0f;
         bool ok = true;
         for (int j = 0; j < tiles && ok; ++j) {
-            const int b = j & 1;
-            if (!__all_sync(0xffffffffu, mbar_poll(&s_full[b], (j >> 1) & 1u, status, 89))) {
+            const int b = j % L::s_bufs;
+            if (!__all_sync(0xffffffffu, mbar_poll(&s_full[b], (j / L::s_bufs) & 1u, status, 89))) {
                 ok = false;
                 break;
             }
@@ -317,12 +330,14 @@ __global__ void __launch_bounds__(kTcThreads, 1) attention_tc_kernel(const TcArg
             float sv[kKeys];  // raw scores Q . K (scale applied in the exponent)
 #pragma unroll
             for (int c0 = 0; c0 < kKeys; c0 += 32) {
-                uint32_t sh[32], sc[32];
-                tc_ld_32x32b_x32(tmem_base + lane_addr + L::s_col(b) + c0, sh);
-                tc_ld_32x32b_x32(tmem_base + lane_addr + L::s_col(b) + kKeys + c0, sc);
+                uint32_t s0[32], s1[32], s2[32];
+                tc_ld_32x32b_x32(tmem_base + lane_addr + L::s_col(b) + c0, s0);
+                tc_ld_32x32b_x32(tmem_base + lane_addr + L::s_col(b) + kKeys + c0, s1);
+                tc_ld_32x32b_x32(tmem_base + lane_addr + L::s_col(b) + 2 * kKeys + c0, s2);
                 tc_wait_ld();
 #pragma unroll
-                for (int c = 0; c < 32; ++c) sv[c0 + c] = __uint_as_float(sh[c]) + __uint_as_float(sc[c]);
+                for (int c = 0; c < 32; ++c)
+                    sv[c0 + c] = __uint_as_float(s0[c]) + (__uint_as_float(s1[c]) + __uint_as_float(s2[c]));
             }
             tc_fence_before();
             __syncwarp();
