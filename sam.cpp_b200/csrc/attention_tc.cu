@@ -258,11 +258,12 @@ __global__ void __launch_bounds__(kTcThreads, 1) attention_tc_kernel(const TcArg
             constexpr uint32_t id_o = idesc_tf32_mn(kQ, HD);
             const uint32_t qh = smem_u32(smem + L::q_off), ql = qh + L::q_bytes;
             bool ok = mbar_wait(q_full, 0, status, 82);
-            auto issue_s = [&](int j) -> bool {
+            // Issue S_js and P_jo V_jo in whichever order their inputs become
+            // ready (S_{j+1} runs ahead of P_j V_j by at most one tile).  The
+            // readiness probes do not block; the loop is bounded by the wait
+            // timeout like every other wait.
+            auto issue_s = [&](int j) {
                 const int s = j % L::stages, b = j % L::s_bufs;
-                if (!mbar_poll(&kv_full[s], (j / L::stages) & 1u, status, 83)) return false;
-                if (!mbar_poll(&s_empty[b], ((j / L::s_bufs) & 1u) ^ 1u, status, 84)) return false;
-                tc_fence_after();
                 const uint32_t kh = smem_u32(smem + L::k_off + s * 2 * L::k_bytes), kl = kh + L::k_bytes;
                 const uint32_t d0 = tmem_base + L::s_col(b), d1 = d0 + kKeys, d2 = d0 + 2 * kKeys;
 #pragma unroll
@@ -274,13 +275,9 @@ __global__ void __launch_bounds__(kTcThreads, 1) attention_tc_kernel(const TcArg
                     mma_tf32(d2, smem_desc_sw128(ql + qo), smem_desc_sw128(kh + ko), id_s, acc);
                 }
                 tc_commit(&s_full[b]);
-                return true;
             };
-            auto issue_o = [&](int j) -> bool {
+            auto issue_o = [&](int j) {
                 const int s = j % L::stages, b = j % L::o_bufs, pb = j % L::p_bufs;
-                if (!mbar_poll(&p_full[pb], (j / L::p_bufs) & 1u, status, 85)) return false;
-                if (!mbar_poll(&o_empty[b], ((j / L::o_bufs) & 1u) ^ 1u, status, 86)) return false;
-                tc_fence_after();
                 const uint32_t vh = smem_u32(smem + L::v_off + s * 2 * L::v_bytes), vl = vh + L::v_bytes;
                 const uint32_t ph = smem_u32(smem + L::p_off + pb * 2 * L::p_bytes), pl = ph + L::p_bytes;
                 const uint32_t d0 = tmem_base + L::o_col(b), d1 = d0 + HD, d2 = d0 + 2 * HD;
@@ -294,18 +291,36 @@ __global__ void __launch_bounds__(kTcThreads, 1) attention_tc_kernel(const TcArg
                 }
                 tc_commit(&o_full[b]);
                 tc_commit(&kv_empty[s]);
-                return true;
             };
-            if (ok && tiles > 0) ok = issue_s(0);
-            for (int j = 0; j < tiles && ok; ++j) {
-                if (L::stages >= 2) {
-                    // S_{j+1} ahead of P_j V_j: the softmax of tile j + 1 overlaps P_j V_j.
-                    if (j + 1 < tiles && !issue_s(j + 1)) break;
-                    ok = issue_o(j);
-                } else {
-                    // One K / V stage: it holds tile j until P_j V_j is done.
-                    ok = issue_o(j);
-                    if (ok && j + 1 < tiles) ok = issue_s(j + 1);
+            int js = 0, jo = 0;  // next S / next P V to issue
+            uint64_t last = global_timer_ns();  // time of the last issue
+            uint32_t spin = 0;
+            while (ok && jo < tiles) {
+                bool progressed = false;
+                // S_js needs its K tile, a free S buffer, and (to keep at most one
+                // tile of lookahead over P V) js <= jo + 1.
+                if (js < tiles && js <= jo + 1 && mbar_test_wait(&kv_full[js % L::stages], (js / L::stages) & 1u) &&
+                    mbar_test_wait(&s_empty[js % L::s_bufs], ((js / L::s_bufs) & 1u) ^ 1u)) {
+                    tc_fence_after();
+                    issue_s(js++);
+                    progressed = true;
+                }
+                if (jo < js && mbar_test_wait(&p_full[jo % L::p_bufs], (jo / L::p_bufs) & 1u) &&
+                    mbar_test_wait(&o_empty[jo % L::o_bufs], ((jo / L::o_bufs) & 1u) ^ 1u)) {
+                    tc_fence_after();
+                    issue_o(jo++);
+                    progressed = true;
+                }
+                if (progressed) {
+                    spin = 0;
+                } else if ((++spin & 63u) == 0) {
+                    const uint64_t now = global_timer_ns();
+                    if (spin == 64) last = now;  // first check of this stall
+                    if (now - last > kWaitTimeoutNs) {  // no issue possible for a whole wait limit
+                        atomicOr(&status->flags, kStatusTimeout);
+                        atomicExch(&status->timeout_site, 83u);
+                        ok = false;
+                    }
                 }
             }
             tc_commit(drain);
@@ -348,20 +363,26 @@ __global__ void __launch_bounds__(kTcThreads, 1) attention_tc_kernel(const TcArg
                 for (int c = 0; c < kKeys; ++c)
                     if (key0 + c >= a.lk) sv[c] = -INFINITY;
             }
-            float mx = m;
+            float pm[8];
 #pragma unroll
-            for (int c = 0; c < kKeys; ++c) mx = fmaxf(mx, sv[c]);
+            for (int i = 0; i < 8; ++i) pm[i] = sv[i];
+#pragma unroll
+            for (int c = 8; c < kKeys; ++c) pm[c & 7] = fmaxf(pm[c & 7], sv[c]);
+            const float mx = fmaxf(fmaxf(fmaxf(fmaxf(pm[0], pm[1]), fmaxf(pm[2], pm[3])), fmaxf(fmaxf(pm[4], pm[5]), fmaxf(pm[6], pm[7]))), m);
             // exp(scale (s - m)) = 2^(s c - m c), c = scale log2(e): one FMA and the
             // MUFU exponential (relative error ~2^-22) per score.
             const float m_use = mx == -INFINITY ? 0.0f : mx;
             const float mc = m_use * a.scale_log2e;
             const float alpha = ex2_mufu(fmaf(m, a.scale_log2e, -mc));
-            float sum = 0.0f;
+            float ps[8];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) ps[i] = 0.0f;
 #pragma unroll
             for (int c = 0; c < kKeys; ++c) {
                 sv[c] = ex2_mufu(fmaf(sv[c], a.scale_log2e, -mc));
-                sum += sv[c];
+                ps[c & 7] += sv[c];
             }
+            const float sum = ((ps[0] + ps[1]) + (ps[2] + ps[3])) + ((ps[4] + ps[5]) + (ps[6] + ps[7]));
             l = fmaf(l, alpha, sum);
             m = mx;
             // P buffer j % p_bufs is free once P V of its previous tile is done:
