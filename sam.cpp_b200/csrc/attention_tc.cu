@@ -12,14 +12,17 @@
 //   S = Q K^T:  M = 128 queries, N = 64 keys, K = head dim (32 / 64)
 //   O = P V:    M = 128 queries, N = head dim, K = 64 keys
 // The online softmax runs in f32 registers of the softmax warps (one query row
-// per thread, read from TMEM); P goes to shared memory as its hi / lo split.
+// per thread, read from TMEM); P goes back to TMEM as its hi / lo split and is
+// the A operand of P V straight from there, so the P V MMAs read only V from
+// shared memory (with 4-byte operands, shared-memory bandwidth for A would
+// otherwise bound every MMA).
 // Per 64-key tile the output O_t is a fresh accumulator and the softmax warps
 // add it as o = o * alpha + O_t (the blocked sum of the SIMT kernel).
 //
 // One CTA per (128 queries, head), 224 threads (7 warps, so no SM
 // sub-partition holds more than two and every thread may use 255 registers):
 //   warps 0-1  loaders: Q once, then K and V^T tiles (hi / lo, 128-byte swizzle)
-//   warp 2     TMEM owner and MMA issuer (S_j is issued ahead of P_{j-1} V_{j-1})
+//   warp 2     TMEM owner and MMA issuer (S and P V in readiness order)
 //   warps 3-6  softmax (TMEM lane quarter = warp % 4)
 // No TMA multicast; every mbarrier wait is bounded (kStatusTimeout on expiry).
 #include <algorithm>
@@ -51,31 +54,43 @@ __device__ __forceinline__ void mma_tf32(uint32_t tmem_d, uint64_t adesc, uint64
         : "memory");
 }
 
+// D (+)= A(tmem) * B(smem desc)^T, kind::tf32: A is M lanes x K columns of TMEM.
+__device__ __forceinline__ void mma_tf32_ts(uint32_t tmem_d, uint32_t tmem_a, uint64_t bdesc, uint32_t idesc,
+                                            uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::tf32 [%0], [%1], %2, %3, p;\n\t}" ::"r"(tmem_d),
+        "r"(tmem_a), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
 template <int HD>
 struct TcLayout {
-    static constexpr int stages = HD == 32 ? 2 : 1;
-    static constexpr int p_bufs = HD == 32 ? 2 : 1;           // P double-buffered where shared memory allows
-    static constexpr int s_bufs = HD == 32 ? 2 : 1;           // S buffers in TMEM (3 accumulators each)
-    static constexpr int o_bufs = 1;                          // O buffers in TMEM (3 accumulators each)
+    static constexpr int stages = HD == 32 ? 4 : 2;           // K / V tiles in flight
+    static constexpr int p_bufs = 1;                          // P (TMEM), S and O: one buffer each
+    static constexpr int s_bufs = 1;
+    static constexpr int o_bufs = 1;
     static constexpr int chunks = HD / 32;                    // 128-byte swizzle rows along the head dim
     static constexpr int q_bytes = chunks * kQ * 128;         // one of hi / lo
     static constexpr int k_bytes = chunks * kKeys * 128;      // K tile [64 keys][HD], one of hi / lo
     static constexpr int v_bytes = 2 * HD * 128;              // V^T tile [HD][64 keys], one of hi / lo
-    static constexpr int p_bytes = 2 * kQ * 128;              // P [128][64 keys], one of hi / lo
     static constexpr int q_off = 0;
     static constexpr int k_off = q_off + 2 * q_bytes;
     static constexpr int v_off = k_off + stages * 2 * k_bytes;
-    static constexpr int p_off = v_off + stages * 2 * v_bytes;
-    static constexpr int bar_off = p_off + p_bufs * 2 * p_bytes;
+    static constexpr int bar_off = v_off + stages * 2 * v_bytes;
     static constexpr int bars = 1 + 2 * stages + 2 * s_bufs + p_bufs + 2 * o_bufs + 1;
     static constexpr int total = bar_off + bars * 8 + 16 + 1024;
-    // TMEM columns: S buffers of three accumulators (hi*hi, hi*lo, lo*hi: three
-    // independent MMA chains instead of one long one), then O likewise.
-    __host__ __device__ static constexpr uint32_t s_col(int b) { return static_cast<uint32_t>(b * 3 * kKeys); }
-    __host__ __device__ static constexpr uint32_t o_col(int b) {
-        return static_cast<uint32_t>(s_bufs * 3 * kKeys + b * 3 * HD);
+    // TMEM columns: P hi, P lo (64 each), S as three accumulators (hi*hi,
+    // hi*lo, lo*hi: independent MMA chains), O likewise.
+    static constexpr uint32_t p_col = 0;
+    __host__ __device__ static constexpr uint32_t s_col(int b) {
+        return static_cast<uint32_t>(2 * kKeys + b * 3 * kKeys);
     }
-    static_assert(s_bufs * 3 * kKeys + o_bufs * 3 * HD <= 512, "TMEM columns");
+    __host__ __device__ static constexpr uint32_t o_col(int b) {
+        return static_cast<uint32_t>(2 * kKeys + s_bufs * 3 * kKeys + b * 3 * HD);
+    }
+    static_assert(2 * kKeys + s_bufs * 3 * kKeys + o_bufs * 3 * HD <= 512, "TMEM columns");
 };
 
 // Byte offset of element (row, k) of a K-major operand tile stored as
@@ -277,17 +292,17 @@ __global__ void __launch_bounds__(kTcThreads, 1) attention_tc_kernel(const TcArg
                 tc_commit(&s_full[b]);
             };
             auto issue_o = [&](int j) {
-                const int s = j % L::stages, b = j % L::o_bufs, pb = j % L::p_bufs;
+                const int s = j % L::stages, b = j % L::o_bufs;
                 const uint32_t vh = smem_u32(smem + L::v_off + s * 2 * L::v_bytes), vl = vh + L::v_bytes;
-                const uint32_t ph = smem_u32(smem + L::p_off + pb * 2 * L::p_bytes), pl = ph + L::p_bytes;
+                const uint32_t ph = tmem_base + L::p_col, pl = ph + kKeys;
                 const uint32_t d0 = tmem_base + L::o_col(b), d1 = d0 + HD, d2 = d0 + 2 * HD;
 #pragma unroll
                 for (int t = 0; t < kKeys / 8; ++t) {
-                    const uint32_t po = (t >> 2) * kQ * 128 + (t & 3) * 32, vo = (t >> 2) * HD * 128 + (t & 3) * 32;
+                    const uint32_t vo = (t >> 2) * HD * 128 + (t & 3) * 32;
                     const uint32_t acc = t != 0 ? 1u : 0u;
-                    mma_tf32(d0, smem_desc_sw128(ph + po), smem_desc_sw128(vh + vo), id_o, acc);
-                    mma_tf32(d1, smem_desc_sw128(ph + po), smem_desc_sw128(vl + vo), id_o, acc);
-                    mma_tf32(d2, smem_desc_sw128(pl + po), smem_desc_sw128(vh + vo), id_o, acc);
+                    mma_tf32_ts(d0, ph + 8 * t, smem_desc_sw128(vh + vo), id_o, acc);
+                    mma_tf32_ts(d1, ph + 8 * t, smem_desc_sw128(vl + vo), id_o, acc);
+                    mma_tf32_ts(d2, pl + 8 * t, smem_desc_sw128(vh + vo), id_o, acc);
                 }
                 tc_commit(&o_full[b]);
                 tc_commit(&kv_empty[s]);
@@ -385,40 +400,31 @@ __global__ void __launch_bounds__(kTcThreads, 1) attention_tc_kernel(const TcArg
             const float sum = ((ps[0] + ps[1]) + (ps[2] + ps[3])) + ((ps[4] + ps[5]) + (ps[6] + ps[7]));
             l = fmaf(l, alpha, sum);
             m = mx;
-            // P buffer j % p_bufs is free once P V of its previous tile is done:
-            // with one buffer that is tile j - 1 (taken here, before the write),
-            // with two it is j - 2 (taken in the previous iteration).
-            if (L::p_bufs == 1 && j > 0) {
+            // P (TMEM) is free once P_{j-1} V_{j-1} is done: take O_{j-1} first.
+            if (j > 0) {
                 if (!take_o<HD, L>(o, alpha_prev, j - 1, o_full, o_empty, tmem_base + lane_addr, lane, status)) {
                     ok = false;
                     break;
                 }
-                alpha_prev = alpha;
             }
-            uint8_t* sph = smem + L::p_off + (j % L::p_bufs) * 2 * L::p_bytes;
-            uint8_t* spl = sph + L::p_bytes;
+            alpha_prev = alpha;
 #pragma unroll
-            for (int c4 = 0; c4 < kKeys / 4; ++c4) {
-                float4 hi, lo;
-                split_tf32(sv[4 * c4], hi.x, lo.x);
-                split_tf32(sv[4 * c4 + 1], hi.y, lo.y);
-                split_tf32(sv[4 * c4 + 2], hi.z, lo.z);
-                split_tf32(sv[4 * c4 + 3], hi.w, lo.w);
-                const uint32_t off = sw_off(row, 4 * c4, kQ);
-                *reinterpret_cast<float4*>(sph + off) = hi;
-                *reinterpret_cast<float4*>(spl + off) = lo;
-            }
-            fence_proxy_async_smem();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&p_full[j % L::p_bufs]);
-            if (L::p_bufs == 2) {
-                if (j > 0 &&
-                    !take_o<HD, L>(o, alpha_prev, j - 1, o_full, o_empty, tmem_base + lane_addr, lane, status)) {
-                    ok = false;
-                    break;
+            for (int c0 = 0; c0 < kKeys; c0 += 32) {
+                uint32_t hi[32], lo[32];
+#pragma unroll
+                for (int c = 0; c < 32; ++c) {
+                    float h, lw;
+                    split_tf32(sv[c0 + c], h, lw);
+                    hi[c] = __float_as_uint(h);
+                    lo[c] = __float_as_uint(lw);
                 }
-                alpha_prev = alpha;
+                tc_st_32x32b_x32(tmem_base + lane_addr + L::p_col + c0, hi);
+                tc_st_32x32b_x32(tmem_base + lane_addr + L::p_col + kKeys + c0, lo);
             }
+            tc_wait_st();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&p_full[0]);
         }
         if (ok && tiles > 0)
             ok = take_o<HD, L>(o, alpha_prev, tiles - 1, o_full, o_empty, tmem_base + lane_addr, lane, status);
