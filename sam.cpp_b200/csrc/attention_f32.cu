@@ -76,6 +76,23 @@ __global__ void __launch_bounds__(256) rope_f32_kernel(const float* __restrict__
     }
 }
 
+// In place on f32 qkv rows [rows][ldq] (Q at columns 0.., K at embed..): the
+// RoPE of sam3_apply_rope for token position r % group_n of every row r.
+__global__ void __launch_bounds__(256) rope_rows_kernel(float* __restrict__ qkv, int64_t ldq, int64_t embed,
+                                                        int64_t rows, int group_n, const float* __restrict__ freqs) {
+    const int64_t per_row = 2 * embed / 4;  // float4 units of Q and K
+    const int64_t units = rows * per_row;
+    for (int64_t u = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; u < units; u += int64_t(gridDim.x) * blockDim.x) {
+        const int64_t r = u / per_row, c4 = u - r * per_row;
+        const int64_t pos = r % group_n;
+        const int64_t col = c4 * 4;  // Q: col, K: col (>= embed)
+        const int64_t in_head = (col % embed) % kHd;
+        float4* p = reinterpret_cast<float4*>(qkv + r * ldq + col);
+        const float4 f = __ldg(reinterpret_cast<const float4*>(freqs + (pos * (kHd / 2) + in_head / 2) * 2));
+        *p = rope4(*p, f);
+    }
+}
+
 __device__ __forceinline__ float dot4(float4 a, float4 b, float acc) {
     acc = fmaf(a.x, b.x, acc);
     acc = fmaf(a.y, b.y, acc);
@@ -543,6 +560,15 @@ void launch_attention_gen(const float* q, int64_t ldq, const float* k, int64_t l
                        "attention_combine_kernel launch", static_cast<const float*>(partials), splits, heads, lq, out,
                        ldo);
     }
+}
+
+void launch_rope_rows(float* qkv, int64_t ldq, int64_t embed, int64_t rows, int group_n, const float* freqs,
+                      cudaStream_t stream) {
+    const int64_t units = rows * (2 * embed / 4);
+    if (units == 0) return;
+    const int64_t blocks = std::min<int64_t>((units + 255) / 256, int64_t(148) * 16);
+    rope_rows_kernel<<<static_cast<unsigned>(blocks), 256, 0, stream>>>(qkv, ldq, embed, rows, group_n, freqs);
+    check_cuda(cudaGetLastError(), "rope_rows_kernel launch");
 }
 
 void launch_rope_f32(const float* x, const float* freqs, int64_t tokens, int64_t head_batches, float* out,

@@ -107,6 +107,11 @@ struct TcArgs {
     float* out;
     int64_t ldq, ldk, ldv, ldo;
     int lq, lk;
+    // Groups (blockIdx.z): independent attention problems of lq queries / lk
+    // keys whose rows follow each other in q, k, v (ViT windows or images).
+    // Output row of (group g, query n): g * lq + n, or with out_window > 0 the
+    // raster token of window g in a grid out_grid_w wide (ggml_win_unpart).
+    int out_window, out_grid_w;
     float scale_log2e;  // softmax scale x log2(e)
     DeviceStatus* status;
 };
@@ -156,8 +161,11 @@ __global__ void __launch_bounds__(kTcThreads, 1) attention_tc_kernel(const TcArg
     DeviceStatus* status = a.status;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int q0 = blockIdx.x * kQ, h = blockIdx.y;
+    const int q0 = blockIdx.x * kQ, h = blockIdx.y, g = blockIdx.z;
     const int tiles = (a.lk + kKeys - 1) / kKeys;
+    const float* gq = a.q + int64_t(g) * a.lq * a.ldq;
+    const float* gk = a.k + int64_t(g) * a.lk * a.ldk;
+    const float* gv = a.v + int64_t(g) * a.lk * a.ldv;
 
     if (threadIdx.x == 0) {
         mbar_init(q_full, kLoaders);
@@ -198,7 +206,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) attention_tc_kernel(const TcArg
 #pragma unroll
             for (int i = 0; i < kQLoads; ++i) {
                 const int idx = t + kLt * i, r = idx / (HD / 4), d4 = idx % (HD / 4), n = q0 + r;
-                x[i] = n < a.lq ? __ldg(reinterpret_cast<const float4*>(a.q + int64_t(n) * a.ldq + h * HD) + d4)
+                x[i] = n < a.lq ? __ldg(reinterpret_cast<const float4*>(gq + int64_t(n) * a.ldq + h * HD) + d4)
                                 : make_float4(0.f, 0.f, 0.f, 0.f);
             }
 #pragma unroll
@@ -226,9 +234,9 @@ __global__ void __launch_bounds__(kTcThreads, 1) attention_tc_kernel(const TcArg
                 const int idx = t + kLt * i;
                 const int rk = idx / (HD / 4), dk = idx % (HD / 4), nk = key0 + rk;
                 const int rv = idx % kKeys, dv = idx / kKeys, nv = key0 + rv;
-                xk[i] = nk < a.lk ? __ldg(reinterpret_cast<const float4*>(a.k + int64_t(nk) * a.ldk + h * HD) + dk)
+                xk[i] = nk < a.lk ? __ldg(reinterpret_cast<const float4*>(gk + int64_t(nk) * a.ldk + h * HD) + dk)
                                   : make_float4(0.f, 0.f, 0.f, 0.f);
-                xv[i] = nv < a.lk ? __ldg(reinterpret_cast<const float4*>(a.v + int64_t(nv) * a.ldv + h * HD) + dv)
+                xv[i] = nv < a.lk ? __ldg(reinterpret_cast<const float4*>(gv + int64_t(nv) * a.ldv + h * HD) + dv)
                                   : make_float4(0.f, 0.f, 0.f, 0.f);
             }
             if (!__all_sync(0xffffffffu, mbar_poll(&kv_empty[s], ((j / L::stages) & 1u) ^ 1u, status, 81))) break;
@@ -431,7 +439,13 @@ __global__ void __launch_bounds__(kTcThreads, 1) attention_tc_kernel(const TcArg
         pdl_trigger();
         const int n = q0 + row;
         if (ok && n < a.lq) {
-            float* dst = a.out + int64_t(n) * a.ldo + h * HD;
+            int64_t orow = int64_t(g) * a.lq + n;
+            if (a.out_window > 0) {
+                const int per_row = a.out_grid_w / a.out_window;
+                const int wy = g / per_row, wx = g % per_row, ly = n / a.out_window, lx = n % a.out_window;
+                orow = int64_t(wy * a.out_window + ly) * a.out_grid_w + wx * a.out_window + lx;
+            }
+            float* dst = a.out + orow * a.ldo + h * HD;
 #pragma unroll
             for (int c4 = 0; c4 < HD / 4; ++c4) {
                 float4 r4;
@@ -453,6 +467,16 @@ __global__ void __launch_bounds__(kTcThreads, 1) attention_tc_kernel(const TcArg
 
 }  // namespace
 
+template <int HD>
+void launch_tc(const TcArgs& a, int heads, int groups, DeviceState& state, cudaStream_t stream) {
+    using L = TcLayout<HD>;
+    static_assert(L::total <= 232448, "shared memory budget");
+    set_smem_limit_once(state, reinterpret_cast<const void*>(attention_tc_kernel<HD>), L::total,
+                        "cudaFuncSetAttribute(attention_tc smem)");
+    const dim3 grid((a.lq + kQ - 1) / kQ, heads, groups);
+    launch_pdl(attention_tc_kernel<HD>, grid, dim3(kTcThreads), L::total, stream, "attention_tc_kernel launch", a);
+}
+
 bool attention_tc_eligible(int lq, int lk, int head_dim, int causal, const float* bias, const float* out,
                            int64_t ldo) {
     return (head_dim == 32 || head_dim == 64) && !causal && bias == nullptr && lq >= 1024 && lk >= 256 &&
@@ -462,21 +486,22 @@ bool attention_tc_eligible(int lq, int lk, int head_dim, int causal, const float
 void launch_attention_tc(const float* q, int64_t ldq, const float* k, int64_t ldk, const float* v, int64_t ldv,
                          int lq, int lk, int heads, int head_dim, float scale, float* out, int64_t ldo,
                          DeviceState& state, cudaStream_t stream) {
-    TcArgs a{q, k, v, out, ldq, ldk, ldv, ldo, lq, lk, scale * 1.4426950408889634f, state.status};
-    const dim3 grid((lq + kQ - 1) / kQ, heads);
-    if (head_dim == 64) {
-        using L = TcLayout<64>;
-        static_assert(L::total <= 232448, "shared memory budget");
-        set_smem_limit_once(state, reinterpret_cast<const void*>(attention_tc_kernel<64>), L::total,
-                            "cudaFuncSetAttribute(attention_tc smem)");
-        launch_pdl(attention_tc_kernel<64>, grid, dim3(kTcThreads), L::total, stream, "attention_tc_kernel launch", a);
-    } else {
-        using L = TcLayout<32>;
-        static_assert(L::total <= 232448, "shared memory budget");
-        set_smem_limit_once(state, reinterpret_cast<const void*>(attention_tc_kernel<32>), L::total,
-                            "cudaFuncSetAttribute(attention_tc smem)");
-        launch_pdl(attention_tc_kernel<32>, grid, dim3(kTcThreads), L::total, stream, "attention_tc_kernel launch", a);
-    }
+    TcArgs a{q, k, v, out, ldq, ldk, ldv, ldo, lq, lk, 0, 0, scale * 1.4426950408889634f, state.status};
+    if (head_dim == 64)
+        launch_tc<64>(a, heads, 1, state, stream);
+    else
+        launch_tc<32>(a, heads, 1, state, stream);
+}
+
+void launch_attention_tc_groups(const float* qkv, int64_t ldq, int64_t embed, int groups, int group_n, int heads,
+                                int head_dim, float scale, float* out, int64_t ldo, int out_window, int out_grid_w,
+                                DeviceState& state, cudaStream_t stream) {
+    TcArgs a{qkv, qkv + embed, qkv + 2 * embed, out, ldq, ldq, ldq, ldo, group_n, group_n, out_window, out_grid_w,
+             scale * 1.4426950408889634f, state.status};
+    if (head_dim == 64)
+        launch_tc<64>(a, heads, groups, state, stream);
+    else
+        launch_tc<32>(a, heads, groups, state, stream);
 }
 
 }  // namespace samq

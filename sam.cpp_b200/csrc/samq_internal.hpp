@@ -198,6 +198,16 @@ bool attention_tc_eligible(int lq, int lk, int head_dim, int causal, const float
 void launch_attention_tc(const float* q, int64_t ldq, const float* k, int64_t ldk, const float* v, int64_t ldv,
                          int lq, int lk, int heads, int head_dim, float scale, float* out, int64_t ldo,
                          DeviceState& state, cudaStream_t stream);
+// Grouped form for the ViT: qkv rows [groups * group_n][ldq] (Q, K, V at
+// column 0, embed, 2 embed), one attention per group; output rows in raster
+// token order when out_window > 0 (windows of a grid out_grid_w wide).
+void launch_attention_tc_groups(const float* qkv, int64_t ldq, int64_t embed, int groups, int group_n, int heads,
+                                int head_dim, float scale, float* out, int64_t ldo, int out_window, int out_grid_w,
+                                DeviceState& state, cudaStream_t stream);
+// RoPE (GGML rounding) in place on the Q and K columns of f32 qkv rows, token
+// position r % group_n.
+void launch_rope_rows(float* qkv, int64_t ldq, int64_t embed, int64_t rows, int group_n, const float* freqs,
+                      cudaStream_t stream);
 void launch_attention_gen(const float* q, int64_t ldq, const float* k, int64_t ldk, const float* v, int64_t ldv,
                           int lq, int lk, int heads, int head_dim, float scale, int causal, const float* bias,
                           int64_t bias_h, int64_t bias_q, float* out, int64_t ldo, DeviceState& state,

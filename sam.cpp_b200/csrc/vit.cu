@@ -291,8 +291,20 @@ void launch_vit_block(const VitBlockArgs& blk, float* x, int batch, int grid_w, 
         ep.y = qkv32;
         ep.ldy = 3 * embed;
         launch_gemm(a1, embed, blk.qkv->operand, tokens, 3 * embed, embed, ep, state, stream);
-        launch_attention_f32(qkv32, 3 * embed, blk.window > 0, grid_w, grid_h, heads, blk.window, batch, blk.freqs,
-                             nullptr, a1, embed, state, stream);
+        if (mlp * 2 >= embed * 4) {
+            // On the tensor cores (three-term TF32, attention_tc.cu): RoPE in
+            // place on the f32 Q / K rows, one attention per window (or image),
+            // f32 output rows in raster order in the fc2-operand region (free
+            // until fc1), then the proj operand staged from them (K1).
+            launch_rope_rows(qkv32, 3 * embed, embed, tokens, group_n, blk.freqs, stream);
+            float* att32 = reinterpret_cast<float*>(a3);
+            launch_attention_tc_groups(qkv32, 3 * embed, embed, static_cast<int>(tokens / group_n), group_n, heads, 64,
+                                       0.125f, att32, embed, blk.window, grid_w, state, stream);
+            launch_act_f16(att32, tokens, embed, embed, a1, nullptr, state.status, stream);
+        } else {
+            launch_attention_f32(qkv32, 3 * embed, blk.window > 0, grid_w, grid_h, heads, blk.window, batch,
+                                 blk.freqs, nullptr, a1, embed, state, stream);
+        }
     } else {
         ep.mode = kOutQkvPack;
         ep.bias = blk.qkv_b;
