@@ -450,6 +450,8 @@ attention_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
         }
         tc_fence_before();
     }
+    // Reconverge each warp before the aligned CTA barrier (lane-0 role loops).
+    __syncwarp();
     __syncthreads();
     if (warp == 1) {
         tc_fence_after();

@@ -458,6 +458,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) attention_tc_kernel(const TcArg
         }
     }
     tc_fence_before();
+    // Reconverge each warp before the aligned CTA barrier (lane-0 role loops).
+    __syncwarp();
     __syncthreads();
     if (warp == kMmaWarp) {
         tc_fence_after();

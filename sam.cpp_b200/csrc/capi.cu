@@ -12,6 +12,7 @@
 #include <memory>
 #include <vector>
 
+#include <map>
 #include <set>
 
 #include "samq_internal.hpp"
@@ -116,6 +117,31 @@ void set_smem_limit_once(DeviceState& state, const void* kernel, int bytes, cons
     DeviceGuard guard(state.device);
     check_cuda(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes), what);
     done.insert({kernel, state.device});
+}
+
+int pair_clusters_resident(DeviceState& state, const void* kernel, int threads, int smem, const char* what) {
+    static std::mutex mutex;
+    static std::map<std::pair<const void*, int>, int> cache;
+    std::lock_guard<std::mutex> lock(mutex);
+    auto it = cache.find({kernel, state.device});
+    if (it != cache.end()) return it->second;
+    DeviceGuard guard(state.device);
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(2);
+    cfg.blockDim = dim3(threads);
+    cfg.dynamicSmemBytes = smem;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int clusters = 0;
+    check_cuda(cudaOccupancyMaxActiveClusters(&clusters, kernel, &cfg), what);
+    if (clusters <= 0) fail(SAMQ_ERR_CUDA, "no CTA pair of the GEMM kernel fits on this device");
+    cache[{kernel, state.device}] = clusters;
+    return clusters;
 }
 
 void encode_tensor_map_2d(CUtensorMap* map, CUtensorMapDataType dtype, const void* base, uint64_t inner,

@@ -390,6 +390,8 @@ dense_gemm_kernel(const __grid_constant__ CUtensorMap tm_ah, const __grid_consta
         }
     }
     tc_fence_before();
+    // Reconverge each warp before the aligned CTA barrier (lane-0 role loops).
+    __syncwarp();
     __syncthreads();
     if (warp == 1) {
         tc_fence_after();

@@ -26,12 +26,15 @@
 //              erf-GELU in registers, swizzled staging in shared memory, TMA
 //              store (clipped at the m / n edges).  The next tile's MMAs
 //              overlap this epilogue.
-// Measured on B200 (ViT shapes, M=5184): without the epilogue the mainloop
-// runs at ~90% of the measured bf16 peak per tile, so the epilogue and wave
-// quantization set the pace.  EW=8 with 4 stages is best without GELU, EW=16
-// with 3 stages with erf-GELU.  A CTA-pair (cta_group::2, 256xBN tile)
-// variant was built and verified but measured slower (qkv mainloop 29.2 vs
-// 26.6 us), so it is not used.
+// Measured on B200 (ViT shapes, M=5184, %globaltimer stamps per tile): the
+// epilogue of a tile (2.5-3.5 us) hides behind the next tile's mainloop
+// (6-8 us); the mainloop waits for its operand stages ~40% of the time, as
+// the L2-to-shared-memory stream delivers ~100 GB/s per SM against the
+// ~170 GB/s per SM full-rate MMAs would consume, the same rate whether the
+// operands come from HBM or are L2-resident (a latency bound: ~180 KB in
+// flight per SM).  EW=8 is used without GELU, EW=16 with erf-GELU.
+// gemm_f16_pair_kernel below (cta_group::2, 256 x BN tiles) moves a third
+// fewer operand bytes per FLOP and is used where a pair runs 3 or more tiles.
 // No TMA load uses cluster multicast.  Every mbarrier wait is bounded and
 // reports kStatusTimeout instead of hanging.
 #include <algorithm>
@@ -434,6 +437,10 @@ gemm_f16_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant
         __syncwarp();
     }
     tc_fence_before();
+    // Reconverge each warp before the CTA barrier: __syncthreads is an aligned
+    // barrier (every thread of a warp executes it together), and lane 0 alone
+    // ran the producer and MMA loops.
+    __syncwarp();
     __syncthreads();
     if (warp == 1) {
         tc_fence_after();
@@ -441,22 +448,224 @@ gemm_f16_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant
     }
 }
 
+// ---------------------------------------------------------------------------
+// CTA-pair variant: a cluster of two CTAs on the two SMs of a TPC computes a
+// 256 x BN tile with tcgen05.mma.cta_group::2 (M=256, N=BN, K=16).  CTA r of
+// the pair loads A rows [128r, 128r+128) and B rows [r*BN/2, (r+1)*BN/2) of
+// the tile into its own shared memory; the pair MMA reads both CTAs' halves,
+// and each CTA's TMEM holds its 128 rows x BN columns of the accumulator.
+// Per SM and 64-deep K step this moves (128 + BN/2) x 128 bytes of operands
+// instead of (128 + BN) x 128 for the same tensor work, and a stage covers
+// 1.5-1.8x more MMA time against the load latency.  Measured on B200, the
+// single-CTA mainloop waits for its operands ~40% of each tile (it streams
+// ~100 GB/s per SM from L2, the same rate as a loads-only copy of it).
+//   warp 0 of each CTA: TMA producer of its halves; both signal the even
+//       CTA's `full` barrier (the even CTA's expect_tx covers both halves);
+//   warp 1: TMEM (both CTAs allocate together); in the even CTA one thread
+//       issues the pair MMAs, whose commits release `empty` stages and
+//       publish `tfull` in both CTAs;
+//   warps 2.. of both CTAs: the epilogue of their own 128 rows (drain_tile,
+//       every output mode); they return the accumulator through the even
+//       CTA's `tempty` barrier.
+// No TMA load uses multicast; remote signals go through mapa addresses.
+constexpr int kPairTmemCols = 2 * kAccStride;
+
+// Operand stages per CTA that fit in 227 KB beside EW staging buffers.
+constexpr int pair_stages_for(int bn, int ew) {
+    return (232448 - 1024 - 256 - ew * 4096) / (BM * BK * 2 + (bn / 2) * BK * 2) > 8
+               ? 8
+               : (232448 - 1024 - 256 - ew * 4096) / (BM * BK * 2 + (bn / 2) * BK * 2);
+}
+
+template <int BN, int STAGES, int EW>
+struct PairLayout {
+    static constexpr int a_bytes = BM * BK * 2;
+    static constexpr int b_bytes = (BN / 2) * BK * 2;
+    static constexpr int stage_tx = 2 * (a_bytes + b_bytes);  // both CTAs' halves
+    static constexpr int a_off = 0;
+    static constexpr int b_off = STAGES * a_bytes;
+    static constexpr int out_off = b_off + STAGES * b_bytes;
+    static constexpr int bar_off = out_off + EW * kOutBuffers * kOutChunkBytes;
+    static constexpr int bar_bytes = (2 * STAGES + 5) * 8 + 8;
+    static constexpr int total = bar_off + bar_bytes + 1024;  // + alignment slack
+};
+
 template <int BN, int STAGES, int EW, int MODE, bool GELU>
-void run(const __half* a, int64_t lda, const __half* b, int64_t m, int64_t n, int64_t k, const Epilogue& ep,
-         DeviceState& state, cudaStream_t stream) {
-    using L = Layout<BN, STAGES, EW>;
-    CUtensorMap ta, tb, ty, tk, tv;
-    encode_tensor_map_2d(&ta, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, a, k, m, lda * 2, BK, BM,
-                         CU_TENSOR_MAP_SWIZZLE_128B);
-    encode_tensor_map_2d(&tb, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, b, k, n, k * 2, BK, BN,
-                         CU_TENSOR_MAP_SWIZZLE_128B);
+__global__ void __launch_bounds__(threads_for(EW), 1)
+gemm_f16_pair_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_b,
+                     const __grid_constant__ CUtensorMap tma_y, const __grid_constant__ CUtensorMap tma_k,
+                     const __grid_constant__ CUtensorMap tma_v, const Epilogue ep, int m, int n, int k,
+                     DeviceStatus* status) {
+    using L = PairLayout<BN, STAGES, EW>;
+    static_assert(L::total <= 232448, "shared memory budget");
+    static_assert(BN % 32 == 0 && BN <= 256, "pair tile width");
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* sa = smem + L::a_off;
+    uint8_t* sb = smem + L::b_off;
+    uint8_t* sout = smem + L::out_off;
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + L::bar_off);
+    uint64_t* empty = full + STAGES;
+    uint64_t* tfull = empty + STAGES;
+    uint64_t* tempty = tfull + 2;
+    uint64_t* drain = tempty + 2;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t rank = cluster_cta_rank();
+    const int pair = blockIdx.x >> 1, pairs = gridDim.x >> 1;
+    const int m_tiles = (m + 2 * BM - 1) / (2 * BM), n_tiles = (n + BN - 1) / BN;
+    const int tiles = m_tiles * n_tiles;
+    const int kblocks = (k + BK - 1) / BK;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&tfull[b], 1);
+            mbar_init(&tempty[b], 2 * EW);
+        }
+        mbar_init(drain, 1);
+        fence_barrier_init();
+        tma_prefetch_desc(&tma_a);
+        tma_prefetch_desc(&tma_b);
+        tma_prefetch_desc(&tma_y);
+        tma_prefetch_desc(&tma_k);
+        tma_prefetch_desc(&tma_v);
+    }
+    if (warp == 1) tmem_alloc_pair(tmem_slot, kPairTmemCols);
+    tc_fence_before();
+    cluster_sync_all();  // barriers of both CTAs initialised, TMEM allocated
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+    // Everything above overlaps the previous kernel; A (and the output buffer)
+    // may be in use by it until it completes.
+    pdl_wait();
+
+    if (warp == 0) {
+        if (lane == 0) {
+            int s = 0;
+            uint32_t ph = 0;
+            bool ok = true, any = false;
+            for (int tile = pair; tile < tiles && ok; tile += pairs) {
+                const int mt = tile / n_tiles, nt = tile % n_tiles;
+                for (int kb = 0; kb < kblocks; ++kb) {
+                    if (!mbar_wait(&empty[s], ph ^ 1u, status, 11)) {
+                        ok = false;
+                        break;
+                    }
+                    const uint32_t full_even = cluster_map(&full[s], 0);
+                    if (rank == 0) mbar_arrive_expect_tx(&full[s], L::stage_tx);
+                    tma_load_2d_pair(sa + s * L::a_bytes, &tma_a, full_even, kb * BK,
+                                     mt * 2 * BM + static_cast<int>(rank) * BM);
+                    tma_load_2d_pair(sb + s * L::b_bytes, &tma_b, full_even, kb * BK,
+                                     nt * BN + static_cast<int>(rank) * (BN / 2));
+                    any = true;
+                    if (++s == STAGES) {
+                        s = 0;
+                        ph ^= 1u;
+                    }
+                }
+            }
+            pdl_trigger();  // all loads issued: the next kernel may begin its prologue
+            if (!ok && any) {
+                // Copies in flight signal the even CTA's barrier; give them time to land.
+                const uint64_t start = global_timer_ns();
+                while (global_timer_ns() - start < 2000000ull) __nanosleep(1000);
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0 && rank == 0) {
+            constexpr uint32_t idesc = idesc_f16_f32(2 * BM, BN);
+            int s = 0;
+            uint32_t ph = 0;
+            int acc = 0;
+            uint32_t acc_ph = 0;
+            bool ok = true;
+            for (int tile = pair; tile < tiles && ok; tile += pairs) {
+                if (!mbar_wait_cluster(&tempty[acc], acc_ph ^ 1u, status, 12)) break;
+                tc_fence_after();
+                const uint32_t d = tmem_base + static_cast<uint32_t>(acc * kAccStride);
+                for (int kb = 0; kb < kblocks; ++kb) {
+                    if (!mbar_wait(&full[s], ph, status, 13)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t a_addr = smem_u32(sa + s * L::a_bytes);
+                    const uint32_t b_addr = smem_u32(sb + s * L::b_bytes);
+#pragma unroll
+                    for (int kk = 0; kk < BK / 16; ++kk)
+                        tc_mma_f16_pair(d, smem_desc_sw128(a_addr + kk * 32), smem_desc_sw128(b_addr + kk * 32),
+                                        idesc, (kb | kk) != 0 ? 1u : 0u);
+                    tc_commit_pair(cluster_map(&empty[s], 0));
+                    tc_commit_pair(cluster_map(&empty[s], 1));
+                    if (++s == STAGES) {
+                        s = 0;
+                        ph ^= 1u;
+                    }
+                }
+                if (!ok) break;
+                tc_commit_pair(cluster_map(&tfull[acc], 0));
+                tc_commit_pair(cluster_map(&tfull[acc], 1));
+                acc ^= 1;
+                if (acc == 0) acc_ph ^= 1u;
+            }
+            // Wait for every MMA this thread issued before TMEM is released.
+            tc_commit_pair(cluster_map(drain, 0));
+            mbar_wait(drain, 0, status, 16);
+        }
+    } else {
+        const int quarter = warp & 3;          // TMEM lanes 32*quarter .. +31
+        const int part = (warp - 2) >> 2;      // column part of the tile (EW/4 parts)
+        uint8_t* stage_buf = sout + (warp - 2) * kOutBuffers * kOutChunkBytes;
+        const uint32_t tempty_even[2] = {cluster_map(&tempty[0], 0), cluster_map(&tempty[1], 0)};
+        int acc = 0;
+        uint32_t acc_ph = 0;
+        int buf = 0;
+        for (int tile = pair; tile < tiles; tile += pairs) {
+            const int mt = tile / n_tiles, nt = tile % n_tiles;
+            const int row0 = mt * 2 * BM + static_cast<int>(rank) * BM + quarter * 32;
+            ChunkInputs<MODE> first;
+            if constexpr (MODE == kOutF32Residual) {
+                const int first_col = nt * BN + (part * (BN / 32) / (EW / 4)) * 32;
+                if (first_col < n) load_chunk_inputs<MODE>(ep, first_col, row0 + lane, m, n, lane, first);
+            }
+            // Warp-uniform: the tcgen05.ld in drain_tile is warp-collective.
+            if (!__all_sync(0xffffffffu, mbar_wait(&tfull[acc], acc_ph, status, 14))) break;
+            tc_fence_after();
+            drain_tile<BN, EW / 4, MODE, GELU>(tmem_base, quarter, part, acc, row0, nt * BN, m, n, ep, &tma_y, &tma_k,
+                                               &tma_v, stage_buf, buf, lane, first, status);
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive_cluster(tempty_even[acc]);
+            acc ^= 1;
+            if (acc == 0) acc_ph ^= 1u;
+        }
+        if (lane == 0) bulk_wait_group_read<0>();
+        __syncwarp();
+    }
+    tc_fence_before();
+    __syncwarp();        // converged for the aligned cluster barrier
+    cluster_sync_all();  // both CTAs done with TMEM and with each other's barriers
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc_pair(tmem_base, kPairTmemCols);
+    }
+}
+
+// The output tensor maps of an epilogue (maps a mode does not use cover A:
+// valid, never stored to).
+void encode_output_maps(const __half* a, int64_t lda, int64_t m, int64_t n, int64_t k, const Epilogue& ep,
+                        CUtensorMap& ty, CUtensorMap& tk, CUtensorMap& tv) {
     if (ep.mode == kOutF32 || ep.mode == kOutF32Residual)
         encode_tensor_map_2d(&ty, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, ep.y, n, m, ep.ldy * 4, 32, 32,
                              CU_TENSOR_MAP_SWIZZLE_128B);
     else if (ep.mode == kOutF16Staged)
         encode_tensor_map_2d(&ty, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, ep.h, n, m, ep.ldh * 2, 32, 32,
                              CU_TENSOR_MAP_SWIZZLE_64B);
-    // Maps a mode does not use cover A (valid, never stored to).
     encode_tensor_map_2d(&tk, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, a, k, m, lda * 2, 32, 32, CU_TENSOR_MAP_SWIZZLE_64B);
     tv = tk;
     if (ep.mode == kOutQkvPack) {
@@ -472,6 +681,18 @@ void run(const __half* a, int64_t lda, const __half* b, int64_t m, int64_t n, in
     } else if (ep.mode != kOutF32 && ep.mode != kOutF32Residual && ep.mode != kOutF16Staged) {
         ty = tk;
     }
+}
+
+template <int BN, int STAGES, int EW, int MODE, bool GELU>
+void run(const __half* a, int64_t lda, const __half* b, int64_t m, int64_t n, int64_t k, const Epilogue& ep,
+         DeviceState& state, cudaStream_t stream) {
+    using L = Layout<BN, STAGES, EW>;
+    CUtensorMap ta, tb, ty, tk, tv;
+    encode_tensor_map_2d(&ta, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, a, k, m, lda * 2, BK, BM,
+                         CU_TENSOR_MAP_SWIZZLE_128B);
+    encode_tensor_map_2d(&tb, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, b, k, n, k * 2, BK, BN,
+                         CU_TENSOR_MAP_SWIZZLE_128B);
+    encode_output_maps(a, lda, m, n, k, ep, ty, tk, tv);
     auto kernel = gemm_f16_kernel<BN, STAGES, EW, MODE, GELU>;
     set_smem_limit_once(state, reinterpret_cast<const void*>(kernel), L::total, "cudaFuncSetAttribute(gemm smem)");
     const int64_t tiles = ((m + BM - 1) / BM) * ((n + BN - 1) / BN);
@@ -480,34 +701,92 @@ void run(const __half* a, int64_t lda, const __half* b, int64_t m, int64_t n, in
                ep, static_cast<int>(m), static_cast<int>(n), static_cast<int>(k), state.status);
 }
 
+template <int BN, int EW, int MODE, bool GELU>
+void run_pair(const __half* a, int64_t lda, const __half* b, int64_t m, int64_t n, int64_t k, const Epilogue& ep,
+              DeviceState& state, cudaStream_t stream) {
+    constexpr int kStages = pair_stages_for(BN, EW);
+    using L = PairLayout<BN, kStages, EW>;
+    CUtensorMap ta, tb, ty, tk, tv;
+    encode_tensor_map_2d(&ta, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, a, k, m, lda * 2, BK, BM,
+                         CU_TENSOR_MAP_SWIZZLE_128B);
+    encode_tensor_map_2d(&tb, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, b, k, n, k * 2, BK, BN / 2,
+                         CU_TENSOR_MAP_SWIZZLE_128B);
+    encode_output_maps(a, lda, m, n, k, ep, ty, tk, tv);
+    auto kernel = gemm_f16_pair_kernel<BN, kStages, EW, MODE, GELU>;
+    set_smem_limit_once(state, reinterpret_cast<const void*>(kernel), L::total,
+                        "cudaFuncSetAttribute(pair gemm smem)");
+    const int resident = pair_clusters_resident(state, reinterpret_cast<const void*>(kernel), threads_for(EW),
+                                                L::total, "cudaOccupancyMaxActiveClusters(pair gemm)");
+    const int64_t tiles = ((m + 2 * BM - 1) / (2 * BM)) * ((n + BN - 1) / BN);
+    const int64_t pairs = std::min<int64_t>(tiles, resident);
+    launch_pdl_pairs(kernel, dim3(static_cast<unsigned>(2 * pairs)), dim3(threads_for(EW)), L::total, stream,
+                     "gemm_f16_pair_kernel launch", ta, tb, ty, tk, tv, ep, static_cast<int>(m),
+                     static_cast<int>(n), static_cast<int>(k), state.status);
+}
+
 }  // namespace
 
-// Tile width: the MMA N (multiple of 32 here) that minimizes
-// (waves of tiles over the SMs) x N, i.e. the per-SM critical path; ties go to
-// the wider tile (less operand traffic per FLOP).
-int choose_bn(int64_t m, int64_t n, int sms) {
+// Tile shape: single CTA (128 x BN) or CTA pair (256 x BN), BN a multiple of
+// 32.  Each candidate is scored by its per-SM critical path, (waves of tiles
+// over the SMs or pairs) x the time of one 64-deep K step of a tile, the
+// larger of the tensor time (BN columns) and the operand stream time
+// ((128 + B rows per SM) x 128 bytes at the ~100 GB/s per SM measured for the
+// L2-to-shared-memory stream); the weights 915 : 1000 are those two rates
+// per row (14 TFLOP/s per SM against 100 GB/s per SM, B200, 1.8 GHz).  Ties go
+// to the pair, then to the wider tile (less operand traffic per FLOP).
+// The operand stream is latency-bound rather than byte-bound (the pair moves
+// a third fewer bytes per FLOP but its tiles measured only 10-25% faster), and
+// a pair's start-up and last epilogue cost more, so the pair is taken only
+// where it runs at least kPairMinWaves tiles per pair: measured on B200 at
+// M = 5184 it wins for N = 3072 / 4736 (4 and 6 waves) and loses for N = 1024
+// (2 waves).
+constexpr int64_t kPairMinWaves = 3;
+
+struct GemmShape {
+    bool pair;
+    int bn;
+};
+
+GemmShape choose_shape(int64_t m, int64_t n, int sms) {
     static const int kWidths[4] = {256, 224, 192, 160};
-    int best = 256;
+    GemmShape best{false, 256};
     int64_t best_cost = INT64_MAX;
-    for (int bn : kWidths) {
-        const int64_t tiles = ((m + BM - 1) / BM) * ((n + bn - 1) / bn);
-        const int64_t cost = (tiles + sms - 1) / sms * bn;
-        if (cost < best_cost) {
-            best_cost = cost;
-            best = bn;
+    for (int pair = 1; pair >= 0; --pair) {
+        if (pair && (m <= BM || sms < 2)) continue;
+        const int64_t rows = pair ? 2 * BM : BM, units = pair ? sms / 2 : sms;
+        for (int bn : kWidths) {
+            const int64_t tiles = ((m + rows - 1) / rows) * ((n + bn - 1) / bn);
+            const int64_t waves = (tiles + units - 1) / units;
+            if (pair && waves < kPairMinWaves) continue;
+            const int64_t b_rows = pair ? bn / 2 : bn;
+            const int64_t step = std::max<int64_t>(int64_t(bn) * 915, (BM + b_rows) * 1000);
+            const int64_t cost = waves * step;
+            if (cost < best_cost) {
+                best_cost = cost;
+                best = GemmShape{pair != 0, bn};
+            }
         }
     }
     return best;
 }
 
 template <int EW, int MODE, bool GELU>
-void run_width(int bn, const __half* a, int64_t lda, const __half* b, int64_t m, int64_t n, int64_t k,
+void run_width(GemmShape shape, const __half* a, int64_t lda, const __half* b, int64_t m, int64_t n, int64_t k,
                const Epilogue& ep, DeviceState& state, cudaStream_t stream) {
     if (n <= 128) {
         run<128, 6, 8, MODE, GELU>(a, lda, b, m, n, k, ep, state, stream);
         return;
     }
-    switch (bn) {
+    if (shape.pair) {
+        switch (shape.bn) {
+            case 160: run_pair<160, EW, MODE, GELU>(a, lda, b, m, n, k, ep, state, stream); break;
+            case 192: run_pair<192, EW, MODE, GELU>(a, lda, b, m, n, k, ep, state, stream); break;
+            case 224: run_pair<224, EW, MODE, GELU>(a, lda, b, m, n, k, ep, state, stream); break;
+            default: run_pair<256, EW, MODE, GELU>(a, lda, b, m, n, k, ep, state, stream); break;
+        }
+        return;
+    }
+    switch (shape.bn) {
         case 160: run<160, stages_for(160, EW), EW, MODE, GELU>(a, lda, b, m, n, k, ep, state, stream); break;
         case 192: run<192, stages_for(192, EW), EW, MODE, GELU>(a, lda, b, m, n, k, ep, state, stream); break;
         case 224: run<224, stages_for(224, EW), EW, MODE, GELU>(a, lda, b, m, n, k, ep, state, stream); break;
@@ -521,23 +800,23 @@ void run_width(int bn, const __half* a, int64_t lda, const __half* b, int64_t m,
 void launch_gemm(const __half* a, int64_t lda, const __half* b, int64_t m, int64_t n, int64_t k, const Epilogue& ep,
                  DeviceState& state, cudaStream_t stream) {
     if (m == 0) return;
-    const int bn = choose_bn(m, n, state.sm_count);
+    const GemmShape shape = choose_shape(m, n, state.sm_count);
     switch (ep.mode) {
         case kOutF32:
-            if (ep.gelu) run_width<16, kOutF32, true>(bn, a, lda, b, m, n, k, ep, state, stream);
-            else run_width<8, kOutF32, false>(bn, a, lda, b, m, n, k, ep, state, stream);
+            if (ep.gelu) run_width<16, kOutF32, true>(shape, a, lda, b, m, n, k, ep, state, stream);
+            else run_width<8, kOutF32, false>(shape, a, lda, b, m, n, k, ep, state, stream);
             break;
         case kOutF32Residual:
             if (ep.gelu) fail(SAMQ_ERR_INVALID_ARGUMENT, "residual epilogue takes no GELU");
-            run_width<8, kOutF32Residual, false>(bn, a, lda, b, m, n, k, ep, state, stream);
+            run_width<8, kOutF32Residual, false>(shape, a, lda, b, m, n, k, ep, state, stream);
             break;
         case kOutF16Staged:
-            if (ep.gelu) run_width<16, kOutF16Staged, true>(bn, a, lda, b, m, n, k, ep, state, stream);
-            else run_width<8, kOutF16Staged, false>(bn, a, lda, b, m, n, k, ep, state, stream);
+            if (ep.gelu) run_width<16, kOutF16Staged, true>(shape, a, lda, b, m, n, k, ep, state, stream);
+            else run_width<8, kOutF16Staged, false>(shape, a, lda, b, m, n, k, ep, state, stream);
             break;
         case kOutQkvPack:
             if (ep.gelu) fail(SAMQ_ERR_INVALID_ARGUMENT, "qkv split takes no GELU");
-            run_width<8, kOutQkvPack, false>(bn, a, lda, b, m, n, k, ep, state, stream);
+            run_width<8, kOutQkvPack, false>(shape, a, lda, b, m, n, k, ep, state, stream);
             break;
         default: fail(SAMQ_ERR_INVALID_ARGUMENT, "unknown GEMM output mode");
     }

@@ -352,6 +352,8 @@ gemm_mmq_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant
         __syncwarp();
     }
     tc_fence_before();
+    // Reconverge each warp before the aligned CTA barrier (lane-0 role loops).
+    __syncwarp();
     __syncthreads();
     if (warp == 1) {
         tc_fence_after();

@@ -375,5 +375,107 @@ __host__ __device__ constexpr uint32_t idesc_f16_f32(int m, int n) {
            | (static_cast<uint32_t>(m >> 4) << 24);    // M / 16
 }
 
+// ---- CTA pairs (cluster of 2, tcgen05 cta_group::2) ----------------------
+// Two CTAs on the two SMs of a TPC share one M = 256 tile: each holds 128 rows
+// of A and half of B's rows in its own shared memory, and its own 128 rows of
+// the accumulator in TMEM.  Every TMA load below is a plain load into the
+// issuing CTA's own shared memory (no multicast); only its completion may be
+// signalled on the other CTA's mbarrier.
+
+__device__ __forceinline__ uint32_t cluster_cta_rank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+
+// shared::cluster address of the variable at `local` in CTA `rank` of the cluster.
+__device__ __forceinline__ uint32_t cluster_map(const void* local, uint32_t rank) {
+    uint32_t out;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(out) : "r"(smem_u32(local)), "r"(rank));
+    return out;
+}
+
+// Cluster-wide barrier (aligned: every warp executes it converged).
+__device__ __forceinline__ void cluster_sync_all() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+// Arrive (count 1) on an mbarrier given by its shared::cluster address.
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
+    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+
+// mbar_try_wait with cluster-scope acquire: for barriers that threads of the
+// other CTA of the pair arrive on.
+__device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t* bar, uint32_t parity) {
+    uint32_t done;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(done)
+        : "r"(smem_u32(bar)), "r"(parity), "r"(kSuspendHintNs)
+        : "memory");
+    return done != 0;
+}
+
+// Bounded wait (as mbar_wait) with cluster-scope acquire.
+__device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity, DeviceStatus* status,
+                                                  uint32_t site) {
+    if (mbar_try_wait_cluster(bar, parity)) return true;
+    const uint64_t start = global_timer_ns();
+    for (uint32_t spin = 1;; ++spin) {
+        if (mbar_try_wait_cluster(bar, parity)) return true;
+        if ((spin & 15u) == 0 && global_timer_ns() - start > kWaitTimeoutNs) {
+            if (status) {
+                atomicOr(&status->flags, kStatusTimeout);
+                atomicExch(&status->timeout_site, site);
+            }
+            return false;
+        }
+    }
+}
+
+// 2-D tile load into this CTA's shared memory whose completion is signalled on
+// an mbarrier of either CTA of the pair (cluster address).
+__device__ __forceinline__ void tma_load_2d_pair(void* smem_dst, const CUtensorMap* map, uint32_t bar_cluster_addr,
+                                                 int32_t x, int32_t y) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];" ::
+            "r"(smem_u32(smem_dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(bar_cluster_addr), "r"(x), "r"(y)
+        : "memory");
+}
+
+__device__ __forceinline__ void tmem_alloc_pair(uint32_t* smem_slot, uint32_t ncols) {
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(smem_slot)),
+                 "r"(ncols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+
+// Pair MMA issued by one thread of the even CTA: A rows and B rows are split
+// across the two CTAs' shared memory at the same offsets, D is each CTA's TMEM.
+__device__ __forceinline__ void tc_mma_f16_pair(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                                uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+// Arrive on the mbarrier at `bar_cluster_addr` (either CTA of the pair) once
+// every pair MMA issued so far by this thread is complete.
+__device__ __forceinline__ void tc_commit_pair(uint32_t bar_cluster_addr) {
+    asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                     bar_cluster_addr)
+                 : "memory");
+}
 
 }  // namespace samq

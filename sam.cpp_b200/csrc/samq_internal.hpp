@@ -90,6 +90,32 @@ void launch_pdl(void (*kernel)(KernelArgs...), dim3 grid, dim3 block, size_t sme
     check_cuda(cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...), what);
 }
 
+// launch_pdl for a kernel of CTA pairs: clusters of two CTAs along x.
+template <class... KernelArgs, class... Args>
+void launch_pdl_pairs(void (*kernel)(KernelArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                      const char* what, Args&&... args) {
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    attr[1].id = cudaLaunchAttributeClusterDimension;
+    attr[1].val.clusterDim.x = 2;
+    attr[1].val.clusterDim.y = 1;
+    attr[1].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 2;
+    check_cuda(cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...), what);
+}
+
+// How many clusters of two CTAs of `kernel` (block threads, smem bytes of
+// dynamic shared memory) can be resident on state.device at once; queried
+// once per (kernel, device) and cached.
+int pair_clusters_resident(DeviceState& state, const void* kernel, int threads, int smem, const char* what);
+
 // cuTensorMapEncodeTiled through the runtime's driver entry point (no link
 // dependency on libcuda).
 void encode_tensor_map_2d(CUtensorMap* map, CUtensorMapDataType dtype, const void* base, uint64_t inner,

@@ -210,6 +210,8 @@ gemm_stream_kernel(const uint8_t* __restrict__ packets, const __grid_constant__ 
         }
         tc_fence_before();
     }
+    // Reconverge each warp before the aligned CTA barrier (lane-0 role loops).
+    __syncwarp();
     __syncthreads();
     if (warp == 1) {
         tc_fence_after();
