@@ -710,7 +710,7 @@ def mmq_section(samq, torch, stream, max_over_ranks, xs, ys, biases, rank, warmu
         per, total_ms = {}, 0.0
         for i, (lname, n, k, qtype, epi, seed) in enumerate(LINEARS):
             packed, _ = make_weights(samq.quantize_rows, n, k, 8, seed + 4 * rank)
-            w = samq.MmqWeights(8, k, n, packed, variant=variant)
+            w = samq.MmqWeights(8, k, n, packed, variant=variant, device=torch.cuda.current_device())
             for _ in range(warmup):
                 samq.linear_mmq(w, xs[i], M, k, biases[i], epi, ys[i], n, stream)
             torch.cuda.synchronize()
@@ -1023,7 +1023,7 @@ def gemm_cold_durations(samq, torch, stream, rank, reps=8, replays=3, l2_bytes=2
         ws, As, bs = [], [], []
         for j in range(sets):
             packed, bias = make_weights(samq.quantize_rows, n, k, qtype, seed + 100 * j + 4 * rank)
-            ws.append(samq.Weights(qtype, k, n, packed))
+            ws.append(samq.Weights(qtype, k, n, packed, device=torch.cuda.current_device()))
             x = torch.from_numpy(np.random.default_rng(2000 + j).normal(0, 1, (M, k)).astype(np.float32)).cuda()
             a16 = torch.empty((M, k), dtype=torch.float16, device="cuda")
             samq.stage_f16(x, M, k, k, a16, stream)
