@@ -220,6 +220,31 @@ def test_linear_q8_0_wide_k(samq, oracle):
     w.close()
 
 
+@pytest.mark.parametrize("qtype,m,n,k,epilogue", [
+    (8, 2000, 4736, 1056, 0),   # ragged M (7.8 pair tiles), ragged N (BN 192), K % 64 == 32
+    (8, 2000, 4736, 1056, 1),   # the same with erf-GELU (16 epilogue warps per CTA)
+    (12, 1300, 6144, 1024, 0),  # the last pair tile's second CTA holds only rows past M
+])
+def test_linear_cta_pair_ragged_shapes(samq, oracle, qtype, m, n, k, epilogue):
+    """Shapes whose CTA-pair tiling runs three or more waves (gemm_f16_pair_kernel,
+    cta_group::2), with ragged edges in M, N and K; checked on the first 64 and
+    the last 150 rows against the oracle (every other row lies in a tile of the
+    same kind)."""
+    rng = np.random.default_rng(qtype + m + n + epilogue)
+    rows = oracle.quantize(qtype, weights_matrix(rng, n, k))
+    x = rng.normal(0, 1, (m, k)).astype(np.float32)
+    bias = rng.normal(0, 0.02, n).astype(np.float32)
+    w = samq.Weights(qtype, k, n, rows)
+    y = run_linear(samq, w, x, bias=bias, epilogue=epilogue)
+    pick = np.r_[0:64, m - 150:m]
+    semantic, exact = references(oracle, qtype, rows, x[pick], n, k, bias=bias, epilogue=epilogue)
+    cos, rel = metrics(y[pick], semantic)
+    assert cos >= COS_MIN and rel <= MAX_REL, (cos, rel)
+    assert metrics(y[pick], exact)[1] <= EXACT_OPERAND_REL
+    assert np.isfinite(y).all()
+    w.close()
+
+
 def test_linear_from_staged_q8_1_matches_linear(samq, oracle):
     rng = np.random.default_rng(8)
     m, n, k = 150, 512, 1024
