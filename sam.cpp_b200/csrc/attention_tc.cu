@@ -116,6 +116,59 @@ struct TcArgs {
     DeviceStatus* status;
 };
 
+// K and V^T of every (group, head) split once into TF32 hi / lo planes for the
+// TMA-fed kernel (attention_tc_kernel<HD, true>): K planes [p][gh][lk][HD] and
+// V^T planes [p][gh][HD][lk], p = 0 hi, 1 lo, gh = g * heads + h; a group's
+// key rows follow each other in k / v with stride ld (lk % 4 == 0).  One block
+// per (64 keys, head, group); V goes through shared memory so that V^T rows
+// (keys contiguous) are written coalesced.
+template <int HD>
+__global__ void __launch_bounds__(256) split_kv_kernel(const float* __restrict__ k, const float* __restrict__ v,
+                                                       int64_t ld, int lk, int heads, int groups,
+                                                       float* __restrict__ kp, float* __restrict__ vtp) {
+    pdl_wait();
+    pdl_trigger();
+    __shared__ float vt[64][HD + 1];
+    const int n0 = blockIdx.x * 64, h = blockIdx.y, g = blockIdx.z;
+    const int64_t gh = static_cast<int64_t>(g) * heads + h;
+    const int64_t plane_k = static_cast<int64_t>(groups) * heads * lk * HD;  // elements per hi / lo plane
+    const float* kg = k + static_cast<int64_t>(g) * lk * ld + h * HD;
+    const float* vg = v + static_cast<int64_t>(g) * lk * ld + h * HD;
+    for (int u = threadIdx.x; u < 64 * (HD / 4); u += blockDim.x) {
+        const int r = u / (HD / 4), d4 = u % (HD / 4), n = n0 + r;
+        float4 xv = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (n < lk) {
+            const float4 xk = __ldg(reinterpret_cast<const float4*>(kg + static_cast<int64_t>(n) * ld) + d4);
+            float4 hi, lo;
+            split_tf32(xk.x, hi.x, lo.x);
+            split_tf32(xk.y, hi.y, lo.y);
+            split_tf32(xk.z, hi.z, lo.z);
+            split_tf32(xk.w, hi.w, lo.w);
+            const int64_t o = (gh * lk + n) * HD + 4 * d4;
+            *reinterpret_cast<float4*>(kp + o) = hi;
+            *reinterpret_cast<float4*>(kp + plane_k + o) = lo;
+            xv = __ldg(reinterpret_cast<const float4*>(vg + static_cast<int64_t>(n) * ld) + d4);
+        }
+        vt[r][4 * d4] = xv.x;
+        vt[r][4 * d4 + 1] = xv.y;
+        vt[r][4 * d4 + 2] = xv.z;
+        vt[r][4 * d4 + 3] = xv.w;
+    }
+    __syncthreads();
+    for (int u = threadIdx.x; u < HD * 16; u += blockDim.x) {  // HD rows x 16 groups of 4 keys
+        const int d = u / 16, k4 = u % 16, n = n0 + 4 * k4;
+        if (n >= lk) continue;  // lk % 4 == 0: a group of 4 keys is wholly in or out
+        float4 hi, lo;
+        split_tf32(vt[4 * k4][d], hi.x, lo.x);
+        split_tf32(vt[4 * k4 + 1][d], hi.y, lo.y);
+        split_tf32(vt[4 * k4 + 2][d], hi.z, lo.z);
+        split_tf32(vt[4 * k4 + 3][d], hi.w, lo.w);
+        const int64_t o = (gh * HD + d) * lk + n;
+        *reinterpret_cast<float4*>(vtp + o) = hi;
+        *reinterpret_cast<float4*>(vtp + plane_k + o) = lo;
+    }
+}
+
 // Softmax warps: wait for P_j V_j (O buffer j % 2), add it as
 // o = o * alpha + (hi*hi + corrections), release the buffer.
 template <int HD, class L>
@@ -142,8 +195,15 @@ __device__ __forceinline__ bool take_o(float (&o)[HD], float alpha, int j, uint6
     return true;
 }
 
-template <int HD>
-__global__ void __launch_bounds__(kTcThreads, 1) attention_tc_kernel(const TcArgs a) {
+// SPLIT: K and V^T come as the TF32 hi / lo planes of split_kv_kernel through
+// TMA (tm_k: [2 x groups x heads][lk][HD], tm_vt: [2 x groups x heads][HD][lk],
+// boxes of 32 f32 x 64 keys / HD channels, 128-byte swizzle), issued by one
+// thread of loader warp 0; otherwise the two loader warps read the f32 rows
+// and split them.  Q is read and split by the loader warps in both forms.
+template <int HD, bool SPLIT>
+__global__ void __launch_bounds__(kTcThreads, 1) attention_tc_kernel(const TcArgs a,
+                                                                     const __grid_constant__ CUtensorMap tm_k,
+                                                                     const __grid_constant__ CUtensorMap tm_vt) {
     using L = TcLayout<HD>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -170,7 +230,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) attention_tc_kernel(const TcArg
     if (threadIdx.x == 0) {
         mbar_init(q_full, kLoaders);
         for (int s = 0; s < L::stages; ++s) {
-            mbar_init(&kv_full[s], kLoaders);
+            mbar_init(&kv_full[s], SPLIT ? 1 : kLoaders);
             mbar_init(&kv_empty[s], 1);
         }
         for (int b = 0; b < L::s_bufs; ++b) {
@@ -225,7 +285,37 @@ __global__ void __launch_bounds__(kTcThreads, 1) attention_tc_kernel(const TcArg
         fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) mbar_arrive(q_full);
-        for (int j = 0; j < tiles; ++j) {
+        if constexpr (SPLIT) {
+            if (warp == 0 && lane == 0) {
+                const int gh = g * gridDim.y + h, planes = gridDim.z * gridDim.y;
+                uint32_t issued = 0, issued_phase = 0;  // per stage: loads in flight and their phase parity
+                for (int j = 0; j < tiles; ++j) {
+                    const int s = j % L::stages, key0 = j * kKeys;
+                    const uint32_t par = static_cast<uint32_t>(j / L::stages) & 1u;
+                    if (!mbar_wait(&kv_empty[s], par ^ 1u, status, 81)) break;
+                    mbar_arrive_expect_tx(&kv_full[s], 2 * L::k_bytes + 2 * L::v_bytes);
+                    uint8_t* kh = smem + L::k_off + s * 2 * L::k_bytes;
+                    uint8_t* vh = smem + L::v_off + s * 2 * L::v_bytes;
+#pragma unroll
+                    for (int pl = 0; pl < 2; ++pl) {
+#pragma unroll
+                        for (int c = 0; c < HD / 32; ++c)
+                            tma_load_3d(kh + pl * L::k_bytes + c * kKeys * 128, &tm_k, &kv_full[s], c * 32, key0,
+                                        gh + pl * planes);
+#pragma unroll
+                        for (int c = 0; c < kKeys / 32; ++c)
+                            tma_load_3d(vh + pl * L::v_bytes + c * HD * 128, &tm_vt, &kv_full[s], key0 + c * 32, 0,
+                                        gh + pl * planes);
+                    }
+                    issued |= 1u << s;
+                    issued_phase = (issued_phase & ~(1u << s)) | (par << s);
+                }
+                // Let every copy in flight land before the CTA can exit.
+                for (int s = 0; s < L::stages; ++s)
+                    if (issued & (1u << s)) mbar_wait(&kv_full[s], (issued_phase >> s) & 1u, status, 81);
+            }
+        }
+        for (int j = 0; j < tiles && !SPLIT; ++j) {
             const int s = j % L::stages;
             const int key0 = j * kKeys;
             float4 xk[kKvLoads], xv[kKvLoads];
@@ -469,14 +559,16 @@ __global__ void __launch_bounds__(kTcThreads, 1) attention_tc_kernel(const TcArg
 
 }  // namespace
 
-template <int HD>
-void launch_tc(const TcArgs& a, int heads, int groups, DeviceState& state, cudaStream_t stream) {
+template <int HD, bool SPLIT>
+void launch_tc(const TcArgs& a, int heads, int groups, const CUtensorMap& tm_k, const CUtensorMap& tm_vt,
+               DeviceState& state, cudaStream_t stream) {
     using L = TcLayout<HD>;
     static_assert(L::total <= 232448, "shared memory budget");
-    set_smem_limit_once(state, reinterpret_cast<const void*>(attention_tc_kernel<HD>), L::total,
+    auto kernel = attention_tc_kernel<HD, SPLIT>;
+    set_smem_limit_once(state, reinterpret_cast<const void*>(kernel), L::total,
                         "cudaFuncSetAttribute(attention_tc smem)");
     const dim3 grid((a.lq + kQ - 1) / kQ, heads, groups);
-    launch_pdl(attention_tc_kernel<HD>, grid, dim3(kTcThreads), L::total, stream, "attention_tc_kernel launch", a);
+    launch_pdl(kernel, grid, dim3(kTcThreads), L::total, stream, "attention_tc_kernel launch", a, tm_k, tm_vt);
 }
 
 bool attention_tc_eligible(int lq, int lk, int head_dim, int causal, const float* bias, const float* out,
@@ -489,21 +581,48 @@ void launch_attention_tc(const float* q, int64_t ldq, const float* k, int64_t ld
                          int lq, int lk, int heads, int head_dim, float scale, float* out, int64_t ldo,
                          DeviceState& state, cudaStream_t stream) {
     TcArgs a{q, k, v, out, ldq, ldk, ldv, ldo, lq, lk, 0, 0, scale * 1.4426950408889634f, state.status};
+    CUtensorMap none{};  // not read by the loader-fed kernel
     if (head_dim == 64)
-        launch_tc<64>(a, heads, 1, state, stream);
+        launch_tc<64, false>(a, heads, 1, none, none, state, stream);
     else
-        launch_tc<32>(a, heads, 1, state, stream);
+        launch_tc<32, false>(a, heads, 1, none, none, state, stream);
+}
+
+size_t attention_tc_plane_bytes(int groups, int group_n, int heads, int head_dim) {
+    return static_cast<size_t>(4) * groups * group_n * heads * head_dim * sizeof(float);
+}
+
+template <int HD>
+void launch_groups(const TcArgs& a, int heads, int groups, float* planes, DeviceState& state, cudaStream_t stream) {
+    const int lk = a.lk;
+    if (planes == nullptr || lk % 4 != 0) {
+        CUtensorMap none{};
+        launch_tc<HD, false>(a, heads, groups, none, none, state, stream);
+        return;
+    }
+    // K / V^T split once into TF32 hi / lo planes, then loaded by TMA.
+    const uint64_t gh2 = static_cast<uint64_t>(2) * groups * heads;
+    float* kp = planes;
+    float* vtp = planes + static_cast<int64_t>(2) * groups * heads * lk * HD;
+    launch_pdl(split_kv_kernel<HD>, dim3((lk + 63) / 64, heads, groups), dim3(256), 0, stream, "split_kv_kernel launch",
+               a.k, a.v, a.ldk, lk, heads, groups, kp, vtp);
+    CUtensorMap tm_k, tm_vt;
+    encode_tensor_map_3d(&tm_k, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, kp, HD, lk, gh2, HD * 4,
+                         static_cast<uint64_t>(lk) * HD * 4, 32, kKeys, CU_TENSOR_MAP_SWIZZLE_128B);
+    encode_tensor_map_3d(&tm_vt, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, vtp, lk, HD, gh2, static_cast<uint64_t>(lk) * 4,
+                         static_cast<uint64_t>(lk) * HD * 4, 32, HD, CU_TENSOR_MAP_SWIZZLE_128B);
+    launch_tc<HD, true>(a, heads, groups, tm_k, tm_vt, state, stream);
 }
 
 void launch_attention_tc_groups(const float* qkv, int64_t ldq, int64_t embed, int groups, int group_n, int heads,
                                 int head_dim, float scale, float* out, int64_t ldo, int out_window, int out_grid_w,
-                                DeviceState& state, cudaStream_t stream) {
+                                float* planes, DeviceState& state, cudaStream_t stream) {
     TcArgs a{qkv, qkv + embed, qkv + 2 * embed, out, ldq, ldq, ldq, ldo, group_n, group_n, out_window, out_grid_w,
              scale * 1.4426950408889634f, state.status};
     if (head_dim == 64)
-        launch_tc<64>(a, heads, groups, state, stream);
+        launch_groups<64>(a, heads, groups, planes, state, stream);
     else
-        launch_tc<32>(a, heads, groups, state, stream);
+        launch_groups<32>(a, heads, groups, planes, state, stream);
 }
 
 }  // namespace samq

@@ -226,10 +226,14 @@ void launch_attention_tc(const float* q, int64_t ldq, const float* k, int64_t ld
                          DeviceState& state, cudaStream_t stream);
 // Grouped form for the ViT: qkv rows [groups * group_n][ldq] (Q, K, V at
 // column 0, embed, 2 embed), one attention per group; output rows in raster
-// token order when out_window > 0 (windows of a grid out_grid_w wide).
+// token order when out_window > 0 (windows of a grid out_grid_w wide).  With
+// `planes` (attention_tc_plane_bytes of device memory, 16-byte aligned) and
+// group_n % 4 == 0, K and V^T are first split into TF32 hi / lo planes there
+// and the kernel loads them by TMA; otherwise its loader warps split the rows.
+size_t attention_tc_plane_bytes(int groups, int group_n, int heads, int head_dim);
 void launch_attention_tc_groups(const float* qkv, int64_t ldq, int64_t embed, int groups, int group_n, int heads,
                                 int head_dim, float scale, float* out, int64_t ldo, int out_window, int out_grid_w,
-                                DeviceState& state, cudaStream_t stream);
+                                float* planes, DeviceState& state, cudaStream_t stream);
 // RoPE (GGML rounding) in place on the Q and K columns of f32 qkv rows, token
 // position r % group_n.
 void launch_rope_rows(float* qkv, int64_t ldq, int64_t embed, int64_t rows, int group_n, const float* freqs,

@@ -246,8 +246,10 @@ void by_width(int embed, Fn&& fn) {
 size_t vit_block_scratch_bytes(int64_t tokens, int64_t embed, int64_t mlp, int compute) {
     // A1 [T][E] + packed Q, K, V^T 3 [T][E] + fc2 operand [T][MLP], all f16;
     // in F32 mode the middle region holds the f32 qkv rows [T][3E] instead.
-    const int64_t middle = compute == SAMQ_COMPUTE_F32 ? 3 * embed * 2 : 3 * embed;
-    return static_cast<size_t>(tokens) * (embed + middle + mlp) * sizeof(__half) + 3 * 256;
+    // F32 mode also holds the TF32 hi / lo planes of K and V^T (4 x [T][E] f32)
+    // for the tensor-core attention's TMA loads.
+    const int64_t middle = compute == SAMQ_COMPUTE_F32 ? (3 + 4) * embed * 2 : 3 * embed;
+    return static_cast<size_t>(tokens) * (embed + middle + mlp) * sizeof(__half) + 4 * 256;
 }
 
 void launch_ln_stage(const float* x, int64_t rows, int64_t embed, int grid_w, int window, const float* w,
@@ -274,6 +276,8 @@ void launch_vit_block(const VitBlockArgs& blk, float* x, int batch, int grid_w, 
     cursor = align(cursor + tokens * embed * sizeof(__half));
     __half* packed = reinterpret_cast<__half*>(cursor);  // F16: Q, K, V^T; F32: the f32 qkv rows
     cursor = align(cursor + (f32 ? 3 * tokens * embed * sizeof(float) : 3 * tokens * embed * sizeof(__half)));
+    float* planes = f32 ? reinterpret_cast<float*>(cursor) : nullptr;  // F32: K / V^T TF32 hi / lo planes
+    if (f32) cursor = align(cursor + 4 * tokens * embed * sizeof(float));
     __half* a3 = reinterpret_cast<__half*>(cursor);
     __half* q = packed;
     __half* k = packed + tokens * embed;
@@ -299,7 +303,7 @@ void launch_vit_block(const VitBlockArgs& blk, float* x, int batch, int grid_w, 
             launch_rope_rows(qkv32, 3 * embed, embed, tokens, group_n, blk.freqs, stream);
             float* att32 = reinterpret_cast<float*>(a3);
             launch_attention_tc_groups(qkv32, 3 * embed, embed, static_cast<int>(tokens / group_n), group_n, heads, 64,
-                                       0.125f, att32, embed, blk.window, grid_w, state, stream);
+                                       0.125f, att32, embed, blk.window, grid_w, planes, state, stream);
             launch_act_f16(att32, tokens, embed, embed, a1, nullptr, state.status, stream);
         } else {
             launch_attention_f32(qkv32, 3 * embed, blk.window > 0, grid_w, grid_h, heads, blk.window, batch,
