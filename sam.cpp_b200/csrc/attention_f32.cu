@@ -516,6 +516,13 @@ void launch_attention_f32(const float* qkv, int64_t ldq, bool qkv_window_major, 
     }
 }
 
+size_t attention_gen_plane_bytes(int lq, int lk, int heads, int head_dim, int causal, const float* bias,
+                                 const float* out, int64_t ldo) {
+    return attention_tc_eligible(lq, lk, head_dim, causal, bias, out, ldo)
+               ? attention_tc_plane_bytes(1, lk, heads, head_dim) + 16
+               : 0;
+}
+
 size_t attention_partial_floats(int lq, int lk, int heads, int head_dim, int causal, int sms) {
     const int splits = key_splits(lq, lk, heads, causal, sms);
     return splits > 1 ? static_cast<size_t>(splits) * heads * lq * (head_dim + 2) : 0;
@@ -524,10 +531,10 @@ size_t attention_partial_floats(int lq, int lk, int heads, int head_dim, int cau
 void launch_attention_gen(const float* q, int64_t ldq, const float* k, int64_t ldk, const float* v, int64_t ldv,
                           int lq, int lk, int heads, int head_dim, float scale, int causal, const float* bias,
                           int64_t bias_h, int64_t bias_q, float* out, int64_t ldo, DeviceState& state,
-                          cudaStream_t stream, float* partials, size_t partial_floats) {
+                          cudaStream_t stream, float* partials, size_t partial_floats, float* tc_planes) {
     if (lq == 0) return;
     if (attention_tc_eligible(lq, lk, head_dim, causal, bias, out, ldo)) {
-        launch_attention_tc(q, ldq, k, ldk, v, ldv, lq, lk, heads, head_dim, scale, out, ldo, state, stream);
+        launch_attention_tc(q, ldq, k, ldk, v, ldv, lq, lk, heads, head_dim, scale, out, ldo, tc_planes, state, stream);
         return;
     }
     AttnGenArgs a{q, k, v, bias, out, ldq, ldk, ldv, ldo, bias_h, bias_q, lq, lk, causal, scale, nullptr, 0};

@@ -119,26 +119,26 @@ struct TcArgs {
 // K and V^T of every (group, head) split once into TF32 hi / lo planes for the
 // TMA-fed kernel (attention_tc_kernel<HD, true>): K planes [p][gh][lk][HD] and
 // V^T planes [p][gh][HD][lk], p = 0 hi, 1 lo, gh = g * heads + h; a group's
-// key rows follow each other in k / v with stride ld (lk % 4 == 0).  One block
+// key rows follow each other in k / v with strides ldk / ldv (lk % 4 == 0).  One block
 // per (64 keys, head, group); V goes through shared memory so that V^T rows
 // (keys contiguous) are written coalesced.
 template <int HD>
-__global__ void __launch_bounds__(256) split_kv_kernel(const float* __restrict__ k, const float* __restrict__ v,
-                                                       int64_t ld, int lk, int heads, int groups,
-                                                       float* __restrict__ kp, float* __restrict__ vtp) {
+__global__ void __launch_bounds__(256) split_kv_kernel(const float* __restrict__ k, int64_t ldk,
+                                                       const float* __restrict__ v, int64_t ldv, int lk, int heads,
+                                                       int groups, float* __restrict__ kp, float* __restrict__ vtp) {
     pdl_wait();
     pdl_trigger();
     __shared__ float vt[64][HD + 1];
     const int n0 = blockIdx.x * 64, h = blockIdx.y, g = blockIdx.z;
     const int64_t gh = static_cast<int64_t>(g) * heads + h;
     const int64_t plane_k = static_cast<int64_t>(groups) * heads * lk * HD;  // elements per hi / lo plane
-    const float* kg = k + static_cast<int64_t>(g) * lk * ld + h * HD;
-    const float* vg = v + static_cast<int64_t>(g) * lk * ld + h * HD;
+    const float* kg = k + static_cast<int64_t>(g) * lk * ldk + h * HD;
+    const float* vg = v + static_cast<int64_t>(g) * lk * ldv + h * HD;
     for (int u = threadIdx.x; u < 64 * (HD / 4); u += blockDim.x) {
         const int r = u / (HD / 4), d4 = u % (HD / 4), n = n0 + r;
         float4 xv = make_float4(0.f, 0.f, 0.f, 0.f);
         if (n < lk) {
-            const float4 xk = __ldg(reinterpret_cast<const float4*>(kg + static_cast<int64_t>(n) * ld) + d4);
+            const float4 xk = __ldg(reinterpret_cast<const float4*>(kg + static_cast<int64_t>(n) * ldk) + d4);
             float4 hi, lo;
             split_tf32(xk.x, hi.x, lo.x);
             split_tf32(xk.y, hi.y, lo.y);
@@ -147,7 +147,7 @@ __global__ void __launch_bounds__(256) split_kv_kernel(const float* __restrict__
             const int64_t o = (gh * lk + n) * HD + 4 * d4;
             *reinterpret_cast<float4*>(kp + o) = hi;
             *reinterpret_cast<float4*>(kp + plane_k + o) = lo;
-            xv = __ldg(reinterpret_cast<const float4*>(vg + static_cast<int64_t>(n) * ld) + d4);
+            xv = __ldg(reinterpret_cast<const float4*>(vg + static_cast<int64_t>(n) * ldv) + d4);
         }
         vt[r][4 * d4] = xv.x;
         vt[r][4 * d4 + 1] = xv.y;
@@ -577,17 +577,6 @@ bool attention_tc_eligible(int lq, int lk, int head_dim, int causal, const float
            ldo % 4 == 0 && (reinterpret_cast<uintptr_t>(out) & 15u) == 0;
 }
 
-void launch_attention_tc(const float* q, int64_t ldq, const float* k, int64_t ldk, const float* v, int64_t ldv,
-                         int lq, int lk, int heads, int head_dim, float scale, float* out, int64_t ldo,
-                         DeviceState& state, cudaStream_t stream) {
-    TcArgs a{q, k, v, out, ldq, ldk, ldv, ldo, lq, lk, 0, 0, scale * 1.4426950408889634f, state.status};
-    CUtensorMap none{};  // not read by the loader-fed kernel
-    if (head_dim == 64)
-        launch_tc<64, false>(a, heads, 1, none, none, state, stream);
-    else
-        launch_tc<32, false>(a, heads, 1, none, none, state, stream);
-}
-
 size_t attention_tc_plane_bytes(int groups, int group_n, int heads, int head_dim) {
     return static_cast<size_t>(4) * groups * group_n * heads * head_dim * sizeof(float);
 }
@@ -595,8 +584,8 @@ size_t attention_tc_plane_bytes(int groups, int group_n, int heads, int head_dim
 template <int HD>
 void launch_groups(const TcArgs& a, int heads, int groups, float* planes, DeviceState& state, cudaStream_t stream) {
     const int lk = a.lk;
-    if (planes == nullptr || lk % 4 != 0) {
-        CUtensorMap none{};
+    if (planes == nullptr || lk % 4 != 0 || (reinterpret_cast<uintptr_t>(planes) & 15u) != 0) {
+        CUtensorMap none{};  // not read by the loader-fed kernel
         launch_tc<HD, false>(a, heads, groups, none, none, state, stream);
         return;
     }
@@ -605,13 +594,23 @@ void launch_groups(const TcArgs& a, int heads, int groups, float* planes, Device
     float* kp = planes;
     float* vtp = planes + static_cast<int64_t>(2) * groups * heads * lk * HD;
     launch_pdl(split_kv_kernel<HD>, dim3((lk + 63) / 64, heads, groups), dim3(256), 0, stream, "split_kv_kernel launch",
-               a.k, a.v, a.ldk, lk, heads, groups, kp, vtp);
+               a.k, a.ldk, a.v, a.ldv, lk, heads, groups, kp, vtp);
     CUtensorMap tm_k, tm_vt;
     encode_tensor_map_3d(&tm_k, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, kp, HD, lk, gh2, HD * 4,
                          static_cast<uint64_t>(lk) * HD * 4, 32, kKeys, CU_TENSOR_MAP_SWIZZLE_128B);
     encode_tensor_map_3d(&tm_vt, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, vtp, lk, HD, gh2, static_cast<uint64_t>(lk) * 4,
                          static_cast<uint64_t>(lk) * HD * 4, 32, HD, CU_TENSOR_MAP_SWIZZLE_128B);
     launch_tc<HD, true>(a, heads, groups, tm_k, tm_vt, state, stream);
+}
+
+void launch_attention_tc(const float* q, int64_t ldq, const float* k, int64_t ldk, const float* v, int64_t ldv,
+                         int lq, int lk, int heads, int head_dim, float scale, float* out, int64_t ldo, float* planes,
+                         DeviceState& state, cudaStream_t stream) {
+    TcArgs a{q, k, v, out, ldq, ldk, ldv, ldo, lq, lk, 0, 0, scale * 1.4426950408889634f, state.status};
+    if (head_dim == 64)
+        launch_groups<64>(a, heads, 1, planes, state, stream);
+    else
+        launch_groups<32>(a, heads, 1, planes, state, stream);
 }
 
 void launch_attention_tc_groups(const float* qkv, int64_t ldq, int64_t embed, int groups, int group_n, int heads,

@@ -745,11 +745,16 @@ samq_status samq_attention_v1(const float* q, int64_t ldq, const float* k, int64
         require(q && k && v && out && aligned16(q) && aligned16(k) && aligned16(v), "q, k, v must be 16-byte aligned");
         DeviceState& state = device_state(current_device());
         cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
+        // Scratch: the key-split partials of the SIMT kernel, or the K / V^T
+        // TF32 planes of the tensor-core kernel (never both).
         const size_t part = attention_partial_floats(lq, lk, heads, head_dim, causal, state.sm_count);
+        const size_t plane_bytes = attention_gen_plane_bytes(lq, lk, heads, head_dim, causal, bias, out, ldo);
         float* partials = nullptr;
-        if (part > 0) partials = static_cast<float*>(scratch_for(state, stream, part * sizeof(float)).ptr);
+        float* planes = nullptr;
+        if (plane_bytes > 0) planes = static_cast<float*>(scratch_for(state, stream, plane_bytes).ptr);
+        else if (part > 0) partials = static_cast<float*>(scratch_for(state, stream, part * sizeof(float)).ptr);
         launch_attention_gen(q, ldq, k, ldk, v, ldv, lq, lk, heads, head_dim, scale, causal, bias, bias_h, bias_q,
-                             out, ldo, state, stream, partials, part);
+                             out, ldo, state, stream, partials, part, planes);
     });
 }
 

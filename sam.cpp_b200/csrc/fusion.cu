@@ -108,8 +108,10 @@ size_t fusion_layer_scratch_bytes(const samq_fusion_layer_v1& ly, int64_t tokens
         linear = std::max(linear, linear_scratch_bytes(*l, tokens, sms));
     linear = std::max(linear, linear_scratch_bytes(ly.linear2, tokens, sms));
     linear = std::max(linear, linear_scratch_bytes(ly.ca_in_proj, prompt_tokens, sms));
-    // h, qk_in [T][D]; q|k [T][2D]; v, att, y [T][D]; ffn [T][F]; prompt k|v [P][2D]
-    const size_t floats = static_cast<size_t>(tokens) * (D * 2 + 2 * D + 3 * D + F) + prompt_tokens * 2 * D;
+    // h, qk_in [T][D]; q|k [T][2D]; v, att, y [T][D]; ffn [T][F]; prompt k|v [P][2D];
+    // the self-attention's K / V^T TF32 hi / lo planes 4 [T][D]
+    const size_t floats = static_cast<size_t>(tokens) * (D * 2 + 2 * D + 3 * D + F) + prompt_tokens * 2 * D +
+                          static_cast<size_t>(tokens) * 4 * D;
     return floats * sizeof(float) + linear + 16 * 256;
 }
 
@@ -134,6 +136,7 @@ void launch_fusion_layer(const samq_fusion_layer_v1& ly, float* x, const float* 
     float* y = take(tokens * D);
     float* ffn = take(tokens * F);
     float* pkv = take(prompt_tokens * 2 * D);
+    float* planes = take(tokens * 4 * D);
     void* lin = reinterpret_cast<void*>(cursor);
 
     // Self-attention: positions added to the queries' and keys' input only.
@@ -142,7 +145,7 @@ void launch_fusion_layer(const samq_fusion_layer_v1& ly, float* x, const float* 
     apply_linear(ly.sa_in_proj, 0, 2 * D, qk_in, D, tokens, SAMQ_EPILOGUE_NONE, qk, 2 * D, lin, state, stream);
     apply_linear(ly.sa_in_proj, 2 * D, D, h, D, tokens, SAMQ_EPILOGUE_NONE, v, D, lin, state, stream);
     launch_attention_gen(qk, 2 * D, qk + D, 2 * D, v, D, static_cast<int>(tokens), static_cast<int>(tokens), heads, hd,
-                         scale, 0, nullptr, 0, 0, att, D, state, stream);
+                         scale, 0, nullptr, 0, 0, att, D, state, stream, nullptr, 0, planes);
     apply_linear(ly.sa_out_proj, 0, D, att, D, tokens, SAMQ_EPILOGUE_NONE, y, D, lin, state, stream);
     launch_add_rows(x, D, y, D, tokens, static_cast<int>(D), stream);
     // Cross-attention to the prompt tokens (key padding bias).

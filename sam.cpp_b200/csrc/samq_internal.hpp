@@ -221,8 +221,9 @@ size_t attention_partial_floats(int lq, int lk, int heads, int head_dim, int cau
 // for many queries and keys without a mask.
 bool attention_tc_eligible(int lq, int lk, int head_dim, int causal, const float* bias, const float* out,
                            int64_t ldo);
+// `planes` as for launch_attention_tc_groups (nullptr: the loader-fed kernel).
 void launch_attention_tc(const float* q, int64_t ldq, const float* k, int64_t ldk, const float* v, int64_t ldv,
-                         int lq, int lk, int heads, int head_dim, float scale, float* out, int64_t ldo,
+                         int lq, int lk, int heads, int head_dim, float scale, float* out, int64_t ldo, float* planes,
                          DeviceState& state, cudaStream_t stream);
 // Grouped form for the ViT: qkv rows [groups * group_n][ldq] (Q, K, V at
 // column 0, embed, 2 embed), one attention per group; output rows in raster
@@ -241,7 +242,12 @@ void launch_rope_rows(float* qkv, int64_t ldq, int64_t embed, int64_t rows, int 
 void launch_attention_gen(const float* q, int64_t ldq, const float* k, int64_t ldk, const float* v, int64_t ldv,
                           int lq, int lk, int heads, int head_dim, float scale, int causal, const float* bias,
                           int64_t bias_h, int64_t bias_q, float* out, int64_t ldo, DeviceState& state,
-                          cudaStream_t stream, float* partials = nullptr, size_t partial_floats = 0);
+                          cudaStream_t stream, float* partials = nullptr, size_t partial_floats = 0,
+                          float* tc_planes = nullptr);
+// Scratch a launch_attention_gen caller may pass as `tc_planes`: the K / V^T
+// TF32 planes of the tensor-core path when the shape takes it, else 0.
+size_t attention_gen_plane_bytes(int lq, int lk, int heads, int head_dim, int causal, const float* bias,
+                                 const float* out, int64_t ldo);
 // sam3_apply_rope on [head_batches][tokens][64] f32 with GGML's rounding.
 void launch_rope_f32(const float* x, const float* freqs, int64_t tokens, int64_t head_batches, float* out,
                      cudaStream_t stream);
