@@ -519,7 +519,7 @@ void launch_attention_f32(const float* qkv, int64_t ldq, bool qkv_window_major, 
 size_t attention_gen_plane_bytes(int lq, int lk, int heads, int head_dim, int causal, const float* bias,
                                  const float* out, int64_t ldo) {
     return attention_tc_eligible(lq, lk, head_dim, causal, bias, out, ldo)
-               ? attention_tc_plane_bytes(1, lk, heads, head_dim) + 16
+               ? attention_tc_scratch_bytes(lq, lk, heads, head_dim)
                : 0;
 }
 
@@ -567,6 +567,17 @@ void launch_attention_gen(const float* q, int64_t ldq, const float* k, int64_t l
                        "attention_combine_kernel launch", static_cast<const float*>(partials), splits, heads, lq, out,
                        ldo);
     }
+}
+
+void launch_attention_combine(const float* part, int splits, int heads, int lq, int head_dim, float* out,
+                              int64_t ldo, cudaStream_t stream) {
+    const unsigned blocks = static_cast<unsigned>((int64_t(heads) * lq * 32 + 255) / 256);
+    if (head_dim == 64)
+        launch_pdl(attention_combine_kernel<64>, dim3(blocks), dim3(256), 0, stream, "attention_combine_kernel launch",
+                   part, splits, heads, lq, out, ldo);
+    else
+        launch_pdl(attention_combine_kernel<32>, dim3(blocks), dim3(256), 0, stream, "attention_combine_kernel launch",
+                   part, splits, heads, lq, out, ldo);
 }
 
 void launch_rope_rows(float* qkv, int64_t ldq, int64_t embed, int64_t rows, int group_n, const float* freqs,

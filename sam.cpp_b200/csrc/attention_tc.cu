@@ -121,6 +121,12 @@ struct TcArgs {
     int out_window, out_grid_w;
     float scale_log2e;  // softmax scale x log2(e)
     DeviceStatus* status;
+    // Key split (one group only): with `part`, CTA z covers keys
+    // [z kps, (z + 1) kps) (kps a multiple of 64) and writes its unnormalized
+    // O, row maximum (natural-log units) and row sum to part
+    // [splits][heads][lq][HD + 2] for launch_attention_combine.
+    float* part = nullptr;
+    int kps = 0;
 };
 
 // K and V^T of every (group, head) split once into TF32 hi / lo planes for the
@@ -228,8 +234,14 @@ __global__ void __launch_bounds__(kTcThreads, 1) attention_tc_kernel(const TcArg
     DeviceStatus* status = a.status;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int q0 = blockIdx.x * kQ, h = blockIdx.y, g = blockIdx.z;
-    const int tiles = (a.lk + kKeys - 1) / kKeys;
+    const int q0 = blockIdx.x * kQ, h = blockIdx.y;
+    const int g = a.part ? 0 : static_cast<int>(blockIdx.z);
+    const int split = a.part ? static_cast<int>(blockIdx.z) : 0;
+    // This CTA's key tiles: all of them, or its split's range [t_begin, +tiles).
+    const int all_tiles = (a.lk + kKeys - 1) / kKeys;
+    const int t_begin = a.part ? split * (a.kps / kKeys) : 0;
+    const int tiles = a.part ? max(0, min(all_tiles, t_begin + a.kps / kKeys) - t_begin) : all_tiles;
+    const int key_base = t_begin * kKeys;
     const float* gq = a.q + int64_t(g) * a.lq * a.ldq;
     const float* gk = a.k + int64_t(g) * a.lk * a.ldk;
     const float* gv = a.v + int64_t(g) * a.lk * a.ldv;
@@ -294,10 +306,10 @@ __global__ void __launch_bounds__(kTcThreads, 1) attention_tc_kernel(const TcArg
         if (lane == 0) mbar_arrive(q_full);
         if constexpr (SPLIT) {
             if (warp == 0 && lane == 0) {
-                const int gh = g * gridDim.y + h, planes = gridDim.z * gridDim.y;
+                const int gh = g * gridDim.y + h, planes = (a.part ? 1 : gridDim.z) * gridDim.y;
                 uint32_t issued = 0, issued_phase = 0;  // per stage: loads in flight and their phase parity
                 for (int j = 0; j < tiles; ++j) {
-                    const int s = j % L::stages, key0 = j * kKeys;
+                    const int s = j % L::stages, key0 = key_base + j * kKeys;
                     const uint32_t par = static_cast<uint32_t>(j / L::stages) & 1u;
                     if (!mbar_wait(&kv_empty[s], par ^ 1u, status, 81)) break;
                     mbar_arrive_expect_tx(&kv_full[s], 2 * L::k_bytes + 2 * L::v_bytes);
@@ -324,7 +336,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) attention_tc_kernel(const TcArg
         }
         for (int j = 0; j < tiles && !SPLIT; ++j) {
             const int s = j % L::stages;
-            const int key0 = j * kKeys;
+            const int key0 = key_base + j * kKeys;
             float4 xk[kKvLoads], xv[kKvLoads];
 #pragma unroll
             for (int i = 0; i < kKvLoads; ++i) {
@@ -477,7 +489,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) attention_tc_kernel(const TcArg
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&s_empty[b]);
-            const int key0 = j * kKeys;
+            const int key0 = key_base + j * kKeys;
             if (key0 + kKeys > a.lk) {
 #pragma unroll
                 for (int c = 0; c < kKeys; ++c)
@@ -535,7 +547,15 @@ __global__ void __launch_bounds__(kTcThreads, 1) attention_tc_kernel(const TcArg
             ok = take_o<HD, L>(o, alpha_prev, tiles - 1, o_full, o_empty, tmem_base + lane_addr, lane, status);
         pdl_trigger();
         const int n = q0 + row;
-        if (ok && n < a.lq) {
+        if (ok && n < a.lq && a.part != nullptr) {
+            // Key-split partial: O unnormalized, the row maximum in natural-log
+            // units (P = 2^((s - m) c) = e^((s - m) scale)), the row sum.
+            float* dst = a.part + ((int64_t(split) * gridDim.y + h) * a.lq + n) * (HD + 2);
+#pragma unroll
+            for (int c = 0; c < HD; ++c) dst[c] = o[c];
+            dst[HD] = m == -INFINITY ? -INFINITY : m * (a.scale_log2e * 0.6931471805599453f);
+            dst[HD + 1] = l;
+        } else if (ok && n < a.lq) {
             int64_t orow = int64_t(g) * a.lq + n;
             if (a.out_window > 0) {
                 const int per_row = a.out_grid_w / a.out_window;
@@ -588,36 +608,86 @@ size_t attention_tc_plane_bytes(int groups, int group_n, int heads, int head_dim
     return static_cast<size_t>(4) * groups * group_n * heads * head_dim * sizeof(float);
 }
 
+// Key splits of the one-group form: CTAs run one per SM, so a grid of a few
+// waves loses its last wave's idle SMs.  s splits make waves of 1 / s of a
+// CTA's keys (plus a fixed per-CTA start, ~3 % of a full CTA at the fusion
+// shape); the smallest s within 2 % of the least critical path is taken, with
+// at least 8 key tiles per split.
+constexpr int kMaxKeySplits = 4;
+
+int tc_key_splits(int lq, int lk, int heads, int sms) {
+    const int64_t ctas = int64_t((lq + kQ - 1) / kQ) * heads;
+    const int tiles = (lk + kKeys - 1) / kKeys;
+    double cost[kMaxKeySplits + 1] = {};
+    double best = 1e30;
+    for (int s = 1; s <= kMaxKeySplits; ++s) {
+        if (s > 1 && tiles / s < 8) break;
+        const int64_t waves = (ctas * s + sms - 1) / sms;
+        cost[s] = static_cast<double>(waves) * (1.0 / s + 0.03);
+        best = std::min(best, cost[s]);
+    }
+    for (int s = 1; s <= kMaxKeySplits; ++s)
+        if (cost[s] > 0.0 && cost[s] <= best * 1.02) return s;
+    return 1;
+}
+
+size_t tc_partial_floats(int lq, int heads, int head_dim) {
+    return static_cast<size_t>(kMaxKeySplits) * heads * lq * (head_dim + 2);
+}
+
 template <int HD>
-void launch_groups(const TcArgs& a, int heads, int groups, float* planes, DeviceState& state, cudaStream_t stream) {
+void launch_groups(TcArgs a, int heads, int groups, float* planes, float* part, DeviceState& state,
+                   cudaStream_t stream) {
     const int lk = a.lk;
+    int splits = 1;
+    if (part != nullptr && groups == 1 && a.out_window == 0) splits = tc_key_splits(a.lq, lk, heads, state.sm_count);
+    float* out = a.out;
+    const int64_t ldo = a.ldo;
+    int z = groups;
+    if (splits > 1) {
+        const int tiles = (lk + kKeys - 1) / kKeys;
+        a.kps = (tiles + splits - 1) / splits * kKeys;
+        splits = (tiles * kKeys + a.kps - 1) / a.kps;  // splits actually holding keys
+        a.part = part;
+        z = splits;
+    }
     if (planes == nullptr || lk % 4 != 0 || (reinterpret_cast<uintptr_t>(planes) & 15u) != 0) {
         CUtensorMap none{};  // not read by the loader-fed kernel
-        launch_tc<HD, false>(a, heads, groups, none, none, state, stream);
-        return;
+        launch_tc<HD, false>(a, heads, z, none, none, state, stream);
+    } else {
+        // K / V^T split once into TF32 hi / lo planes, then loaded by TMA.
+        const uint64_t gh2 = static_cast<uint64_t>(2) * groups * heads;
+        float* kp = planes;
+        float* vtp = planes + static_cast<int64_t>(2) * groups * heads * lk * HD;
+        launch_pdl(split_kv_kernel<HD>, dim3((lk + 63) / 64, heads, groups), dim3(256), 0, stream,
+                   "split_kv_kernel launch", a.k, a.ldk, a.v, a.ldv, lk, heads, groups, kp, vtp);
+        CUtensorMap tm_k, tm_vt;
+        encode_tensor_map_3d(&tm_k, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, kp, HD, lk, gh2, HD * 4,
+                             static_cast<uint64_t>(lk) * HD * 4, 32, kKeys, CU_TENSOR_MAP_SWIZZLE_128B);
+        encode_tensor_map_3d(&tm_vt, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, vtp, lk, HD, gh2, static_cast<uint64_t>(lk) * 4,
+                             static_cast<uint64_t>(lk) * HD * 4, 32, HD, CU_TENSOR_MAP_SWIZZLE_128B);
+        launch_tc<HD, true>(a, heads, z, tm_k, tm_vt, state, stream);
     }
-    // K / V^T split once into TF32 hi / lo planes, then loaded by TMA.
-    const uint64_t gh2 = static_cast<uint64_t>(2) * groups * heads;
-    float* kp = planes;
-    float* vtp = planes + static_cast<int64_t>(2) * groups * heads * lk * HD;
-    launch_pdl(split_kv_kernel<HD>, dim3((lk + 63) / 64, heads, groups), dim3(256), 0, stream, "split_kv_kernel launch",
-               a.k, a.ldk, a.v, a.ldv, lk, heads, groups, kp, vtp);
-    CUtensorMap tm_k, tm_vt;
-    encode_tensor_map_3d(&tm_k, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, kp, HD, lk, gh2, HD * 4,
-                         static_cast<uint64_t>(lk) * HD * 4, 32, kKeys, CU_TENSOR_MAP_SWIZZLE_128B);
-    encode_tensor_map_3d(&tm_vt, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, vtp, lk, HD, gh2, static_cast<uint64_t>(lk) * 4,
-                         static_cast<uint64_t>(lk) * HD * 4, 32, HD, CU_TENSOR_MAP_SWIZZLE_128B);
-    launch_tc<HD, true>(a, heads, groups, tm_k, tm_vt, state, stream);
+    if (splits > 1) launch_attention_combine(part, splits, heads, a.lq, HD, out, ldo, stream);
 }
 
 void launch_attention_tc(const float* q, int64_t ldq, const float* k, int64_t ldk, const float* v, int64_t ldv,
-                         int lq, int lk, int heads, int head_dim, float scale, float* out, int64_t ldo, float* planes,
+                         int lq, int lk, int heads, int head_dim, float scale, float* out, int64_t ldo, float* scratch,
                          DeviceState& state, cudaStream_t stream) {
     TcArgs a{q, k, v, out, ldq, ldk, ldv, ldo, lq, lk, 0, 0, scale * 1.4426950408889634f, state.status};
+    // scratch: the K / V^T planes, then the key-split partials (attention_tc_scratch_bytes).
+    float* part = nullptr;
+    if (scratch != nullptr)
+        part = scratch + (attention_tc_plane_bytes(1, lk, heads, head_dim) + 255) / 256 * 64;  // 256-byte aligned
     if (head_dim == 64)
-        launch_groups<64>(a, heads, 1, planes, state, stream);
+        launch_groups<64>(a, heads, 1, scratch, part, state, stream);
     else
-        launch_groups<32>(a, heads, 1, planes, state, stream);
+        launch_groups<32>(a, heads, 1, scratch, part, state, stream);
+}
+
+size_t attention_tc_scratch_bytes(int lq, int lk, int heads, int head_dim) {
+    return (attention_tc_plane_bytes(1, lk, heads, head_dim) + 255) / 256 * 256 +
+           tc_partial_floats(lq, heads, head_dim) * sizeof(float);
 }
 
 void launch_attention_tc_groups(const float* qkv, int64_t ldq, int64_t embed, int groups, int group_n, int heads,
@@ -626,9 +696,9 @@ void launch_attention_tc_groups(const float* qkv, int64_t ldq, int64_t embed, in
     TcArgs a{qkv, qkv + embed, qkv + 2 * embed, out, ldq, ldq, ldq, ldo, group_n, group_n, out_window, out_grid_w,
              scale * 1.4426950408889634f, state.status};
     if (head_dim == 64)
-        launch_groups<64>(a, heads, groups, planes, state, stream);
+        launch_groups<64>(a, heads, groups, planes, nullptr, state, stream);
     else
-        launch_groups<32>(a, heads, groups, planes, state, stream);
+        launch_groups<32>(a, heads, groups, planes, nullptr, state, stream);
 }
 
 }  // namespace samq

@@ -109,10 +109,11 @@ size_t fusion_layer_scratch_bytes(const samq_fusion_layer_v1& ly, int64_t tokens
     linear = std::max(linear, linear_scratch_bytes(ly.linear2, tokens, sms));
     linear = std::max(linear, linear_scratch_bytes(ly.ca_in_proj, prompt_tokens, sms));
     // h, qk_in [T][D]; q|k [T][2D]; v, att, y [T][D]; ffn [T][F]; prompt k|v [P][2D];
-    // the self-attention's K / V^T TF32 hi / lo planes 4 [T][D]
-    const size_t floats = static_cast<size_t>(tokens) * (D * 2 + 2 * D + 3 * D + F) + prompt_tokens * 2 * D +
-                          static_cast<size_t>(tokens) * 4 * D;
-    return floats * sizeof(float) + linear + 16 * 256;
+    // the self-attention's tensor-core scratch (K / V^T TF32 planes, key-split partials)
+    const size_t floats = static_cast<size_t>(tokens) * (D * 2 + 2 * D + 3 * D + F) + prompt_tokens * 2 * D;
+    return floats * sizeof(float) + attention_tc_scratch_bytes(static_cast<int>(tokens), static_cast<int>(tokens), ly.heads,
+                                                               static_cast<int>(D / ly.heads)) +
+           linear + 16 * 256;
 }
 
 void launch_fusion_layer(const samq_fusion_layer_v1& ly, float* x, const float* pos, int64_t tokens,
@@ -136,7 +137,8 @@ void launch_fusion_layer(const samq_fusion_layer_v1& ly, float* x, const float* 
     float* y = take(tokens * D);
     float* ffn = take(tokens * F);
     float* pkv = take(prompt_tokens * 2 * D);
-    float* planes = take(tokens * 4 * D);
+    float* planes = take(static_cast<int64_t>(
+        attention_tc_scratch_bytes(static_cast<int>(tokens), static_cast<int>(tokens), heads, hd) / sizeof(float)));
     void* lin = reinterpret_cast<void*>(cursor);
 
     // Self-attention: positions added to the queries' and keys' input only.

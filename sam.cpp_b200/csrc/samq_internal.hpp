@@ -221,9 +221,12 @@ size_t attention_partial_floats(int lq, int lk, int heads, int head_dim, int cau
 // for many queries and keys without a mask.
 bool attention_tc_eligible(int lq, int lk, int head_dim, int causal, const float* bias, const float* out,
                            int64_t ldo);
-// `planes` as for launch_attention_tc_groups (nullptr: the loader-fed kernel).
+// `scratch` (attention_tc_scratch_bytes, 256-byte aligned; nullptr: the
+// loader-fed kernel over all keys) holds the K / V^T TF32 planes and the
+// key-split partials merged by launch_attention_combine.
+size_t attention_tc_scratch_bytes(int lq, int lk, int heads, int head_dim);
 void launch_attention_tc(const float* q, int64_t ldq, const float* k, int64_t ldk, const float* v, int64_t ldv,
-                         int lq, int lk, int heads, int head_dim, float scale, float* out, int64_t ldo, float* planes,
+                         int lq, int lk, int heads, int head_dim, float scale, float* out, int64_t ldo, float* scratch,
                          DeviceState& state, cudaStream_t stream);
 // Grouped form for the ViT: qkv rows [groups * group_n][ldq] (Q, K, V at
 // column 0, embed, 2 embed), one attention per group; output rows in raster
@@ -244,8 +247,13 @@ void launch_attention_gen(const float* q, int64_t ldq, const float* k, int64_t l
                           int64_t bias_h, int64_t bias_q, float* out, int64_t ldo, DeviceState& state,
                           cudaStream_t stream, float* partials = nullptr, size_t partial_floats = 0,
                           float* tc_planes = nullptr);
+// Merge of key-split partials [splits][heads][lq][head_dim + 2] (unnormalized
+// O, the row maximum in natural-log units, the row sum) into out rows.
+void launch_attention_combine(const float* part, int splits, int heads, int lq, int head_dim, float* out,
+                              int64_t ldo, cudaStream_t stream);
 // Scratch a launch_attention_gen caller may pass as `tc_planes`: the K / V^T
-// TF32 planes of the tensor-core path when the shape takes it, else 0.
+// TF32 planes of the tensor-core path when the shape takes it (plus the
+// key-split partials it may use), else 0.
 size_t attention_gen_plane_bytes(int lq, int lk, int heads, int head_dim, int causal, const float* bias,
                                  const float* out, int64_t ldo);
 // sam3_apply_rope on [head_batches][tokens][64] f32 with GGML's rounding.
