@@ -615,7 +615,7 @@ size_t attention_tc_plane_bytes(int groups, int group_n, int heads, int head_dim
 // at least 8 key tiles per split.
 constexpr int kMaxKeySplits = 4;
 
-int tc_key_splits(int lq, int lk, int heads, int sms) {
+static int tc_key_splits(int lq, int lk, int heads, int sms) {
     const int64_t ctas = int64_t((lq + kQ - 1) / kQ) * heads;
     const int tiles = (lk + kKeys - 1) / kKeys;
     double cost[kMaxKeySplits + 1] = {};
@@ -631,12 +631,12 @@ int tc_key_splits(int lq, int lk, int heads, int sms) {
     return 1;
 }
 
-size_t tc_partial_floats(int lq, int heads, int head_dim) {
+static size_t tc_partial_floats(int lq, int heads, int head_dim) {
     return static_cast<size_t>(kMaxKeySplits) * heads * lq * (head_dim + 2);
 }
 
 template <int HD>
-void launch_groups(TcArgs a, int heads, int groups, float* planes, float* part, DeviceState& state,
+static void launch_groups(TcArgs a, int heads, int groups, float* planes, float* part, DeviceState& state,
                    cudaStream_t stream) {
     const int lk = a.lk;
     int splits = 1;
