@@ -509,7 +509,8 @@ def main():
     gemm_flops = [2.0 * M * n * k for _, n, k, *_ in LINEARS]
     achieved = sum(gemm_flops) / (sum(gemm_ms) / 1e3) / 1e12
     traffic = profiled_traffic()
-    roofline = {"bound": "tensor", "kernel": "gemm_f16_kernel (tcgen05 kind::f16, f32 accumulate)",
+    roofline = {"bound": "tensor", "kernel": "K2: gemm_f16_pair_kernel (cta_group::2, qkv / fc1) and gemm_f16_kernel "
+                          "(proj / fc2); tcgen05 kind::f16, f32 accumulate",
                 "achieved": achieved, "peak": pk["bf16_tflops"], "unit": "TFLOP/s",
                 "frac": achieved / pk["bf16_tflops"], "peak_source": f"{pk['source']} bf16 (of measured)",
                 "frac_of_sustained": achieved / pk["bf16_tflops_sustained"],
